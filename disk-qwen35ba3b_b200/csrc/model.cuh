@@ -1,0 +1,85 @@
+// model.cuh -- the HBM-resident expert pool and per-layer trunk weights
+// (the device-side replacement of the reference's disk pool + LRU cache,
+// src/cache.c:140-214 / src/st.c:127-180), and the MoE-step workspace.
+#pragma once
+
+#include "common.cuh"
+
+namespace ds4f {
+
+struct ModelDesc {
+    int fmt;              // DS4F_FMT_FP8 or DS4F_FMT_MXFP4 (routed experts)
+    int n_layers;
+    int hidden;           // H
+    int moe_inter;        // M
+    int n_experts;        // E
+    int topk;             // K
+    int renorm;           // norm_topk_prob
+    int expert_first;     // expert shard [first, first + count) held here
+    int expert_count;
+    int router_exact;     // 1: every router logit in the reference's exact
+                          //    sequential fp32 order (slow, bit-exact weights)
+};
+
+// Expert slot layout: gate, up, down, each values then scales, in the
+// reference converter's manifest order (tools/convert-ds4f.py:1321-1356).
+struct SlotLayout {
+    int64_t rel_v[3], rel_s[3], nbytes;
+};
+
+// Per-layer trunk (bf16) offsets, in elements from the layer base.
+struct TrunkLayout {
+    int64_t norm, router, sh_gate, sh_up, sh_down, sh_gw, n;
+};
+
+// Device workspace for one token's layer step.
+struct Work {
+    float *xin;           // [H] normed input
+    double *S;            // [E] router logits (exact-sum in double)
+    double *Bnd;          // [E] bound |reference fp32 logit - S|
+    int *idx;             // [K] selected experts, selection order
+    float *w;             // [K] routing weights (after renorm)
+    float *chain;         // [(K+1) M] silu(g)*u per selection, shared last
+    float *sgate;         // [1] shared_expert_gate logit
+    float *acc;           // [H] moe output before the residual
+    unsigned *diag;       // [4] 0: layers routed, 1: exact fallbacks, 2: error
+};
+
+struct Model {
+    ModelDesc d;
+    SlotLayout slot;
+    TrunkLayout tr;
+    int device;
+    uint8_t *pool;        // [L][count] slots
+    uint16_t *trunk;      // [L] trunk blocks
+    Work w;
+    void *ws_base;
+    float *state_dev;     // [Bmax H] staging for the host-buffer API
+    int *idx_dev;
+    float *w_dev;
+    int bmax;
+    cudaStream_t stream;
+    cudaGraphExec_t graph;       // captured stack step (B = 1)
+    float *graph_state;
+    int graph_ok;
+};
+
+int slot_layout(int fmt, int H, int M, SlotLayout *s);
+int trunk_layout(int H, int M, int E, TrunkLayout *t);
+
+// One token through layer L: state (device, [H]) updated in place; idx / w
+// (device, [K]) optional copies of the routing.
+int moe_layer_launch(Model *m, int L, float *state, int *idx_out,
+                     float *w_out, cudaStream_t st);
+
+// GPU copy of the seeded fixture generator (oracle/fixture.c): fills the
+// model's trunk and expert shard.
+int synth_model(Model *m, uint64_t seed, double sigma, cudaStream_t st);
+int synth_f32(float *dst, int64_t n, uint64_t key, double sigma, cudaStream_t st);
+
+inline const uint8_t *expert_ptr(const Model *m, int L, int e) {
+    return m->pool + ((int64_t)L * m->d.expert_count + (e - m->d.expert_first)) *
+                         m->slot.nbytes;
+}
+
+}  // namespace ds4f

@@ -1,0 +1,592 @@
+// moe.cu -- one Qwen3.5 MoE layer for one token on the GPU: RMSNorm,
+// router logits, certified top-k + softmax + renorm, fused gate/up +
+// SiLU-mul for the top-k experts and the shared expert, fused down +
+// selection-order combine + shared-gate + residual.
+//
+// Reference: ds4f_moe_step (src/moe.c:948-1456, Qwen3.5 no-mHC branch),
+// its router call site (src/main.c:1014-1088) and ds4f_topk
+// (src/moe.c:531-561). The host/GPU round trips of the reference's Metal
+// path (two dispatches plus a CPU SiLU per layer, src/moe.c:1105-1150)
+// become four kernels that never leave the device.
+#include "model.cuh"
+
+#include <algorithm>
+
+namespace ds4f {
+
+namespace {
+
+constexpr int kRouteWarps = 8;
+constexpr double kUnitRoundoff = 5.9604644775390625e-08;   // 2^-24
+
+// ---------------------------------------------------------------------------
+// RMSNorm into shared memory (src/moe.c:841-851; the router's copy
+// src/main.c:1014-1033 is identical): sum of squares in double, r =
+// sqrtf(float(ss / H) + 1e-6f), x / r * w with IEEE division. The sum
+// order is a fixed tree (thread-strided partials, xor-butterfly, warps in
+// order), so every CTA and every run gets the same bits.
+// ---------------------------------------------------------------------------
+__device__ void rmsnorm_smem(const float *__restrict__ state,
+                             const uint16_t *__restrict__ norm, int H,
+                             float *xs, double *red, float prescale) {
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        double v = (double)state[i];
+        ss = __dadd_rn(ss, __dmul_rn(v, v));
+    }
+    ss = warp_sum_d(ss);
+    int nw = blockDim.x >> 5;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < nw; k++) t = __dadd_rn(t, red[k]);
+        red[32] = t;
+    }
+    __syncthreads();
+    float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(red[32], (double)H)),
+                                   1e-6f));
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+        xs[i] = __fmul_rn(__fmul_rn(__fdiv_rn(state[i], r), bf16_to_f32(norm[i])),
+                          prescale);
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Router logits with a certificate. The reference sums each row
+// sequentially in fp32: s_c = fl(s_{c-1} + p_c), p_c = fl(w_c x_c)
+// (ds4f_bf16_matvec scalar, src/kernels.c:97-102). Here S = sum p_c in
+// double (products bit-identical to the reference's), and
+//   |s_n - S| <= u sum_c |S_c| / (1 - n u),   S_c = exact prefix sums,
+// bounded per 8-element chunk q (prefix P_q) by 8|P_q| + sum_t |p_t|(8-t).
+// Bnd = 1.001 u * that sum (the 1.001 covers 1/(1-nu) and double rounding).
+// k_topk decides the top-k from [S - Bnd, S + Bnd] and recomputes exact
+// fp32 sums only when two candidates' intervals overlap.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+k_route(const float *__restrict__ state, const uint16_t *__restrict__ trunk_l,
+        TrunkLayout tr, int H, int E, float *__restrict__ xin_out,
+        double *__restrict__ S, double *__restrict__ Bnd) {
+    extern __shared__ float xs[];
+    __shared__ double red[33];
+    rmsnorm_smem(state, trunk_l + tr.norm, H, xs, red, 1.0f);
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < H; i += blockDim.x) xin_out[i] = xs[i];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x * kRouteWarps + warp;
+    if (e >= E) return;
+    const uint16_t *row = trunk_l + tr.router + (int64_t)e * H;
+    const int rounds = H / 256;
+    double base = 0.0, bsum = 0.0;
+    for (int k = 0; k < rounds; k++) {
+        int q = lane + 32 * k;
+        uint4 w = ldg_stream(row + q * 8);
+        const float *x = xs + q * 8;
+        uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        double T = 0.0, A = 0.0;
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            uint32_t h = (t & 1) ? (ww[t >> 1] & 0xFFFF0000u) : (ww[t >> 1] << 16);
+            float p = __fmul_rn(__uint_as_float(h), x[t]);
+            T = __dadd_rn(T, (double)p);
+            A = __dadd_rn(A, (double)fabsf(p) * (double)(8 - t));
+        }
+        double incl = T;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl = __dadd_rn(incl, y);
+        }
+        double excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+        if (lane == 0) excl = 0.0;
+        double P = __dadd_rn(base, excl);
+        bsum = __dadd_rn(bsum, __dadd_rn(8.0 * fabs(P), A));
+        base = __dadd_rn(base, __shfl_sync(0xFFFFFFFFu, incl, 31));
+    }
+    bsum = warp_sum_d(bsum);
+    if (lane == 0) {
+        S[e] = base;
+        Bnd[e] = 1.001 * kUnitRoundoff * bsum + 1e-300;
+    }
+}
+
+// Exact reference-order fp32 logit of router row e (the fallback).
+__device__ float exact_logit(const uint16_t *__restrict__ row,
+                             const float *__restrict__ xs, int H) {
+    float acc = 0.0f;
+    for (int c = 0; c < H; c++)
+        acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(row[c]), xs[c]));
+    return acc;   // + 0.0f bias (src/kernels.c:101) changes nothing but -0
+}
+
+// ---------------------------------------------------------------------------
+// Top-k (src/moe.c:531-561) from the certified logits, one CTA.
+// Selection: descending, lower index first among equal values. Weights:
+// softmax over all E in double with the max subtracted, the selected
+// probabilities kept, then (renorm) divided by their fp32 sum in j order.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
+       const float *__restrict__ xin, const uint16_t *__restrict__ router,
+       int H, int E, int K, int renorm, int exact_all, int *__restrict__ idx_out,
+       float *__restrict__ w_out, unsigned *__restrict__ diag) {
+    extern __shared__ unsigned char sm[];
+    double *lo = (double *)sm;
+    double *hi = lo + E;
+    float *v = (float *)(hi + E);
+    int *cand = (int *)(v + E);
+    int *rk = cand + E;
+    float *xs = (float *)(rk + E);
+    __shared__ double lk_s, red[8];
+    __shared__ int ncand_s, cert_s, sel_s[64];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < E; e += blockDim.x) {
+        double b = exact_all ? 0.0 : Bnd[e];
+        lo[e] = S[e] - b;
+        hi[e] = S[e] + b;
+        v[e] = (float)S[e];
+    }
+    if (tid == 0) { ncand_s = 0; cert_s = 1; }
+    __syncthreads();
+    if (!exact_all) {
+        // K-th largest lower bound
+        for (int e = tid; e < E; e += blockDim.x) {
+            int r = 0;
+            double le = lo[e];
+            for (int f = 0; f < E; f++) r += (lo[f] > le) || (lo[f] == le && f < e);
+            if (r == K - 1) lk_s = le;
+        }
+        __syncthreads();
+        double lk = lk_s;
+        for (int e = tid; e < E; e += blockDim.x) {
+            cand[e] = hi[e] >= lk;
+            if (cand[e]) atomicAdd(&ncand_s, 1);
+        }
+        __syncthreads();
+        if (ncand_s != K) cert_s = 0;
+        __syncthreads();
+        if (cert_s) {
+            // order by S among candidates; adjacent intervals must separate
+            for (int e = tid; e < E; e += blockDim.x) {
+                rk[e] = -1;
+                if (!cand[e]) continue;
+                int r = 0;
+                for (int f = 0; f < E; f++)
+                    r += cand[f] && (S[f] > S[e] || (S[f] == S[e] && f < e));
+                rk[e] = r;
+                sel_s[r] = e;
+            }
+            __syncthreads();
+            for (int r = tid; r + 1 < K; r += blockDim.x)
+                if (!(lo[sel_s[r]] > hi[sel_s[r + 1]])) cert_s = 0;
+            __syncthreads();
+        }
+    }
+    if (exact_all || !cert_s) {
+        // exact reference-order logits for every candidate (all experts in
+        // exact mode), then select on them
+        for (int i = tid; i < H; i += blockDim.x) xs[i] = xin[i];
+        __syncthreads();
+        for (int e = tid; e < E; e += blockDim.x) {
+            if (exact_all) cand[e] = 1;
+            if (cand[e]) v[e] = exact_logit(router + (int64_t)e * H, xs, H);
+        }
+        __syncthreads();
+        for (int e = tid; e < E; e += blockDim.x) {
+            if (!cand[e]) continue;
+            int r = 0;
+            for (int f = 0; f < E; f++)
+                r += cand[f] && (v[f] > v[e] || (v[f] == v[e] && f < e));
+            if (r < K) sel_s[r] = e;
+        }
+        if (tid == 0 && !exact_all) atomicAdd(diag + 1, 1u);
+        __syncthreads();
+    }
+    // softmax over all E in double, max subtracted
+    double mx = -1e300;
+    for (int e = 0; e < E; e++) mx = fmax(mx, (double)v[e]);
+    double part = 0.0;
+    for (int e = tid; e < E; e += blockDim.x) part += exp((double)v[e] - mx);
+    part = warp_sum_d(part);
+    if ((tid & 31) == 0) red[tid >> 5] = part;
+    __syncthreads();
+    if (tid == 0) {
+        double sw = 0.0;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) sw += red[k];
+        float wj[64];
+        float s = 0.0f;
+        for (int j = 0; j < K; j++) {
+            int e = sel_s[j];
+            wj[j] = (float)(exp((double)v[e] - mx) / sw);
+            s = __fadd_rn(s, wj[j]);
+        }
+        for (int j = 0; j < K; j++) {
+            idx_out[j] = sel_s[j];
+            w_out[j] = (renorm && s > 0.0f) ? __fdiv_rn(wj[j], s) : wj[j];
+        }
+        atomicAdd(diag, 1u);
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// Row-dot building blocks. A lane holds its columns of x in registers and
+// dots them with 16-byte chunks of a weight row of C elements:
+//   FP8   chunk = 16 E4M3,  MXFP4 chunk = 32 E2M1,  BF16 chunk = 8 bf16.
+// lpr = lanes per row = min(32, C / chunk); a warp covers 32 / lpr rows per
+// step; lane chunks are q = lane % lpr + lpr * k, k < kch. x is pre-scaled
+// by 2^64 (common.cuh) so every product stays a normal float; each
+// chunk's partial dot is rescaled with its block scale.
+// ---------------------------------------------------------------------------
+template <int FMT> struct Chunk;
+template <> struct Chunk<DS4F_FMT_FP8>   { static constexpr int ce = 16; };
+template <> struct Chunk<DS4F_FMT_MXFP4> { static constexpr int ce = 32; };
+template <> struct Chunk<3>              { static constexpr int ce = 8; };   // bf16
+constexpr int kBF16 = 3;
+
+template <int FMT, int C>
+struct RowGeom {
+    static constexpr int ce = Chunk<FMT>::ce;
+    static constexpr int nq = C / ce;
+    static constexpr int lpr = nq < 32 ? nq : 32;
+    static constexpr int kch = nq / lpr;
+    static constexpr int rps = 32 / lpr;
+    static constexpr int bytes = FMT == DS4F_FMT_FP8 ? C : FMT == DS4F_FMT_MXFP4 ? C / 2 : 2 * C;
+    static_assert(nq * ce == C && kch * lpr == nq && (lpr & (lpr - 1)) == 0,
+                  "row length must split into power-of-two lane groups");
+};
+
+template <int FMT, int C>
+__device__ __forceinline__ void load_x(float (&x)[RowGeom<FMT, C>::kch * RowGeom<FMT, C>::ce],
+                                       const float *xs) {
+    using G = RowGeom<FMT, C>;
+    const int ql = (threadIdx.x & 31) % G::lpr;
+#pragma unroll
+    for (int k = 0; k < G::kch; k++) {
+        const float4 *src = (const float4 *)(xs + (ql + G::lpr * k) * G::ce);
+#pragma unroll
+        for (int e = 0; e < G::ce / 4; e++) {
+            float4 v = src[e];
+            x[k * G::ce + 4 * e] = v.x;     x[k * G::ce + 4 * e + 1] = v.y;
+            x[k * G::ce + 4 * e + 2] = v.z; x[k * G::ce + 4 * e + 3] = v.w;
+        }
+    }
+}
+
+template <int FMT, int C>
+__device__ __forceinline__ void load_row(uint4 (&b)[RowGeom<FMT, C>::kch],
+                                         const uint8_t *row) {
+    using G = RowGeom<FMT, C>;
+    const int ql = (threadIdx.x & 31) % G::lpr;
+#pragma unroll
+    for (int k = 0; k < G::kch; k++) b[k] = ldg_stream(row + (ql + G::lpr * k) * 16);
+}
+
+// Sum over the row of chunk_dot * scale(q); returned per lane (reduce over
+// the lpr lanes of the row with row_reduce).
+template <int FMT, int C, typename ScaleFn>
+__device__ __forceinline__ float row_partial(const uint4 (&b)[RowGeom<FMT, C>::kch],
+                                             const float (&x)[RowGeom<FMT, C>::kch * RowGeom<FMT, C>::ce],
+                                             ScaleFn scale) {
+    using G = RowGeom<FMT, C>;
+    const int ql = (threadIdx.x & 31) % G::lpr;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < G::kch; k++) {
+        const int q = ql + G::lpr * k;
+        if constexpr (FMT == DS4F_FMT_FP8) {
+            acc = fmaf(f8_dot16(b[k], x + k * G::ce) * DS4F_F8_POST, scale(q), acc);
+        } else if constexpr (FMT == DS4F_FMT_MXFP4) {
+            acc = fmaf(e2m1_dot32(b[k], x + k * G::ce) * DS4F_E2M1_POST, scale(q), acc);
+        } else {
+            acc += bf16_dot8(b[k], x + k * G::ce);
+        }
+    }
+    return acc;
+}
+
+template <int LPR>
+__device__ __forceinline__ float row_reduce(float v) {
+#pragma unroll
+    for (int o = LPR >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// FP8 fp32 128x128 block scale for (row r, chunk q) of a [R x C] matrix.
+template <int C>
+__device__ __forceinline__ float f8s(const float *s, int r, int q) {
+    return __ldg(s + (r >> 7) * (C / 128) + (q >> 3));
+}
+// MXFP4 E8M0 scale for (row r, chunk q): flat block (r*C + 32q) / 32.
+template <int C>
+__device__ __forceinline__ float mxs(const uint8_t *s, int r, int q) {
+    return e8m0_to_f32(__ldg(s + r * (C / 32) + q));
+}
+
+struct LayerArgs {
+    const uint8_t *pool_l;       // expert slots of layer L (first expert = efirst)
+    int64_t slot_bytes;
+    SlotLayout slot;
+    const uint16_t *trunk_l;
+    TrunkLayout tr;
+    int E, K, efirst, ecount;
+    const int *idx;
+    const float *w;
+    const float *xin;
+    float *chain;                // [(K+1) M]
+    float *sgate;
+    float *state;                // [H] in/out
+    float *acc_out;              // [H] or null
+};
+
+// ---------------------------------------------------------------------------
+// gate/up + SiLU-mul. Static partition: CTA c of G owns routed (selection,
+// row) pairs [c KM/G, (c+1) KM/G) and shared rows [c M/G, (c+1) M/G); each
+// warp takes two pairs at a time (gate and up rows of both in flight). The
+// shared_expert_gate dot (1 x H bf16) goes to the last CTA.
+// chain[j M + i] = silu(gate_j x)_i * (up_j x)_i   (src/moe.c:619-649)
+// ---------------------------------------------------------------------------
+template <int FMT, int H, int M>
+__global__ void __launch_bounds__(256)
+k_gateup(LayerArgs a) {
+    __shared__ __align__(16) float xs[H];
+    using G = RowGeom<FMT, H>;
+    using GB = RowGeom<kBF16, H>;
+    static_assert(G::lpr == 32 && GB::lpr == 32, "gate/up rows span a warp");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = a.xin[i] * DS4F_X_PRESCALE;
+    __syncthreads();
+    const int nb = gridDim.x, cb = blockIdx.x;
+    const int P = a.K * M;
+    const int p0 = (int)((int64_t)cb * P / nb), p1 = (int)((int64_t)(cb + 1) * P / nb);
+    {
+        float x[G::kch * G::ce];
+        load_x<FMT, H>(x, xs);
+        for (int pp = p0 + 2 * warp; pp < p1; pp += 16) {
+            uint4 bg[2][G::kch], bu[2][G::kch];
+            const uint8_t *base[2];
+            int ii[2], jj[2];
+#pragma unroll
+            for (int t = 0; t < 2; t++) {
+                int p = min(pp + t, p1 - 1);
+                jj[t] = p / M; ii[t] = p % M;
+                base[t] = a.pool_l + (int64_t)(a.idx[jj[t]] - a.efirst) * a.slot_bytes;
+                load_row<FMT, H>(bg[t], base[t] + a.slot.rel_v[0] + (int64_t)ii[t] * G::bytes);
+                load_row<FMT, H>(bu[t], base[t] + a.slot.rel_v[1] + (int64_t)ii[t] * G::bytes);
+            }
+#pragma unroll
+            for (int t = 0; t < 2; t++) {
+                float g, u;
+                if constexpr (FMT == DS4F_FMT_FP8) {
+                    const float *sg = (const float *)(base[t] + a.slot.rel_s[0]);
+                    const float *su = (const float *)(base[t] + a.slot.rel_s[1]);
+                    g = row_partial<FMT, H>(bg[t], x, [&](int q) { return f8s<H>(sg, ii[t], q); });
+                    u = row_partial<FMT, H>(bu[t], x, [&](int q) { return f8s<H>(su, ii[t], q); });
+                } else {
+                    const uint8_t *sg = base[t] + a.slot.rel_s[0];
+                    const uint8_t *su = base[t] + a.slot.rel_s[1];
+                    g = row_partial<FMT, H>(bg[t], x, [&](int q) { return mxs<H>(sg, ii[t], q); });
+                    u = row_partial<FMT, H>(bu[t], x, [&](int q) { return mxs<H>(su, ii[t], q); });
+                }
+                g = warp_sum(g);
+                u = warp_sum(u);
+                if (lane == 0 && pp + t < p1) a.chain[jj[t] * M + ii[t]] = silu_mul(g, u);
+            }
+        }
+    }
+    {
+        float x[GB::kch * GB::ce];
+        load_x<kBF16, H>(x, xs);
+        const int s0 = (int)((int64_t)cb * M / nb), s1 = (int)((int64_t)(cb + 1) * M / nb);
+        const uint8_t *tg = (const uint8_t *)(a.trunk_l + a.tr.sh_gate);
+        const uint8_t *tu = (const uint8_t *)(a.trunk_l + a.tr.sh_up);
+        auto none = [](int) { return 1.0f; };
+        for (int i = s0 + warp; i < s1; i += 8) {
+            uint4 bg[GB::kch], bu[GB::kch];
+            load_row<kBF16, H>(bg, tg + (int64_t)i * GB::bytes);
+            load_row<kBF16, H>(bu, tu + (int64_t)i * GB::bytes);
+            float g = warp_sum(row_partial<kBF16, H>(bg, x, none)) * DS4F_BF16_POST;
+            float u = warp_sum(row_partial<kBF16, H>(bu, x, none)) * DS4F_BF16_POST;
+            if (lane == 0) a.chain[a.K * M + i] = silu_mul(g, u);
+        }
+        if (cb == nb - 1 && warp == 7) {
+            uint4 bw[GB::kch];
+            load_row<kBF16, H>(bw, (const uint8_t *)(a.trunk_l + a.tr.sh_gw));
+            float g = warp_sum(row_partial<kBF16, H>(bw, x, none)) * DS4F_BF16_POST;
+            if (lane == 0) *a.sgate = g;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// down + combine + shared gate + residual. CTA c owns output rows
+// [c H/G, (c+1) H/G). Warp j < K computes down_j(chain_j) for those rows,
+// warp K the shared expert's bf16 down; then one thread per row combines
+// in selection order (src/moe.c:1203-1227), adds sigmoid(sgate) * shared
+// (:1279-1282) and the residual (:1424).
+// ---------------------------------------------------------------------------
+constexpr int kDownMaxRows = 32;
+
+template <int FMT, int H, int M>
+__global__ void __launch_bounds__(544)
+k_down(LayerArgs a) {
+    __shared__ __align__(16) float cs[17][M];
+    __shared__ float outs[17][kDownMaxRows];
+    using G = RowGeom<FMT, M>;
+    using GB = RowGeom<kBF16, M>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int K = a.K;
+    for (int i = threadIdx.x; i < (K + 1) * M; i += blockDim.x)
+        cs[i / M][i % M] = a.chain[i] * DS4F_X_PRESCALE;
+    __syncthreads();
+    const int nb = gridDim.x, cb = blockIdx.x;
+    const int r0 = (int)((int64_t)cb * H / nb), r1 = (int)((int64_t)(cb + 1) * H / nb);
+    const int nr = r1 - r0;
+    if (warp < K) {
+        float x[G::kch * G::ce];
+        load_x<FMT, M>(x, cs[warp]);
+        const uint8_t *base = a.pool_l + (int64_t)(a.idx[warp] - a.efirst) * a.slot_bytes;
+        const uint8_t *dv = base + a.slot.rel_v[2];
+        const int sub = lane / G::lpr;
+        for (int rr = 0; rr < nr; rr += 4 * G::rps) {
+            uint4 b[4][G::kch];
+            int rows[4];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                rows[t] = min(r0 + rr + t * G::rps + sub, r1 - 1);
+                load_row<FMT, M>(b[t], dv + (int64_t)rows[t] * G::bytes);
+            }
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                float v;
+                if constexpr (FMT == DS4F_FMT_FP8) {
+                    const float *sd = (const float *)(base + a.slot.rel_s[2]);
+                    v = row_partial<FMT, M>(b[t], x, [&](int q) { return f8s<M>(sd, rows[t], q); });
+                } else {
+                    const uint8_t *sd = base + a.slot.rel_s[2];
+                    v = row_partial<FMT, M>(b[t], x, [&](int q) { return mxs<M>(sd, rows[t], q); });
+                }
+                v = row_reduce<G::lpr>(v);
+                int lr = rr + t * G::rps + sub;
+                if (lane % G::lpr == 0 && lr < nr) outs[warp][lr] = v;
+            }
+        }
+    } else if (warp == K) {
+        float x[GB::kch * GB::ce];
+        load_x<kBF16, M>(x, cs[K]);
+        const uint8_t *dv = (const uint8_t *)(a.trunk_l + a.tr.sh_down);
+        const int sub = lane / GB::lpr;
+        auto none = [](int) { return 1.0f; };
+        for (int rr = 0; rr < nr; rr += 4 * GB::rps) {
+            uint4 b[4][GB::kch];
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+                load_row<kBF16, M>(b[t], dv + (int64_t)min(r0 + rr + t * GB::rps + sub, r1 - 1) * GB::bytes);
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                float v = row_reduce<GB::lpr>(row_partial<kBF16, M>(b[t], x, none)) * DS4F_BF16_POST;
+                int lr = rr + t * GB::rps + sub;
+                if (lane % GB::lpr == 0 && lr < nr) outs[K][lr] = v;
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < nr) {
+        const int t = threadIdx.x, r = r0 + t;
+        float acc = 0.0f;
+        for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(a.w[j], outs[j][t]));
+        float sg = sigmoid_ref(*a.sgate);
+        acc = __fadd_rn(acc, __fmul_rn(sg, outs[K][t]));
+        if (a.acc_out) a.acc_out[r] = acc;
+        a.state[r] = __fadd_rn(a.state[r], acc);
+    }
+}
+
+int num_sms() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+template <int FMT, int H, int M>
+int launch_chain(const LayerArgs &a, cudaStream_t st) {
+    int G = num_sms();
+    k_gateup<FMT, H, M><<<G, 256, 0, st>>>(a);
+    DS4F_CUDA(cudaGetLastError());
+    int Gd = std::max(G, (H + kDownMaxRows - 1) / kDownMaxRows);
+    k_down<FMT, H, M><<<Gd, 32 * (a.K + 1), 0, st>>>(a);
+    DS4F_CUDA(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace
+
+int slot_layout(int fmt, int H, int M, SlotLayout *s) {
+    int64_t mh = (int64_t)M * H, vb, sb;
+    if (fmt == DS4F_FMT_FP8) {
+        DS4F_REQUIRE(H % 128 == 0 && M % 128 == 0, "FP8 pool needs H, M multiples of 128");
+        vb = mh; sb = (int64_t)(M / 128) * (H / 128) * 4;
+    } else if (fmt == DS4F_FMT_MXFP4) {
+        DS4F_REQUIRE(H % 32 == 0 && M % 32 == 0, "MXFP4 pool needs H, M multiples of 32");
+        vb = mh / 2; sb = mh / 32;
+    } else {
+        DS4F_REQUIRE(false, "unknown expert format %d", fmt);
+    }
+    int64_t off = 0;
+    for (int t = 0; t < 3; t++) {
+        s->rel_v[t] = off; off += vb;
+        s->rel_s[t] = off; off += sb;
+    }
+    s->nbytes = off;
+    return 0;
+}
+
+int trunk_layout(int H, int M, int E, TrunkLayout *t) {
+    auto al = [](int64_t n) { return (n + 127) / 128 * 128; };   // 256 B
+    int64_t o = 0;
+    t->norm = o; o += al(H);
+    t->router = o; o += al((int64_t)E * H);
+    t->sh_gate = o; o += al((int64_t)M * H);
+    t->sh_up = o; o += al((int64_t)M * H);
+    t->sh_down = o; o += al((int64_t)H * M);
+    t->sh_gw = o; o += al(H);
+    t->n = o;
+    return 0;
+}
+
+int moe_layer_launch(Model *m, int L, float *state, int *idx_out, float *w_out,
+                     cudaStream_t st) {
+    const ModelDesc &d = m->d;
+    const int H = d.hidden, M = d.moe_inter, E = d.n_experts, K = d.topk;
+    const uint16_t *trunk_l = m->trunk + (int64_t)L * m->tr.n;
+    Work &w = m->w;
+    k_route<<<(E + kRouteWarps - 1) / kRouteWarps, 256, H * sizeof(float), st>>>(
+        state, trunk_l, m->tr, H, E, w.xin, w.S, w.Bnd);
+    DS4F_CUDA(cudaGetLastError());
+    size_t tk_smem = (size_t)E * (8 + 8 + 4 + 4 + 4) + (size_t)H * 4;
+    k_topk<<<1, 256, tk_smem, st>>>(w.S, w.Bnd, w.xin, trunk_l + m->tr.router, H, E,
+                                    K, d.renorm, d.router_exact, w.idx, w.w, w.diag);
+    DS4F_CUDA(cudaGetLastError());
+    LayerArgs a;
+    a.pool_l = m->pool + (int64_t)L * d.expert_count * m->slot.nbytes;
+    a.slot_bytes = m->slot.nbytes;
+    a.slot = m->slot;
+    a.trunk_l = trunk_l;
+    a.tr = m->tr;
+    a.E = E; a.K = K; a.efirst = d.expert_first; a.ecount = d.expert_count;
+    a.idx = w.idx; a.w = w.w; a.xin = w.xin; a.chain = w.chain; a.sgate = w.sgate;
+    a.state = state; a.acc_out = w.acc;
+    int rc;
+    if (d.fmt == DS4F_FMT_FP8 && H == 2048 && M == 512) rc = launch_chain<DS4F_FMT_FP8, 2048, 512>(a, st);
+    else if (d.fmt == DS4F_FMT_MXFP4 && H == 2048 && M == 512) rc = launch_chain<DS4F_FMT_MXFP4, 2048, 512>(a, st);
+    else if (d.fmt == DS4F_FMT_FP8 && H == 1024 && M == 256) rc = launch_chain<DS4F_FMT_FP8, 1024, 256>(a, st);
+    else if (d.fmt == DS4F_FMT_MXFP4 && H == 1024 && M == 256) rc = launch_chain<DS4F_FMT_MXFP4, 1024, 256>(a, st);
+    else { set_error("moe layer: no kernel for fmt %d H %d M %d", d.fmt, H, M); return -1; }
+    if (rc) return rc;
+    if (idx_out) DS4F_CUDA(cudaMemcpyAsync(idx_out, w.idx, K * sizeof(int), cudaMemcpyDeviceToDevice, st));
+    if (w_out) DS4F_CUDA(cudaMemcpyAsync(w_out, w.w, K * sizeof(float), cudaMemcpyDeviceToDevice, st));
+    return 0;
+}
+
+}  // namespace ds4f

@@ -1,0 +1,277 @@
+"""ctypes binding of libds4f_cuda (include/ds4f/gpu_cuda.h).
+
+The C ABI is the product boundary; this module mirrors it for Python
+callers (tests, bench). It loads the in-tree libds4f_cuda.so and fails
+loudly when it is missing: there is no CPU fallback.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libds4f_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "ds4f", "gpu_cuda.h")
+
+FMT_MXFP4, FMT_MLX4, FMT_FP8, FMT_BF16 = 0, 1, 2, 3
+SCALE_E8M0, SCALE_F32 = 0, 1
+
+_vp = C.c_void_p
+
+
+class GpuError(RuntimeError):
+    pass
+
+
+class Ds4fMvJob(C.Structure):
+    _fields_ = [("w", _vp), ("scales", _vp), ("x", _vp), ("y", _vp),
+                ("R", C.c_int), ("C", C.c_int), ("SR", C.c_int), ("SC", C.c_int),
+                ("fmt", C.c_int), ("scale_kind", C.c_int), ("bsize", C.c_int),
+                ("canon", C.c_int)]
+
+
+class Ds4fGpuModelDesc(C.Structure):
+    _fields_ = [("fmt", C.c_int), ("n_layers", C.c_int), ("hidden", C.c_int),
+                ("moe_inter", C.c_int), ("n_experts", C.c_int), ("topk", C.c_int),
+                ("renorm", C.c_int), ("expert_first", C.c_int),
+                ("expert_count", C.c_int), ("router_exact", C.c_int)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise GpuError(f"{LIB_PATH} is not built (run __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        L.ds4f_gpu_last_error.restype = C.c_char_p
+        L.ds4f_gpu_free.restype = None
+        L.ds4f_gpu_model_destroy.restype = None
+        L.ds4f_gpu_mv_plan_free.restype = None
+        sig = {
+            "ds4f_gpu_f8_matvec": [_vp, C.c_int, _vp] + [C.c_int] * 4 + [_vp, _vp],
+            "ds4f_gpu_mxfp4_matvec": [_vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp],
+            "ds4f_gpu_bf16_matvec": [_vp, C.c_int, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_mlx4_matvec": [_vp, _vp, _vp, C.c_int, C.c_int, _vp, _vp],
+            "ds4f_gpu_mlx4_batch": [_vp] * 6 + [C.c_int] * 3,
+            "ds4f_gpu_f8_decode_rows": [_vp, C.c_int, _vp] + [C.c_int] * 6 + [_vp],
+            "ds4f_gpu_mxfp4_decode": [_vp, _vp, C.c_int64, C.c_int, _vp],
+            "ds4f_gpu_mv_plan": [_vp, C.c_int, _vp],
+            "ds4f_gpu_mv_run": [_vp, _vp],
+            "ds4f_gpu_mv_plan_free": [_vp],
+            "ds4f_gpu_model_create": [C.POINTER(Ds4fGpuModelDesc), _vp],
+            "ds4f_gpu_model_destroy": [_vp],
+            "ds4f_gpu_model_slot": [_vp, _vp, _vp, _vp],
+            "ds4f_gpu_model_synth": [_vp, C.c_uint64],
+            "ds4f_gpu_model_set_trunk": [_vp, C.c_int] + [_vp] * 6,
+            "ds4f_gpu_model_get_trunk": [_vp, C.c_int] + [_vp] * 6,
+            "ds4f_gpu_model_set_expert": [_vp, C.c_int, C.c_int, _vp],
+            "ds4f_gpu_model_get_expert": [_vp, C.c_int, C.c_int, _vp],
+            "ds4f_gpu_pool_load": [_vp, C.c_char_p],
+            "ds4f_gpu_moe_layer": [_vp, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_moe_layer_dev": [_vp, C.c_int, _vp, _vp, _vp, _vp],
+            "ds4f_gpu_moe_stack": [_vp, _vp, C.c_int],
+            "ds4f_gpu_moe_stack_dev": [_vp, _vp, C.c_int, _vp],
+            "ds4f_gpu_model_stats": [_vp, _vp],
+            "ds4f_gpu_synth_f32": [_vp, C.c_int64, C.c_uint64, C.c_uint32, C.c_uint32,
+                                   C.c_uint32, C.c_uint32, C.c_double, _vp],
+        }
+        for name, args in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            if name not in ("ds4f_gpu_mv_plan_free", "ds4f_gpu_model_destroy"):
+                fn.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def header_symbols():
+    """Function names declared in include/ds4f/gpu_cuda.h."""
+    import re
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(ds4f_gpu_\w+)\s*\(", txt)))
+
+
+def check(rc):
+    if rc != 0:
+        raise GpuError(lib().ds4f_gpu_last_error().decode())
+
+
+def ptr(a):
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return C.c_void_p(a.data_ptr())
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def init():
+    check(lib().ds4f_gpu_init())
+
+
+# ---- matvec (host buffers) -------------------------------------------
+
+def f8_matvec(W, scale_kind, scales, SR, SC, x):
+    W = np.ascontiguousarray(W, np.uint8)
+    R, Cc = W.shape
+    y = np.zeros(R, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    s = None if scales is None else np.ascontiguousarray(scales)
+    check(lib().ds4f_gpu_f8_matvec(ptr(W), scale_kind, ptr(s), R, Cc, SR, SC, ptr(x), ptr(y)))
+    return y
+
+
+def mxfp4_matvec(vals, scales, R, Cc, x, bsize=32):
+    y = np.zeros(R, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    check(lib().ds4f_gpu_mxfp4_matvec(ptr(np.ascontiguousarray(vals)),
+                                      ptr(np.ascontiguousarray(scales)), R, Cc, bsize,
+                                      ptr(x), ptr(y)))
+    return y
+
+
+def bf16_matvec(W, x, bias=None):
+    W = np.ascontiguousarray(W, np.uint16)
+    R, Cc = W.shape
+    y = np.zeros(R, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    check(lib().ds4f_gpu_bf16_matvec(ptr(W), R, Cc, ptr(x), ptr(b), ptr(y)))
+    return y
+
+
+def mlx4_matvec(vals, scales, biases, R, Cc, x):
+    y = np.zeros(R, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    check(lib().ds4f_gpu_mlx4_matvec(ptr(np.ascontiguousarray(vals, np.uint32)),
+                                     ptr(np.ascontiguousarray(scales, np.uint16)),
+                                     ptr(None if biases is None else
+                                         np.ascontiguousarray(biases, np.uint16)),
+                                     R, Cc, ptr(x), ptr(y)))
+    return y
+
+
+def f8_decode_rows(W, scale_kind, scales, SR, SC, r0, r1):
+    W = np.ascontiguousarray(W, np.uint8)
+    R, Cc = W.shape
+    out = np.zeros((r1 - r0, Cc), np.float32)
+    s = None if scales is None else np.ascontiguousarray(scales)
+    check(lib().ds4f_gpu_f8_decode_rows(ptr(W), scale_kind, ptr(s), R, Cc, SR, SC, r0, r1,
+                                        ptr(out)))
+    return out
+
+
+def mxfp4_decode(vals, scales, n, bsize=32):
+    out = np.zeros(n, np.float32)
+    check(lib().ds4f_gpu_mxfp4_decode(ptr(np.ascontiguousarray(vals)),
+                                      ptr(np.ascontiguousarray(scales)), n, bsize, ptr(out)))
+    return out
+
+
+class MvPlan:
+    """A planned list of device matvec jobs (all run in one launch)."""
+
+    def __init__(self, jobs):
+        arr = (Ds4fMvJob * len(jobs))(*jobs)
+        h = C.c_void_p()
+        check(lib().ds4f_gpu_mv_plan(C.cast(arr, _vp), len(jobs), C.byref(h)))
+        self.h = h
+
+    def run(self, stream=None):
+        check(lib().ds4f_gpu_mv_run(self.h, stream))
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.ds4f_gpu_mv_plan_free(self.h)
+            self.h = None
+
+
+# ---- model -----------------------------------------------------------
+
+class Model:
+    def __init__(self, fmt, n_layers, hidden=2048, moe_inter=512, n_experts=256, topk=8,
+                 renorm=True, expert_first=0, expert_count=None, router_exact=False):
+        self.h = None
+        d = Ds4fGpuModelDesc(fmt, n_layers, hidden, moe_inter, n_experts, topk,
+                             1 if renorm else 0, expert_first,
+                             n_experts if expert_count is None else expert_count,
+                             1 if router_exact else 0)
+        h = C.c_void_p()
+        check(lib().ds4f_gpu_model_create(C.byref(d), C.byref(h)))
+        self.h, self.d = h, d
+        self.H, self.M, self.E, self.K, self.L = hidden, moe_inter, n_experts, topk, n_layers
+        rv = (C.c_int64 * 3)()
+        rs = (C.c_int64 * 3)()
+        nb = C.c_int64()
+        check(lib().ds4f_gpu_model_slot(h, rv, rs, C.byref(nb)))
+        self.rel_v, self.rel_s, self.slot_bytes = list(rv), list(rs), nb.value
+
+    def close(self):
+        if self.h and _lib is not None:
+            _lib.ds4f_gpu_model_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def synth(self, seed):
+        check(lib().ds4f_gpu_model_synth(self.h, seed))
+
+    def set_trunk(self, L, norm, router, sh_gate, sh_up, sh_down, sh_gw):
+        a = [np.ascontiguousarray(t, np.uint16) for t in (norm, router, sh_gate, sh_up,
+                                                          sh_down, sh_gw)]
+        check(lib().ds4f_gpu_model_set_trunk(self.h, L, *[ptr(t) for t in a]))
+
+    def get_trunk(self, L):
+        H, M, E = self.H, self.M, self.E
+        out = [np.zeros(H, np.uint16), np.zeros((E, H), np.uint16),
+               np.zeros((M, H), np.uint16), np.zeros((M, H), np.uint16),
+               np.zeros((H, M), np.uint16), np.zeros(H, np.uint16)]
+        check(lib().ds4f_gpu_model_get_trunk(self.h, L, *[ptr(t) for t in out]))
+        return out
+
+    def set_expert(self, L, X, slot):
+        check(lib().ds4f_gpu_model_set_expert(self.h, L, X,
+                                              ptr(np.ascontiguousarray(slot, np.uint8))))
+
+    def get_expert(self, L, X):
+        out = np.zeros(self.slot_bytes, np.uint8)
+        check(lib().ds4f_gpu_model_get_expert(self.h, L, X, ptr(out)))
+        return out
+
+    def pool_load(self, path):
+        check(lib().ds4f_gpu_pool_load(self.h, path.encode()))
+
+    def layer(self, L, state):
+        st = np.array(state, np.float32, copy=True)
+        idx = np.zeros(self.K, np.int32)
+        w = np.zeros(self.K, np.float32)
+        check(lib().ds4f_gpu_moe_layer(self.h, L, ptr(st), ptr(idx), ptr(w)))
+        return st, idx, w
+
+    def stack(self, state, n_steps):
+        st = np.array(state, np.float32, copy=True)
+        check(lib().ds4f_gpu_moe_stack(self.h, ptr(st), n_steps))
+        return st
+
+    def stack_host_inplace(self, st, n_steps):
+        """End-to-end call on a caller-owned (e.g. pinned) host buffer."""
+        check(lib().ds4f_gpu_moe_stack(self.h, ptr(st), n_steps))
+
+    def layer_dev(self, L, state, idx=None, w=None, stream=None):
+        check(lib().ds4f_gpu_moe_layer_dev(self.h, L, ptr(state), ptr(idx), ptr(w), stream))
+
+    def stack_dev(self, state, n_steps, stream=None):
+        check(lib().ds4f_gpu_moe_stack_dev(self.h, ptr(state), n_steps, stream))
+
+    def stats(self):
+        out = (C.c_uint64 * 2)()
+        check(lib().ds4f_gpu_model_stats(self.h, out))
+        return list(out)
+
+
+def synth_f32_dev(dst, n, seed, layer, kind, x, t, sigma, stream=None):
+    check(lib().ds4f_gpu_synth_f32(ptr(dst), n, seed, layer, kind, x, t, sigma, stream))

@@ -1,0 +1,188 @@
+/*
+ * gpu_cuda.h -- libds4f_cuda: the B200 (sm_100a) implementation of the
+ * engine's GPU shim and of its routed-expert hot path.
+ *
+ * Drop-in boundary. The reference engine (C99) calls its GPU shim through
+ * include/ds4f/gpu.h, implemented by src/gpu_stub.c (always -1) or
+ * src/gpu_metal.mm (Apple Metal). libds4f_cuda links in their place: it
+ * exports the four gpu.h symbols unchanged and adds the entry points below
+ * for the FP8 / MXFP4 expert path. Plain C types only; no CUDA or torch
+ * types appear in any signature (streams are `void *`, a cudaStream_t).
+ *
+ * Conventions (as gpu.h:20-21): every int-returning call returns 0 on
+ * success and -1 on failure; ds4f_gpu_last_error() then holds a message
+ * (per host thread). Unlike the reference there is NO CPU fallback behind
+ * these calls: a caller that gets -1 reports the message and stops.
+ * Host-buffer calls are synchronous on return. `_dev` calls take device
+ * pointers and enqueue on the given stream (NULL = the library's stream).
+ * One host thread per model; calls are not re-entrant.
+ */
+#ifndef DS4F_GPU_CUDA_H
+#define DS4F_GPU_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- the reference shim, unchanged (include/ds4f/gpu.h:22-52) ------- */
+
+/* gpu.h:22 -- 0 when a CUDA device is usable. */
+int ds4f_gpu_init(void);
+/* gpu.h:23 */
+void ds4f_gpu_free(void);
+/* gpu.h:30 -- MLX-4bit matvec. Implemented (y = sum_c (q*s+b) x_c, the
+ * layout of ds4f_mlx4_matvec, src/kernels.c:154-222). */
+int ds4f_gpu_mlx4_matvec(const uint32_t *vals, const uint16_t *scales,
+                         const uint16_t *biases, int R, int C,
+                         const float *x, float *y);
+/* gpu.h:47-52 -- batched MLX-4bit jobs with weights cached per stable id
+ * (the reference arena, src/gpu_metal.mm:186-254). */
+int ds4f_gpu_mlx4_batch(const uint32_t *const *vals,
+                        const uint16_t *const *scales,
+                        const uint16_t *const *biases,
+                        const float *const *xs, float *const *ys,
+                        const void *const *ids, int R, int C, int njobs);
+
+/* Last error message of this host thread ("" if none). New. */
+const char *ds4f_gpu_last_error(void);
+
+/* ---- formats ------------------------------------------------------- */
+#define DS4F_FMT_MXFP4 0        /* e2m1 + E8M0 per bsize (moe.h:28 fmt 0) */
+#define DS4F_FMT_FP8   2        /* E4M3 + block scales                   */
+#define DS4F_FMT_BF16  3        /* bf16 (router, shared expert)          */
+#define DS4F_SCALE_E8M0 0       /* FP8 block scales as E8M0 bytes        */
+#define DS4F_SCALE_F32  1       /* FP8 block scales as fp32              */
+
+/* ---- dequant-matvec, host buffers ---------------------------------- */
+
+/* Replaces ds4f_f8_matvec (src/kernels.c:243-270, kernels.h:48-56):
+ * y[r] = sum_c e4m3(W[r,c]) * s[r*SR/R][c*SC/C] * x[c]. scale_kind picks
+ * E8M0 bytes (the reference) or fp32 (BASELINE's 128x128 scales). E4M3
+ * bytes with exponent 15 decode to +-448 as in the reference table. */
+int ds4f_gpu_f8_matvec(const uint8_t *W, int scale_kind, const void *scales,
+                       int R, int C, int SR, int SC, const float *x, float *y);
+/* Replaces ds4f_mxfp4_matvec (src/kernels.c:48-62, kernels.h:31-35);
+ * bsize 16 or 32. No scratch: decode is fused. */
+int ds4f_gpu_mxfp4_matvec(const uint8_t *vals, const uint8_t *scales, int R,
+                          int C, int bsize, const float *x, float *y);
+/* Replaces ds4f_bf16_matvec (src/kernels.c:91-103, kernels.h:45-46). */
+int ds4f_gpu_bf16_matvec(const uint16_t *W, int R, int C, const float *x,
+                         const float *bias, float *y);
+/* Dequantised values, bit-exact: replaces ds4f_f8_decode_row
+ * (src/kernels.c:294-306) for rows [r0, r1) -> out[(r1-r0) x C]. */
+int ds4f_gpu_f8_decode_rows(const uint8_t *W, int scale_kind,
+                            const void *scales, int R, int C, int SR, int SC,
+                            int r0, int r1, float *out);
+/* Replaces ds4f_mxfp4_decode (src/kernels.c:34-46). */
+int ds4f_gpu_mxfp4_decode(const uint8_t *vals, const uint8_t *scales,
+                          int64_t n, int bsize, float *out);
+
+/* ---- dequant-matvec, device job lists ------------------------------ */
+
+/* One y = W x on device pointers. fmt DS4F_FMT_*; scales: FP8 block
+ * scales (scale_kind), MXFP4 E8M0 bytes per bsize, BF16 optional fp32
+ * bias. canon: apply the e=15 -> 448 rule in-kernel (needed unless the
+ * bytes came from a canonicalised pool). */
+typedef struct Ds4fMvJob {
+    const void *w;
+    const void *scales;
+    const float *x;
+    float *y;
+    int R, C, SR, SC;
+    int fmt, scale_kind, bsize, canon;
+} Ds4fMvJob;
+
+typedef struct Ds4fMvPlan Ds4fMvPlan;
+/* Plan a job list (copied to the device once). The batched form of the
+ * reference's per-expert matvecs (src/moe.c:619-640, :728-740) and of its
+ * Metal batch dispatch (gpu_metal.mm:256-367): all jobs in one launch. */
+int  ds4f_gpu_mv_plan(const Ds4fMvJob *jobs, int njobs, Ds4fMvPlan **plan);
+int  ds4f_gpu_mv_run(const Ds4fMvPlan *plan, void *stream);
+void ds4f_gpu_mv_plan_free(Ds4fMvPlan *plan);
+
+/* ---- resident expert pool + MoE step ------------------------------- */
+
+typedef struct Ds4fGpuModelDesc {
+    int fmt;              /* DS4F_FMT_FP8 or DS4F_FMT_MXFP4              */
+    int n_layers;         /* Ds4fCfg.n_layers (ds4f.h:57)                */
+    int hidden;           /* H  (Ds4fCfg.hidden)                         */
+    int moe_inter;        /* M  (Ds4fCfg.moe_inter)                      */
+    int n_experts;        /* E  (Ds4fCfg.n_experts)                      */
+    int topk;             /* K  (Ds4fCfg.topk)                           */
+    int renorm;           /* norm_topk_prob: 1 divides the top-k weights by
+                             their sum (the reference keeps them raw,
+                             src/moe.c:547-560)                          */
+    int expert_first;     /* this device's expert shard [first, first+count) */
+    int expert_count;     /* (count = n_experts: the whole pool)          */
+    int router_exact;     /* 1: all router logits in the reference's exact
+                             sequential order (bit-exact weights, slower) */
+} Ds4fGpuModelDesc;
+
+typedef struct Ds4fGpuModel Ds4fGpuModel;
+
+/* Allocate the HBM-resident pool for the shard (the device-side
+ * replacement of the expert cache, src/cache.c:140-214, with the memory
+ * plan refusing past 95% of free HBM like ds4f_mem_refuses, mem.c). */
+int  ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out);
+void ds4f_gpu_model_destroy(Ds4fGpuModel *m);
+/* Bytes of one expert slot (gate, up, down; values then scales each, the
+ * converter's order, tools/convert-ds4f.py:1321-1356) and its offsets. */
+int  ds4f_gpu_model_slot(const Ds4fGpuModel *m, int64_t rel_v[3],
+                         int64_t rel_s[3], int64_t *nbytes);
+/* Fill the whole shard with the seeded synthetic weights (sigma 0.02). */
+int  ds4f_gpu_model_synth(Ds4fGpuModel *m, uint64_t seed);
+/* Upload one layer's resident bf16 weights (the trunk tensors the
+ * reference reads at src/main.c:1014-1083 and src/moe.c:1235-1293):
+ * norm [H], router [E x H], shared gate/up [M x H], down [H x M],
+ * shared_expert_gate [H]. */
+int  ds4f_gpu_model_set_trunk(Ds4fGpuModel *m, int layer, const uint16_t *norm,
+                              const uint16_t *router, const uint16_t *sh_gate,
+                              const uint16_t *sh_up, const uint16_t *sh_down,
+                              const uint16_t *sh_gw);
+int  ds4f_gpu_model_get_trunk(const Ds4fGpuModel *m, int layer, uint16_t *norm,
+                              uint16_t *router, uint16_t *sh_gate,
+                              uint16_t *sh_up, uint16_t *sh_down,
+                              uint16_t *sh_gw);
+/* Upload / download one expert slot (host bytes, slot layout above). FP8
+ * bytes are canonicalised on upload (e=15 -> +-448, value-preserving under
+ * the reference table). */
+int  ds4f_gpu_model_set_expert(Ds4fGpuModel *m, int layer, int expert,
+                               const uint8_t *slot);
+int  ds4f_gpu_model_get_expert(const Ds4fGpuModel *m, int layer, int expert,
+                               uint8_t *slot);
+/* Load this shard from a packed pool file: [u64 expert_nbytes][u64
+ * n_layers][u64 n_experts] then slots layer-major, expert N of layer L at
+ * 24 + (L*E + N)*nbytes (ds4f_pool_open_packed, src/st.c:127-180). */
+int  ds4f_gpu_pool_load(Ds4fGpuModel *m, const char *path);
+
+/* One token through one layer (host buffers): state[H] in/out; idx[K],
+ * w[K] receive the routing (may be NULL). Replaces the reference's
+ * per-layer route (src/main.c:1014-1088) + ds4f_moe_step
+ * (src/moe.c:948-1456) for Qwen3.5 layers. */
+int  ds4f_gpu_moe_layer(Ds4fGpuModel *m, int layer, float *state, int *idx,
+                        float *w);
+int  ds4f_gpu_moe_layer_dev(Ds4fGpuModel *m, int layer, float *state,
+                            int *idx, float *w, void *stream);
+/* n_steps decode steps of the whole layer stack: each step runs layers
+ * 0..n_layers-1 on state[H], carried through the residual (the per-token
+ * loop of src/main.c:848-1138, MoE part). */
+int  ds4f_gpu_moe_stack(Ds4fGpuModel *m, float *state, int n_steps);
+int  ds4f_gpu_moe_stack_dev(Ds4fGpuModel *m, float *state, int n_steps,
+                            void *stream);
+/* Counters: [0] layers routed, [1] router exact-fallbacks taken. */
+int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
+
+/* Seeded N(0, sigma) fp32 vector on the device (the synthetic activations
+ * of the BASELINE configs): element i of tensor (seed, layer, kind, x, t). */
+int  ds4f_gpu_synth_f32(float *dst_dev, int64_t n, uint64_t seed,
+                        uint32_t layer, uint32_t kind, uint32_t x, uint32_t t,
+                        double sigma, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DS4F_GPU_CUDA_H */

@@ -133,6 +133,32 @@ void orc_mxfp4_matvec(const uint8_t *vals, const uint8_t *scales, int R,
     }
 }
 
+/* Scalar fallback of ds4f_mlx4_matvec (src/kernels.c:201-221). Element
+ * k = r*C + c is nibble k%8 of word k/8; group g = k/64 rebuilds the table
+ * lut[q] = (float)q * s + b when g changes. */
+void orc_mlx4_matvec(const uint32_t *vals, const uint16_t *scales,
+                     const uint16_t *biases, int R, int C, const float *x,
+                     float *y) {
+    float lut[16];
+    long gcur = -1;
+    for (int r = 0; r < R; r++) {
+        float acc = 0.0f;
+        for (int c = 0; c < C; c++) {
+            long k = (long)r * C + c;
+            long g = k / 64;
+            if (g != gcur) {
+                gcur = g;
+                float s = orc_bf16_to_f32(scales[g]);
+                float b = biases ? orc_bf16_to_f32(biases[g]) : 0.0f;
+                for (int q = 0; q < 16; q++) lut[q] = (float)q * s + b;
+            }
+            int q = (int)((vals[k >> 3] >> (4 * (int)(k & 7))) & 0xFu);
+            acc += lut[q] * x[c];
+        }
+        y[r] = acc;
+    }
+}
+
 /* Scalar ds4f_bf16_matvec (src/kernels.c:97-102). */
 void orc_bf16_matvec(const uint16_t *W, int R, int C, const float *x,
                      const float *bias, float *y) {

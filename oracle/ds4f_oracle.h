@@ -52,6 +52,11 @@ void orc_f8_matvec(const uint8_t *W, int scale_kind, const void *scales,
 void orc_mxfp4_matvec(const uint8_t *vals, const uint8_t *scales, int R,
                       int C, int bsize, const float *x, float *y,
                       float *scratch);
+/* Scalar ds4f_mlx4_matvec (src/kernels.c:201-221): per 64-element group a
+ * 16-entry table lut[q] = q*s + b (bf16 scale/bias), acc += lut[q]*x. */
+void orc_mlx4_matvec(const uint32_t *vals, const uint16_t *scales,
+                     const uint16_t *biases, int R, int C, const float *x,
+                     float *y);
 /* src/kernels.c:91-103 (scalar branch :97-102). bias may be NULL. */
 void orc_bf16_matvec(const uint16_t *W, int R, int C, const float *x,
                      const float *bias, float *y);

@@ -91,6 +91,8 @@ def lib():
                                        C.c_void_p, C.c_void_p]
         L.orc_bf16_matvec.argtypes = [C.c_void_p, C.c_int, C.c_int,
                                       C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_mlx4_matvec.argtypes = [C.c_void_p] * 3 + [C.c_int, C.c_int,
+                                                         C.c_void_p, C.c_void_p]
         L.orc_rmsnorm.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
         L.orc_topk.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                C.c_void_p]
@@ -133,6 +135,8 @@ def ref():
             [C.c_int] * 4 + [C.c_void_p, C.c_void_p]
         R.ds4f_f8_decode_row.argtypes = [C.c_void_p, C.c_void_p] + \
             [C.c_int] * 5 + [C.c_void_p]
+        R.ds4f_mlx4_matvec.argtypes = [C.c_void_p] * 3 + [C.c_int, C.c_int,
+                                                          C.c_void_p, C.c_void_p]
         R.ds4f_topk.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                 C.c_void_p]
         _ref = R
@@ -172,6 +176,13 @@ def bf16_matvec(W, x, bias=None):
     R, Cc = W.shape
     y = np.zeros(R, np.float32)
     lib().orc_bf16_matvec(ptr(W), R, Cc, ptr(x), ptr(bias), ptr(y))
+    return y
+
+
+def mlx4_matvec(vals, scales, biases, R, Cc, x):
+    y = np.zeros(R, np.float32)
+    lib().orc_mlx4_matvec(ptr(vals), ptr(scales), ptr(biases), R, Cc, ptr(x),
+                          ptr(y))
     return y
 
 
@@ -242,6 +253,26 @@ class Layer:
                 if L.fx_expert(fmt, H, M, seed, layer, x, sigma,
                                ptr(row)) != 0:
                     raise ValueError("bad expert shape")
+
+    @classmethod
+    def from_arrays(cls, fmt, H, M, E, trunk, experts):
+        """A layer from given bytes: trunk = (norm, router, sh_gate, sh_up,
+        sh_down, sh_gw) bf16 arrays, experts [E, slot_bytes] uint8."""
+        self = cls.__new__(cls)
+        self.fmt, self.H, self.M, self.E = fmt, H, M, E
+        self.lay = expert_layout(fmt, H, M)
+        (self.norm, self.router, self.sh_gate, self.sh_up, self.sh_down,
+         self.sh_gw) = [np.ascontiguousarray(t, np.uint16) for t in trunk]
+        self.experts = experts
+        return self
+
+    def route(self, state, K, renorm=True):
+        """Router only (src/main.c:1014-1088 + topk + renorm)."""
+        xin = np.array(state, np.float32, copy=True)
+        lib().orc_rmsnorm(ptr(self.norm), self.H, ptr(xin))
+        sc = bf16_matvec(self.router, xin)
+        idx, w = topk(sc, K, renorm)
+        return idx, w, sc, xin
 
     def w(self):
         return OrcLayerW(ptr(self.norm), ptr(self.router), ptr(self.sh_gate),

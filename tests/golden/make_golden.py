@@ -104,6 +104,21 @@ def main():
     g["bfmv_W"], g["bfmv_x"], g["bfmv_bias"] = Wb, x, bias
     g["bfmv_y"], g["bfmv_yb"] = y, yb
 
+    # MLX-4bit matvec (scalar table path), with and without biases.
+    r, c = 16, 256
+    V = rng.integers(0, 2**32, r * c // 8, dtype=np.uint64).astype(np.uint32)
+    Sf = (rng.random(r * c // 64) * 0.02 + 0.001).astype(np.float32)
+    Bf = (rng.standard_normal(r * c // 64) * 0.05).astype(np.float32)
+    Sb = (Sf.view(np.uint32) >> 16).astype(np.uint16)
+    Bb = (Bf.view(np.uint32) >> 16).astype(np.uint16)
+    x = rng.standard_normal(c).astype(np.float32)
+    y = np.zeros(r, np.float32)
+    y0 = np.zeros(r, np.float32)
+    R.ds4f_mlx4_matvec(ptr(V), ptr(Sb), ptr(Bb), r, c, ptr(x), ptr(y))
+    R.ds4f_mlx4_matvec(ptr(V), ptr(Sb), None, r, c, ptr(x), ptr(y0))
+    g["mlx_V"], g["mlx_S"], g["mlx_B"], g["mlx_x"] = V, Sb, Bb, x
+    g["mlx_y"], g["mlx_y0"] = y, y0
+
     # top-k with softmax (no renorm, as the reference), including ties.
     T, E, K = 24, 256, 8
     sc = rng.standard_normal((T, E)).astype(np.float32)

@@ -212,6 +212,15 @@ def test_golden_bf16_matvec(g):
     assert np.array_equal(bits(yb), bits(g["bfmv_yb"]))
 
 
+def test_golden_mlx4_matvec(g):
+    V, S, B, x = g["mlx_V"], g["mlx_S"], g["mlx_B"], g["mlx_x"]
+    r, c = 16, 256
+    y = po.mlx4_matvec(V, S, B, r, c, x)
+    assert np.array_equal(bits(y), bits(g["mlx_y"]))
+    y0 = po.mlx4_matvec(V, S, None, r, c, x)
+    assert np.array_equal(bits(y0), bits(g["mlx_y0"]))
+
+
 def test_golden_topk(g):
     sc = g["topk_scores"]
     for t in range(sc.shape[0]):
