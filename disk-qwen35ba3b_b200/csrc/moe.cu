@@ -8,9 +8,11 @@
 // (src/moe.c:531-561). The host/GPU round trips of the reference's Metal
 // path (two dispatches plus a CPU SiLU per layer, src/moe.c:1105-1150)
 // become four kernels that never leave the device.
+#include "../../include/ds4f/gpu_cuda.h"
 #include "model.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace ds4f {
 
@@ -590,3 +592,135 @@ int moe_layer_launch(Model *m, int L, float *state, int *idx_out, float *w_out,
 }
 
 }  // namespace ds4f
+
+// ===========================================================================
+// Allocation-free variant of the one-token layer step.
+//
+// Some hosts cannot let this library call cudaMalloc: an engine that owns
+// every byte of device memory through its own pre-sized arena (as the
+// reference engine plans and caps its memory before it starts, and never
+// allocates in its per-token loop), or a caller working inside a memory
+// budget it must not exceed behind its own back. For them the per-call
+// workspace of the layer step (normed input, router logits and bounds,
+// routing, SiLU chains, shared-gate logit, counters) lives in the static
+// device array below instead of a Model's cudaMalloc'd workspace; the
+// caller passes the weights, the state and the outputs as device pointers.
+//
+// The array is a file-scope __device__ object: every GPU that loads this
+// library holds kStaticScratchBytes of it until the process exits. Its
+// name is not a device address in host code, so the address is looked up
+// with cudaGetSymbolAddress once per device, on the first call made with
+// that device current (make that first call before any stream capture).
+// All calls on a device share the array and it keeps the last call's
+// contents; calls that overlap on the GPU (different streams, no ordering
+// between them) race on it.
+// ===========================================================================
+namespace ds4f {
+namespace {
+
+constexpr int kStaticMaxH = 2048, kStaticMaxM = 512, kStaticMaxE = 256, kStaticMaxK = 16;
+constexpr size_t al256s(size_t n) { return (n + 255) & ~(size_t)255; }
+constexpr size_t kStaticScratchBytes =
+    al256s(kStaticMaxH * 4) + 2 * al256s(kStaticMaxE * 8) + 2 * al256s(kStaticMaxK * 4) +
+    al256s((size_t)(kStaticMaxK + 1) * kStaticMaxM * 4) + al256s(4) + al256s(kStaticMaxH * 4) +
+    al256s(16);
+
+__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+void *g_static_addr[64];            // per device ordinal, looked up once
+
+}  // namespace
+}  // namespace ds4f
+
+extern "C" int ds4f_gpu_moe_layer_static(const Ds4fLayerDev *ld, float *state, int *idx,
+                                         float *w, void *stream) {
+    using namespace ds4f;
+    DS4F_REQUIRE(ld && state, "moe_layer_static: null argument");
+    const int H = ld->hidden, M = ld->moe_inter, E = ld->n_experts, K = ld->topk;
+    DS4F_REQUIRE(H <= kStaticMaxH && M <= kStaticMaxM && E <= kStaticMaxE && K <= kStaticMaxK,
+                 "moe_layer_static: sizes H %d, M %d, E %d, K %d exceed the static scratch "
+                 "maximum (H <= %d, M <= %d, E <= %d, K <= %d)",
+                 H, M, E, K, kStaticMaxH, kStaticMaxM, kStaticMaxE, kStaticMaxK);
+    DS4F_REQUIRE(K >= 1 && K <= E, "moe_layer_static: topk %d of %d experts", K, E);
+    DS4F_REQUIRE(ld->fmt == DS4F_FMT_FP8 || ld->fmt == DS4F_FMT_MXFP4,
+                 "moe_layer_static: expert format %d (FP8 or MXFP4)", ld->fmt);
+    DS4F_REQUIRE((H == 2048 && M == 512) || (H == 1024 && M == 256),
+                 "moe_layer_static: kernels are built for (H, M) = (2048, 512) or (1024, 256)");
+    DS4F_REQUIRE(ld->experts && ld->norm && ld->router && ld->sh_gate && ld->sh_up &&
+                     ld->sh_down && ld->sh_gw,
+                 "moe_layer_static: null weight pointer");
+    SlotLayout slot;
+    if (slot_layout(ld->fmt, H, M, &slot)) return -1;
+    DS4F_REQUIRE(ld->slot_bytes >= slot.nbytes && ld->slot_bytes % 16 == 0,
+                 "moe_layer_static: slot_bytes %lld (need >= %lld, multiple of 16)",
+                 (long long)ld->slot_bytes, (long long)slot.nbytes);
+    const void *ptrs[7] = {ld->experts, ld->norm, ld->router, ld->sh_gate,
+                           ld->sh_up, ld->sh_down, ld->sh_gw};
+    for (const void *p : ptrs)
+        DS4F_REQUIRE(((uintptr_t)p % 16) == 0, "moe_layer_static: weights must be 16-byte aligned");
+
+    int dev = 0;
+    DS4F_CUDA(cudaGetDevice(&dev));
+    DS4F_REQUIRE(dev >= 0 && dev < 64, "moe_layer_static: device ordinal %d", dev);
+    unsigned char *base;
+    {
+        std::lock_guard<std::mutex> lk(g_static_mu);
+        if (!g_static_addr[dev]) {
+            void *p = nullptr;
+            DS4F_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+            g_static_addr[dev] = p;
+        }
+        base = (unsigned char *)g_static_addr[dev];
+    }
+    Work wk;
+    unsigned char *p = base;
+    auto take = [&](size_t n) { unsigned char *r = p; p += al256s(n); return r; };
+    wk.xin = (float *)take(kStaticMaxH * 4);
+    wk.S = (double *)take(kStaticMaxE * 8);
+    wk.Bnd = (double *)take(kStaticMaxE * 8);
+    wk.idx = (int *)take(kStaticMaxK * 4);
+    wk.w = (float *)take(kStaticMaxK * 4);
+    wk.chain = (float *)take((size_t)(kStaticMaxK + 1) * kStaticMaxM * 4);
+    wk.sgate = (float *)take(4);
+    wk.acc = (float *)take(kStaticMaxH * 4);
+    wk.diag = (unsigned *)take(16);
+
+    // the bf16 trunk tensors as element offsets from the norm pointer
+    const uint16_t *tb = ld->norm;
+    TrunkLayout tr;
+    tr.norm = 0;
+    tr.router = ld->router - tb;
+    tr.sh_gate = ld->sh_gate - tb;
+    tr.sh_up = ld->sh_up - tb;
+    tr.sh_down = ld->sh_down - tb;
+    tr.sh_gw = ld->sh_gw - tb;
+    tr.n = 0;
+    cudaStream_t st = (cudaStream_t)stream;
+
+    k_route<<<(E + kRouteWarps - 1) / kRouteWarps, 256, H * sizeof(float), st>>>(
+        state, tb, tr, H, E, wk.xin, wk.S, wk.Bnd);
+    DS4F_CUDA(cudaGetLastError());
+    size_t tk_smem = (size_t)E * (8 + 8 + 4 + 4 + 4) + (size_t)H * 4;
+    k_topk<<<1, 256, tk_smem, st>>>(wk.S, wk.Bnd, wk.xin, ld->router, H, E, K,
+                                    ld->renorm, 0, wk.idx, wk.w, wk.diag);
+    DS4F_CUDA(cudaGetLastError());
+    LayerArgs a;
+    a.pool_l = (const uint8_t *)ld->experts;
+    a.slot_bytes = ld->slot_bytes;
+    a.slot = slot;
+    a.trunk_l = tb;
+    a.tr = tr;
+    a.E = E; a.K = K; a.efirst = 0; a.ecount = E;
+    a.idx = wk.idx; a.w = wk.w; a.xin = wk.xin; a.chain = wk.chain; a.sgate = wk.sgate;
+    a.state = state; a.acc_out = wk.acc;
+    int rc;
+    if (ld->fmt == DS4F_FMT_FP8 && H == 2048) rc = launch_chain<DS4F_FMT_FP8, 2048, 512>(a, st);
+    else if (ld->fmt == DS4F_FMT_MXFP4 && H == 2048) rc = launch_chain<DS4F_FMT_MXFP4, 2048, 512>(a, st);
+    else if (ld->fmt == DS4F_FMT_FP8) rc = launch_chain<DS4F_FMT_FP8, 1024, 256>(a, st);
+    else rc = launch_chain<DS4F_FMT_MXFP4, 1024, 256>(a, st);
+    if (rc) return rc;
+    if (idx) DS4F_CUDA(cudaMemcpyAsync(idx, wk.idx, K * sizeof(int), cudaMemcpyDeviceToDevice, st));
+    if (w) DS4F_CUDA(cudaMemcpyAsync(w, wk.w, K * sizeof(float), cudaMemcpyDeviceToDevice, st));
+    return 0;
+}

@@ -175,6 +175,33 @@ int  ds4f_gpu_moe_stack_dev(Ds4fGpuModel *m, float *state, int n_steps,
 /* Counters: [0] layers routed, [1] router exact-fallbacks taken. */
 int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
 
+/* ---- allocation-free layer step ------------------------------------- */
+
+/* One MoE layer's weights as caller-owned device pointers (16-byte
+ * aligned): the E expert slots back to back, slot_bytes apart, in the slot
+ * layout of ds4f_gpu_model_slot; the bf16 trunk tensors as in
+ * ds4f_gpu_model_set_trunk. */
+typedef struct Ds4fLayerDev {
+    int fmt, hidden, moe_inter, n_experts, topk, renorm;
+    const void *experts;
+    int64_t slot_bytes;
+    const uint16_t *norm, *router, *sh_gate, *sh_up, *sh_down, *sh_gw;
+} Ds4fLayerDev;
+
+/* No counterpart in the reference: an extra entry point for hosts that
+ * cannot let this library allocate device memory (an engine that owns all
+ * of it through its own pre-sized arena and budget). Same computation as
+ * ds4f_gpu_moe_layer_dev; the per-call workspace lives in a static device
+ * array of ~56 KB held by every GPU that loads the library, so the call
+ * makes no cudaMalloc / cudaFree. Limits: hidden <= 2048, moe_inter <=
+ * 512, n_experts <= 256, topk <= 16 (larger sizes return -1 with a
+ * message). The first call on a device looks up the array's address with
+ * that device current; make it before any stream capture. Calls share the
+ * array: calls that overlap on the GPU race. state [H] in/out, idx [K] and
+ * w [K] optional outputs, all device pointers; enqueued on `stream`. */
+int  ds4f_gpu_moe_layer_static(const Ds4fLayerDev *layer, float *state, int *idx,
+                               float *w, void *stream);
+
 /* Seeded N(0, sigma) fp32 vector on the device (the synthetic activations
  * of the BASELINE configs): element i of tensor (seed, layer, kind, x, t). */
 int  ds4f_gpu_synth_f32(float *dst_dev, int64_t n, uint64_t seed,
