@@ -226,6 +226,7 @@ def run_gpu(args, rank, world, local_rank):
                                 device_id=torch.device("cuda", local_rank))
     model = dc.Model(dc.FMT_FP8, LAYERS, H, M, E, K)
     model.synth(0)
+    model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(state, H, 0, 0, 4, rank, 0, 1.0)
     torch.cuda.synchronize()
@@ -288,12 +289,13 @@ def run_gpu(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": None, "peak_source": src,
-                         "kernel": "whole decode step (route, top-k, gate/up, down per layer; CUDA graph)",
+                         "kernel": ("whole decode step: 4 kernels per layer in a CUDA graph" if args.layered
+                                    else "k_decode: the whole 40-layer step in one persistent launch"),
                          "algorithmic_bytes_per_token": bpt},
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
                     "timer": "host clock around the synchronous C-ABI call"},
-            "gpu_launches": 4 * LAYERS * args.steps,
+            "gpu_launches": (4 * LAYERS if args.layered else 1) * args.steps,
             "router_exact_fallbacks": int(fallbacks),
             "clocks": clocks,
         }
@@ -310,6 +312,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layered", action="store_true",
+                    help="per-layer kernels (CUDA graph) instead of the persistent kernel")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -404,12 +404,13 @@ int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
     trunk_layout(d.hidden, d.moe_inter, d.n_experts, &m.tr);
     DS4F_CUDA(cudaGetDevice(&m.device));
     const int H = d.hidden, M = d.moe_inter, E = d.n_experts, K = d.topk;
-    size_t pool_b = (size_t)d.n_layers * d.expert_count * m.slot.nbytes;
+    // + 4 KB: bulk copies of small scale runs round up to 16 bytes
+    size_t pool_b = (size_t)d.n_layers * d.expert_count * m.slot.nbytes + 4096;
     size_t trunk_b = (size_t)d.n_layers * m.tr.n * 2;
     m.bmax = 64;
     size_t ws_b = al256(H * 4) + al256(E * 8) * 2 + al256(K * 4) * 2 +
                   al256((size_t)(K + 1) * M * 4) + al256(4) + al256(H * 4) + al256(16) +
-                  al256((size_t)m.bmax * H * 4) + al256((size_t)m.bmax * K * 4) * 2;
+                  al256((size_t)m.bmax * H * 4) + al256((size_t)m.bmax * K * 4) * 2 + al256(3 * 128);
     // memory plan first (invariant 5 of the reference, ds4f.h:32-35 /
     // mem.c): refuse past 95% of free device memory, allocate nothing.
     size_t fre = 0, tot = 0;
@@ -438,6 +439,7 @@ int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
     m.state_dev = (float *)take((size_t)m.bmax * H * 4);
     m.idx_dev = (int *)take((size_t)m.bmax * K * 4);
     m.w_dev = (float *)take((size_t)m.bmax * K * 4);
+    m.w.ctr = (unsigned *)take(3 * 128);
     cudaMemset(m.ws_base, 0, ws_b);
     if (cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking) != cudaSuccess) {
         cudaFree(m.pool); cudaFree(m.trunk); cudaFree(m.ws_base);
@@ -458,6 +460,7 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     cudaSetDevice(m.device);
     if (m.stream) cudaStreamSynchronize(m.stream);
     if (m.graph) cudaGraphExecDestroy(m.graph);
+    if (m.trace) cudaFree(m.trace);
     cudaFree(m.pool);
     cudaFree(m.trunk);
     cudaFree(m.ws_base);
@@ -656,6 +659,8 @@ int ds4f_gpu_moe_layer(Ds4fGpuModel *h, int layer, float *state, int *idx, float
 // One decode step of the layer stack, captured once into a CUDA graph per
 // state buffer and replayed.
 static int stack_step(Model &m, float *state, cudaStream_t st) {
+    if (m.path != 1 && decode_eligible(&m)) return decode_launch(&m, state, 1, st);
+    DS4F_REQUIRE(m.path != 2, "moe_stack: the persistent decode kernel does not cover this model");
     if (!m.graph || m.graph_state != state) {
         if (m.graph) { cudaGraphExecDestroy(m.graph); m.graph = nullptr; }
         cudaGraph_t g;
@@ -681,10 +686,48 @@ int ds4f_gpu_moe_stack_dev(Ds4fGpuModel *h, float *state, int n_steps, void *str
     DS4F_REQUIRE(m.d.expert_count == m.d.n_experts,
                  "moe_stack: model holds a shard; use the expert-parallel path");
     return on_model_stream(m, stream, [&](cudaStream_t st) {
+        if (n_steps > 0 && m.path != 1 && decode_eligible(&m))
+            return decode_launch(&m, state, n_steps, st);
         for (int s = 0; s < n_steps; s++)
             if (stack_step(m, state, st)) return -1;
         return 0;
     });
+}
+
+// Error word of the persistent kernel (set on a barrier or copy timeout).
+static int check_decode_error(const Model &m) {
+    unsigned d[4];
+    DS4F_CUDA(cudaMemcpy(d, m.w.diag, sizeof d, cudaMemcpyDeviceToHost));
+    DS4F_REQUIRE(d[2] == 0, "decode kernel gave up waiting (code %u at CTA %u): a phase "
+                 "barrier or weight copy did not complete", d[2], d[3]);
+    return 0;
+}
+
+int ds4f_gpu_model_trace(Ds4fGpuModel *h, int64_t n_stamps) {
+    DS4F_REQUIRE(h && n_stamps >= 0, "model_trace: bad arguments");
+    Model &m = h->m;
+    DS4F_CUDA(cudaStreamSynchronize(m.stream));
+    if (m.trace) { cudaFree(m.trace); m.trace = nullptr; m.trace_n = 0; }
+    if (n_stamps == 0) return 0;
+    DS4F_CUDA(cudaMalloc(&m.trace, (size_t)n_stamps * 8));
+    DS4F_CUDA(cudaMemset(m.trace, 0, (size_t)n_stamps * 8));
+    m.trace_n = n_stamps;
+    return 0;
+}
+
+int ds4f_gpu_model_trace_read(const Ds4fGpuModel *h, uint64_t *out, int64_t n_stamps) {
+    DS4F_REQUIRE(h && out && h->m.trace && n_stamps <= h->m.trace_n, "model_trace_read: bad arguments");
+    DS4F_CUDA(cudaStreamSynchronize(h->m.stream));
+    DS4F_CUDA(cudaMemcpy(out, h->m.trace, (size_t)n_stamps * 8, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int ds4f_gpu_model_set_path(Ds4fGpuModel *h, int path) {
+    DS4F_REQUIRE(h && path >= 0 && path <= 2, "model_set_path: bad arguments");
+    DS4F_REQUIRE(path != 2 || decode_eligible(&h->m),
+                 "model_set_path: the persistent decode kernel does not cover this model");
+    h->m.path = path;
+    return 0;
 }
 
 int ds4f_gpu_moe_stack(Ds4fGpuModel *h, float *state, int n_steps) {
@@ -695,16 +738,17 @@ int ds4f_gpu_moe_stack(Ds4fGpuModel *h, float *state, int n_steps) {
     if (ds4f_gpu_moe_stack_dev(h, m.state_dev, n_steps, m.stream)) return -1;
     DS4F_CUDA(cudaMemcpyAsync(state, m.state_dev, H * 4, cudaMemcpyDeviceToHost, m.stream));
     DS4F_CUDA(cudaStreamSynchronize(m.stream));
-    return 0;
+    return check_decode_error(m);
 }
 
 int ds4f_gpu_model_stats(const Ds4fGpuModel *h, uint64_t out[2]) {
     DS4F_REQUIRE(h && out, "model_stats: null argument");
     unsigned d[4];
+    DS4F_CUDA(cudaStreamSynchronize(h->m.stream));
     DS4F_CUDA(cudaMemcpy(d, h->m.w.diag, sizeof d, cudaMemcpyDeviceToHost));
     out[0] = d[0];
     out[1] = d[1];
-    return 0;
+    return check_decode_error(h->m);
 }
 
 int ds4f_gpu_synth_f32(float *dst, int64_t n, uint64_t seed, uint32_t layer, uint32_t kind,

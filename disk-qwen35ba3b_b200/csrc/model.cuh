@@ -43,6 +43,8 @@ struct Work {
     float *sgate;         // [1] shared_expert_gate logit
     float *acc;           // [H] moe output before the residual
     unsigned *diag;       // [4] 0: layers routed, 1: exact fallbacks, 2: error
+                          //     code of the persistent kernel, 3: its CTA
+    unsigned *ctr;        // [3 x 32] persistent-kernel phase counters
 };
 
 struct Model {
@@ -62,6 +64,9 @@ struct Model {
     cudaGraphExec_t graph;       // captured stack step (B = 1)
     float *graph_state;
     int graph_ok;
+    int path;                    // 0 auto, 1 per-layer kernels, 2 persistent
+    unsigned long long *trace;   // optional phase stamps of the persistent kernel
+    int64_t trace_n;
 };
 
 int slot_layout(int fmt, int H, int M, SlotLayout *s);
@@ -71,6 +76,10 @@ int trunk_layout(int H, int M, int E, TrunkLayout *t);
 // (device, [K]) optional copies of the routing.
 int moe_layer_launch(Model *m, int L, float *state, int *idx_out,
                      float *w_out, cudaStream_t st);
+
+// Whole decode steps in one persistent cooperative launch (decode.cu).
+bool decode_eligible(const Model *m);
+int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st);
 
 // GPU copy of the seeded fixture generator (oracle/fixture.c): fills the
 // model's trunk and expert shard.

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "libds4f_cuda.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "ds4f", "gpu_cuda.h")
 
 FMT_MXFP4, FMT_MLX4, FMT_FP8, FMT_BF16 = 0, 1, 2, 3
+PATH_AUTO, PATH_LAYERED, PATH_PERSISTENT = 0, 1, 2
 SCALE_E8M0, SCALE_F32 = 0, 1
 
 _vp = C.c_void_p
@@ -75,6 +76,9 @@ def lib():
             "ds4f_gpu_moe_stack": [_vp, _vp, C.c_int],
             "ds4f_gpu_moe_stack_dev": [_vp, _vp, C.c_int, _vp],
             "ds4f_gpu_model_stats": [_vp, _vp],
+            "ds4f_gpu_model_set_path": [_vp, C.c_int],
+            "ds4f_gpu_model_trace": [_vp, C.c_int64],
+            "ds4f_gpu_model_trace_read": [_vp, _vp, C.c_int64],
             "ds4f_gpu_synth_f32": [_vp, C.c_int64, C.c_uint64, C.c_uint32, C.c_uint32,
                                    C.c_uint32, C.c_uint32, C.c_double, _vp],
         }
@@ -266,6 +270,18 @@ class Model:
 
     def stack_dev(self, state, n_steps, stream=None):
         check(lib().ds4f_gpu_moe_stack_dev(self.h, ptr(state), n_steps, stream))
+
+    def set_path(self, path):
+        """0 auto, 1 per-layer kernels, 2 persistent decode kernel."""
+        check(lib().ds4f_gpu_model_set_path(self.h, path))
+
+    def trace(self, n_stamps):
+        check(lib().ds4f_gpu_model_trace(self.h, n_stamps))
+
+    def trace_read(self, n_stamps):
+        out = np.zeros(n_stamps, np.uint64)
+        check(lib().ds4f_gpu_model_trace_read(self.h, ptr(out), n_stamps))
+        return out
 
     def stats(self):
         out = (C.c_uint64 * 2)()

@@ -172,7 +172,25 @@ int  ds4f_gpu_moe_layer_dev(Ds4fGpuModel *m, int layer, float *state,
 int  ds4f_gpu_moe_stack(Ds4fGpuModel *m, float *state, int n_steps);
 int  ds4f_gpu_moe_stack_dev(Ds4fGpuModel *m, float *state, int n_steps,
                             void *stream);
-/* Counters: [0] layers routed, [1] router exact-fallbacks taken. */
+/* Decode-step implementation: DS4F_PATH_AUTO (persistent kernel where it
+ * covers the model: top-8, (H, M) = (2048, 512) or (1024, 256), 64 or 256
+ * experts, whole pool on this device), DS4F_PATH_LAYERED (four kernels per
+ * layer in a CUDA graph), DS4F_PATH_PERSISTENT (fail if not covered). */
+#define DS4F_PATH_AUTO 0
+#define DS4F_PATH_LAYERED 1
+#define DS4F_PATH_PERSISTENT 2
+int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
+/* Phase trace of the persistent decode kernel (the counterpart of the
+ * reference's per-phase timers, src/main.c:253-258, 1522-1546): with
+ * n_stamps > 0 every launch whose layers x steps x SMs x 10 stamps fit
+ * records %globaltimer (ns) per (layer-step, CTA) at 10 phase boundaries:
+ * start, state ready, normed, router+shared done, routes visible, top-k
+ * done, copies issued, chains done, chains visible, state written.
+ * n_stamps = 0 turns it off. */
+int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
+int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
+/* Counters: [0] layers routed, [1] router exact-fallbacks taken. Also
+ * reports (-1) a persistent-kernel wait that gave up. */
 int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
 
 /* ---- allocation-free layer step ------------------------------------- */

@@ -198,3 +198,82 @@ def test_pool_load_packed_file(tmp_path, fmt):
 def test_memory_plan_refuses_oversized_pool():
     with pytest.raises(dc.GpuError, match="refusing"):
         dc.Model(dc.FMT_FP8, 4000, 2048, 512, 256, 8)
+
+
+# ---- the persistent decode kernel (one cooperative launch per step) ----------
+
+def _stack_path(m, x0, steps, path):
+    m.set_path(path)
+    return m.stack(x0, steps)
+
+
+@pytest.mark.parametrize("fmt", [dc.FMT_FP8, dc.FMT_MXFP4])
+@pytest.mark.parametrize("shape", [(1024, 256, 64, 4), (2048, 512, 256, 2)])
+def test_persistent_matches_layered_and_oracle(fmt, shape):
+    H, M, E, L = shape
+    m = dc.Model(fmt, L, H, M, E, 8)
+    m.synth(41)
+    x0 = po.fill_f32(H, po.key(41, 0, 4, 0, 0), 1.0)
+    got_p = _stack_path(m, x0, 2, dc.PATH_PERSISTENT)
+    got_l = _stack_path(m, x0, 2, dc.PATH_LAYERED)
+    assert relerr(got_p - x0, got_l - x0) < CHAIN_TOL
+    # free-running oracle over the same 2 steps
+    st = x0.copy()
+    for s in range(2):
+        for layer in range(L):
+            lay = oracle_layer(m, layer, fmt, st)
+            st, _, _, _, _ = lay.moe(st, 8)
+    assert relerr(got_p - x0, st - x0) < CHAIN_TOL
+    m.close()
+
+
+def test_persistent_multi_step_launch_equals_single_steps():
+    import torch
+    m = dc.Model(dc.FMT_FP8, 3, 1024, 256, 64, 8)
+    m.synth(5)
+    m.set_path(dc.PATH_PERSISTENT)
+    x0 = po.fill_f32(1024, po.key(5, 0, 4, 0, 0), 1.0)
+    a = torch.from_numpy(x0.copy()).cuda()
+    b = torch.from_numpy(x0.copy()).cuda()
+    m.stack_dev(a, 4)                      # one launch, 4 steps
+    for _ in range(4):
+        m.stack_dev(b, 1)                  # four launches
+    torch.cuda.synchronize()
+    assert np.array_equal(a.cpu().numpy(), b.cpu().numpy())
+    assert m.stats()[0] > 0
+    m.close()
+
+
+def test_persistent_tie_uses_exact_fallback():
+    m = dc.Model(dc.FMT_FP8, 1, 1024, 256, 64, 8)
+    m.synth(8)
+    tr = m.get_trunk(0)
+    x = po.fill_f32(1024, po.key(8, 0, 4, 0, 0), 1.0)
+    lay = oracle_layer(m, 0, dc.FMT_FP8, x)
+    idx, _, _, _ = lay.route(x, 8)
+    a = int(idx[3])
+    b = [e for e in range(64) if e not in idx and e > a][0]
+    tr[1][b] = tr[1][a]
+    m.set_trunk(0, *tr)
+    m.set_path(dc.PATH_PERSISTENT)
+    before = m.stats()[1]
+    got = m.stack(x, 1)
+    lay = oracle_layer(m, 0, dc.FMT_FP8, x, [a, b])
+    st_o, idx_o, _, _, acc_o = lay.moe(x, 8)
+    assert a in idx_o.tolist() and b in idx_o.tolist()
+    assert m.stats()[1] > before
+    assert relerr(got.astype(np.float64) - x, acc_o) < CHAIN_TOL
+    m.close()
+
+
+def test_persistent_router_exact_mode():
+    m = dc.Model(dc.FMT_MXFP4, 2, 1024, 256, 64, 8, router_exact=True)
+    m.synth(9)
+    m.set_path(dc.PATH_PERSISTENT)
+    x = po.fill_f32(1024, po.key(9, 0, 4, 0, 0), 1.0)
+    got = m.stack(x, 1)
+    st = x.copy()
+    for layer in range(2):
+        st, _, _, _, _ = oracle_layer(m, layer, dc.FMT_MXFP4, st).moe(st, 8)
+    assert relerr(got - x, st - x) < CHAIN_TOL
+    m.close()
