@@ -410,7 +410,8 @@ int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
     m.bmax = 64;
     size_t ws_b = al256(H * 4) + al256(E * 8) * 2 + al256(K * 4) * 2 +
                   al256((size_t)(K + 1) * M * 4) + al256(4) + al256(H * 4) + al256(16) +
-                  al256((size_t)m.bmax * H * 4) + al256((size_t)m.bmax * K * 4) * 2 + al256(3 * 128);
+                  al256((size_t)m.bmax * H * 4) + al256((size_t)m.bmax * K * 4) * 2 +
+                  al256((size_t)H * 8) + al256((size_t)E * 32) + al256(((size_t)(K + 1) * M + 2) * 8);
     // memory plan first (invariant 5 of the reference, ds4f.h:32-35 /
     // mem.c): refuse past 95% of free device memory, allocate nothing.
     size_t fre = 0, tot = 0;
@@ -439,7 +440,9 @@ int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
     m.state_dev = (float *)take((size_t)m.bmax * H * 4);
     m.idx_dev = (int *)take((size_t)m.bmax * K * 4);
     m.w_dev = (float *)take((size_t)m.bmax * K * 4);
-    m.w.ctr = (unsigned *)take(3 * 128);
+    m.w.st_ll = (uint64_t *)take((size_t)H * 8);
+    m.w.sb_ll = (uint64_t *)take((size_t)E * 32);
+    m.w.ch_ll = (uint64_t *)take(((size_t)(K + 1) * M + 2) * 8);   // + pad word
     cudaMemset(m.ws_base, 0, ws_b);
     if (cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking) != cudaSuccess) {
         cudaFree(m.pool); cudaFree(m.trunk); cudaFree(m.ws_base);

@@ -1,31 +1,33 @@
 // decode.cu -- persistent decode kernel: every layer of a decode step (and
 // several steps) for one token in ONE cooperative launch, one CTA per SM.
 //
-// Per layer, each CTA c of G owns a static slice of every phase:
-//   router rows   [c E/G, (c+1) E/G)     shared gate/up rows [c M/G, ...)
-//   routed (selection, row) pairs [c K M/G, ...)    output rows [c H/G, ...)
-// and runs
-//   (A) wait for the layer's input state        (flag: state counter)
-//   (B) RMSNorm of the full state into shared memory
-//   (C) its router rows: S, bound (certified logits, see moe.cu); its shared
-//       gate/up rows -> shared SiLU chain; publish      (flag: route counter)
-//   (E) TMA-prefetch the next layer's router and shared gate/up rows
-//   (F) wait for all router rows; top-k + softmax + renorm (every CTA, same
-//       bits); exact reference-order logits for near-ties
-//   (G) TMA the selected experts' gate/up rows (2-stage ring) and down rows
-//   (H) gate/up dots + SiLU-mul -> chains; publish      (flag: chain counter)
-//   (J) down rows (routed + shared, prefetched) -> selection-order combine,
-//       shared gate, residual on its output rows        (flag: state counter)
-//   (K) TMA-prefetch the next layer's shared down rows
-// Weights never round-trip through the host; the router and shared-expert
-// bytes stream during the routing bubble, the routed bytes right after it.
-// Reference: ds4f_moe_step (src/moe.c:948-1456) and its router call site
-// (src/main.c:1014-1088), per layer, for the decode loop (src/main.c:848).
+// Per layer, CTA c of G owns a static slice of every phase: router rows
+// [cE/G, (c+1)E/G), shared gate/up rows [cM/G, ...), routed (selection,
+// row) pairs [cKM/G, ...) and output rows [cH/G, ...). A layer is
+//   (A) the layer's input state (tagged words, see below)
+//   (B) RMSNorm of the full state (src/moe.c:841-851)
+//   (C) its router rows -> certified logits S and bounds B, published
+//   (D) its shared-expert gate/up rows -> shared SiLU chain, published
+//   (F) every CTA: poll all S/B, top-k + softmax + renorm (same bits in
+//       every CTA); exact reference-order logits only for near-ties
+//   (G) TMA bulk copies of ALL of its routed gate/up rows and down rows
+//       (about 176 KB per SM for FP8, in flight at once), 4 sub-barriers
+//   (H) gate/up dots + SiLU-mul as the bytes land -> chains, published
+//   (I) down rows (routed + prefetched shared) against the polled chains,
+//       selection-order combine, shared gate, residual -> state, published
+// The next layer's router rows + norm weights and shared down rows are
+// prefetched by TMA during the current layer.
 //
-// Waits are bounded (flag spins and mbarrier waits give up after ~2 s,
-// record an error code and drain this CTA's copies before returning).
-// Data written by other CTAs is read with ld.global.cg (L2), never through
-// the incoherent L1 / read-only paths.
+// Publication: a value written by one CTA for the others is an 8-byte word
+// (tag << 32 | bits) stored with st.relaxed.gpu; a reader polls the word
+// with ld.relaxed.gpu until the tag is the one of this layer, so the data
+// itself is the signal (one L2 round trip, no counters or atomics). Tags
+// are (launch epoch << 16) | (layer-step + 1). Every wait is bounded: a
+// poll or copy wait that gives up records an error code, the CTA drains its
+// own copies and returns; the host reports it.
+//
+// Reference: ds4f_moe_step (src/moe.c:948-1456) and its router call site
+// (src/main.c:1014-1088), per layer of the decode loop (src/main.c:848).
 #include "model.cuh"
 
 #include <algorithm>
@@ -36,10 +38,12 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kGmin = 128;                 // smem is sized for grids >= this
-constexpr int kStagePairs = 8;
-constexpr long kSpinLimit = 1L << 25;      // x ~64 ns sleep: ~2 s
+constexpr int kGmin = 144;                 // shared memory is sized for G >= this
+constexpr int kGroupPairs = 8;             // gate/up pairs per copy group
+constexpr int kGroups = 4;
+constexpr long kSpin = 1L << 24;           // polls (with backoff) before giving up
 constexpr double kU = 5.9604644775390625e-08;
+constexpr int kTracePts = 20;
 
 // ---- PTX helpers ------------------------------------------------------------
 __device__ __forceinline__ uint32_t sa(const void *p) {
@@ -60,7 +64,6 @@ __device__ __forceinline__ bool mbar_test(uint64_t *b, uint32_t parity) {
         : "=r"(ok) : "r"(sa(b)), "r"(parity) : "memory");
     return ok != 0;
 }
-// global -> this CTA's shared memory, completion counted on mbarrier b
 __device__ __forceinline__ void bulk(void *dst, const void *src, uint32_t bytes, uint64_t *b) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -69,13 +72,28 @@ __device__ __forceinline__ void bulk(void *dst, const void *src, uint32_t bytes,
 __device__ __forceinline__ void fence_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-// 16-byte shared-memory load (asm volatile: not hoisted across the
-// mbarrier waits that publish the TMA-written bytes)
 __device__ __forceinline__ uint4 lds16(const void *p) {
     uint4 r;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(sa(p)) : "memory");
     return r;
+}
+__device__ __forceinline__ void st_tag(uint64_t *p, uint32_t tag, uint32_t bits) {
+    uint64_t w = ((uint64_t)tag << 32) | bits;
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// order-preserving 32-bit key of a float
+__device__ __forceinline__ uint32_t fkey(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
 // ---- shapes -------------------------------------------------------------------
@@ -84,46 +102,56 @@ struct Shape {
     static constexpr int row_b = FMT == DS4F_FMT_FP8 ? H : H / 2;     // gate/up row bytes
     static constexpr int drow_b = FMT == DS4F_FMT_FP8 ? M : M / 2;    // down row bytes
     static constexpr int ce = FMT == DS4F_FMT_FP8 ? 16 : 32;          // elements / 16 B
-    static constexpr int gq = H / ce;                                  // chunks per gate row
-    static constexpr int gk = gq / 32;                                 // chunks per lane
+    static constexpr int gk = H / ce / 32;                             // gate chunks per lane
     static constexpr int dq = M / ce;                                  // chunks per down row
     static constexpr int dlpr = dq < 32 ? dq : 32;                     // lanes per down row
     static constexpr int dk = dq / dlpr;
     static constexpr int bq = M / 8;                                   // bf16 down chunks
     static constexpr int blpr = bq < 32 ? bq : 32;
     static constexpr int bk = bq / blpr;
-    // FP8: whole scale blocks; MXFP4: E8M0 per 32 along K, per row
     static constexpr int gsc_b = FMT == DS4F_FMT_FP8 ? (M / 128) * (H / 128) * 4 : H / 32;
     static constexpr int dsc_b = FMT == DS4F_FMT_FP8 ? (H / 128) * (M / 128) * 4 : M / 32;
-    static_assert(gk >= 1 && gq % 32 == 0, "gate/up rows must span the warp");
+    static constexpr int cpl = H / 32;                                 // router cols per lane
+    static_assert(gk >= 1 && H % (ce * 32) == 0, "gate/up rows must span the warp");
+    static_assert(cpl % 8 == 0, "router rows: whole 8-element chunks per lane");
 };
 
 template <int FMT, int H, int M, int E, int K>
 struct Smem {
     using S = Shape<FMT, H, M>;
-    static constexpr int RT = (E + kGmin - 1) / kGmin;          // router rows per CTA
-    static constexpr int SG = (M + kGmin - 1) / kGmin;          // shared rows per CTA
-    static constexpr int RR = (H + kGmin - 1) / kGmin;          // output rows per CTA
-    static constexpr int GSC_SEG = FMT == DS4F_FMT_FP8 ? S::gsc_b : kStagePairs * S::gsc_b;
-    static constexpr int DSC = FMT == DS4F_FMT_FP8 ? S::dsc_b : (RR * S::dsc_b + 48 + 15) / 16 * 16;
-    // byte offsets (16-byte aligned)
     static constexpr int a16(int n) { return (n + 15) / 16 * 16; }
+    static constexpr int RT = (E + kGmin - 1) / kGmin;          // router rows per CTA
+    static constexpr int RR = (H + kGmin - 1) / kGmin;          // output rows per CTA
+    static constexpr int PP = (K * M + kGmin - 1) / kGmin;      // gate/up pairs per CTA
+    static constexpr int GSC = FMT == DS4F_FMT_FP8 ? kGroups * 2 * 2 * S::gsc_b   // [group][seg][mat]
+                                                   : PP * 2 * S::gsc_b;          // [mat][pair]
+    static constexpr int DSC = FMT == DS4F_FMT_FP8 ? S::dsc_b : a16(RR * S::dsc_b + 48);
+    static_assert(PP <= kGroups * kGroupPairs, "gate/up pairs exceed the copy groups");
     static constexpr int o_bar = 0;                                   // 8 mbarriers
     static constexpr int o_xin = 128;
-    static constexpr int o_rt = o_xin + a16(H * 4);
-    static constexpr int o_sgu = o_rt + a16(RT * H * 2);
-    static constexpr int o_sd = o_sgu + a16(SG * 2 * H * 2);
+    static constexpr int o_nw = o_xin + a16(H * 4);
+    static constexpr int o_rt = o_nw + a16(H * 2);
+    static constexpr int o_sd = o_rt + a16(RT * H * 2);
     static constexpr int o_dn = o_sd + a16(RR * M * 2);
     static constexpr int o_dsc = o_dn + a16(K * RR * S::drow_b);
-    static constexpr int o_stage = o_dsc + a16(K * DSC);
-    static constexpr int stage_w = kStagePairs * S::row_b;           // gate rows of a stage
-    static constexpr int stage_b = a16(2 * stage_w + 2 * 2 * GSC_SEG);
-    static constexpr int o_red = o_stage + 2 * stage_b;
-    static constexpr int o_out = o_red + 1024;                        // (K+1) x RR floats
-    static constexpr int o_chain = o_out + a16((K + 1) * RR * 4);     // (K+1) x M floats
-    static constexpr int o_topk = o_chain + a16((K + 1) * M * 4);     // tk[E] doubles
-    static constexpr int o_cand = o_topk + a16(E * 8);                // candf[E] ints
-    static constexpr int o_sel = o_cand + a16(E * 4);                 // sel[64], wsel[64], ctl[16]
+    // gate rows then up rows; between uses it receives the tagged-word
+    // gathers (state, router logits, chains)
+    static constexpr int GATH = 8 * ((H > 4 * E ? H : 4 * E) > (K + 1) * M + 2
+                                         ? (H > 4 * E ? H : 4 * E) : (K + 1) * M + 2);
+    // + the chains unpacked to floats after the tagged words
+    static constexpr int UNP = GATH + 4 * ((K + 1) * M + 4);
+    static constexpr int GU = 2 * PP * S::row_b > UNP ? 2 * PP * S::row_b : UNP;
+    static constexpr int o_gu = o_dsc + a16(K * DSC);
+    static constexpr int o_gsc = o_gu + a16(GU);
+    static constexpr int o_srow = o_gsc + a16(GSC);
+    static constexpr int o_outs = o_srow + a16(RR * 4);
+    // 1 KB scratch: doubles [0, 64) for reductions and the top-k ranks,
+    // floats [192, 200) for the shared gate/up partial sums
+    static constexpr int o_red = o_outs + a16((K + 1) * RR * 4);
+    static constexpr int o_tk = o_red + 1024;                         // [E] doubles
+    static constexpr int o_cand = o_tk + a16(E * 8);                  // [E] ints
+    static constexpr int o_cl = o_cand + a16(E * 4);                  // candidates: 4 x 32 doubles
+    static constexpr int o_sel = o_cl + 4 * 32 * 8;                   // sel[64], wsel[64], ctl[16]
     static constexpr int bytes = o_sel + 64 * 4 + 64 * 4 + 16 * 4;
 };
 
@@ -135,58 +163,59 @@ struct DecodeArgs {
     int64_t trunk_n;            // elements per layer block
     TrunkLayout tr;
     int n_layers, n_steps, E, renorm, exact_all;
-    float *state;               // [H] in/out
-    double *S, *B;              // [E]
-    float *chain;               // [(K+1) M]
-    float *sgate;
-    unsigned *ctr;              // [3 * 32]: route, chain, state counters (128 B apart)
+    uint32_t epoch;             // 1..65535, distinct from the previous launch's
+    float *state;               // [H] in (read at layer 0) / out (last layer)
+    uint64_t *st_ll;            // [H] tagged state words
+    uint64_t *sb_ll;            // [E][4] tagged S (lo, hi) and B (lo, hi) words
+    uint64_t *ch_ll;            // [(K+1) M + 1] tagged chains, then the shared-gate logit
     unsigned *diag;             // [4]: layers, fallbacks, error code, failing CTA
     unsigned long long *trace;  // optional [T][G][kTracePts] %globaltimer stamps
 };
 
-constexpr int kTracePts = 10;
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-
 __device__ __forceinline__ bool aborted(const DecodeArgs &a) {
     return *(volatile unsigned *)(a.diag + 2) != 0;
 }
-
-// thread 0 only: spin until *ctr >= target; false on abort / timeout
-__device__ bool flag_wait(const DecodeArgs &a, const unsigned *ctr, unsigned target, unsigned code) {
-    long it = 0;
-    while (true) {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-        if (v >= target) return true;
-        if (aborted(a)) return false;
-        if (++it > kSpinLimit) {
-            if (atomicCAS(a.diag + 2, 0u, code) == 0u) a.diag[3] = blockIdx.x;
-            return false;
-        }
-        __nanosleep(64);
-    }
+__device__ void give_up(const DecodeArgs &a, unsigned code) {
+    if (atomicCAS(a.diag + 2, 0u, code) == 0u) a.diag[3] = blockIdx.x;
 }
 
-__device__ __forceinline__ void flag_arrive(unsigned *ctr) {
-    __threadfence();
-    atomicAdd(ctr, 1u);
-}
-
-// all threads: wait for mbarrier phase; false on timeout (error recorded)
 __device__ bool mbar_wait(const DecodeArgs &a, uint64_t *b, uint32_t parity, unsigned code) {
     long it = 0;
     while (!mbar_test(b, parity)) {
-        if (++it > kSpinLimit) {
-            if (atomicCAS(a.diag + 2, 0u, code) == 0u) a.diag[3] = blockIdx.x;
-            return false;
-        }
-        __nanosleep(32);
+        if (++it > kSpin) { give_up(a, code); return false; }
+        if (it > 16) __nanosleep(32);
     }
     return true;
+}
+
+// CTA-wide, every thread calls it: TMA-copy the tagged words src[0, n)
+// into shared memory until the first `ncheck` of them carry `tag` (re-copy
+// while any is still from an earlier layer); n is even (16-byte copies).
+// One bulk copy per round instead of per-thread polls. false (uniformly)
+// on timeout or abort.
+__device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &ph, bool &pend,
+                          uint64_t *dst, const uint64_t *src, int n, int ncheck, uint32_t tag,
+                          unsigned code) {
+    const int tid = threadIdx.x;
+    for (long it = 0;; it++) {
+        if (tid == 0) {
+            fence_async();
+            mbar_expect(bar, n * 8);
+            bulk(dst, src, n * 8, bar);
+        }
+        pend = true;
+        if (!__syncthreads_and(mbar_wait(a, bar, ph, code))) return false;
+        ph ^= 1;
+        pend = false;
+        bool all = true;
+        for (int i = tid; i < ncheck; i += kThreads) all = all && (uint32_t)(dst[i] >> 32) == tag;
+        if (__syncthreads_and(all)) return true;
+        if (__syncthreads_or(it > (1L << 20) || aborted(a))) {
+            if (tid == 0 && !aborted(a)) give_up(a, code);
+            return false;
+        }
+        __nanosleep(128);
+    }
 }
 
 template <int FMT, int H, int M, int E, int K>
@@ -195,128 +224,106 @@ k_decode(DecodeArgs a) {
     using S = Shape<FMT, H, M>;
     using L = Smem<FMT, H, M, E, K>;
     extern __shared__ __align__(128) unsigned char sm[];
+    // bar 0: router rows + norm weights; 1: shared down rows;
+    // 2..5: gate/up copy groups; 6: routed down rows; 7: tagged gathers
     uint64_t *bar = (uint64_t *)(sm + L::o_bar);
-    // bar[0]: router + shared gate/up rows; bar[1]: shared down rows;
-    // bar[2], bar[3]: gate/up ring; bar[4]: routed down rows
     float *xin = (float *)(sm + L::o_xin);
+    uint16_t *nw = (uint16_t *)(sm + L::o_nw);
     uint16_t *rt = (uint16_t *)(sm + L::o_rt);
-    uint16_t *sgu = (uint16_t *)(sm + L::o_sgu);
     uint16_t *sd = (uint16_t *)(sm + L::o_sd);
     uint8_t *dn = sm + L::o_dn;
     uint8_t *dsc = sm + L::o_dsc;
-    uint8_t *stage = sm + L::o_stage;
-    float *red = (float *)(sm + L::o_red);          // 256 floats of scratch
-    float *outs = (float *)(sm + L::o_out);
-    float *cs = (float *)(sm + L::o_chain);         // staged chains
-    double *tk = (double *)(sm + L::o_topk);        // [E] logit used for softmax
-    int *candf = (int *)(sm + L::o_cand);           // [E] exact-path candidates
-    int *sel = (int *)(sm + L::o_sel);              // [64] selection order
-    float *wsel = (float *)(sel + 64);              // [64] weights
-    int *ctl = (int *)(wsel + 64);                  // control words
+    uint8_t *gu = sm + L::o_gu;
+    uint8_t *gsc = sm + L::o_gsc;
+    float *srow = (float *)(sm + L::o_srow);
+    float *outs = (float *)(sm + L::o_outs);
+    float *red = (float *)(sm + L::o_red);
+    double *tk = (double *)(sm + L::o_tk);
+    int *candf = (int *)(sm + L::o_cand);
+    double *cl = (double *)(sm + L::o_cl);          // [4][32]: S, lo, hi, e
+    int *sel = (int *)(sm + L::o_sel);
+    float *wsel = (float *)(sel + 64);
+    int *ctl = (int *)(wsel + 64);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, c = blockIdx.x;
-    const int rt0 = c * E / G, rt1 = (c + 1) * E / G;
-    const int sg0 = c * M / G, sg1 = (c + 1) * M / G;
-    const int p0 = c * (K * M) / G, p1 = (c + 1) * (K * M) / G;
-    const int r0 = c * H / G, r1 = (c + 1) * H / G, nr = r1 - r0;
-    const int nstages = (p1 - p0 + kStagePairs - 1) / kStagePairs;
-    unsigned *c_route = a.ctr, *c_chain = a.ctr + 32, *c_state = a.ctr + 64;
+    const int rt0 = c * E / G, nrt = (c + 1) * E / G - rt0;
+    const int sg0 = c * M / G, nsg = (c + 1) * M / G - sg0;
+    const int p0 = c * (K * M) / G, np = (c + 1) * (K * M) / G - p0;
+    const int r0 = c * H / G, nr = (c + 1) * H / G - r0;
+    const int ngroups = (np + kGroupPairs - 1) / kGroupPairs;
 
-    uint32_t ph[5] = {0, 0, 0, 0, 0};          // next parity to wait per barrier
-    bool pend[5] = {false, false, false, false, false};
+    uint32_t ph[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    bool pend[8] = {false, false, false, false, false, false, false, false};
     bool ok = true;
 
     if (tid == 0) {
-        for (int i = 0; i < 5; i++) mbar_init(bar + i, 1);
+        for (int i = 0; i < 8; i++) mbar_init(bar + i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
     auto trunk_l = [&](int l) { return a.trunk + (int64_t)l * a.trunk_n; };
     auto expert = [&](int l, int e) { return a.pool + ((int64_t)l * a.E + e) * a.slot_bytes; };
+    auto tag_of = [&](int t) { return (a.epoch << 16) | (uint32_t)(t + 1); };
 
-    // TMA: router + shared gate/up rows of layer l (bar 0)
+    // one thread: router rows + norm weights of layer l (bar 0)
     auto prefetch_rt = [&](int l) {
         const uint16_t *t = trunk_l(l);
-        uint32_t b1 = (rt1 - rt0) * H * 2, b2 = (sg1 - sg0) * H * 2;
-        mbar_expect(bar + 0, b1 + 2 * b2);
+        uint32_t b1 = nrt * H * 2;
+        mbar_expect(bar + 0, b1 + H * 2);
+        bulk(nw, t + a.tr.norm, H * 2, bar + 0);
         if (b1) bulk(rt, t + a.tr.router + (int64_t)rt0 * H, b1, bar + 0);
-        if (b2) {
-            bulk(sgu, t + a.tr.sh_gate + (int64_t)sg0 * H, b2, bar + 0);
-            bulk(sgu + L::SG * H, t + a.tr.sh_up + (int64_t)sg0 * H, b2, bar + 0);
-        }
     };
-    // TMA: shared down rows of layer l (bar 1)
+    // one thread: shared down rows of layer l (bar 1)
     auto prefetch_sd = [&](int l) {
         uint32_t b = nr * M * 2;
         mbar_expect(bar + 1, b);
         if (b) bulk(sd, trunk_l(l) + a.tr.sh_down + (int64_t)r0 * M, b, bar + 1);
     };
-    // TMA: gate/up stage s of layer l into ring slot s & 1 (bar 2 + slot)
-    auto issue_stage = [&](int l, int s) {
-        uint8_t *st = stage + (s & 1) * L::stage_b;
-        uint8_t *wg = st, *wu = st + L::stage_w, *sc = st + 2 * L::stage_w;
-        int q0 = p0 + s * kStagePairs, q1 = min(q0 + kStagePairs, p1);
+    // one thread: gate/up group g of layer l (bar 2 + g)
+    auto issue_group = [&](int l, int g) {
+        const int q0 = p0 + g * kGroupPairs, q1 = min(q0 + kGroupPairs, p0 + np);
         uint32_t total = 0;
-        int seg = 0;
-        struct { int j, i0, i1, slot; } sgs[2];
         for (int q = q0; q < q1;) {
-            int j = q / M, i0 = q % M, n = min(q1 - q, M - i0);
-            sgs[seg] = {j, i0, i0 + n, q - q0};
-            seg++;
+            int i0 = q % M, n = min(q1 - q, M - i0);
+            total += 2 * n * S::row_b + (FMT == DS4F_FMT_FP8 ? 2 * S::gsc_b : 2 * n * S::gsc_b);
             q += n;
         }
-        for (int g = 0; g < seg; g++) {
-            int n = sgs[g].i1 - sgs[g].i0;
-            total += 2 * n * S::row_b;
-            total += FMT == DS4F_FMT_FP8 ? 2 * S::gsc_b : 2 * n * S::gsc_b;
-        }
-        mbar_expect(bar + 2 + (s & 1), total);
-        for (int g = 0; g < seg; g++) {
-            const uint8_t *ex = expert(l, sel[sgs[g].j]);
-            int n = sgs[g].i1 - sgs[g].i0, sl = sgs[g].slot;
-            bulk(wg + sl * S::row_b, ex + a.slot.rel_v[0] + (int64_t)sgs[g].i0 * S::row_b,
-                 n * S::row_b, bar + 2 + (s & 1));
-            bulk(wu + sl * S::row_b, ex + a.slot.rel_v[1] + (int64_t)sgs[g].i0 * S::row_b,
-                 n * S::row_b, bar + 2 + (s & 1));
+        mbar_expect(bar + 2 + g, total);
+        int seg = 0;
+        for (int q = q0; q < q1; seg++) {
+            const int j = q / M, i0 = q % M, n = min(q1 - q, M - i0), slot = q - p0;
+            const uint8_t *ex = expert(l, sel[j]);
+            bulk(gu + slot * S::row_b, ex + a.slot.rel_v[0] + (int64_t)i0 * S::row_b,
+                 n * S::row_b, bar + 2 + g);
+            bulk(gu + (L::PP + slot) * S::row_b, ex + a.slot.rel_v[1] + (int64_t)i0 * S::row_b,
+                 n * S::row_b, bar + 2 + g);
             if (FMT == DS4F_FMT_FP8) {
-                bulk(sc + g * L::GSC_SEG, ex + a.slot.rel_s[0], S::gsc_b, bar + 2 + (s & 1));
-                bulk(sc + (2 + g) * L::GSC_SEG, ex + a.slot.rel_s[1], S::gsc_b, bar + 2 + (s & 1));
+                bulk(gsc + ((g * 2 + seg) * 2 + 0) * S::gsc_b, ex + a.slot.rel_s[0], S::gsc_b, bar + 2 + g);
+                bulk(gsc + ((g * 2 + seg) * 2 + 1) * S::gsc_b, ex + a.slot.rel_s[1], S::gsc_b, bar + 2 + g);
             } else {
-                bulk(sc + sl * S::gsc_b, ex + a.slot.rel_s[0] + (int64_t)sgs[g].i0 * S::gsc_b,
-                     n * S::gsc_b, bar + 2 + (s & 1));
-                bulk(sc + L::GSC_SEG * 2 + sl * S::gsc_b,
-                     ex + a.slot.rel_s[1] + (int64_t)sgs[g].i0 * S::gsc_b, n * S::gsc_b,
-                     bar + 2 + (s & 1));
+                bulk(gsc + slot * S::gsc_b, ex + a.slot.rel_s[0] + (int64_t)i0 * S::gsc_b,
+                     n * S::gsc_b, bar + 2 + g);
+                bulk(gsc + (L::PP + slot) * S::gsc_b, ex + a.slot.rel_s[1] + (int64_t)i0 * S::gsc_b,
+                     n * S::gsc_b, bar + 2 + g);
             }
+            q += n;
         }
     };
-    // TMA: routed down rows [r0, r1) of the K selected experts (bar 4)
-    auto issue_down = [&](int l) {
-        uint32_t total = K * nr * S::drow_b;
-        int64_t sa0 = 0, sab = 0;
-        if (FMT == DS4F_FMT_FP8) {
-            total += K * S::dsc_b;
-        } else {
-            sa0 = ((int64_t)r0 * S::dsc_b) / 16 * 16;
-            sab = (((int64_t)r1 * S::dsc_b + 15) / 16) * 16 - sa0;
-            total += K * (uint32_t)sab;
-        }
-        mbar_expect(bar + 4, total);
-        for (int j = 0; j < K; j++) {
-            const uint8_t *ex = expert(l, sel[j]);
-            if (nr)
-                bulk(dn + j * L::RR * S::drow_b, ex + a.slot.rel_v[2] + (int64_t)r0 * S::drow_b,
-                     nr * S::drow_b, bar + 4);
-            if (FMT == DS4F_FMT_FP8)
-                bulk(dsc + j * L::DSC, ex + a.slot.rel_s[2], S::dsc_b, bar + 4);
-            else
-                bulk(dsc + j * L::DSC, ex + a.slot.rel_s[2] + sa0, (uint32_t)sab, bar + 4);
-        }
+    // bytes of the routed down copies (rows + scales of K experts)
+    const int sa0 = FMT == DS4F_FMT_FP8 ? 0 : (r0 * S::dsc_b) / 16 * 16;
+    const int sab = FMT == DS4F_FMT_FP8 ? S::dsc_b : ((r0 + nr) * S::dsc_b + 15) / 16 * 16 - sa0;
+    const uint32_t dn_total = K * (nr * S::drow_b + sab);
+    // lane j < K of warp 0: down rows + scales of selection j (bar 6)
+    auto issue_down_j = [&](int l, int j) {
+        const uint8_t *ex = expert(l, sel[j]);
+        if (nr)
+            bulk(dn + j * L::RR * S::drow_b, ex + a.slot.rel_v[2] + (int64_t)r0 * S::drow_b,
+                 nr * S::drow_b, bar + 6);
+        bulk(dsc + j * L::DSC, ex + a.slot.rel_s[2] + sa0, sab, bar + 6);
     };
 
-    // layer-0 prefetches
     if (tid == 0) {
         prefetch_rt(0);
         prefetch_sd(0);
@@ -324,201 +331,243 @@ k_decode(DecodeArgs a) {
     pend[0] = pend[1] = true;
 
     const int T = a.n_layers * a.n_steps;
-    // phase stamps: 0 start, 1 state ready, 2 normed, 3 router+shared done,
-    // 4 routes visible, 5 top-k done, 6 copies issued + softmax, 7 chains done,
-    // 8 chains visible, 9 state rows written
 #define DS4F_TRACE(k) \
     if (a.trace && tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + (k)] = gtimer()
-    for (int t = 0; t < T && ok; t++) {
-        const int l = t % a.n_layers;
-        DS4F_TRACE(0);
-        const int ln = (t + 1) % a.n_layers;
+    for (int t = 0; t < T; t++) {
+        const int l = t % a.n_layers, ln = (t + 1) % a.n_layers;
         const bool more = t + 1 < T;
-        // (A) input state of this layer
-        if (t > 0) {
-            if (tid == 0) ctl[0] = flag_wait(a, c_state, (unsigned)(t * G), 1);
-            __syncthreads();
-            if (!ctl[0]) { ok = false; break; }
-        }
-        DS4F_TRACE(1);
-        // (B) RMSNorm (src/moe.c:841-851): double sum of squares, fixed tree
+        const uint32_t tg = tag_of(t);            // words this layer publishes
+        DS4F_TRACE(0);
+        // (A) input state: PER words per thread
         {
+            constexpr int PER = (H + kThreads - 1) / kThreads;
+            float v[PER];
+            bool got = true;
+            if (t == 0) {
+#pragma unroll
+                for (int k = 0; k < PER; k++)
+                    v[k] = (tid + k * kThreads < H) ? __ldcg(a.state + tid + k * kThreads) : 0.f;
+            } else {
+                static_assert(H % kThreads == 0, "state words split evenly over threads");
+                const uint64_t *sw = (const uint64_t *)gu;
+                got = gather_ll(a, bar + 7, ph[7], pend[7], (uint64_t *)gu, a.st_ll, H, H,
+                                tag_of(t - 1), 1);
+#pragma unroll
+                for (int k = 0; k < PER; k++) v[k] = __uint_as_float((uint32_t)sw[tid + k * kThreads]);
+            }
             double ss = 0.0;
-            for (int i = tid; i < H; i += kThreads) {
-                float v = __ldcg(a.state + i);
-                xin[i] = v;
-                double d = (double)v;
-                ss = __dadd_rn(ss, __dmul_rn(d, d));
+#pragma unroll
+            for (int k = 0; k < PER; k++) {
+                const int i = tid + k * kThreads;
+                if (i < H) {
+                    xin[i] = v[k];
+                    if (i >= r0 && i < r0 + nr) srow[i - r0] = v[k];
+                    double d = (double)v[k];
+                    ss = __dadd_rn(ss, __dmul_rn(d, d));
+                }
             }
             ss = warp_sum_d(ss);
             double *rd = (double *)red;
             if (lane == 0) rd[warp] = ss;
+            if (!got) { ok = false; break; }          // uniform: gather_ll's result
             __syncthreads();
+            DS4F_TRACE(1);
             if (tid == 0) {
                 double s2 = 0.0;
                 for (int k = 0; k < kWarps; k++) s2 = __dadd_rn(s2, rd[k]);
                 rd[16] = s2;
             }
-            __syncthreads();
+            // (B) norm weights arrive with the router rows (bar 0)
+            bool okb = mbar_wait(a, bar + 0, ph[0], 2);
+            if (!__syncthreads_and(okb)) { ok = false; break; }
+            ph[0] ^= 1; pend[0] = false;
             float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(rd[16], (double)H)), 1e-6f));
-            const uint16_t *nw = trunk_l(l) + a.tr.norm;
             for (int i = tid; i < H; i += kThreads)
-                xin[i] = __fmul_rn(__fdiv_rn(xin[i], r), bf16_to_f32(__ldg(nw + i)));
+                xin[i] = __fmul_rn(__fdiv_rn(xin[i], r), bf16_to_f32(nw[i]));
             __syncthreads();
         }
         DS4F_TRACE(2);
-        // (C) router rows + shared gate/up rows (weights prefetched, bar 0)
-        if (!__syncthreads_and(mbar_wait(a, bar + 0, ph[0], 2))) { ok = false; break; }
-        ph[0] ^= 1; pend[0] = false;
-        if (warp < rt1 - rt0) {
+        // (C) router rows (warps 0 .. nrt-1); lane owns columns
+        //     [lane * cpl, (lane + 1) * cpl) so one warp scan gives prefixes
+        if (warp < nrt) {
             const int e = rt0 + warp;
-            const uint16_t *row = rt + warp * H;
-            double base = 0.0, bsum = 0.0;
-            for (int k = 0; k < H / 256; k++) {
-                int q = lane + 32 * k;
-                uint4 w = lds16(row + q * 8);
-                uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-                double Tq = 0.0, Aq = 0.0;
+            const uint16_t *row = rt + warp * H + lane * S::cpl;
+            constexpr int NCH = S::cpl / 8;
+            double Tq[NCH], Aq[NCH];
+#pragma unroll
+            for (int k = 0; k < NCH; k++) {
+                uint4 w = lds16(row + k * 8);
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+                const float *x = xin + lane * S::cpl + k * 8;
+                double p8[8];
+                double ab = 0.0;
 #pragma unroll
                 for (int u = 0; u < 8; u++) {
                     uint32_t h = (u & 1) ? (ww[u >> 1] & 0xFFFF0000u) : (ww[u >> 1] << 16);
-                    float p = __fmul_rn(__uint_as_float(h), xin[q * 8 + u]);
-                    Tq = __dadd_rn(Tq, (double)p);
-                    Aq = __dadd_rn(Aq, (double)fabsf(p) * (double)(8 - u));
+                    float p = __fmul_rn(__uint_as_float(h), x[u]);   // the reference's product
+                    p8[u] = (double)p;
+                    ab = __dadd_rn(ab, (double)fabsf(p) * (double)(8 - u));
                 }
-                double incl = Tq;
+                Tq[k] = __dadd_rn(__dadd_rn(__dadd_rn(p8[0], p8[1]), __dadd_rn(p8[2], p8[3])),
+                                  __dadd_rn(__dadd_rn(p8[4], p8[5]), __dadd_rn(p8[6], p8[7])));
+                Aq[k] = ab;
+            }
+            double tot = 0.0;
 #pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-                    if (lane >= o) incl = __dadd_rn(incl, y);
-                }
-                double excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-                if (lane == 0) excl = 0.0;
-                bsum = __dadd_rn(bsum, __dadd_rn(8.0 * fabs(__dadd_rn(base, excl)), Aq));
-                base = __dadd_rn(base, __shfl_sync(0xFFFFFFFFu, incl, 31));
+            for (int k = 0; k < NCH; k++) tot = __dadd_rn(tot, Tq[k]);
+            double incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl = __dadd_rn(incl, y);
             }
-            bsum = warp_sum_d(bsum);
-            if (lane == 0) {
-                __stcg(a.S + e, base);
-                __stcg(a.B + e, 1.001 * kU * bsum + 1e-300);
+            double P = __dsub_rn(incl, tot);            // prefix before this lane
+            double bs = 0.0, loc = 0.0;
+#pragma unroll
+            for (int k = 0; k < NCH; k++) {
+                bs = __dadd_rn(bs, __dadd_rn(8.0 * fabs(__dadd_rn(P, loc)), Aq[k]));
+                loc = __dadd_rn(loc, Tq[k]);
             }
-        } else if (warp >= L::RT && warp < L::RT + 2 * (sg1 - sg0)) {
-            // shared gate (even) / up (odd) row dots, bf16, x unscaled
-            const int w2 = warp - L::RT, i = w2 >> 1, m = w2 & 1;
-            const uint16_t *row = sgu + m * L::SG * H + i * H;
+            // the prefixes carry double rounding of their own: widen by 1e-12
+            bs = warp_sum_d(bs) * (1.0 + 1e-12);
+            const double Sv = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            const double Bv = 1.001 * kU * bs + 1e-300;
+            if (lane < 4) {
+                const uint64_t sb = (uint64_t)__double_as_longlong(Sv);
+                const uint64_t bb = (uint64_t)__double_as_longlong(Bv);
+                const uint32_t word = lane == 0 ? (uint32_t)sb : lane == 1 ? (uint32_t)(sb >> 32)
+                                    : lane == 2 ? (uint32_t)bb : (uint32_t)(bb >> 32);
+                st_tag(a.sb_ll + 4 * e + lane, tg, word);
+            }
+        } else if (warp >= L::RT && warp < L::RT + 2 * nsg) {
+            // (D) shared gate (even) / up (odd) rows through registers
+            const int w2 = warp - L::RT, i = sg0 + (w2 >> 1), m = w2 & 1;
+            const uint16_t *row = trunk_l(l) + (m ? a.tr.sh_up : a.tr.sh_gate) + (int64_t)i * H;
+            uint4 b[H / 256];
+#pragma unroll
+            for (int k = 0; k < H / 256; k++) b[k] = ldg_stream(row + (lane + 32 * k) * 8);
             float acc = 0.f;
 #pragma unroll
-            for (int k = 0; k < H / 256; k++) {
-                int q = lane + 32 * k;
-                acc += bf16_dot8(lds16(row + q * 8), xin + q * 8);
-            }
+            for (int k = 0; k < H / 256; k++) acc += bf16_dot8(b[k], xin + (lane + 32 * k) * 8);
             acc = warp_sum(acc);
-            if (lane == 0) red[64 + w2] = acc;
+            if (lane == 0) red[192 + w2] = acc;     // bytes 768..: clear of rd[0..63]
         } else if (warp == kWarps - 1 && c == G - 1) {
             const uint16_t *gw = trunk_l(l) + a.tr.sh_gw;
+            uint4 b[H / 256];
+#pragma unroll
+            for (int k = 0; k < H / 256; k++) b[k] = ldg_stream(gw + (lane + 32 * k) * 8);
             float acc = 0.f;
-            for (int k = 0; k < H / 256; k++) {
-                int q = lane + 32 * k;
-                acc += bf16_dot8(__ldg((const uint4 *)(gw + q * 8)), xin + q * 8);
-            }
+#pragma unroll
+            for (int k = 0; k < H / 256; k++) acc += bf16_dot8(b[k], xin + (lane + 32 * k) * 8);
             acc = warp_sum(acc);
-            if (lane == 0) __stcg(a.sgate, acc);
+            if (lane == 0) st_tag(a.ch_ll + (K + 1) * M, tg, __float_as_uint(acc));
         }
-        __syncthreads();
-        if (tid < sg1 - sg0)
-            __stcg(a.chain + K * M + sg0 + tid, silu_mul(red[64 + 2 * tid], red[64 + 2 * tid + 1]));
-        __syncthreads();
-        if (tid == 0) {
-            flag_arrive(c_route);
-            // (E) next layer's router + shared gate/up rows into the freed buffers
-            if (more) { fence_async(); prefetch_rt(ln); }
-        }
-        pend[0] = more;
         DS4F_TRACE(3);
-        // (F) routing: every CTA, identical bits
-        if (tid == 0) ctl[0] = flag_wait(a, c_route, (unsigned)((t + 1) * G), 3);
-        __syncthreads();
-        if (!ctl[0]) { ok = false; break; }
-        DS4F_TRACE(4);
+        // (F) routing: gather every S/B word, then warp 0 takes the
+        //     certified top-K
+        static_assert(E % 32 == 0 && (4 * E * 8) % 16 == 0, "router width: whole warps of experts");
+        if (!gather_ll(a, bar + 7, ph[7], pend[7], (uint64_t *)gu, a.sb_ll, 4 * E, 4 * E, tg, 3)) {
+            ok = false;
+            break;
+        }
         if (warp == 0) {
-            // certified top-K from [S - B, S + B]; lane holds e = lane + 32 i
-            constexpr int NE = (E + 31) / 32;
+            constexpr int NE = E / 32;
             double sv[NE], lo[NE], hi[NE];
+            // experts lane + 32 i, words 4e .. 4e+3 (S lo/hi, B lo/hi)
+            uint32_t wv[4 * NE];
+            const uint64_t *sbw = (const uint64_t *)gu;
+#pragma unroll
+            for (int i = 0; i < NE; i++)
+#pragma unroll
+                for (int h = 0; h < 4; h++) wv[4 * i + h] = (uint32_t)sbw[4 * (lane + 32 * i) + h];
+            bool got = true;
 #pragma unroll
             for (int i = 0; i < NE; i++) {
-                int e = lane + 32 * i;
-                if (e < E) {
-                    double s = __ldcg(a.S + e), b = a.exact_all ? 0.0 : __ldcg(a.B + e);
-                    sv[i] = s; lo[i] = s - b; hi[i] = s + b;
-                } else {
-                    sv[i] = lo[i] = hi[i] = -1e300;
-                }
+                const double s = __longlong_as_double((long long)(((uint64_t)wv[4 * i + 1] << 32) | wv[4 * i]));
+                const double b = a.exact_all ? 0.0
+                    : __longlong_as_double((long long)(((uint64_t)wv[4 * i + 3] << 32) | wv[4 * i + 2]));
+                sv[i] = s; lo[i] = s - b; hi[i] = s + b;
             }
-            // K rounds of arg-max of lo (lower index wins ties)
-            unsigned taken = 0;
-            double lk = 0.0;
-            for (int k = 0; k < K; k++) {
-                double bv = -2e300; int be = 0x7FFFFFFF;
+            got = __all_sync(0xFFFFFFFFu, got);
+            if (lane == 0) { ctl[3] = got; ctl[1] = 0; }
+            if (got) {
+                // K-th largest lower bound from float keys rounded down: a
+                // lower bound of the true one, so candidates can only grow
+                uint32_t key[NE];
 #pragma unroll
-                for (int i = 0; i < NE; i++) {
-                    int e = lane + 32 * i;
-                    if (!(taken >> i & 1) && e < E && (lo[i] > bv || (lo[i] == bv && e < be))) { bv = lo[i]; be = e; }
+                for (int i = 0; i < NE; i++)
+                    key[i] = (lane + 32 * i < E) ? fkey(__double2float_rd(lo[i])) : 0u;
+                uint32_t taken = 0, thr = 0;
+                int rem = K;
+                for (int it = 0; it < K; it++) {
+                    uint32_t mloc = 0;
+#pragma unroll
+                    for (int i = 0; i < NE; i++) if (!(taken >> i & 1)) mloc = max(mloc, key[i]);
+                    const uint32_t gmax = __reduce_max_sync(0xFFFFFFFFu, mloc);
+                    uint32_t cl_ = 0;
+#pragma unroll
+                    for (int i = 0; i < NE; i++)
+                        if (!(taken >> i & 1) && key[i] == gmax) { cl_++; taken |= 1u << i; }
+                    const int cnt = (int)__reduce_add_sync(0xFFFFFFFFu, cl_);
+                    thr = gmax;
+                    if (cnt >= rem) break;
+                    rem -= cnt;
                 }
+                const double lk = (double)fkey_inv(thr);
+                int nmine = 0;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-                    int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-                    if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-                }
-                if ((be & 31) == lane) taken |= 1u << (be >> 5);
-                lk = bv;
-            }
-            int mine = 0;
-#pragma unroll
-            for (int i = 0; i < NE; i++) mine += (lane + 32 * i < E) && hi[i] >= lk;
-            int ncand = mine;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ncand += __shfl_xor_sync(0xFFFFFFFFu, ncand, o);
-            bool cert = !a.exact_all && ncand == K;
-            double prev_lo = 0.0;
-            if (cert) {
-                // order the K candidates (= the taken set) by S, check separation
-                unsigned used = 0;
-                for (int k = 0; k < K; k++) {
-                    double bv = -2e300; int be = 0x7FFFFFFF; double blo = 0.0, bhi = 0.0;
+                for (int i = 0; i < NE; i++) nmine += (lane + 32 * i < E) && hi[i] >= lk;
+                const int ncand = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
+                bool cert = !a.exact_all && ncand == K;
+                if (cert) {
+                    // compact the K candidates, rank them by S (lower index
+                    // first on equal S), check adjacent intervals separate
+                    int base = 0;
 #pragma unroll
                     for (int i = 0; i < NE; i++) {
-                        int e = lane + 32 * i;
-                        if ((taken >> i & 1) && !(used >> i & 1) && (sv[i] > bv || (sv[i] == bv && e < be))) {
-                            bv = sv[i]; be = e; blo = lo[i]; bhi = hi[i];
+                        const bool cf = (lane + 32 * i < E) && hi[i] >= lk;
+                        const unsigned msk = __ballot_sync(0xFFFFFFFFu, cf);
+                        if (cf) {
+                            const int pos = base + __popc(msk & ((1u << lane) - 1));
+                            cl[pos] = sv[i]; cl[32 + pos] = lo[i]; cl[64 + pos] = hi[i];
+                            cl[96 + pos] = (double)(lane + 32 * i);
                         }
+                        base += __popc(msk);
                     }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-                        int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
-                        double ol = __shfl_xor_sync(0xFFFFFFFFu, blo, o);
-                        double oh = __shfl_xor_sync(0xFFFFFFFFu, bhi, o);
-                        if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; blo = ol; bhi = oh; }
+                    __syncwarp();
+                    double *rd = (double *)red;
+                    if (lane < K) {
+                        const double s = cl[lane], ex = cl[96 + lane];
+                        int rk = 0;
+                        for (int q = 0; q < K; q++)
+                            rk += (cl[q] > s) || (cl[q] == s && cl[96 + q] < ex);
+                        sel[rk] = (int)ex;
+                        rd[rk] = cl[32 + lane];            // lo by rank
+                        rd[16 + rk] = cl[64 + lane];       // hi by rank
                     }
-                    if ((be & 31) == lane) used |= 1u << (be >> 5);
-                    if (k > 0 && !(prev_lo > bhi)) cert = false;
-                    prev_lo = blo;
-                    if (lane == 0) sel[k] = be;
+                    __syncwarp();
+                    const bool sep = lane >= K - 1 || rd[lane] > rd[16 + lane + 1];
+                    cert = __all_sync(0xFFFFFFFFu, sep);
                 }
-            }
-            // tk[e] = value used for softmax; candidate flags for the exact path
 #pragma unroll
-            for (int i = 0; i < NE; i++) {
-                int e = lane + 32 * i;
-                if (e < E) {
-                    tk[e] = (double)(float)sv[i];
-                    candf[e] = a.exact_all || hi[i] >= lk;
+                for (int i = 0; i < NE; i++) {
+                    const int e = lane + 32 * i;
+                    if (e < E) {
+                        tk[e] = (double)(float)sv[i];
+                        candf[e] = a.exact_all || hi[i] >= lk;
+                    }
                 }
+                if (lane == 0) ctl[1] = cert ? 1 : 0;
             }
-            if (lane == 0) { ctl[1] = cert ? 1 : 0; ctl[2] = ncand; }
         }
+        // ctl[] is read after the barrier (a __syncthreads_and predicate
+        // would be evaluated before warp 0 wrote it)
         __syncthreads();
+        if (!ctl[3]) { ok = false; break; }
+        DS4F_TRACE(4);
+        if (tid < nsg)
+            st_tag(a.ch_ll + K * M + sg0 + tid, tg,
+                   __float_as_uint(silu_mul(red[192 + 2 * tid], red[192 + 2 * tid + 1])));
         if (!ctl[1]) {
             // exact reference-order logits (src/kernels.c:97-102) of every
             // candidate, one thread each, then select on them
@@ -535,7 +584,7 @@ k_decode(DecodeArgs a) {
             for (int e = tid; e < E; e += kThreads) {
                 if (!candf[e]) continue;
                 int r = 0;
-                double ve = tk[e];
+                const double ve = tk[e];
                 for (int f = 0; f < E; f++) r += candf[f] && (tk[f] > ve || (tk[f] == ve && f < e));
                 if (r < K) sel[r] = e;
             }
@@ -543,45 +592,49 @@ k_decode(DecodeArgs a) {
             __syncthreads();
         }
         DS4F_TRACE(5);
-        // (G) stream the selected experts: gate/up ring + down rows
-        if (tid == 0) {
+        // (G) every routed byte of this CTA in flight; next layer's router
+        //     rows + norm weights into the buffers (B) and (C) are done with
+        if (warp == 0) {
             fence_async();
-            for (int s = 0; s < 2 && s < nstages; s++) issue_stage(l, s);
-            issue_down(l);
+            if (lane < ngroups) issue_group(l, lane);
+            if (lane == 8) mbar_expect(bar + 6, dn_total);
+            __syncwarp();
+            if (lane >= 8 && lane < 8 + K) issue_down_j(l, lane - 8);
+            if (lane == 31 && more) prefetch_rt(ln);
         }
-        pend[2] = nstages > 0; pend[3] = nstages > 1; pend[4] = true;
-        // softmax over all E (double, max subtracted) + renorm, while the
-        // copies fly
+#pragma unroll
+        for (int g = 0; g < kGroups; g++) pend[2 + g] = g < ngroups;
+        pend[6] = true;
+        pend[0] = more;
+        DS4F_TRACE(6);
+        // softmax over all E (double, max subtracted) + renorm
         {
             double *rd = (double *)red;
             double mx = tid < E ? tk[tid] : -1e300;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-            if (lane == 0) rd[16 + warp] = mx;
+            if (lane == 0) rd[32 + warp] = mx;
             __syncthreads();
-            mx = rd[16];
-            for (int k = 1; k < kWarps; k++) mx = fmax(mx, rd[16 + k]);
-            double part = 0.0;
-            if (tid < E) part = exp(tk[tid] - mx);
+            mx = rd[32];
+            for (int k = 1; k < kWarps; k++) mx = fmax(mx, rd[32 + k]);
+            double part = tid < E ? exp(tk[tid] - mx) : 0.0;
             part = warp_sum_d(part);
-            if (lane == 0) rd[warp] = part;
+            if (lane == 0) rd[48 + warp] = part;
             __syncthreads();
-            if (tid == 0) {
+            if (warp == 0) {
                 double sw = 0.0;
-                for (int k = 0; k < kWarps; k++) sw += rd[k];
+                for (int k = 0; k < kWarps; k++) sw += rd[48 + k];
+                const float wj = lane < K ? (float)(exp(tk[sel[lane]] - mx) / sw) : 0.0f;
                 float s = 0.0f;
-                for (int j = 0; j < K; j++) {
-                    wsel[j] = (float)(exp(tk[sel[j]] - mx) / sw);
-                    s = __fadd_rn(s, wsel[j]);
-                }
-                if (a.renorm && s > 0.0f)
-                    for (int j = 0; j < K; j++) wsel[j] = __fdiv_rn(wsel[j], s);
-                if (c == 0) atomicAdd(a.diag, 1u);
+                for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, wj, j));
+                if (lane < K) wsel[lane] = (a.renorm && s > 0.0f) ? __fdiv_rn(wj, s) : wj;
+                if (lane == 0 && c == 0) atomicAdd(a.diag, 1u);
             }
             __syncthreads();
         }
-        DS4F_TRACE(6);
-        // (H) gate/up dots: warp w -> slot w/2 of the stage, gate (even) / up
+        DS4F_TRACE(7);
+        // (H) gate/up as the groups land: warp w -> pair w/2 of the group,
+        //     gate (even) / up (odd); x pre-scaled by 2^64 in registers
         {
             float xr[S::gk * S::ce];
 #pragma unroll
@@ -594,32 +647,28 @@ k_decode(DecodeArgs a) {
                     xr[k * S::ce + e + 2] = v.z * DS4F_X_PRESCALE;
                     xr[k * S::ce + e + 3] = v.w * DS4F_X_PRESCALE;
                 }
-            for (int s = 0; s < nstages; s++) {
-                const int slot = s & 1;
-                if (!__syncthreads_and(mbar_wait(a, bar + 2 + slot, ph[2 + slot], 4))) { ok = false; break; }
-                ph[2 + slot] ^= 1;
-                uint8_t *st = stage + slot * L::stage_b;
-                const int q0 = p0 + s * kStagePairs, nq = min(kStagePairs, p1 - q0);
+            for (int g = 0; g < ngroups; g++) {
+                const bool okg = mbar_wait(a, bar + 2 + g, ph[2 + g], 4);
+                if (!__syncthreads_and(okg)) { ok = false; break; }
+                ph[2 + g] ^= 1; pend[2 + g] = false;
+                if (g == 0) DS4F_TRACE(8);
+                const int q0 = p0 + g * kGroupPairs, nq = min(kGroupPairs, p0 + np - q0);
                 const int ps = warp >> 1, m = warp & 1;
                 if (ps < nq) {
-                    const int q = q0 + ps, i = q % M;
-                    const int jfirst = q0 / M;
-                    const int g = q / M - jfirst;                  // segment 0 or 1
-                    const uint8_t *row = st + m * L::stage_w + ps * S::row_b;
+                    const int q = q0 + ps, i = q % M, slot = q - p0;
+                    const int seg = q / M - q0 / M;
+                    const uint8_t *row = gu + (m * L::PP + slot) * S::row_b;
                     float acc = 0.f;
 #pragma unroll
                     for (int k = 0; k < S::gk; k++) {
                         const int qq = lane + 32 * k;
                         uint4 w = lds16(row + qq * 16);
                         if constexpr (FMT == DS4F_FMT_FP8) {
-                            const float *sc = (const float *)(st + 2 * L::stage_w + (2 * m + g) * L::GSC_SEG);
-                            float s8 = sc[(i >> 7) * (H / 128) + (qq >> 3)];
+                            const float *sc = (const float *)(gsc + ((g * 2 + seg) * 2 + m) * S::gsc_b);
+                            const float s8 = sc[(i >> 7) * (H / 128) + (qq >> 3)];
                             acc = fmaf(f8_dot16(w, xr + k * S::ce) * DS4F_F8_POST, s8, acc);
                         } else {
-                            // gate scales at [0, GSC_SEG), up at [2 GSC_SEG, 3 GSC_SEG),
-                            // one E8M0 byte per 32-element chunk, row by slot
-                            const uint8_t *sc = st + 2 * L::stage_w + m * 2 * L::GSC_SEG;
-                            float s4 = e8m0_to_f32(sc[ps * S::gsc_b + qq]);
+                            const float s4 = e8m0_to_f32(gsc[(m * L::PP + slot) * S::gsc_b + qq]);
                             acc = fmaf(e2m1_dot32(w, xr + k * S::ce) * DS4F_E2M1_POST, s4, acc);
                         }
                     }
@@ -629,36 +678,46 @@ k_decode(DecodeArgs a) {
                 __syncthreads();
                 if (tid < nq) {
                     const int q = q0 + tid;
-                    __stcg(a.chain + (q / M) * M + (q % M), silu_mul(red[2 * tid], red[2 * tid + 1]));
+                    st_tag(a.ch_ll + (q / M) * M + (q % M), tg,
+                           __float_as_uint(silu_mul(red[2 * tid], red[2 * tid + 1])));
                 }
                 __syncthreads();
-                if (tid == 0 && s + 2 < nstages) { fence_async(); issue_stage(l, s + 2); }
-                pend[2 + slot] = s + 2 < nstages;
             }
             if (!ok) break;
         }
-        __syncthreads();
-        DS4F_TRACE(7);
-        if (tid == 0) flag_arrive(c_chain);
-        // (I) all chains
-        if (tid == 0) ctl[0] = flag_wait(a, c_chain, (unsigned)((t + 1) * G), 5);
-        __syncthreads();
-        if (!ctl[0]) { ok = false; break; }
-        DS4F_TRACE(8);
-        for (int i = tid; i < (K + 1) * M; i += kThreads) cs[i] = __ldcg(a.chain + i);
-        // (J) down rows: routed (bar 4) and shared (bar 1)
-        if (!__syncthreads_and(mbar_wait(a, bar + 4, ph[4], 6))) { ok = false; break; }
-        ph[4] ^= 1; pend[4] = false;
-        if (!__syncthreads_and(mbar_wait(a, bar + 1, ph[1], 7))) { ok = false; break; }
-        ph[1] ^= 1; pend[1] = false;
+        DS4F_TRACE(9);
+        // (I) down rows: routed (bar 6) and shared (bar 1); chains polled
         {
-            // row-dots (j, r), j-major, j = K the shared expert; warp w takes
-            // a contiguous range so its chain registers change at most twice
+            const bool okd = mbar_wait(a, bar + 6, ph[6], 6) && mbar_wait(a, bar + 1, ph[1], 7);
+            if (!__syncthreads_and(okd)) { ok = false; break; }
+            ph[6] ^= 1; pend[6] = false;
+            ph[1] ^= 1; pend[1] = false;
+            DS4F_TRACE(10);
+            // every chain word (routed, shared, then the shared-gate logit)
+            // into shared memory, over the gate/up rows (H) is done with
+            // (K+1) M chain words + the logit, copied as an even count (the
+            // workspace allocation is padded past the last word)
+            constexpr int NCW = (K + 1) * M + 1;
+            if (!gather_ll(a, bar + 7, ph[7], pend[7], (uint64_t *)gu, a.ch_ll, (NCW + 1) / 2 * 2,
+                           NCW, tg, 5)) {
+                ok = false;
+                break;
+            }
+            // unpack the values next to the words (consecutive threads,
+            // consecutive words: no bank conflicts), then every warp loads
+            // its chain registers from the packed floats
+            float *chf = (float *)(gu + L::GATH);
+            {
+                const uint64_t *chw = (const uint64_t *)gu;
+                for (int i = tid; i < NCW; i += kThreads) chf[i] = __uint_as_float((uint32_t)chw[i]);
+            }
+            __syncthreads();
+            DS4F_TRACE(12);
             const int ndots = (K + 1) * nr;
             const int d0 = warp * ndots / kWarps, d1 = (warp + 1) * ndots / kWarps;
             int jcur = -1;
-            float xr[S::dk * S::ce];          // routed chain (pre-scaled by 2^64)
-            float xb[S::bk * 8];              // shared chain (bf16 chunk layout)
+            float xr[S::dk * S::ce];          // routed chain, pre-scaled by 2^64
+            float xb[S::bk * 8];              // shared chain, bf16 chunk layout
             for (int d = d0; d < d1; d++) {
                 const int j = d / nr, rr = d % nr;
                 if (j != jcur) {
@@ -669,19 +728,17 @@ k_decode(DecodeArgs a) {
 #pragma unroll
                             for (int e = 0; e < S::ce; e++)
                                 xr[k * S::ce + e] =
-                                    cs[j * M + ((lane % S::dlpr) + S::dlpr * k) * S::ce + e] * DS4F_X_PRESCALE;
+                                    chf[j * M + ((lane % S::dlpr) + S::dlpr * k) * S::ce + e] * DS4F_X_PRESCALE;
                     } else {
 #pragma unroll
                         for (int k = 0; k < S::bk; k++)
 #pragma unroll
                             for (int e = 0; e < 8; e++)
-                                xb[k * 8 + e] = cs[K * M + ((lane % S::blpr) + S::blpr * k) * 8 + e];
+                                xb[k * 8 + e] = chf[K * M + ((lane % S::blpr) + S::blpr * k) * 8 + e];
                     }
                 }
                 float v = 0.f;
                 if (j < K) {
-                    // rows shorter than a warp: lane groups repeat the row and
-                    // only lane 0's sum is kept
                     const uint8_t *row = dn + (j * L::RR + rr) * S::drow_b;
                     const int ql = lane % S::dlpr;
 #pragma unroll
@@ -690,12 +747,10 @@ k_decode(DecodeArgs a) {
                         uint4 w = lds16(row + q * 16);
                         if constexpr (FMT == DS4F_FMT_FP8) {
                             const float *sc = (const float *)(dsc + j * L::DSC);
-                            float s8 = sc[((r0 + rr) >> 7) * (M / 128) + (q >> 3)];
+                            const float s8 = sc[((r0 + rr) >> 7) * (M / 128) + (q >> 3)];
                             v = fmaf(f8_dot16(w, xr + k * S::ce) * DS4F_F8_POST, s8, v);
                         } else {
-                            const int sa0 = (r0 * S::dsc_b) / 16 * 16;
-                            const uint8_t *sc = dsc + j * L::DSC;
-                            float s4 = e8m0_to_f32(sc[(r0 + rr) * S::dsc_b - sa0 + q]);
+                            const float s4 = e8m0_to_f32(dsc[j * L::DSC + (r0 + rr) * S::dsc_b - sa0 + q]);
                             v = fmaf(e2m1_dot32(w, xr + k * S::ce) * DS4F_E2M1_POST, s4, v);
                         }
                     }
@@ -705,15 +760,15 @@ k_decode(DecodeArgs a) {
                     const uint16_t *row = sd + rr * M;
                     const int ql = lane % S::blpr;
 #pragma unroll
-                    for (int k = 0; k < S::bk; k++) {
-                        const int q = ql + S::blpr * k;
-                        v += bf16_dot8(lds16(row + q * 8), xb + k * 8);
-                    }
+                    for (int k = 0; k < S::bk; k++)
+                        v += bf16_dot8(lds16(row + (ql + S::blpr * k) * 8), xb + k * 8);
 #pragma unroll
                     for (int o = S::blpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
                 }
                 if (lane == 0) outs[j * L::RR + rr] = v;
             }
+            DS4F_TRACE(13);
+            if (tid == 0) red[0] = sigmoid_ref(chf[(K + 1) * M]);
             __syncthreads();
             // selection-order combine (src/moe.c:1224-1225), shared gate
             // (:1279-1282), residual (:1424)
@@ -721,30 +776,22 @@ k_decode(DecodeArgs a) {
                 const int r = r0 + tid;
                 float acc = 0.0f;
                 for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(wsel[j], outs[j * L::RR + tid]));
-                float sg = sigmoid_ref(__ldcg(a.sgate));
-                acc = __fadd_rn(acc, __fmul_rn(sg, outs[K * L::RR + tid]));
-                __stcg(a.state + r, __fadd_rn(__ldcg(a.state + r), acc));
+                acc = __fadd_rn(acc, __fmul_rn(red[0], outs[K * L::RR + tid]));
+                const float ns = __fadd_rn(srow[tid], acc);
+                st_tag(a.st_ll + r, tg, __float_as_uint(ns));
+                if (!more) __stcg(a.state + r, ns);
             }
             __syncthreads();
         }
-        DS4F_TRACE(9);
-        if (tid == 0) {
-            flag_arrive(c_state);
-            if (more) { fence_async(); prefetch_sd(ln); }
-        }
+        DS4F_TRACE(11);        // (stamps 12, 13: inside the down phase, above)
+        if (tid == 0 && more) { fence_async(); prefetch_sd(ln); }
         pend[1] = more;
     }
 #undef DS4F_TRACE
     // drain this CTA's copies before exit (bounded)
-    for (int i = 0; i < 5; i++)
+    for (int i = 0; i < 8; i++)
         if (pend[i]) mbar_wait(a, bar + i, ph[i], 8);
 }
-
-}  // namespace
-}  // namespace ds4f
-
-namespace ds4f {
-namespace {
 
 template <int FMT, int H, int M, int E, int K>
 int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
@@ -768,32 +815,36 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     a.trunk_n = m->tr.n;
     a.tr = m->tr;
     a.n_layers = m->d.n_layers;
-    a.n_steps = n_steps;
     a.E = E;
     a.renorm = m->d.renorm;
     a.exact_all = m->d.router_exact;
-    a.state = state;
-    a.S = m->w.S;
-    a.B = m->w.Bnd;
-    a.chain = m->w.chain;
-    a.sgate = m->w.sgate;
-    a.ctr = m->w.ctr;
+    a.st_ll = m->w.st_ll;
+    a.sb_ll = m->w.sb_ll;
+    a.ch_ll = m->w.ch_ll;
     a.diag = m->w.diag;
-    a.trace = nullptr;
-    if (m->trace && (int64_t)m->d.n_layers * n_steps * sms * kTracePts <= m->trace_n) a.trace = m->trace;
-    DS4F_CUDA(cudaMemsetAsync(m->w.ctr, 0, 3 * 128, st));
     DS4F_CUDA(cudaMemsetAsync(m->w.diag + 2, 0, 2 * sizeof(unsigned), st));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(sms);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = L::bytes;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeCooperative;
-    at[0].val.cooperative = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    DS4F_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+    // tags carry 16 bits of layer-step: split long runs into launches
+    const int per = std::max(1, 65000 / m->d.n_layers);
+    for (int s0 = 0; s0 < n_steps; s0 += per) {
+        const int ns = std::min(per, n_steps - s0);
+        m->epoch = m->epoch % 65535 + 1;
+        a.epoch = (uint32_t)m->epoch;
+        a.n_steps = ns;
+        a.state = state;
+        a.trace = nullptr;
+        if (m->trace && (int64_t)m->d.n_layers * ns * sms * kTracePts <= m->trace_n) a.trace = m->trace;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(sms);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = L::bytes;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeCooperative;
+        at[0].val.cooperative = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        DS4F_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+    }
     return 0;
 }
 

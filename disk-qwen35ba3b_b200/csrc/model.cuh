@@ -44,7 +44,9 @@ struct Work {
     float *acc;           // [H] moe output before the residual
     unsigned *diag;       // [4] 0: layers routed, 1: exact fallbacks, 2: error
                           //     code of the persistent kernel, 3: its CTA
-    unsigned *ctr;        // [3 x 32] persistent-kernel phase counters
+    uint64_t *st_ll;      // [H] persistent kernel: tagged state words
+    uint64_t *sb_ll;      // [E][4] tagged router logits and bounds
+    uint64_t *ch_ll;      // [(K+1) M + 1] tagged chains + shared-gate logit
 };
 
 struct Model {
@@ -67,6 +69,7 @@ struct Model {
     int path;                    // 0 auto, 1 per-layer kernels, 2 persistent
     unsigned long long *trace;   // optional phase stamps of the persistent kernel
     int64_t trace_n;
+    int epoch;                   // last persistent launch's tag epoch
 };
 
 int slot_layout(int fmt, int H, int M, SlotLayout *s);

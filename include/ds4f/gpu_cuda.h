@@ -182,10 +182,12 @@ int  ds4f_gpu_moe_stack_dev(Ds4fGpuModel *m, float *state, int n_steps,
 int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
 /* Phase trace of the persistent decode kernel (the counterpart of the
  * reference's per-phase timers, src/main.c:253-258, 1522-1546): with
- * n_stamps > 0 every launch whose layers x steps x SMs x 10 stamps fit
- * records %globaltimer (ns) per (layer-step, CTA) at 10 phase boundaries:
- * start, state ready, normed, router+shared done, routes visible, top-k
- * done, copies issued, chains done, chains visible, state written.
+ * n_stamps > 0 every launch whose layers x steps x SMs x 20 stamps fit
+ * records %globaltimer (ns) per (layer-step, CTA) in 20 slots, of which
+ * 0..13 are used: start, state ready, normed, router rows done, routes
+ * visible, top-k done, copies issued, softmax done, first gate/up group
+ * landed, chains done, down rows landed, state written (11), chains
+ * gathered (12), row-dots done (13).
  * n_stamps = 0 turns it off. */
 int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
 int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
