@@ -133,6 +133,54 @@ __device__ __forceinline__ float f8_dot16(uint4 q, const float *x) {
     return a + b;
 }
 
+// Dot of the 4 canonical E4M3 bytes of w (byte k = element k) with x[0..3],
+// in units of 2^-120 (x pre-scaled by 2^64: result in units of 2^-56).
+__device__ __forceinline__ float f8_dot4(uint32_t w, const float *x) {
+    float a = f8_raw<0>(w) * x[0], b = f8_raw<1>(w) * x[1];
+    a = fmaf(f8_raw<2>(w), x[2], a);
+    b = fmaf(f8_raw<3>(w), x[3], b);
+    return a + b;
+}
+
+// E4M3 bytes (0, 1) and (2, 3) of a canonical word -> fp32 x 2^-120, the
+// same bits as f8_raw: an arithmetic shift by 4 puts e and m at bits 20..26
+// and copies the sign into bits 27..31, of which the mask keeps bit 31.
+__device__ __forceinline__ float2 f8_lo2(uint32_t w) {
+    return make_float2(__int_as_float(((int)(w << 24) >> 4) & (int)0x87F00000),
+                       __int_as_float(((int)(w << 16) >> 4) & (int)0x87F00000));
+}
+__device__ __forceinline__ float2 f8_hi2(uint32_t w) {
+    return make_float2(__int_as_float(((int)(w << 8) >> 4) & (int)0x87F00000),
+                       __int_as_float(((int)w >> 4) & (int)0x87F00000));
+}
+// acc + (Σ of the 4 products of w's bytes with x01, x23) * s, as two lanes
+// of packed fp32 (sm_100 FFMA2).
+__device__ __forceinline__ float2 f8_fma4(uint32_t w, float2 x01, float2 x23, float s, float2 acc) {
+    float2 p = __fmul2_rn(f8_lo2(w), x01);
+    p = __ffma2_rn(f8_hi2(w), x23, p);
+    return __ffma2_rn(p, make_float2(s, s), acc);
+}
+
+// Dot of the 8 E2M1 nibbles of w (even index low nibble) with x[0..7], in
+// units of 2^-126.
+__device__ __forceinline__ float e2m1_dot8(uint32_t w, const float *x) {
+    float a = e2m1_raw(w & 0xFu) * x[0], b = e2m1_raw((w >> 4) & 0xFu) * x[1];
+#pragma unroll
+    for (int k = 2; k < 8; k += 2) {
+        a = fmaf(e2m1_raw((w >> (4 * k)) & 0xFu), x[k], a);
+        b = fmaf(e2m1_raw((w >> (4 * k + 4)) & 0xFu), x[k + 1], b);
+    }
+    return a + b;
+}
+
+// Dot of 4 bf16 (q.x low, q.x high, q.y low, q.y high) with x.
+__device__ __forceinline__ float bf16_dot4(uint2 q, float4 x) {
+    float a = __uint_as_float(q.x << 16) * x.x, b = __uint_as_float(q.x & 0xFFFF0000u) * x.y;
+    a = fmaf(__uint_as_float(q.y << 16), x.z, a);
+    b = fmaf(__uint_as_float(q.y & 0xFFFF0000u), x.w, b);
+    return a + b;
+}
+
 __device__ __forceinline__ uint4 f8_canon16(uint4 q) {
     return make_uint4(f8_canon4(q.x), f8_canon4(q.y), f8_canon4(q.z),
                       f8_canon4(q.w));

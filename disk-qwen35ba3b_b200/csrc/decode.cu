@@ -101,18 +101,16 @@ template <int FMT, int H, int M>
 struct Shape {
     static constexpr int row_b = FMT == DS4F_FMT_FP8 ? H : H / 2;     // gate/up row bytes
     static constexpr int drow_b = FMT == DS4F_FMT_FP8 ? M : M / 2;    // down row bytes
-    static constexpr int ce = FMT == DS4F_FMT_FP8 ? 16 : 32;          // elements / 16 B
-    static constexpr int gk = H / ce / 32;                             // gate chunks per lane
-    static constexpr int dq = M / ce;                                  // chunks per down row
-    static constexpr int dlpr = dq < 32 ? dq : 32;                     // lanes per down row
-    static constexpr int dk = dq / dlpr;
-    static constexpr int bq = M / 8;                                   // bf16 down chunks
-    static constexpr int blpr = bq < 32 ? bq : 32;
-    static constexpr int bk = bq / blpr;
+    static constexpr int cpl = H / 32;                                 // router cols per lane
+    // 4-byte weight granules: lane l of a row-dot reads granules 32 j + l
+    static constexpr int gb = FMT == DS4F_FMT_FP8 ? 4 : 8;             // elements / granule
+    static constexpr int ng = H / (32 * gb);                           // gate/up granules / lane
+    static constexpr int dg = M / (32 * gb);                           // down granules / lane
+    static constexpr int bn = M / 128;                                 // bf16 8-byte granules / lane
+    static_assert(ng >= 1 && H % (32 * gb) == 0 && dg >= 1 && M % (32 * gb) == 0 && M % 128 == 0,
+                  "granules span the warp");
     static constexpr int gsc_b = FMT == DS4F_FMT_FP8 ? (M / 128) * (H / 128) * 4 : H / 32;
     static constexpr int dsc_b = FMT == DS4F_FMT_FP8 ? (H / 128) * (M / 128) * 4 : M / 32;
-    static constexpr int cpl = H / 32;                                 // router cols per lane
-    static_assert(gk >= 1 && H % (ce * 32) == 0, "gate/up rows must span the warp");
     static_assert(cpl % 8 == 0, "router rows: whole 8-element chunks per lane");
 };
 
@@ -193,20 +191,21 @@ __device__ bool mbar_wait(const DecodeArgs &a, uint64_t *b, uint32_t parity, uns
 // while any is still from an earlier layer); n is even (16-byte copies).
 // One bulk copy per round instead of per-thread polls. false (uniformly)
 // on timeout or abort.
-__device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &ph, bool &pend,
+__device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uint32_t &pendb,
                           uint64_t *dst, const uint64_t *src, int n, int ncheck, uint32_t tag,
-                          unsigned code) {
+                          unsigned code, unsigned long long *rounds = nullptr) {
     const int tid = threadIdx.x;
     for (long it = 0;; it++) {
+        if (rounds && tid == 0) *rounds = (unsigned long long)(it + 1);
         if (tid == 0) {
             fence_async();
             mbar_expect(bar, n * 8);
             bulk(dst, src, n * 8, bar);
         }
-        pend = true;
-        if (!__syncthreads_and(mbar_wait(a, bar, ph, code))) return false;
-        ph ^= 1;
-        pend = false;
+        pendb |= 1u << 7;
+        if (!__syncthreads_and(mbar_wait(a, bar, (phb >> 7) & 1u, code))) return false;
+        phb ^= 1u << 7;
+        pendb &= ~(1u << 7);
         bool all = true;
         for (int i = tid; i < ncheck; i += kThreads) all = all && (uint32_t)(dst[i] >> 32) == tag;
         if (__syncthreads_and(all)) return true;
@@ -253,8 +252,12 @@ k_decode(DecodeArgs a) {
     const int r0 = c * H / G, nr = (c + 1) * H / G - r0;
     const int ngroups = (np + kGroupPairs - 1) / kGroupPairs;
 
-    uint32_t ph[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    bool pend[8] = {false, false, false, false, false, false, false, false};
+    // mbarrier i: its phase parity (bit i of phb) and whether a copy on it
+    // is still in flight (bit i of pendb) -- two registers, not sixteen
+    uint32_t phb = 0, pendb = 0;
+#define PH(i) ((phb >> (i)) & 1u)
+#define FLIP(i) (phb ^= 1u << (i))
+#define PEND(i, v) (pendb = (v) ? (pendb | (1u << (i))) : (pendb & ~(1u << (i))))
     bool ok = true;
 
     if (tid == 0) {
@@ -281,58 +284,68 @@ k_decode(DecodeArgs a) {
         mbar_expect(bar + 1, b);
         if (b) bulk(sd, trunk_l(l) + a.tr.sh_down + (int64_t)r0 * M, b, bar + 1);
     };
-    // one thread: gate/up group g of layer l (bar 2 + g)
-    auto issue_group = [&](int l, int g) {
+    // Copies are issued one per lane: a bulk copy holds its issuing thread
+    // for ~160 ns whatever its size, while a warp's lanes together get one
+    // accepted every ~40 ns.
+    // Lane (g, k) of warp 0, g = lane / 8: copy k of gate/up group g of
+    // layer l (bar 2 + g). A group is <= 2 segments (one per expert), each
+    // gate rows (k & 3 == 0), up rows (1), gate scales (2), up scales (3).
+    auto issue_group_lane = [&](int l, int lane) {
+        const int g = lane >> 3, sg = (lane >> 2) & 1, kind = lane & 3;
         const int q0 = p0 + g * kGroupPairs, q1 = min(q0 + kGroupPairs, p0 + np);
-        uint32_t total = 0;
-        for (int q = q0; q < q1;) {
-            int i0 = q % M, n = min(q1 - q, M - i0);
-            total += 2 * n * S::row_b + (FMT == DS4F_FMT_FP8 ? 2 * S::gsc_b : 2 * n * S::gsc_b);
-            q += n;
-        }
-        mbar_expect(bar + 2 + g, total);
-        int seg = 0;
-        for (int q = q0; q < q1; seg++) {
-            const int j = q / M, i0 = q % M, n = min(q1 - q, M - i0), slot = q - p0;
-            const uint8_t *ex = expert(l, sel[j]);
-            bulk(gu + slot * S::row_b, ex + a.slot.rel_v[0] + (int64_t)i0 * S::row_b,
-                 n * S::row_b, bar + 2 + g);
-            bulk(gu + (L::PP + slot) * S::row_b, ex + a.slot.rel_v[1] + (int64_t)i0 * S::row_b,
-                 n * S::row_b, bar + 2 + g);
-            if (FMT == DS4F_FMT_FP8) {
-                bulk(gsc + ((g * 2 + seg) * 2 + 0) * S::gsc_b, ex + a.slot.rel_s[0], S::gsc_b, bar + 2 + g);
-                bulk(gsc + ((g * 2 + seg) * 2 + 1) * S::gsc_b, ex + a.slot.rel_s[1], S::gsc_b, bar + 2 + g);
-            } else {
-                bulk(gsc + slot * S::gsc_b, ex + a.slot.rel_s[0] + (int64_t)i0 * S::gsc_b,
-                     n * S::gsc_b, bar + 2 + g);
-                bulk(gsc + (L::PP + slot) * S::gsc_b, ex + a.slot.rel_s[1] + (int64_t)i0 * S::gsc_b,
-                     n * S::gsc_b, bar + 2 + g);
+        const int split = min(q1, (q0 / M + 1) * M);
+        if (g < ngroups && (lane & 7) == 0) {
+            uint32_t total = 0;
+            for (int q = q0; q < q1;) {
+                int i0 = q % M, n = min(q1 - q, M - i0);
+                total += 2 * n * S::row_b + (FMT == DS4F_FMT_FP8 ? 2 * S::gsc_b : 2 * n * S::gsc_b);
+                q += n;
             }
-            q += n;
+            mbar_expect(bar + 2 + g, total);
         }
+        __syncwarp();                        // every lane: expects before copies
+        if (g >= ngroups) return;
+        const int qa = sg == 0 ? q0 : split, qb = sg == 0 ? split : q1;
+        if (qa >= qb) return;
+        const int j = qa / M, i0 = qa % M, n = qb - qa, slot = qa - p0, mat = kind & 1;
+        const uint8_t *ex = expert(l, sel[j]);
+        if (kind < 2)
+            bulk(gu + (mat * L::PP + slot) * S::row_b, ex + a.slot.rel_v[mat] + (int64_t)i0 * S::row_b,
+                 n * S::row_b, bar + 2 + g);
+        else if (FMT == DS4F_FMT_FP8)
+            bulk(gsc + ((g * 2 + sg) * 2 + mat) * S::gsc_b, ex + a.slot.rel_s[mat], S::gsc_b, bar + 2 + g);
+        else
+            bulk(gsc + (mat * L::PP + slot) * S::gsc_b, ex + a.slot.rel_s[mat] + (int64_t)i0 * S::gsc_b,
+                 n * S::gsc_b, bar + 2 + g);
     };
     // bytes of the routed down copies (rows + scales of K experts)
     const int sa0 = FMT == DS4F_FMT_FP8 ? 0 : (r0 * S::dsc_b) / 16 * 16;
     const int sab = FMT == DS4F_FMT_FP8 ? S::dsc_b : ((r0 + nr) * S::dsc_b + 15) / 16 * 16 - sa0;
     const uint32_t dn_total = K * (nr * S::drow_b + sab);
-    // lane j < K of warp 0: down rows + scales of selection j (bar 6)
-    auto issue_down_j = [&](int l, int j) {
+    // lane 2 j + h < 2 K of warp 1: down rows (h = 0) or scales (h = 1) of
+    // selection j (bar 6)
+    auto issue_down_lane = [&](int l, int lane) {
+        const int j = lane >> 1;
         const uint8_t *ex = expert(l, sel[j]);
-        if (nr)
-            bulk(dn + j * L::RR * S::drow_b, ex + a.slot.rel_v[2] + (int64_t)r0 * S::drow_b,
-                 nr * S::drow_b, bar + 6);
-        bulk(dsc + j * L::DSC, ex + a.slot.rel_s[2] + sa0, sab, bar + 6);
+        if ((lane & 1) == 0) {
+            if (nr)
+                bulk(dn + j * L::RR * S::drow_b, ex + a.slot.rel_v[2] + (int64_t)r0 * S::drow_b,
+                     nr * S::drow_b, bar + 6);
+        } else {
+            bulk(dsc + j * L::DSC, ex + a.slot.rel_s[2] + sa0, sab, bar + 6);
+        }
     };
 
     if (tid == 0) {
         prefetch_rt(0);
         prefetch_sd(0);
     }
-    pend[0] = pend[1] = true;
+    pendb |= 3u;
 
     const int T = a.n_layers * a.n_steps;
 #define DS4F_TRACE(k) \
     if (a.trace && tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + (k)] = gtimer()
+#define DS4F_ROUNDS(k) (a.trace ? a.trace + ((int64_t)t * G + c) * kTracePts + (k) : nullptr)
     for (int t = 0; t < T; t++) {
         const int l = t % a.n_layers, ln = (t + 1) % a.n_layers;
         const bool more = t + 1 < T;
@@ -350,8 +363,8 @@ k_decode(DecodeArgs a) {
             } else {
                 static_assert(H % kThreads == 0, "state words split evenly over threads");
                 const uint64_t *sw = (const uint64_t *)gu;
-                got = gather_ll(a, bar + 7, ph[7], pend[7], (uint64_t *)gu, a.st_ll, H, H,
-                                tag_of(t - 1), 1);
+                got = gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.st_ll, H, H,
+                                tag_of(t - 1), 1, DS4F_ROUNDS(14));
 #pragma unroll
                 for (int k = 0; k < PER; k++) v[k] = __uint_as_float((uint32_t)sw[tid + k * kThreads]);
             }
@@ -378,9 +391,9 @@ k_decode(DecodeArgs a) {
                 rd[16] = s2;
             }
             // (B) norm weights arrive with the router rows (bar 0)
-            bool okb = mbar_wait(a, bar + 0, ph[0], 2);
+            bool okb = mbar_wait(a, bar + 0, PH(0), 2);
             if (!__syncthreads_and(okb)) { ok = false; break; }
-            ph[0] ^= 1; pend[0] = false;
+            FLIP(0); PEND(0, false);
             float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(rd[16], (double)H)), 1e-6f));
             for (int i = tid; i < H; i += kThreads)
                 xin[i] = __fmul_rn(__fdiv_rn(xin[i], r), bf16_to_f32(nw[i]));
@@ -393,20 +406,23 @@ k_decode(DecodeArgs a) {
             const int e = rt0 + warp;
             const uint16_t *row = rt + warp * H + lane * S::cpl;
             constexpr int NCH = S::cpl / 8;
-            double Tq[NCH], Aq[NCH];
+            double Tq[NCH];
+            float Aq[NCH];
 #pragma unroll
             for (int k = 0; k < NCH; k++) {
                 uint4 w = lds16(row + k * 8);
                 const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
                 const float *x = xin + lane * S::cpl + k * 8;
                 double p8[8];
-                double ab = 0.0;
+                // the bound's |p| (8 - u) terms: positive, summed in fp32 (<= 64
+                // terms per lane, relative error < 4e-6, inside the 1.001 margin)
+                float ab = 0.f;
 #pragma unroll
                 for (int u = 0; u < 8; u++) {
                     uint32_t h = (u & 1) ? (ww[u >> 1] & 0xFFFF0000u) : (ww[u >> 1] << 16);
                     float p = __fmul_rn(__uint_as_float(h), x[u]);   // the reference's product
                     p8[u] = (double)p;
-                    ab = __dadd_rn(ab, (double)fabsf(p) * (double)(8 - u));
+                    ab = fmaf(fabsf(p), (float)(8 - u), ab);
                 }
                 Tq[k] = __dadd_rn(__dadd_rn(__dadd_rn(p8[0], p8[1]), __dadd_rn(p8[2], p8[3])),
                                   __dadd_rn(__dadd_rn(p8[4], p8[5]), __dadd_rn(p8[6], p8[7])));
@@ -425,7 +441,7 @@ k_decode(DecodeArgs a) {
             double bs = 0.0, loc = 0.0;
 #pragma unroll
             for (int k = 0; k < NCH; k++) {
-                bs = __dadd_rn(bs, __dadd_rn(8.0 * fabs(__dadd_rn(P, loc)), Aq[k]));
+                bs = __dadd_rn(bs, __dadd_rn(8.0 * fabs(__dadd_rn(P, loc)), (double)Aq[k]));
                 loc = __dadd_rn(loc, Tq[k]);
             }
             // the prefixes carry double rounding of their own: widen by 1e-12
@@ -466,7 +482,8 @@ k_decode(DecodeArgs a) {
         // (F) routing: gather every S/B word, then warp 0 takes the
         //     certified top-K
         static_assert(E % 32 == 0 && (4 * E * 8) % 16 == 0, "router width: whole warps of experts");
-        if (!gather_ll(a, bar + 7, ph[7], pend[7], (uint64_t *)gu, a.sb_ll, 4 * E, 4 * E, tg, 3)) {
+        if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.sb_ll, 4 * E, 4 * E, tg, 3,
+                       DS4F_ROUNDS(15))) {
             ok = false;
             break;
         }
@@ -592,180 +609,249 @@ k_decode(DecodeArgs a) {
             __syncthreads();
         }
         DS4F_TRACE(5);
-        // (G) every routed byte of this CTA in flight; next layer's router
-        //     rows + norm weights into the buffers (B) and (C) are done with
+        // (G) every routed byte of this CTA in flight, one copy per lane:
+        //     warp 0 the gate/up groups, warp 1 the down rows, warp 2 the next
+        //     layer's router rows + norm weights (buffers (B) and (C) are
+        //     done with). Meanwhile the other warps load their x registers
+        //     and the last warp takes the softmax alone.
+        static_assert(kGroups * 8 <= 32 && 2 * K <= 32, "one copy per lane");
         if (warp == 0) {
             fence_async();
-            if (lane < ngroups) issue_group(l, lane);
-            if (lane == 8) mbar_expect(bar + 6, dn_total);
+            issue_group_lane(l, lane);
+        } else if (warp == 1) {
+            fence_async();
+            if (lane == 0) mbar_expect(bar + 6, dn_total);
             __syncwarp();
-            if (lane >= 8 && lane < 8 + K) issue_down_j(l, lane - 8);
-            if (lane == 31 && more) prefetch_rt(ln);
+            if (lane < 2 * K) issue_down_lane(l, lane);
+        } else if (warp == 2) {
+            if (lane == 0 && more) { fence_async(); prefetch_rt(ln); }
         }
 #pragma unroll
-        for (int g = 0; g < kGroups; g++) pend[2 + g] = g < ngroups;
-        pend[6] = true;
-        pend[0] = more;
+        for (int g = 0; g < kGroups; g++) PEND(2 + g, g < ngroups);
+        PEND(6, true);
+        PEND(0, more);
         DS4F_TRACE(6);
-        // softmax over all E (double, max subtracted) + renorm
-        {
-            double *rd = (double *)red;
-            double mx = tid < E ? tk[tid] : -1e300;
+        asm volatile("" ::: "memory");        // keep the x loads below the issue code
+        // x registers of the gate/up granules: warp w covers column half
+        // w / 8; lane l holds elements (32 j + l) gb + u of its granules j,
+        // pre-scaled by 2^64 (16-byte reads, consecutive lanes consecutive
+        // addresses)
+        constexpr int NGH = S::ng / 2;
+        static_assert(S::ng % 2 == 0 && kWarps == 2 * kGroupPairs, "two column halves per pair");
+        const int hcol = warp >> 3;
+        float xr[NGH * S::gb];
+#pragma unroll
+        for (int j = 0; j < NGH; j++)
+#pragma unroll
+            for (int u = 0; u < S::gb; u += 4) {
+                const float4 v = *(const float4 *)(xin + (32 * (hcol * NGH + j) + lane) * S::gb + u);
+                xr[j * S::gb + u] = v.x * DS4F_X_PRESCALE;
+                xr[j * S::gb + u + 1] = v.y * DS4F_X_PRESCALE;
+                xr[j * S::gb + u + 2] = v.z * DS4F_X_PRESCALE;
+                xr[j * S::gb + u + 3] = v.w * DS4F_X_PRESCALE;
+            }
+        if (warp == kWarps - 1) {
+            // softmax over all E (double, max subtracted) and the renorm
+            // (src/moe.c:531-561 + norm_topk_prob); wsel is read after the
+            // gate/up phase's barriers
+            constexpr int NE = E / 32;
+            double mx = -1e300;
+#pragma unroll
+            for (int i = 0; i < NE; i++) mx = fmax(mx, tk[lane + 32 * i]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-            if (lane == 0) rd[32 + warp] = mx;
-            __syncthreads();
-            mx = rd[32];
-            for (int k = 1; k < kWarps; k++) mx = fmax(mx, rd[32 + k]);
-            double part = tid < E ? exp(tk[tid] - mx) : 0.0;
-            part = warp_sum_d(part);
-            if (lane == 0) rd[48 + warp] = part;
-            __syncthreads();
-            if (warp == 0) {
-                double sw = 0.0;
-                for (int k = 0; k < kWarps; k++) sw += rd[48 + k];
-                const float wj = lane < K ? (float)(exp(tk[sel[lane]] - mx) / sw) : 0.0f;
-                float s = 0.0f;
-                for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, wj, j));
-                if (lane < K) wsel[lane] = (a.renorm && s > 0.0f) ? __fdiv_rn(wj, s) : wj;
-                if (lane == 0 && c == 0) atomicAdd(a.diag, 1u);
-            }
-            __syncthreads();
+            double sw = 0.0;
+#pragma unroll
+            for (int i = 0; i < NE; i++) sw += exp(tk[lane + 32 * i] - mx);
+            sw = warp_sum_d(sw);
+            const float wj = lane < K ? (float)(exp(tk[sel[lane]] - mx) / sw) : 0.0f;
+            float s = 0.0f;
+            for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, wj, j));
+            if (lane < K) wsel[lane] = (a.renorm && s > 0.0f) ? __fdiv_rn(wj, s) : wj;
+            if (lane == 0 && c == 0) atomicAdd(a.diag, 1u);
         }
         DS4F_TRACE(7);
-        // (H) gate/up as the groups land: warp w -> pair w/2 of the group,
-        //     gate (even) / up (odd); x pre-scaled by 2^64 in registers
+        // (H) gate/up: warp w -> pair w % 8 of every group, gate and up
+        //     rows over column half w / 8 (the two halves meet in red[]);
+        //     each warp takes a group as soon as it has landed (its own wait,
+        //     no block barrier)
         {
-            float xr[S::gk * S::ce];
-#pragma unroll
-            for (int k = 0; k < S::gk; k++)
-#pragma unroll
-                for (int e = 0; e < S::ce; e += 4) {
-                    float4 v = *(const float4 *)(xin + (lane + 32 * k) * S::ce + e);
-                    xr[k * S::ce + e] = v.x * DS4F_X_PRESCALE;
-                    xr[k * S::ce + e + 1] = v.y * DS4F_X_PRESCALE;
-                    xr[k * S::ce + e + 2] = v.z * DS4F_X_PRESCALE;
-                    xr[k * S::ce + e + 3] = v.w * DS4F_X_PRESCALE;
-                }
+            unsigned landed = 0;
+            if (a.trace && tid == 0)
+                for (int g = 0; g < ngroups; g++) landed |= (unsigned)mbar_test(bar + 2 + g, PH(2 + g)) << g;
+            if (a.trace && tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + 17] = landed;
+            const int ps = warp & 7;
+            bool okg = true;
+#pragma unroll 1
             for (int g = 0; g < ngroups; g++) {
-                const bool okg = mbar_wait(a, bar + 2 + g, ph[2 + g], 4);
-                if (!__syncthreads_and(okg)) { ok = false; break; }
-                ph[2 + g] ^= 1; pend[2 + g] = false;
+                okg = mbar_wait(a, bar + 2 + g, PH(2 + g), 4);
+                if (!okg) break;
                 if (g == 0) DS4F_TRACE(8);
-                const int q0 = p0 + g * kGroupPairs, nq = min(kGroupPairs, p0 + np - q0);
-                const int ps = warp >> 1, m = warp & 1;
-                if (ps < nq) {
-                    const int q = q0 + ps, i = q % M, slot = q - p0;
-                    const int seg = q / M - q0 / M;
-                    const uint8_t *row = gu + (m * L::PP + slot) * S::row_b;
-                    float acc = 0.f;
+                // rows past the CTA's pairs read slot 0 and are dropped
+                const int q0 = p0 + g * kGroupPairs;
+                const bool valid = ps < min(kGroupPairs, p0 + np - q0);
+                const int q = valid ? q0 + ps : p0, slot = q - p0;
+                const uint8_t *rg = gu + slot * S::row_b, *ru = gu + (L::PP + slot) * S::row_b;
+                float ag, au;
+                if constexpr (FMT == DS4F_FMT_FP8) {
+                    // granule j lies in column block j: one scale per warp
+                    const int seg = valid ? q / M - q0 / M : 0;
+                    const int sb = (((valid ? g : 0) * 2 + seg) * 2) * S::gsc_b;
+                    const float *sg = (const float *)(gsc + sb) + ((q % M) >> 7) * (H / 128) + hcol * NGH;
+                    const float *su = (const float *)(gsc + sb + S::gsc_b) + ((q % M) >> 7) * (H / 128) + hcol * NGH;
+                    float2 g2 = make_float2(0.f, 0.f), u2 = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int k = 0; k < S::gk; k++) {
-                        const int qq = lane + 32 * k;
-                        uint4 w = lds16(row + qq * 16);
-                        if constexpr (FMT == DS4F_FMT_FP8) {
-                            const float *sc = (const float *)(gsc + ((g * 2 + seg) * 2 + m) * S::gsc_b);
-                            const float s8 = sc[(i >> 7) * (H / 128) + (qq >> 3)];
-                            acc = fmaf(f8_dot16(w, xr + k * S::ce) * DS4F_F8_POST, s8, acc);
-                        } else {
-                            const float s4 = e8m0_to_f32(gsc[(m * L::PP + slot) * S::gsc_b + qq]);
-                            acc = fmaf(e2m1_dot32(w, xr + k * S::ce) * DS4F_E2M1_POST, s4, acc);
-                        }
+                    for (int j = 0; j < NGH; j++) {
+                        const int off = (32 * (hcol * NGH + j) + lane) * 4;
+                        const float2 x01 = make_float2(xr[4 * j], xr[4 * j + 1]);
+                        const float2 x23 = make_float2(xr[4 * j + 2], xr[4 * j + 3]);
+                        g2 = f8_fma4(*(const uint32_t *)(rg + off), x01, x23, sg[j], g2);
+                        u2 = f8_fma4(*(const uint32_t *)(ru + off), x01, x23, su[j], u2);
                     }
-                    acc = warp_sum(acc);
-                    if (lane == 0) red[2 * ps + m] = acc;
+                    ag = (g2.x + g2.y) * DS4F_F8_POST;
+                    au = (u2.x + u2.y) * DS4F_F8_POST;
+                } else {
+                    const uint8_t *s4g = gsc + slot * S::gsc_b, *s4u = gsc + (L::PP + slot) * S::gsc_b;
+                    float eg = 0.f, eu = 0.f;
+#pragma unroll
+                    for (int j = 0; j < NGH; j++) {
+                        const int gi = 32 * (hcol * NGH + j) + lane;
+                        eg = fmaf(e2m1_dot8(*(const uint32_t *)(rg + 4 * gi), xr + 8 * j), e8m0_to_f32(s4g[gi >> 2]), eg);
+                        eu = fmaf(e2m1_dot8(*(const uint32_t *)(ru + 4 * gi), xr + 8 * j), e8m0_to_f32(s4u[gi >> 2]), eu);
+                    }
+                    ag = eg * DS4F_E2M1_POST;
+                    au = eu * DS4F_E2M1_POST;
                 }
-                __syncthreads();
-                if (tid < nq) {
-                    const int q = q0 + tid;
-                    st_tag(a.ch_ll + (q / M) * M + (q % M), tg,
-                           __float_as_uint(silu_mul(red[2 * tid], red[2 * tid + 1])));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    ag += __shfl_xor_sync(0xFFFFFFFFu, ag, o);
+                    au += __shfl_xor_sync(0xFFFFFFFFu, au, o);
                 }
-                __syncthreads();
+                // red[] floats: [half][group][pair][gate, up]
+                if (lane == 0) {
+                    red[((hcol * kGroups + g) * kGroupPairs + ps) * 2] = ag;
+                    red[((hcol * kGroups + g) * kGroupPairs + ps) * 2 + 1] = au;
+                }
             }
-            if (!ok) break;
+            if (!__syncthreads_and(okg)) { ok = false; break; }
+#pragma unroll
+            for (int g = 0; g < kGroups; g++)
+                if (g < ngroups) { FLIP(2 + g); PEND(2 + g, false); }
+            if (tid < np) {
+                constexpr int HALF = kGroups * kGroupPairs * 2;
+                const int q = p0 + tid;
+                st_tag(a.ch_ll + (q / M) * M + (q % M), tg,
+                       __float_as_uint(silu_mul(red[2 * tid] + red[HALF + 2 * tid],
+                                                red[2 * tid + 1] + red[HALF + 2 * tid + 1])));
+            }
         }
         DS4F_TRACE(9);
         // (I) down rows: routed (bar 6) and shared (bar 1); chains polled
         {
-            const bool okd = mbar_wait(a, bar + 6, ph[6], 6) && mbar_wait(a, bar + 1, ph[1], 7);
+            const bool okd = mbar_wait(a, bar + 6, PH(6), 6) && mbar_wait(a, bar + 1, PH(1), 7);
             if (!__syncthreads_and(okd)) { ok = false; break; }
-            ph[6] ^= 1; pend[6] = false;
-            ph[1] ^= 1; pend[1] = false;
+            FLIP(6); PEND(6, false);
+            FLIP(1); PEND(1, false);
             DS4F_TRACE(10);
             // every chain word (routed, shared, then the shared-gate logit)
             // into shared memory, over the gate/up rows (H) is done with
             // (K+1) M chain words + the logit, copied as an even count (the
             // workspace allocation is padded past the last word)
             constexpr int NCW = (K + 1) * M + 1;
-            if (!gather_ll(a, bar + 7, ph[7], pend[7], (uint64_t *)gu, a.ch_ll, (NCW + 1) / 2 * 2,
-                           NCW, tg, 5)) {
+            if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.ch_ll, (NCW + 1) / 2 * 2,
+                           NCW, tg, 5, DS4F_ROUNDS(16))) {
                 ok = false;
                 break;
             }
-            // unpack the values next to the words (consecutive threads,
-            // consecutive words: no bank conflicts), then every warp loads
-            // its chain registers from the packed floats
+            // the values next to the words, routed chains pre-scaled by 2^64
             float *chf = (float *)(gu + L::GATH);
             {
                 const uint64_t *chw = (const uint64_t *)gu;
-                for (int i = tid; i < NCW; i += kThreads) chf[i] = __uint_as_float((uint32_t)chw[i]);
+                for (int i = tid; i < NCW; i += kThreads) {
+                    const float v = __uint_as_float((uint32_t)chw[i]);
+                    chf[i] = i < K * M ? v * DS4F_X_PRESCALE : v;
+                }
             }
             __syncthreads();
             DS4F_TRACE(12);
+            // row-dot d: selection d / nr (K = the shared expert), output row
+            // d % nr. Warp w takes a contiguous range of dots, keeps the
+            // chain's floats of its current selection in registers and runs
+            // two rows of that selection at once. Lane l reads the row's
+            // granules 32 g + l and the chain's matching floats (16-byte
+            // reads, consecutive lanes consecutive addresses).
+            constexpr int XC = S::dg * S::gb > 4 * S::bn ? S::dg * S::gb : 4 * S::bn;
+            float xc[XC];
+            auto row_dot = [&](int j, int rr) -> float {
+                if (j < K) {
+                    const uint8_t *row = dn + (j * L::RR + rr) * S::drow_b;
+                    if constexpr (FMT == DS4F_FMT_FP8) {
+                        // granule g lies in column block g
+                        const float *sc = (const float *)(dsc + j * L::DSC) + ((r0 + rr) >> 7) * (M / 128);
+                        float2 a2 = make_float2(0.f, 0.f);
+#pragma unroll
+                        for (int g = 0; g < S::dg; g++)
+                            a2 = f8_fma4(*(const uint32_t *)(row + 4 * (32 * g + lane)),
+                                         make_float2(xc[4 * g], xc[4 * g + 1]),
+                                         make_float2(xc[4 * g + 2], xc[4 * g + 3]), sc[g], a2);
+                        return (a2.x + a2.y) * DS4F_F8_POST;
+                    } else {
+                        const uint8_t *s4 = dsc + j * L::DSC + (r0 + rr) * S::dsc_b - sa0;
+                        float v = 0.f;
+#pragma unroll
+                        for (int g = 0; g < S::dg; g++) {
+                            const int q = 32 * g + lane;
+                            v = fmaf(e2m1_dot8(*(const uint32_t *)(row + 4 * q), xc + 8 * g),
+                                     e8m0_to_f32(s4[q >> 2]), v);
+                        }
+                        return v * DS4F_E2M1_POST;
+                    }
+                }
+                const uint16_t *row = sd + rr * M;
+                float v = 0.f;
+#pragma unroll
+                for (int g = 0; g < S::bn; g++)
+                    v += bf16_dot4(*(const uint2 *)(row + 4 * (32 * g + lane)),
+                                   make_float4(xc[4 * g], xc[4 * g + 1], xc[4 * g + 2], xc[4 * g + 3]));
+                return v;
+            };
             const int ndots = (K + 1) * nr;
             const int d0 = warp * ndots / kWarps, d1 = (warp + 1) * ndots / kWarps;
             int jcur = -1;
-            float xr[S::dk * S::ce];          // routed chain, pre-scaled by 2^64
-            float xb[S::bk * 8];              // shared chain, bf16 chunk layout
-            for (int d = d0; d < d1; d++) {
+            for (int d = d0; d < d1;) {
                 const int j = d / nr, rr = d % nr;
                 if (j != jcur) {
                     jcur = j;
                     if (j < K) {
 #pragma unroll
-                        for (int k = 0; k < S::dk; k++)
+                        for (int g = 0; g < S::dg; g++)
 #pragma unroll
-                            for (int e = 0; e < S::ce; e++)
-                                xr[k * S::ce + e] =
-                                    chf[j * M + ((lane % S::dlpr) + S::dlpr * k) * S::ce + e] * DS4F_X_PRESCALE;
+                            for (int u = 0; u < S::gb; u += 4) {
+                                const float4 v4 = *(const float4 *)(chf + j * M + (32 * g + lane) * S::gb + u);
+                                xc[g * S::gb + u] = v4.x; xc[g * S::gb + u + 1] = v4.y;
+                                xc[g * S::gb + u + 2] = v4.z; xc[g * S::gb + u + 3] = v4.w;
+                            }
                     } else {
 #pragma unroll
-                        for (int k = 0; k < S::bk; k++)
-#pragma unroll
-                            for (int e = 0; e < 8; e++)
-                                xb[k * 8 + e] = chf[K * M + ((lane % S::blpr) + S::blpr * k) * 8 + e];
-                    }
-                }
-                float v = 0.f;
-                if (j < K) {
-                    const uint8_t *row = dn + (j * L::RR + rr) * S::drow_b;
-                    const int ql = lane % S::dlpr;
-#pragma unroll
-                    for (int k = 0; k < S::dk; k++) {
-                        const int q = ql + S::dlpr * k;
-                        uint4 w = lds16(row + q * 16);
-                        if constexpr (FMT == DS4F_FMT_FP8) {
-                            const float *sc = (const float *)(dsc + j * L::DSC);
-                            const float s8 = sc[((r0 + rr) >> 7) * (M / 128) + (q >> 3)];
-                            v = fmaf(f8_dot16(w, xr + k * S::ce) * DS4F_F8_POST, s8, v);
-                        } else {
-                            const float s4 = e8m0_to_f32(dsc[j * L::DSC + (r0 + rr) * S::dsc_b - sa0 + q]);
-                            v = fmaf(e2m1_dot32(w, xr + k * S::ce) * DS4F_E2M1_POST, s4, v);
+                        for (int g = 0; g < S::bn; g++) {
+                            const float4 v4 = *(const float4 *)(chf + K * M + 4 * (32 * g + lane));
+                            xc[4 * g] = v4.x; xc[4 * g + 1] = v4.y; xc[4 * g + 2] = v4.z; xc[4 * g + 3] = v4.w;
                         }
                     }
-#pragma unroll
-                    for (int o = S::dlpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-                } else {
-                    const uint16_t *row = sd + rr * M;
-                    const int ql = lane % S::blpr;
-#pragma unroll
-                    for (int k = 0; k < S::bk; k++)
-                        v += bf16_dot8(lds16(row + (ql + S::blpr * k) * 8), xb + k * 8);
-#pragma unroll
-                    for (int o = S::blpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
                 }
-                if (lane == 0) outs[j * L::RR + rr] = v;
+                const bool two = d + 1 < d1 && rr + 1 < nr;
+                float v0 = row_dot(j, rr);
+                float v1 = two ? row_dot(j, rr + 1) : 0.f;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, o);
+                    v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, o);
+                }
+                if (lane == 0) {
+                    outs[j * L::RR + rr] = v0;
+                    if (two) outs[j * L::RR + rr + 1] = v1;
+                }
+                d += two ? 2 : 1;
             }
             DS4F_TRACE(13);
             if (tid == 0) red[0] = sigmoid_ref(chf[(K + 1) * M]);
@@ -785,12 +871,16 @@ k_decode(DecodeArgs a) {
         }
         DS4F_TRACE(11);        // (stamps 12, 13: inside the down phase, above)
         if (tid == 0 && more) { fence_async(); prefetch_sd(ln); }
-        pend[1] = more;
+        PEND(1, more);
     }
-#undef DS4F_TRACE
     // drain this CTA's copies before exit (bounded)
     for (int i = 0; i < 8; i++)
-        if (pend[i]) mbar_wait(a, bar + i, ph[i], 8);
+        if ((pendb >> i) & 1u) mbar_wait(a, bar + i, PH(i), 8);
+#undef DS4F_TRACE
+#undef DS4F_ROUNDS
+#undef PH
+#undef FLIP
+#undef PEND
 }
 
 template <int FMT, int H, int M, int E, int K>
