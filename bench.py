@@ -49,6 +49,12 @@ def bytes_per_token(fmt_fp8=True):
     return LAYERS * per_layer
 
 
+# DRAM bytes (read + write) of one k_decode launch, from the ncu --set full
+# capture summarised in profiles/k_decode_fp8_4layer_full.md (4-layer case,
+# 135.33 MB) scaled to 40 layers: every layer reads its own weights.
+TRAFFIC_PER_LAUNCH = 10 * 135_330_000
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -59,51 +65,89 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the
-    timed region."""
-    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled during the timed region: NVML
+    every 10 ms from a thread (so short regions still get samples), else
+    nvidia-smi at 200 ms."""
+    BITS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+            0x4: "sw_power_cap"}
 
     def __init__(self, dev):
-        # line-buffered so samples survive the interrupt that ends the loop
-        cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-               "-lms", "200", "-i", str(dev)]
+        import threading
+        self.sm, self.mx, self.reasons, self.p, self.t = [], 0.0, set(), None, None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            try:
+                import torch
+                uid = str(torch.cuda.get_device_properties(dev).uuid)
+                h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uid) if not uid.startswith("GPU-") else uid)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(dev)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_r = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.stop_ev = threading.Event()
+
+            def run():
+                while not self.stop_ev.is_set():
+                    try:
+                        self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                        r = get_r(h)
+                        for bit, name in self.BITS.items():
+                            if r & bit:
+                                self.reasons.add(name)
+                    except Exception:
+                        pass
+                    self.stop_ev.wait(0.01)
+            self.t = threading.Thread(target=run, daemon=True)
+            self.t.start()
+            self.src = "nvml"
+            return
+        except Exception:
+            pass
+        cmd = ["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+               "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200",
+               "-i", str(dev)]
         if shutil.which("stdbuf"):
             cmd = ["stdbuf", "-oL"] + cmd
         try:
-            self.p = subprocess.Popen(cmd, stdout=subprocess.PIPE,
-                                      stderr=subprocess.DEVNULL, text=True)
+            self.p = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.src = "nvidia-smi"
         except Exception:
             self.p = None
 
     def stop(self):
-        if not self.p:
-            return None
-        self.p.send_signal(signal.SIGINT)
-        try:
-            out, _ = self.p.communicate(timeout=5)
-        except Exception:
-            self.p.kill()
-            out, _ = self.p.communicate()
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 6:
-                continue
+        if self.t is not None:
+            self.stop_ev.set()
+            self.t.join(timeout=2)
+        elif self.p is not None:
+            self.p.send_signal(signal.SIGINT)
             try:
-                sm.append(float(f[0]))
-                mx = max(mx, float(f[1]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[2:6]):
-                if v == "Active":
-                    reasons.add(n)
-        if not sm:
+                out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                self.p.kill()
+                out, _ = self.p.communicate()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in out.strip().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 6:
+                    continue
+                try:
+                    self.sm.append(float(f[0]))
+                    self.mx = max(self.mx, float(f[1]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[2:6]):
+                    if v == "Active":
+                        self.reasons.add(n)
+        else:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.sm:
+            return None
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.mx,
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": self.src}
 
 
 # ---- CPU baseline: the reference's own kernels on the host cores -------------
@@ -288,7 +332,9 @@ def run_gpu(args, rank, world, local_rank):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": None, "peak_source": src,
+                         "traffic": (None if args.layered else TRAFFIC_PER_LAUNCH),
+                         "traffic_unit": "bytes per launch (ncu, 4-layer capture x 10)",
+                         "peak_source": src,
                          "kernel": ("whole decode step: 4 kernels per layer in a CUDA graph" if args.layered
                                     else "k_decode: the whole 40-layer step in one persistent launch"),
                          "algorithmic_bytes_per_token": bpt},
