@@ -1,0 +1,351 @@
+// gemm.cu -- block-scaled FP8 GEMM on the 5th-generation tensor cores
+// (tcgen05, TMEM accumulators, TMA-fed 128-byte-swizzled tiles), the
+// building block of the batched prefill (the grouped-by-expert chains of
+// ds4f_moe_step_batch, src/moe.c:1480-1707), and the activation quantiser
+// whose outputs it consumes.
+//
+//   Y[n][r] = sum_kb sW[r/128][kb] sX[n][kb] sum_{c in kb} W[r][c] x~[n][c]
+//
+// W: [R][C] canonical E4M3 (the expert pool's bytes), sW fp32 per 128x128
+// block (the pool's scales). The activations are fp32 in the reference
+// (src/moe.c:1480-1707); here each row's 128-column block is scaled into
+// [-240, 240] and written as ND E4M3 "digits", x~ = d0 + d1/16 + d2/256
+// (relative error <= 2^-13 at ND = 3, against 2^-4 for one digit), so the
+// tensor core works on native FP8 on both sides while the chain keeps the
+// reference's precision. The digits are planes [ND][N][C]; one 3-D TMA box
+// brings a tile's ND x BN rows, and the MMA's N dimension is ND x BN.
+//
+// The tensor core sums each 128-column block exactly as E4M3 x E4M3
+// products in fp32 (tcgen05.mma kind::f8f6f4, 4 instructions of K = 32);
+// the block's two scales differ per output element, so each block's partial
+// sums are read back from TMEM, the digits combined, and added into fp32
+// registers with the scales ("promotion") while the tensor core already
+// works on the next block in the other TMEM buffer.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tc.cuh"
+#include "../../include/ds4f/gpu_cuda.h"
+
+namespace ds4f {
+
+// ---- host: tensor maps -----------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+// 8-bit tensor [rows][inner] (row stride `stride` bytes), boxes of
+// [box_rows][128 bytes] with the 128-byte swizzle; rows past the end read 0.
+int tmap_u8_2d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t stride,
+               uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) { set_error("cuTensorMapEncodeTiled is unavailable"); return -1; }
+    if (((uintptr_t)base & 15) || (stride & 15) || inner % 128 || box_rows < 1 || box_rows > 256) {
+        set_error("tensor map: base/stride must be 16-byte aligned, inner a multiple of 128");
+        return -1;
+    }
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {stride};
+    cuuint32_t box[2] = {128, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return -1; }
+    return 0;
+}
+
+// 8-bit tensor [planes][rows][inner], boxes of [planes][box_rows][128 bytes].
+int tmap_u8_3d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t planes,
+               uint64_t row_stride, uint64_t plane_stride, uint32_t box_rows, uint32_t box_planes) {
+    auto fn = encode_fn();
+    if (!fn) { set_error("cuTensorMapEncodeTiled is unavailable"); return -1; }
+    if (((uintptr_t)base & 15) || (row_stride & 15) || (plane_stride & 15) || inner % 128 ||
+        box_rows < 1 || box_rows > 256 || box_planes < 1 || box_planes > 256) {
+        set_error("tensor map: base/strides must be 16-byte aligned, inner a multiple of 128");
+        return -1;
+    }
+    cuuint64_t dims[3] = {inner, rows, planes};
+    cuuint64_t strides[2] = {row_stride, plane_stride};
+    cuuint32_t box[3] = {128, box_rows, box_planes};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return -1; }
+    return 0;
+}
+
+namespace {
+
+// ---- activation quantiser -------------------------------------------------------
+// Per (row, 128-column block): a = max |x|; r = 240 / a and s = a / 240 (fp32,
+// correctly rounded; a = 0: r = 0, s = 1); y = x * r; then ND digits
+//   d0 = E4M3(y),  e = (y - d0) * 16,  d1 = E4M3(e),  e = (e - d1) * 16, ...
+// E4M3() rounds to nearest even, saturating. Every digit stays within
+// [-240, 240] (exponent field <= 14), where the reference's E4M3 table and
+// standard E4M3 agree. Output planes q[d][row][col].
+__device__ __forceinline__ uint32_t e4m3_2(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float e4m3_val(uint32_t b) {      // exact
+    return __int_as_float(((int)(b << 24) >> 4) & (int)0x87F00000) * DS4F_F8_UNSCALE;
+}
+__global__ void k_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t *q, float *s) {
+    const int nb = C / 128;
+    const int64_t blk = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;   // one warp per block
+    if (blk >= (int64_t)N * nb) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t off = (blk / nb) * (int64_t)C + (blk % nb) * 128 + 4 * lane;
+    const float4 v = *(const float4 *)(x + off);
+    float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    const float r = a > 0.f ? __fdiv_rn(240.0f, a) : 0.f;
+    float y[4] = {__fmul_rn(v.x, r), __fmul_rn(v.y, r), __fmul_rn(v.z, r), __fmul_rn(v.w, r)};
+    for (int d = 0; d < ND; d++) {
+        const uint32_t w = e4m3_2(y[0], y[1]) | (e4m3_2(y[2], y[3]) << 16);
+        *(uint32_t *)(q + (int64_t)d * N * C + off) = w;
+#pragma unroll
+        for (int i = 0; i < 4; i++) y[i] = __fmul_rn(__fsub_rn(y[i], e4m3_val((w >> (8 * i)) & 0xFF)), 16.0f);
+    }
+    if (lane == 0) s[blk] = a > 0.f ? __fdiv_rn(a, 240.0f) : 1.0f;
+}
+
+// ---- block-scaled FP8 GEMM ---------------------------------------------------------
+constexpr int kStages = 4;
+constexpr int kGemmThreads = 192;          // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+
+template <int BN, int ND>
+struct GemmSmem {
+    static constexpr int NM = BN * ND;                // MMA N: the digit rows of BN columns
+    static constexpr int A = 128 * 128;               // one 128-row x 128-byte tile
+    static constexpr int B = NM * 128;
+    static constexpr int STAGE = A + B;
+    static constexpr int o_bar = kStages * STAGE;     // full[S], empty[S], tfull[2], tempty[2], done
+    static constexpr int o_slot = o_bar + (2 * kStages + 5) * 8;
+    static constexpr int o_sx = o_slot + 16;
+    static constexpr int bytes(int kb) { return o_sx + BN * kb * 4 + 1024; }   // + alignment slack
+    static constexpr uint32_t NCOLS = 2 * NM <= 32 ? 32 : 2 * NM <= 64 ? 64 : 2 * NM <= 128 ? 128
+                                    : 2 * NM <= 256 ? 256 : 512;
+    static_assert(B % 1024 == 0, "B tiles keep 1024-byte alignment");
+    static_assert(NM % 16 == 0 && NM <= 256 && 2 * NM <= 512, "MMA N and TMEM columns");
+};
+
+// Epilogue: combine the digit columns of token n (n, BN + n, 2 BN + n) as
+// (D0 + D1 / 16) + D2 / 256, then acc[n] += that * (sW * sX[n]).
+template <int BN, int ND>
+__device__ __forceinline__ void promote(uint32_t t, const float *sxt, int KB, int kb, float w, float (&acc)[BN]) {
+#pragma unroll
+    for (int c = 0; c < BN / 16; c++) {
+        float v[16];
+        tc::tmem_ld16(t + c * 16, v);
+        if (ND > 1) {
+            float v1[16];
+            tc::tmem_ld16(t + BN + c * 16, v1);
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = __fadd_rn(v[i], __fmul_rn(v1[i], 0.0625f));
+        }
+        if (ND > 2) {
+            float v2[16];
+            tc::tmem_ld16(t + 2 * BN + c * 16, v2);
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = __fadd_rn(v[i], __fmul_rn(v2[i], 0.00390625f));
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            acc[c * 16 + i] = fmaf(v[i], __fmul_rn(w, sxt[(c * 16 + i) * KB + kb]), acc[c * 16 + i]);
+    }
+}
+
+template <int BN, int ND>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tX,
+          const float *__restrict__ sW, const float *__restrict__ sX, float *__restrict__ Y,
+          int R, int C, int N, unsigned *err) {
+    using L = GemmSmem<BN, ND>;
+    constexpr uint32_t ID = tc::idesc(128, L::NM, 0, 0);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
+    uint64_t *full = (uint64_t *)(sm + L::o_bar), *empty = full + kStages;
+    uint64_t *tfull = empty + kStages, *tempty = tfull + 2, *done = tempty + 2;
+    uint32_t *slot = (uint32_t *)(sm + L::o_slot);
+    float *sxt = (float *)(sm + L::o_sx);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r0 = blockIdx.x * 128, n0 = blockIdx.y * BN, KB = C / 128;
+
+    if (warp == 1) tc::tmem_alloc(slot, L::NCOLS);
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+        for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, 4); }
+        tc::mbar_init(done, 1);
+        tc::mbar_fence_init();
+        tc::prefetch_tmap(&tW);
+        tc::prefetch_tmap(&tX);
+    }
+    for (int i = tid - 64; i >= 0 && i < BN * KB; i += 128) {
+        const int n = n0 + i / KB;
+        sxt[i] = n < N ? sX[(int64_t)n * KB + i % KB] : 0.f;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t taddr = *slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int kb = 0;
+            for (; kb < KB; kb++) {
+                const int s = kb % kStages;
+                if (kb >= kStages && !tc::mbar_wait(empty + s, ((kb / kStages) - 1) & 1, err, 1)) break;
+                uint8_t *a = sm + s * L::STAGE;
+                tc::mbar_expect(full + s, L::STAGE);
+                tc::tma_load_2d(a, &tW, kb * 128, r0, full + s);
+                tc::tma_load_3d(a + L::A, &tX, kb * 128, n0, 0, full + s);
+            }
+            // every issued load has landed before the CTA may exit
+            for (int k = kb - 1; k >= 0 && k >= kb - kStages; k--)
+                tc::mbar_wait(full + k % kStages, (k / kStages) & 1, err, 2, true);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int kb = 0; kb < KB; kb++) {
+                const int s = kb % kStages, b = kb & 1;
+                if (!tc::mbar_wait(full + s, (kb / kStages) & 1, err, 3)) break;
+                if (kb >= 2 && !tc::mbar_wait(tempty + b, ((kb >> 1) - 1) & 1, err, 4)) break;
+                tc::fence_after_sync();
+                const uint8_t *a = sm + s * L::STAGE;
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    tc::mma_f8f6f4(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
+                                   tc::sdesc_sw128(a + L::A + 32 * k), ID, k > 0);
+                tc::commit(empty + s);
+                tc::commit(tfull + b);
+            }
+            tc::commit(done);
+            tc::mbar_wait(done, 0, err, 5, true);      // every MMA finished
+        }
+    } else {
+        // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows
+        const int q = warp & 3, row = q * 32 + lane;
+        float acc[BN];
+#pragma unroll
+        for (int j = 0; j < BN; j++) acc[j] = 0.f;
+        const float *swr = sW + (int64_t)(r0 / 128) * KB;
+        for (int kb = 0; kb < KB; kb++) {
+            const int b = kb & 1;
+            if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
+            tc::fence_after_sync();
+            promote<BN, ND>(taddr + ((uint32_t)(q * 32) << 16) + b * L::NM, sxt, KB, kb, swr[kb], acc);
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(tempty + b);
+        }
+        if (r0 + row < R)
+#pragma unroll
+            for (int j = 0; j < BN; j++)
+                if (n0 + j < N) Y[(int64_t)(n0 + j) * R + r0 + row] = acc[j];
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(taddr, L::NCOLS);
+    }
+}
+
+constexpr int kGemmBN = 64;
+
+template <int ND>
+int f8_gemm_launch_t(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
+                     int R, int C, int N, unsigned *err, cudaStream_t st) {
+    using L = GemmSmem<kGemmBN, ND>;
+    CUtensorMap tW, tX;
+    if (tmap_u8_2d(&tW, W, C, R, C, 128) ||
+        tmap_u8_3d(&tX, X, C, N, ND, C, (uint64_t)N * C, kGemmBN, ND))
+        return -1;
+    const int smem = L::bytes(C / 128);
+    if (smem > 227 * 1024) { set_error("f8_gemm: C too large for the scale tile"); return -1; }
+    static bool attr = false;
+    if (!attr) {
+        DS4F_CUDA(cudaFuncSetAttribute(k_f8_gemm<kGemmBN, ND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024));
+        attr = true;
+    }
+    dim3 grid(R / 128, (N + kGemmBN - 1) / kGemmBN);
+    k_f8_gemm<kGemmBN, ND><<<grid, kGemmThreads, smem, st>>>(tW, tX, sW, sX, Y, R, C, N, err);
+    DS4F_CUDA(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace
+
+int f8_gemm_launch(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
+                   int R, int C, int N, int ND, unsigned *err, cudaStream_t st) {
+    if (R <= 0 || C <= 0 || N <= 0 || R % 128 || C % 128) {
+        set_error("f8_gemm: R and C must be positive multiples of 128, N > 0");
+        return -1;
+    }
+    switch (ND) {
+    case 1: return f8_gemm_launch_t<1>(W, sW, X, sX, Y, R, C, N, err, st);
+    case 2: return f8_gemm_launch_t<2>(W, sW, X, sX, Y, R, C, N, err, st);
+    case 3: return f8_gemm_launch_t<3>(W, sW, X, sX, Y, R, C, N, err, st);
+    }
+    set_error("f8_gemm: digits must be 1, 2 or 3");
+    return -1;
+}
+
+int quant_f8_digits_launch(const float *x, int N, int C, int ND, uint8_t *q, float *s, cudaStream_t st) {
+    if (N <= 0 || C <= 0 || C % 128 || ND < 1 || ND > 3) {
+        set_error("quant_f8_digits: C must be a positive multiple of 128, digits 1..3");
+        return -1;
+    }
+    const int64_t blocks = (int64_t)N * (C / 128);
+    k_quant_f8_digits<<<(unsigned)((blocks + 7) / 8), 256, 0, st>>>(x, N, C, ND, q, s);
+    DS4F_CUDA(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace ds4f
+
+namespace ds4f { namespace {
+__device__ unsigned g_gemm_err;
+}  // namespace
+}  // namespace ds4f
+
+extern "C" {
+
+int ds4f_gpu_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t *q, float *s, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (ds4f::quant_f8_digits_launch(x, N, C, ND, q, s, st)) return -1;
+    DS4F_CUDA(cudaStreamSynchronize(st));
+    return 0;
+}
+
+int ds4f_gpu_f8_gemm(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
+                     int R, int C, int N, int ND, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned *err = nullptr;
+    DS4F_CUDA(cudaGetSymbolAddress((void **)&err, ds4f::g_gemm_err));
+    DS4F_CUDA(cudaMemsetAsync(err, 0, sizeof(unsigned), st));
+    if (ds4f::f8_gemm_launch(W, sW, X, sX, Y, R, C, N, ND, err, st)) return -1;
+    unsigned h = 0;
+    DS4F_CUDA(cudaMemcpyAsync(&h, err, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    DS4F_CUDA(cudaStreamSynchronize(st));
+    if (h) { ds4f::set_error("f8_gemm: a pipeline wait gave up (code %u)", h); return -1; }
+    return 0;
+}
+
+}  // extern "C"

@@ -81,6 +81,8 @@ def lib():
             "ds4f_gpu_model_trace_read": [_vp, _vp, C.c_int64],
             "ds4f_gpu_synth_f32": [_vp, C.c_int64, C.c_uint64, C.c_uint32, C.c_uint32,
                                    C.c_uint32, C.c_uint32, C.c_double, _vp],
+            "ds4f_gpu_quant_f8_digits": [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_f8_gemm": [_vp] * 5 + [C.c_int] * 4 + [_vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -291,3 +293,16 @@ class Model:
 
 def synth_f32_dev(dst, n, seed, layer, kind, x, t, sigma, stream=None):
     check(lib().ds4f_gpu_synth_f32(ptr(dst), n, seed, layer, kind, x, t, sigma, stream))
+
+
+def quant_f8_digits_dev(x, q, s, nd=3, stream=None):
+    """x [N][C] fp32 (device) -> q [nd][N][C] uint8, s [N][C/128] fp32 (device)."""
+    N, Cc = x.shape
+    check(lib().ds4f_gpu_quant_f8_digits(ptr(x), N, Cc, nd, ptr(q), ptr(s), stream))
+
+
+def f8_gemm_dev(W, sW, q, sx, Y, stream=None):
+    """Y [N][R] = block-scaled FP8 GEMM of W [R][C] with the digit planes q."""
+    R, Cc = W.shape
+    nd, N, _ = q.shape
+    check(lib().ds4f_gpu_f8_gemm(ptr(W), ptr(sW), ptr(q), ptr(sx), ptr(Y), R, Cc, N, nd, stream))

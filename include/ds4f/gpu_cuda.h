@@ -228,6 +228,32 @@ int  ds4f_gpu_synth_f32(float *dst_dev, int64_t n, uint64_t seed,
                         uint32_t layer, uint32_t kind, uint32_t x, uint32_t t,
                         double sigma, void *stream);
 
+/* ---- batched prefill building blocks (tensor cores) ------------------- */
+
+/* Activation quantiser of the batched prefill (no reference counterpart:
+ * the reference's ds4f_moe_step_batch, src/moe.c:1480-1707, multiplies fp32
+ * activations; this build feeds the FP8 tensor cores). Per row and
+ * 128-column block: a = max |x|, r = 240 / a, s = a / 240 (fp32; a = 0:
+ * r = 0, s = 1), y = x r, then ND in 1..3 E4M3 digits (round to nearest
+ * even): d0 = E4M3(y), d1 = E4M3((y - d0) 16), d2 = E4M3(((y - d0) 16 - d1)
+ * 16), so x = s (d0 + d1 / 16 + d2 / 256) within 2^-13 relative at ND 3.
+ * x [N][C] fp32; q [ND][N][C] digit planes; s [N][C/128]; device pointers,
+ * C a multiple of 128. Synchronous on `stream`. */
+int  ds4f_gpu_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t *q, float *s,
+                              void *stream);
+
+/* Block-scaled FP8 GEMM on the tensor cores (tcgen05.mma kind::f8f6f4,
+ * TMEM accumulators, TMA tiles):
+ *   Y[n][r] = sum_kb sW[r/128][kb] sX[n][kb] sum_{c in kb} W[r][c] x~[n][c]
+ * with kb the 128-column blocks and x~ = d0 + d1/16 + d2/256 the digits of
+ * ds4f_gpu_quant_f8_digits (planes X [ND][N][C], scales sX [N][C/128]).
+ * W [R][C] canonical E4M3 with fp32 block scales sW [R/128][C/128] (the FP8
+ * expert tensors, ds4f_f8_matvec's W / scales, src/kernels.c:243-270);
+ * Y [N][R] fp32. Device pointers, 16-byte aligned; R and C multiples of
+ * 128. Synchronous on `stream`. */
+int  ds4f_gpu_f8_gemm(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX,
+                      float *Y, int R, int C, int N, int ND, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

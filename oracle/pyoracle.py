@@ -110,6 +110,9 @@ def lib():
         L.orc_moe_batch.argtypes = [C.c_int] * 6 + [
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_quant_f8_digits.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                          C.c_void_p, C.c_void_p]
+        L.orc_f8_gemm_digits.argtypes = [C.c_void_p] * 5 + [C.c_int] * 4
         _lib = L
     return _lib
 
@@ -307,3 +310,27 @@ class Layer:
                                ptr(w)) != 0:
             raise RuntimeError("orc_moe_batch failed")
         return st, idx, w
+
+
+def quant_f8_digits(x, nd=3):
+    """Activation quantiser of the GPU prefill: x [N][C] fp32 ->
+    (q [nd][N][C] uint8 E4M3 digit planes, s [N][C/128] fp32)."""
+    x = np.ascontiguousarray(x, np.float32)
+    N, Cc = x.shape
+    q = np.zeros((nd, N, Cc), np.uint8)
+    s = np.zeros((N, Cc // 128), np.float32)
+    assert lib().orc_quant_f8_digits(ptr(x), N, Cc, nd, ptr(q), ptr(s)) == 0
+    return q, s
+
+
+def f8_gemm_digits(W, sW, q, sx):
+    """Double-precision reference of the block-scaled digit GEMM: Y [N][R]."""
+    W = np.ascontiguousarray(W, np.uint8)
+    sW = np.ascontiguousarray(sW, np.float32)
+    q = np.ascontiguousarray(q, np.uint8)
+    sx = np.ascontiguousarray(sx, np.float32)
+    R, Cc = W.shape
+    nd, N, _ = q.shape
+    Y = np.zeros((N, R), np.float64)
+    assert lib().orc_f8_gemm_digits(ptr(W), ptr(sW), ptr(q), ptr(sx), ptr(Y), R, Cc, N, nd) == 0
+    return Y

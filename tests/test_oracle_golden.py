@@ -380,3 +380,18 @@ def test_batch_equals_per_token():
         assert np.array_equal(i1, idx[b])
         assert np.array_equal(bits(w1), bits(w[b]))
         assert np.array_equal(bits(s1), bits(st[b]))
+
+
+# ---- the batched prefill's activation quantiser (oracle/prefill.c) --------
+
+def test_prefill_digits_reconstruct_activations():
+    x = po.fill_f32(8 * 256, po.key(21, 0, 4, 0, 0), 1.0).reshape(8, 256)
+    x[0, :128] = 0.0
+    q, s = po.quant_f8_digits(x, 3)
+    val = np.array([po.lib().orc_f8_value(b) for b in range(256)], np.float64)
+    rec = (val[q[0]] + val[q[1]] / 16 + val[q[2]] / 256) * np.repeat(s.astype(np.float64), 128, 1)
+    amax = np.repeat(np.abs(x).reshape(8, 2, 128).max(2), 128, 1)
+    err = np.abs(rec - x) / np.where(amax > 0, amax, 1)
+    assert err.max() < 2.0 ** -12
+    assert (q[:, 0, :128] == 0).all() and (s[0, 0] == 1.0)
+    assert np.abs(val[q]).max() <= 240.0          # digits stay where both E4M3 tables agree
