@@ -130,10 +130,6 @@ struct Ds4fMvPlan {
     int njobs, nitems, device;
 };
 
-struct Ds4fGpuModel {
-    Model m;
-};
-
 namespace ds4f {
 // Enqueue `fn` on the model stream ordered after the caller's stream, and
 // make the caller's stream wait for it (timing on the caller's stream then
@@ -464,6 +460,7 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (m.stream) cudaStreamSynchronize(m.stream);
     if (m.graph) cudaGraphExecDestroy(m.graph);
     if (m.trace) cudaFree(m.trace);
+    if (m.pf_ws) cudaFree(m.pf_ws);
     cudaFree(m.pool);
     cudaFree(m.trunk);
     cudaFree(m.ws_base);

@@ -26,6 +26,7 @@
 
 #include "common.cuh"
 #include "tc.cuh"
+#include "gemm.cuh"
 #include "../../include/ds4f/gpu_cuda.h"
 
 namespace ds4f {
@@ -94,59 +95,53 @@ namespace {
 // E4M3() rounds to nearest even, saturating. Every digit stays within
 // [-240, 240] (exponent field <= 14), where the reference's E4M3 table and
 // standard E4M3 agree. Output planes q[d][row][col].
-__device__ __forceinline__ uint32_t e4m3_2(float lo, float hi) {
-    uint16_t r;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-__device__ __forceinline__ float e4m3_val(uint32_t b) {      // exact
-    return __int_as_float(((int)(b << 24) >> 4) & (int)0x87F00000) * DS4F_F8_UNSCALE;
-}
 __global__ void k_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t *q, float *s) {
     const int nb = C / 128;
     const int64_t blk = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;   // one warp per block
     if (blk >= (int64_t)N * nb) return;
     const int lane = threadIdx.x & 31;
     const int64_t off = (blk / nb) * (int64_t)C + (blk % nb) * 128 + 4 * lane;
-    const float4 v = *(const float4 *)(x + off);
-    float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
-    const float r = a > 0.f ? __fdiv_rn(240.0f, a) : 0.f;
-    float y[4] = {__fmul_rn(v.x, r), __fmul_rn(v.y, r), __fmul_rn(v.z, r), __fmul_rn(v.w, r)};
-    for (int d = 0; d < ND; d++) {
-        const uint32_t w = e4m3_2(y[0], y[1]) | (e4m3_2(y[2], y[3]) << 16);
-        *(uint32_t *)(q + (int64_t)d * N * C + off) = w;
-#pragma unroll
-        for (int i = 0; i < 4; i++) y[i] = __fmul_rn(__fsub_rn(y[i], e4m3_val((w >> (8 * i)) & 0xFF)), 16.0f);
-    }
-    if (lane == 0) s[blk] = a > 0.f ? __fdiv_rn(a, 240.0f) : 1.0f;
+    const float sc = quant_block_digits(*(const float4 *)(x + off), ND, q, (int64_t)N * C, off);
+    if (lane == 0) s[blk] = sc;
 }
 
-// ---- block-scaled FP8 GEMM ---------------------------------------------------------
+// ---- block-scaled GEMM ------------------------------------------------------------
+// Two element kinds share the kernel:
+//   FP8  (BF = false): tcgen05 kind::f8f6f4, 128-column K blocks (4 MMAs of
+//        K = 32), W's fp32 block scales and X's row scales promoted per block;
+//        ND digits combined as D0 + D1 / 16 + D2 / 256.
+//   BF16 (BF = true):  tcgen05 kind::f16 on bf16, 64-column K blocks (4 MMAs
+//        of K = 16), no scales; 2 digits (hi, lo) combined as D0 + D1.
+// A is [slots][R][C] (3-D tensor map; slot = the expert), B the digit planes
+// [ND][rows][C]. Dense mode: tile = blockIdx.y, rows n0 = 64 blockIdx.y,
+// slot 0. Grouped mode: tile t = blockIdx.y < *ntiles names (slot, first B
+// row, valid rows) -- the experts' token groups of the batched prefill.
 constexpr int kStages = 4;
 constexpr int kGemmThreads = 192;          // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
 
-template <int BN, int ND>
+template <int ND, bool BF>
 struct GemmSmem {
-    static constexpr int NM = BN * ND;                // MMA N: the digit rows of BN columns
+    static constexpr int NM = kGemmBN * ND;           // MMA N: the digit rows of 64 columns
     static constexpr int A = 128 * 128;               // one 128-row x 128-byte tile
     static constexpr int B = NM * 128;
     static constexpr int STAGE = A + B;
     static constexpr int o_bar = kStages * STAGE;     // full[S], empty[S], tfull[2], tempty[2], done
     static constexpr int o_slot = o_bar + (2 * kStages + 5) * 8;
     static constexpr int o_sx = o_slot + 16;
-    static constexpr int bytes(int kb) { return o_sx + BN * kb * 4 + 1024; }   // + alignment slack
+    static constexpr int bytes(int kb) { return o_sx + (BF ? 0 : kGemmBN * kb * 4) + 1024; }
     static constexpr uint32_t NCOLS = 2 * NM <= 32 ? 32 : 2 * NM <= 64 ? 64 : 2 * NM <= 128 ? 128
                                     : 2 * NM <= 256 ? 256 : 512;
+    static constexpr uint32_t ID = BF ? tc::idesc(128, NM, 1, 1) : tc::idesc(128, NM, 0, 0);
     static_assert(B % 1024 == 0, "B tiles keep 1024-byte alignment");
     static_assert(NM % 16 == 0 && NM <= 256 && 2 * NM <= 512, "MMA N and TMEM columns");
 };
 
-// Epilogue: combine the digit columns of token n (n, BN + n, 2 BN + n) as
-// (D0 + D1 / 16) + D2 / 256, then acc[n] += that * (sW * sX[n]).
-template <int BN, int ND>
-__device__ __forceinline__ void promote(uint32_t t, const float *sxt, int KB, int kb, float w, float (&acc)[BN]) {
+// Epilogue of one K block: combine the digit columns of column n (n, 64 + n,
+// 128 + n) and add into acc[n] with the block's scales.
+template <int ND, bool BF>
+__device__ __forceinline__ void promote(uint32_t t, const float *sxt, int KB, int kb, float w,
+                                        float (&acc)[kGemmBN]) {
+    constexpr int BN = kGemmBN;
 #pragma unroll
     for (int c = 0; c < BN / 16; c++) {
         float v[16];
@@ -155,7 +150,7 @@ __device__ __forceinline__ void promote(uint32_t t, const float *sxt, int KB, in
             float v1[16];
             tc::tmem_ld16(t + BN + c * 16, v1);
 #pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = __fadd_rn(v[i], __fmul_rn(v1[i], 0.0625f));
+            for (int i = 0; i < 16; i++) v[i] = BF ? __fadd_rn(v[i], v1[i]) : __fadd_rn(v[i], __fmul_rn(v1[i], 0.0625f));
         }
         if (ND > 2) {
             float v2[16];
@@ -163,19 +158,22 @@ __device__ __forceinline__ void promote(uint32_t t, const float *sxt, int KB, in
 #pragma unroll
             for (int i = 0; i < 16; i++) v[i] = __fadd_rn(v[i], __fmul_rn(v2[i], 0.00390625f));
         }
+        if (BF) {
 #pragma unroll
-        for (int i = 0; i < 16; i++)
-            acc[c * 16 + i] = fmaf(v[i], __fmul_rn(w, sxt[(c * 16 + i) * KB + kb]), acc[c * 16 + i]);
+            for (int i = 0; i < 16; i++) acc[c * 16 + i] = __fadd_rn(acc[c * 16 + i], v[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                acc[c * 16 + i] = fmaf(v[i], __fmul_rn(w, sxt[(c * 16 + i) * KB + kb]), acc[c * 16 + i]);
+        }
     }
 }
 
-template <int BN, int ND>
+template <int ND, bool BF>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tX,
-          const float *__restrict__ sW, const float *__restrict__ sX, float *__restrict__ Y,
-          int R, int C, int N, unsigned *err) {
-    using L = GemmSmem<BN, ND>;
-    constexpr uint32_t ID = tc::idesc(128, L::NM, 0, 0);
+k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tX, GemmArgs g) {
+    using L = GemmSmem<ND, BF>;
+    constexpr int BN = kGemmBN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
     uint64_t *full = (uint64_t *)(sm + L::o_bar), *empty = full + kStages;
@@ -183,8 +181,20 @@ k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtens
     uint32_t *slot = (uint32_t *)(sm + L::o_slot);
     float *sxt = (float *)(sm + L::o_sx);
 
+    // this CTA's tile
+    int zs = 0, n0, nv;
+    if (g.tiles) {
+        if ((int)blockIdx.y >= *g.ntiles) return;               // uniform: before any barrier
+        zs = g.tiles[3 * blockIdx.y];
+        n0 = g.tiles[3 * blockIdx.y + 1];
+        nv = g.tiles[3 * blockIdx.y + 2];
+    } else {
+        n0 = blockIdx.y * BN;
+        nv = min(BN, g.N - n0);
+    }
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int r0 = blockIdx.x * 128, n0 = blockIdx.y * BN, KB = C / 128;
+    const int r0 = blockIdx.x * 128, KB = g.KB;
+    unsigned *err = g.err;
 
     if (warp == 1) tc::tmem_alloc(slot, L::NCOLS);
     if (tid == 0) {
@@ -195,10 +205,9 @@ k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtens
         tc::prefetch_tmap(&tW);
         tc::prefetch_tmap(&tX);
     }
-    for (int i = tid - 64; i >= 0 && i < BN * KB; i += 128) {
-        const int n = n0 + i / KB;
-        sxt[i] = n < N ? sX[(int64_t)n * KB + i % KB] : 0.f;
-    }
+    if (!BF)
+        for (int i = tid - 64; i >= 0 && i < BN * KB; i += 128)
+            sxt[i] = i / KB < nv ? g.sX[(int64_t)(n0 + i / KB) * KB + i % KB] : 0.f;
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -212,7 +221,7 @@ k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtens
                 if (kb >= kStages && !tc::mbar_wait(empty + s, ((kb / kStages) - 1) & 1, err, 1)) break;
                 uint8_t *a = sm + s * L::STAGE;
                 tc::mbar_expect(full + s, L::STAGE);
-                tc::tma_load_2d(a, &tW, kb * 128, r0, full + s);
+                tc::tma_load_3d(a, &tW, kb * 128, r0, zs, full + s);
                 tc::tma_load_3d(a + L::A, &tX, kb * 128, n0, 0, full + s);
             }
             // every issued load has landed before the CTA may exit
@@ -228,9 +237,14 @@ k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtens
                 tc::fence_after_sync();
                 const uint8_t *a = sm + s * L::STAGE;
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    tc::mma_f8f6f4(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
-                                   tc::sdesc_sw128(a + L::A + 32 * k), ID, k > 0);
+                for (int k = 0; k < 4; k++) {
+                    if (BF)
+                        tc::mma_f16(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
+                                    tc::sdesc_sw128(a + L::A + 32 * k), L::ID, k > 0);
+                    else
+                        tc::mma_f8f6f4(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
+                                       tc::sdesc_sw128(a + L::A + 32 * k), L::ID, k > 0);
+                }
                 tc::commit(empty + s);
                 tc::commit(tfull + b);
             }
@@ -243,20 +257,22 @@ k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtens
         float acc[BN];
 #pragma unroll
         for (int j = 0; j < BN; j++) acc[j] = 0.f;
-        const float *swr = sW + (int64_t)(r0 / 128) * KB;
+        const float *swr = BF ? nullptr : g.sW + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
         for (int kb = 0; kb < KB; kb++) {
             const int b = kb & 1;
             if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
             tc::fence_after_sync();
-            promote<BN, ND>(taddr + ((uint32_t)(q * 32) << 16) + b * L::NM, sxt, KB, kb, swr[kb], acc);
+            promote<ND, BF>(taddr + ((uint32_t)(q * 32) << 16) + b * L::NM, sxt, KB, kb, BF ? 1.f : swr[kb], acc);
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(tempty + b);
         }
-        if (r0 + row < R)
+        if (r0 + row < g.R) {
+            float *y = g.Y + (int64_t)n0 * g.ldy + g.ycol0 + r0 + row;
 #pragma unroll
             for (int j = 0; j < BN; j++)
-                if (n0 + j < N) Y[(int64_t)(n0 + j) * R + r0 + row] = acc[j];
+                if (j < nv) y[(int64_t)j * g.ldy] = acc[j];
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -266,31 +282,42 @@ k_f8_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtens
     }
 }
 
-constexpr int kGemmBN = 64;
+}  // namespace
 
-template <int ND>
-int f8_gemm_launch_t(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
-                     int R, int C, int N, unsigned *err, cudaStream_t st) {
-    using L = GemmSmem<kGemmBN, ND>;
-    CUtensorMap tW, tX;
-    if (tmap_u8_2d(&tW, W, C, R, C, 128) ||
-        tmap_u8_3d(&tX, X, C, N, ND, C, (uint64_t)N * C, kGemmBN, ND))
+// A: slots x [R][C] elements of `esize` bytes, `slot_stride` bytes apart;
+// B: ND planes [rows][C]. Launches `ntiles_max` tile rows of the grid (the
+// grouped mode's CTAs past *g.ntiles return at once).
+template <int ND, bool BF>
+int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
+                GemmArgs g, int ntiles_max, cudaStream_t st) {
+    using L = GemmSmem<ND, BF>;
+    const int es = BF ? 2 : 1;
+    if (g.R <= 0 || g.C <= 0 || g.R % 128 || (g.C * es) % 128 || ntiles_max <= 0) {
+        set_error("gemm: R and C bytes must be positive multiples of 128");
         return -1;
-    const int smem = L::bytes(C / 128);
-    if (smem > 227 * 1024) { set_error("f8_gemm: C too large for the scale tile"); return -1; }
+    }
+    CUtensorMap tW, tX;
+    if (tmap_u8_3d(&tW, A, (uint64_t)g.C * es, g.R, slots, (uint64_t)g.C * es, slot_stride, 128, 1) ||
+        tmap_u8_3d(&tX, X, (uint64_t)g.C * es, xrows, ND, (uint64_t)g.C * es, (uint64_t)xrows * g.C * es,
+                   kGemmBN, ND))
+        return -1;
+    g.KB = g.C * es / 128;
+    const int smem = L::bytes(g.KB);
+    if (smem > 227 * 1024) { set_error("gemm: C too large for the scale tile"); return -1; }
     static bool attr = false;
     if (!attr) {
-        DS4F_CUDA(cudaFuncSetAttribute(k_f8_gemm<kGemmBN, ND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       227 * 1024));
+        DS4F_CUDA(cudaFuncSetAttribute(k_gemm<ND, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr = true;
     }
-    dim3 grid(R / 128, (N + kGemmBN - 1) / kGemmBN);
-    k_f8_gemm<kGemmBN, ND><<<grid, kGemmThreads, smem, st>>>(tW, tX, sW, sX, Y, R, C, N, err);
+    dim3 grid(g.R / 128, ntiles_max);
+    k_gemm<ND, BF><<<grid, kGemmThreads, smem, st>>>(tW, tX, g);
     DS4F_CUDA(cudaGetLastError());
     return 0;
 }
-
-}  // namespace
+template int gemm_launch<3, false>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
+                                   cudaStream_t);
+template int gemm_launch<2, true>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
+                                  cudaStream_t);
 
 int f8_gemm_launch(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
                    int R, int C, int N, int ND, unsigned *err, cudaStream_t st) {
@@ -298,10 +325,14 @@ int f8_gemm_launch(const uint8_t *W, const float *sW, const uint8_t *X, const fl
         set_error("f8_gemm: R and C must be positive multiples of 128, N > 0");
         return -1;
     }
+    GemmArgs g{};
+    g.sW = sW; g.sw_slot = 0; g.sX = sX; g.Y = Y; g.ldy = R; g.ycol0 = 0;
+    g.R = R; g.C = C; g.N = N; g.err = err;
+    const int nt = (N + kGemmBN - 1) / kGemmBN;
     switch (ND) {
-    case 1: return f8_gemm_launch_t<1>(W, sW, X, sX, Y, R, C, N, err, st);
-    case 2: return f8_gemm_launch_t<2>(W, sW, X, sX, Y, R, C, N, err, st);
-    case 3: return f8_gemm_launch_t<3>(W, sW, X, sX, Y, R, C, N, err, st);
+    case 1: return gemm_launch<1, false>(W, 1, (int64_t)R * C, X, N, g, nt, st);
+    case 2: return gemm_launch<2, false>(W, 1, (int64_t)R * C, X, N, g, nt, st);
+    case 3: return gemm_launch<3, false>(W, 1, (int64_t)R * C, X, N, g, nt, st);
     }
     set_error("f8_gemm: digits must be 1, 2 or 3");
     return -1;

@@ -1,0 +1,64 @@
+// gemm.cuh -- the tensor-core GEMM and the quantisers of the batched
+// prefill (gemm.cu), as used by its orchestration (prefill.cu).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace ds4f {
+
+constexpr int kGemmBN = 64;                // B columns (tokens) per tile
+
+struct GemmArgs {
+    const float *sW;          // FP8: scales of slot 0, [R/128][KB] floats
+    int64_t sw_slot;          // floats between consecutive slots' scales
+    const float *sX;          // FP8: [rows][KB] activation scales
+    float *Y;                 // Y[(first row + n) * ldy + ycol0 + r]
+    int64_t ldy;
+    int ycol0, R, C, KB;      // KB: K blocks of 128 bytes (set by gemm_launch)
+    const int *tiles;         // grouped: [*ntiles][3] = slot, first B row, valid rows
+    const int *ntiles;
+    int N;                    // dense: B rows
+    unsigned *err;
+};
+
+// A: slots x [R][C] elements (FP8 bytes, or bf16 when BF), `slot_stride`
+// bytes apart; X: ND digit planes [xrows][C]. The grid has `ntiles_max` tile
+// rows (grouped: CTAs past *g.ntiles return at once).
+template <int ND, bool BF>
+int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
+                GemmArgs g, int ntiles_max, cudaStream_t st);
+
+int quant_f8_digits_launch(const float *x, int N, int C, int ND, uint8_t *q, float *s, cudaStream_t st);
+
+// ---- the quantisers' per-lane step ------------------------------------------------
+// Two fp32 -> E4M3 bytes (round to nearest even, saturating), lo in the low byte.
+__device__ __forceinline__ uint32_t e4m3_2(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float e4m3_val(uint32_t b) {      // exact
+    return __int_as_float(((int)(b << 24) >> 4) & (int)0x87F00000) * DS4F_F8_UNSCALE;
+}
+// A warp holds one 128-column block, 4 values per lane (columns 4 lane ..):
+// a = max |v|, r = 240 / a, y = v r, then ND E4M3 digits, each written to
+// its plane q + d * plane at byte offset `off`; returns the block scale.
+__device__ __forceinline__ float quant_block_digits(float4 v, int ND, uint8_t *q, int64_t plane,
+                                                    int64_t off) {
+    float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    const float r = a > 0.f ? __fdiv_rn(240.0f, a) : 0.f;
+    float y[4] = {__fmul_rn(v.x, r), __fmul_rn(v.y, r), __fmul_rn(v.z, r), __fmul_rn(v.w, r)};
+    for (int d = 0; d < ND; d++) {
+        const uint32_t w = e4m3_2(y[0], y[1]) | (e4m3_2(y[2], y[3]) << 16);
+        *(uint32_t *)(q + (int64_t)d * plane + off) = w;
+#pragma unroll
+        for (int i = 0; i < 4; i++) y[i] = __fmul_rn(__fsub_rn(y[i], e4m3_val((w >> (8 * i)) & 0xFF)), 16.0f);
+    }
+    return a > 0.f ? __fdiv_rn(a, 240.0f) : 1.0f;
+}
+
+}  // namespace ds4f

@@ -70,6 +70,8 @@ struct Model {
     unsigned long long *trace;   // optional phase stamps of the persistent kernel
     int64_t trace_n;
     int epoch;                   // last persistent launch's tag epoch
+    void *pf_ws;                 // batched-prefill workspace (prefill.cu), grown on demand
+    size_t pf_bytes;
 };
 
 int slot_layout(int fmt, int H, int M, SlotLayout *s);
@@ -89,9 +91,19 @@ int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st);
 int synth_model(Model *m, uint64_t seed, double sigma, cudaStream_t st);
 int synth_f32(float *dst, int64_t n, uint64_t key, double sigma, cudaStream_t st);
 
+// Batched prefill of one layer (prefill.cu): states [T][H] in/out, routing
+// sel / w [T][K] (global expert ids; ids outside this shard are skipped).
+int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w,
+                  cudaStream_t st);
+
 inline const uint8_t *expert_ptr(const Model *m, int L, int e) {
     return m->pool + ((int64_t)L * m->d.expert_count + (e - m->d.expert_first)) *
                          m->slot.nbytes;
 }
 
 }  // namespace ds4f
+
+// The C ABI's opaque model handle.
+struct Ds4fGpuModel {
+    ds4f::Model m;
+};

@@ -1,0 +1,343 @@
+// prefill.cu -- the batched prefill of one MoE layer on the tensor cores:
+// ds4f_moe_step_batch (src/moe.c:1480-1707) for B tokens with the routing
+// given, restated for B200.
+//
+//  1. RMSNorm of every token (src/moe.c:841-851 arithmetic), then the
+//     activation digits (gemm.cu quantiser: 3 E4M3 digits per element).
+//  2. Group the (token, selection) pairs by expert: counts, offsets, a
+//     stable rank in (token, selection) order (the reference sorts with
+//     qsort, src/moe.c:1527, whose order within a group does not matter as
+//     each selection keeps its own output row, :1606-1607), and the tile
+//     list (expert, first row, rows) of 64-row tiles.
+//  3. Gather each selection's digit rows; grouped GEMMs: gate and up
+//     (tcgen05, per expert), SiLU-mul (src/moe.c:645-649) into the chain's
+//     digits, down.
+//  4. Shared expert in bf16 on the tensor cores (tcgen05 kind::f16, the
+//     activations as two bf16 digits hi + lo), its sigmoid gate logit.
+//  5. Combine in selection order (src/moe.c:1614-1630: acc += w_j out_j,
+//     then acc += sigmoid(g) shared, state += acc).
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "model.cuh"
+#include "../../include/ds4f/gpu_cuda.h"
+
+namespace ds4f {
+namespace {
+
+constexpr int kND = 3;           // E4M3 digits per routed activation
+
+// ---- 1. RMSNorm ------------------------------------------------------------------
+__global__ void k_rmsnorm_rows(const float *st, const uint16_t *nw, int H, float *xin) {
+    __shared__ double part[8];
+    const float *x = st + (int64_t)blockIdx.x * H;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = __dadd_rn(ss, __dmul_rn((double)x[i], (double)x[i]));
+    ss = warp_sum_d(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot = __dadd_rn(tot, part[k]);
+    const float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(tot, (double)H)), 1e-6f));
+    float *y = xin + (int64_t)blockIdx.x * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) y[i] = __fmul_rn(__fdiv_rn(x[i], r), bf16_to_f32(nw[i]));
+}
+
+// ---- 2. grouping -------------------------------------------------------------------
+__global__ void k_count(const int *sel, int n, int first, int count, int *cnt) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int e = sel[i] - first;
+    if (e >= 0 && e < count) atomicAdd(cnt + e, 1);
+}
+
+// Exclusive prefix sum over one block (blockDim <= 1024); returns the total.
+__device__ int block_excl_scan(int v, int *out_excl, int *sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) sh[warp] = incl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int k = 0; k < nw; k++) { const int t = sh[k]; sh[k] = run; run += t; }
+        sh[32] = run;
+    }
+    __syncthreads();
+    *out_excl = sh[warp] + incl - v;
+    const int tot = sh[32];
+    __syncthreads();
+    return tot;
+}
+
+// One block of >= count threads: offsets, the 64-row tile list, totals.
+__global__ void k_plan(const int *cnt, int count, int slot0, int *off, int *tiles, int *ntiles, int *nrows) {
+    __shared__ int sh[33];
+    const int e = threadIdx.x;
+    const int c = e < count ? cnt[e] : 0, nt = (c + kGemmBN - 1) / kGemmBN;
+    int o, t0;
+    const int rows = block_excl_scan(c, &o, sh);
+    const int tiles_n = block_excl_scan(nt, &t0, sh);
+    if (e < count) {
+        off[e] = o;
+        for (int i = 0; i < nt; i++) {
+            tiles[3 * (t0 + i)] = slot0 + e;
+            tiles[3 * (t0 + i) + 1] = o + kGemmBN * i;
+            tiles[3 * (t0 + i) + 2] = min(kGemmBN, c - kGemmBN * i);
+        }
+    }
+    if (e == 0) { *ntiles = tiles_n; *nrows = rows; }
+}
+
+// Block e: the selections of expert first + e in (token, selection) order
+// get rows off[e], off[e] + 1, ...; pos[selection] = row, src[row] = selection.
+__global__ void k_rank(const int *sel, int n, int first, const int *off, int *pos, int *src) {
+    __shared__ int sh[33];
+    const int e = blockIdx.x;
+    int base = off[e];
+    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const int f = i < n && sel[i] - first == e;
+        int rank;
+        const int tot = block_excl_scan(f, &rank, sh);
+        if (f) { pos[i] = base + rank; src[base + rank] = i; }
+        base += tot;
+    }
+}
+
+// Row p of the gathered digit planes <- token src[p] / K; one warp per
+// (row, plane); plus the row's scales.
+__global__ void k_gather(const uint8_t *Xq, const float *sx, const int *src, const int *nrows, int K, int T,
+                         int H, uint8_t *Xg, float *sxg, int rows_cap) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int p = (int)(w / kND), d = (int)(w % kND);
+    if (p >= *nrows) return;
+    const int t = src[p] / K;
+    const uint4 *s4 = (const uint4 *)(Xq + ((int64_t)d * T + t) * H);
+    uint4 *d4 = (uint4 *)(Xg + ((int64_t)d * rows_cap + p) * H);
+    for (int i = lane; i < H / 16; i += 32) d4[i] = s4[i];
+    if (d == 0)
+        for (int i = lane; i < H / 128; i += 32) sxg[(int64_t)p * (H / 128) + i] = sx[(int64_t)t * (H / 128) + i];
+}
+
+// ---- 3. SiLU-mul into the chain's digits --------------------------------------------
+// GU [rows][2M] (gate, up) -> Cq [ND][rows_cap][M], sc [rows][M/128]
+__global__ void k_silu_digits(const float *GU, int M, const int *nrows, uint8_t *Cq, float *sc, int rows_cap) {
+    const int nb = M / 128;
+    const int64_t blk = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int p = (int)(blk / nb), b = (int)(blk % nb);
+    if (p >= *nrows) return;
+    const float *g = GU + (int64_t)p * 2 * M + b * 128 + 4 * lane;
+    const float4 gv = *(const float4 *)g, uv = *(const float4 *)(g + M);
+    const float4 c = make_float4(silu_mul(gv.x, uv.x), silu_mul(gv.y, uv.y), silu_mul(gv.z, uv.z),
+                                 silu_mul(gv.w, uv.w));
+    const float s = quant_block_digits(c, kND, Cq, (int64_t)rows_cap * M, (int64_t)p * M + b * 128 + 4 * lane);
+    if (lane == 0) sc[blk] = s;
+}
+
+// ---- 4. shared expert ----------------------------------------------------------------
+// Two bf16 digits: hi = bf16(x), lo = bf16(x - hi) (round to nearest even),
+// planes q[0] = hi, q[1] = lo, each n elements.
+__device__ __forceinline__ void bf16_digits(float x, uint16_t *q, int64_t n, int64_t i) {
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+    q[i] = __bfloat16_as_ushort(hi);
+    q[n + i] = __bfloat16_as_ushort(lo);
+}
+__global__ void k_bf16_digits(const float *x, int64_t n, uint16_t *q) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) bf16_digits(x[i], q, n, i);
+}
+// GS [T][2M] -> chain digits [2][T][M]
+__global__ void k_silu_bf16_digits(const float *GS, int M, int64_t T, uint16_t *q) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * M) return;
+    const int64_t t = i / M, m = i % M;
+    bf16_digits(silu_mul(GS[t * 2 * M + m], GS[t * 2 * M + M + m]), q, T * M, i);
+}
+// shared_expert_gate logit per token (fp32, the reference's bf16 matvec
+// products, src/kernels.c:84-103)
+__global__ void k_gate_logit(const float *xin, const uint16_t *gw, int H, float *sg) {
+    __shared__ float part[8];
+    const float *x = xin + (int64_t)blockIdx.x * H;
+    float a = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) a = fmaf(bf16_to_f32(gw[i]), x[i], a);
+    a = warp_sum(a);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) s += part[k];
+        sg[blockIdx.x] = s;
+    }
+}
+
+// ---- 5. combine ------------------------------------------------------------------------
+__global__ void k_combine(float *states, const float *O, const float *OS, const float *sg, const int *sel,
+                          const float *w, const int *pos, int first, int count, int K, int H) {
+    const int t = blockIdx.x;
+    const float sig = sigmoid_ref(sg[t]);
+    for (int r = threadIdx.x; r < H; r += blockDim.x) {
+        float acc = 0.f;
+        for (int j = 0; j < K; j++) {
+            const int i = t * K + j, e = sel[i] - first;
+            if (e < 0 || e >= count || w[i] == 0.0f) continue;
+            acc = __fadd_rn(acc, __fmul_rn(w[i], O[(int64_t)pos[i] * H + r]));
+        }
+        acc = __fadd_rn(acc, __fmul_rn(sig, OS[(int64_t)t * H + r]));
+        states[(int64_t)t * H + r] = __fadd_rn(states[(int64_t)t * H + r], acc);
+    }
+}
+
+// ---- workspace -----------------------------------------------------------------------
+struct PfWs {
+    float *xin; uint8_t *Xq; float *sx;
+    int *cnt, *off, *tiles, *ntiles, *nrows, *pos, *src;
+    uint8_t *Xg; float *sxg; float *GU; uint8_t *Cq; float *sc; float *O;
+    uint16_t *Xb; float *GS; uint16_t *Cb; float *OS; float *sg;
+    unsigned *err;
+    int tiles_max;
+};
+
+size_t al(size_t n) { return (n + 255) / 256 * 256; }
+
+int pf_workspace(Model *m, int T, PfWs *w) {
+    const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk, count = m->d.expert_count;
+    const int64_t R = (int64_t)T * K;
+    const int tiles_max = (int)(R / kGemmBN) + count;
+    const size_t sizes[] = {
+        al((size_t)T * H * 4), al((size_t)kND * T * H), al((size_t)T * (H / 128) * 4),
+        al(count * 4), al(count * 4), al((size_t)tiles_max * 12), al(4), al(4), al(R * 4), al(R * 4),
+        al((size_t)kND * R * H), al((size_t)R * (H / 128) * 4), al((size_t)R * 2 * M * 4),
+        al((size_t)kND * R * M), al((size_t)R * (M / 128) * 4), al((size_t)R * H * 4),
+        al((size_t)2 * T * H * 2), al((size_t)T * 2 * M * 4), al((size_t)2 * T * M * 2),
+        al((size_t)T * H * 4), al((size_t)T * 4), al(4)};
+    size_t total = 0;
+    for (size_t s : sizes) total += s;
+    if (total > m->pf_bytes) {
+        if (m->pf_ws) { DS4F_CUDA(cudaFree(m->pf_ws)); m->pf_ws = nullptr; m->pf_bytes = 0; }
+        size_t fre = 0, tot = 0;
+        DS4F_CUDA(cudaMemGetInfo(&fre, &tot));
+        DS4F_REQUIRE((double)total <= 0.95 * (double)fre,
+                     "prefill: workspace of %.2f GB for %d tokens, %.2f GB free", total / 1e9, T, fre / 1e9);
+        DS4F_CUDA(cudaMalloc(&m->pf_ws, total));
+        m->pf_bytes = total;
+    }
+    uint8_t *p = (uint8_t *)m->pf_ws;
+    int k = 0;
+    auto take = [&]() { uint8_t *r = p; p += sizes[k++]; return r; };
+    w->xin = (float *)take(); w->Xq = take(); w->sx = (float *)take();
+    w->cnt = (int *)take(); w->off = (int *)take(); w->tiles = (int *)take(); w->ntiles = (int *)take();
+    w->nrows = (int *)take(); w->pos = (int *)take(); w->src = (int *)take();
+    w->Xg = take(); w->sxg = (float *)take(); w->GU = (float *)take(); w->Cq = take(); w->sc = (float *)take();
+    w->O = (float *)take(); w->Xb = (uint16_t *)take(); w->GS = (float *)take(); w->Cb = (uint16_t *)take();
+    w->OS = (float *)take(); w->sg = (float *)take(); w->err = (unsigned *)take();
+    w->tiles_max = tiles_max;
+    return 0;
+}
+
+}  // namespace
+
+int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w, cudaStream_t st) {
+    DS4F_REQUIRE(m->d.fmt == DS4F_FMT_FP8, "prefill: the tensor-core path takes FP8 pools");
+    DS4F_REQUIRE(T > 0 && L >= 0 && L < m->d.n_layers, "prefill: layer %d / tokens %d", L, T);
+    const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk;
+    const int first = m->d.expert_first, count = m->d.expert_count;
+    DS4F_REQUIRE(count <= 1024, "prefill: at most 1024 experts per shard");
+    PfWs ws;
+    if (pf_workspace(m, T, &ws)) return -1;
+    const int64_t R = (int64_t)T * K;
+    const uint16_t *tl = m->trunk + (int64_t)L * m->tr.n;
+    const int64_t total_slots = (int64_t)m->d.n_layers * count;
+
+    // 1
+    k_rmsnorm_rows<<<T, 256, 0, st>>>(states, tl + m->tr.norm, H, ws.xin);
+    if (quant_f8_digits_launch(ws.xin, T, H, kND, ws.Xq, ws.sx, st)) return -1;
+    // 2
+    DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));
+    DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
+    k_count<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.cnt);
+    k_plan<<<1, ((count + 31) / 32) * 32, 0, st>>>(ws.cnt, count, L * count, ws.off, ws.tiles, ws.ntiles,
+                                                   ws.nrows);
+    k_rank<<<count, 256, 0, st>>>(sel, (int)R, first, ws.off, ws.pos, ws.src);
+    k_gather<<<(unsigned)((R * kND * 32 + 255) / 256), 256, 0, st>>>(ws.Xq, ws.sx, ws.src, ws.nrows, K, T, H,
+                                                                    ws.Xg, ws.sxg, (int)R);
+    // 3: gate, up, SiLU digits, down
+    for (int mat = 0; mat < 2; mat++) {
+        GemmArgs g{};
+        g.sW = (const float *)(m->pool + m->slot.rel_s[mat]);
+        g.sw_slot = m->slot.nbytes / 4;
+        g.sX = ws.sxg; g.Y = ws.GU; g.ldy = 2 * M; g.ycol0 = mat * M;
+        g.R = M; g.C = H; g.tiles = ws.tiles; g.ntiles = ws.ntiles; g.err = ws.err;
+        if (gemm_launch<kND, false>(m->pool + m->slot.rel_v[mat], total_slots, m->slot.nbytes, ws.Xg, R, g,
+                                    ws.tiles_max, st))
+            return -1;
+    }
+    k_silu_digits<<<(unsigned)((R * (M / 128) * 32 + 255) / 256), 256, 0, st>>>(ws.GU, M, ws.nrows, ws.Cq,
+                                                                                ws.sc, (int)R);
+    {
+        GemmArgs g{};
+        g.sW = (const float *)(m->pool + m->slot.rel_s[2]);
+        g.sw_slot = m->slot.nbytes / 4;
+        g.sX = ws.sc; g.Y = ws.O; g.ldy = H; g.ycol0 = 0;
+        g.R = H; g.C = M; g.tiles = ws.tiles; g.ntiles = ws.ntiles; g.err = ws.err;
+        if (gemm_launch<kND, false>(m->pool + m->slot.rel_v[2], total_slots, m->slot.nbytes, ws.Cq, R, g,
+                                    ws.tiles_max, st))
+            return -1;
+    }
+    // 4: shared expert
+    k_bf16_digits<<<(unsigned)(((int64_t)T * H + 255) / 256), 256, 0, st>>>(ws.xin, (int64_t)T * H, ws.Xb);
+    const int ntd = (T + kGemmBN - 1) / kGemmBN;
+    for (int mat = 0; mat < 2; mat++) {
+        GemmArgs g{};
+        g.Y = ws.GS; g.ldy = 2 * M; g.ycol0 = mat * M; g.R = M; g.C = H; g.N = T; g.err = ws.err;
+        if (gemm_launch<2, true>(tl + (mat ? m->tr.sh_up : m->tr.sh_gate), 1, (int64_t)M * H * 2, ws.Xb, T, g,
+                                 ntd, st))
+            return -1;
+    }
+    k_silu_bf16_digits<<<(unsigned)(((int64_t)T * M + 255) / 256), 256, 0, st>>>(ws.GS, M, T, ws.Cb);
+    {
+        GemmArgs g{};
+        g.Y = ws.OS; g.ldy = H; g.ycol0 = 0; g.R = H; g.C = M; g.N = T; g.err = ws.err;
+        if (gemm_launch<2, true>(tl + m->tr.sh_down, 1, (int64_t)H * M * 2, ws.Cb, T, g, ntd, st)) return -1;
+    }
+    k_gate_logit<<<T, 256, 0, st>>>(ws.xin, tl + m->tr.sh_gw, H, ws.sg);
+    // 5
+    k_combine<<<T, 256, 0, st>>>(states, ws.O, ws.OS, ws.sg, sel, w, ws.pos, first, count, K, H);
+    DS4F_CUDA(cudaGetLastError());
+    unsigned h = 0;
+    DS4F_CUDA(cudaMemcpyAsync(&h, ws.err, 4, cudaMemcpyDeviceToHost, st));
+    DS4F_CUDA(cudaStreamSynchronize(st));
+    DS4F_REQUIRE(h == 0, "prefill: a tensor-core pipeline wait gave up (code %u)", h);
+    return 0;
+}
+
+}  // namespace ds4f
+
+extern "C" {
+
+int ds4f_gpu_moe_prefill(Ds4fGpuModel *h, int layer, float *states_dev, int T, const int *sel_dev,
+                         const float *w_dev, void *stream) {
+    DS4F_REQUIRE(h && states_dev && sel_dev && w_dev, "moe_prefill: null argument");
+    return ds4f::prefill_layer(&h->m, layer, states_dev, T, sel_dev, w_dev, (cudaStream_t)stream);
+}
+
+int ds4f_gpu_prefill(Ds4fGpuModel *h, float *states_dev, int T, const int *sel_dev, const float *w_dev,
+                     void *stream) {
+    DS4F_REQUIRE(h && states_dev && sel_dev && w_dev, "prefill: null argument");
+    const ds4f::Model &m = h->m;
+    const int64_t per = (int64_t)T * m.d.topk;
+    for (int L = 0; L < m.d.n_layers; L++)
+        if (ds4f::prefill_layer(&h->m, L, states_dev, T, sel_dev + L * per, w_dev + L * per, (cudaStream_t)stream))
+            return -1;
+    return 0;
+}
+
+}  // extern "C"

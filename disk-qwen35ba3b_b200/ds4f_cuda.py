@@ -83,6 +83,8 @@ def lib():
                                    C.c_uint32, C.c_uint32, C.c_double, _vp],
             "ds4f_gpu_quant_f8_digits": [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_f8_gemm": [_vp] * 5 + [C.c_int] * 4 + [_vp],
+            "ds4f_gpu_moe_prefill": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -272,6 +274,14 @@ class Model:
 
     def stack_dev(self, state, n_steps, stream=None):
         check(lib().ds4f_gpu_moe_stack_dev(self.h, ptr(state), n_steps, stream))
+
+    def prefill_layer_dev(self, L, states, sel, w, stream=None):
+        """Batched prefill of layer L: states [T][H], sel / w [T][K] (device)."""
+        check(lib().ds4f_gpu_moe_prefill(self.h, L, ptr(states), states.shape[0], ptr(sel), ptr(w), stream))
+
+    def prefill_dev(self, states, sel, w, stream=None):
+        """Every layer: sel / w [n_layers][T][K] (device)."""
+        check(lib().ds4f_gpu_prefill(self.h, ptr(states), states.shape[0], ptr(sel), ptr(w), stream))
 
     def set_path(self, path):
         """0 auto, 1 per-layer kernels, 2 persistent decode kernel."""

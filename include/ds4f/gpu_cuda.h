@@ -254,6 +254,22 @@ int  ds4f_gpu_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t *q, 
 int  ds4f_gpu_f8_gemm(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX,
                       float *Y, int R, int C, int N, int ND, void *stream);
 
+/* Batched prefill of one MoE layer on the tensor cores: the GPU
+ * counterpart of ds4f_moe_step_batch (include/ds4f/moe.h:171,
+ * src/moe.c:1480-1707) for T tokens with their routing given. Per token
+ * RMSNorm of the state, the routed experts' gate/up/SiLU/down as grouped
+ * GEMMs over the tokens each expert received (FP8 weights x 3-digit E4M3
+ * activations, ds4f_gpu_f8_gemm), the bf16 shared expert and its sigmoid
+ * gate, the selection-order combine and the residual add. states_dev
+ * [T][H] fp32 in/out; sel_dev [T][K] global expert ids (ids outside this
+ * model's shard are skipped: the shard's partial sum); w_dev [T][K]
+ * routing weights. FP8 pools. Synchronous on `stream`. */
+int  ds4f_gpu_moe_prefill(Ds4fGpuModel *m, int layer, float *states_dev, int T,
+                          const int *sel_dev, const float *w_dev, void *stream);
+/* Every layer in order: sel_dev / w_dev [n_layers][T][K]. */
+int  ds4f_gpu_prefill(Ds4fGpuModel *m, float *states_dev, int T, const int *sel_dev,
+                      const float *w_dev, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

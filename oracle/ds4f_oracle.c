@@ -358,19 +358,30 @@ static int sel_cmp(const void *a, const void *b) {
 int orc_moe_batch(int fmt, int H, int M, int E, int K, int renorm,
                   const OrcLayerW *lw, const OrcExpertLayout *lay, int B,
                   float *states, int *idx, float *w) {
+    float *xin = (float *)malloc((size_t)H * sizeof(float));
+    float *sc = (float *)malloc((size_t)E * sizeof(float));
+    if (!xin || !sc || K > E) { free(xin); free(sc); return -1; }
+    for (int b = 0; b < B; b++)
+        route(H, E, K, renorm, lw, states + (int64_t)b * H, xin, sc,
+              idx + (int64_t)b * K, w + (int64_t)b * K);
+    free(xin); free(sc);
+    return orc_moe_batch_sel(fmt, H, M, K, lw, lay, B, states, idx, w);
+}
+
+int orc_moe_batch_sel(int fmt, int H, int M, int K, const OrcLayerW *lw,
+                      const OrcExpertLayout *lay, int B, float *states,
+                      const int *idx, const float *w) {
     int rc = -1;
     int64_t ns = (int64_t)B * K;
     float *xins = (float *)malloc((size_t)B * H * sizeof(float));
     float *acc = (float *)calloc((size_t)B * H, sizeof(float));
     float *dy = (float *)calloc((size_t)ns * H, sizeof(float));
-    float *sc = (float *)malloc((size_t)E * sizeof(float));
     OrcSel *sl = (OrcSel *)malloc((size_t)ns * sizeof(OrcSel));
     int64_t *pos = (int64_t *)malloc((size_t)ns * sizeof(int64_t));
-    if (!xins || !acc || !dy || !sc || !sl || !pos || K > E) goto done;
-    for (int b = 0; b < B; b++)
-        route(H, E, K, renorm, lw, states + (int64_t)b * H,
-              xins + (int64_t)b * H, sc, idx + (int64_t)b * K,
-              w + (int64_t)b * K);
+    if (!xins || !acc || !dy || !sl || !pos) goto done;
+    /* the caller's RMSNorm of each token (src/main.c:1014-1033) */
+    memcpy(xins, states, (size_t)B * H * sizeof(float));
+    for (int b = 0; b < B; b++) orc_rmsnorm(lw->norm, H, xins + (int64_t)b * H);
     int64_t n = 0;
     for (int b = 0; b < B; b++)
         for (int j = 0; j < K; j++) {
@@ -403,6 +414,6 @@ int orc_moe_batch(int fmt, int H, int M, int E, int K, int renorm,
     for (int64_t i = 0; i < (int64_t)B * H; i++) states[i] += acc[i];
     rc = 0;
 done:
-    free(xins); free(acc); free(dy); free(sc); free(sl); free(pos);
+    free(xins); free(acc); free(dy); free(sl); free(pos);
     return rc;
 }

@@ -135,6 +135,14 @@ int orc_moe_batch(int fmt, int H, int M, int E, int K, int renorm,
                   const OrcLayerW *lw, const OrcExpertLayout *lay, int B,
                   float *states, int *idx, float *w);
 
+/* The batched step with the routing given (the reference's
+ * ds4f_moe_step_batch proper, src/moe.c:1480-1707, whose caller routes):
+ * RMSNorm of each state, then chains grouped by expert, selection-order
+ * combine, shared expert, residual. idx / w [B][K]; idx < 0 skipped. */
+int orc_moe_batch_sel(int fmt, int H, int M, int K, const OrcLayerW *lw,
+                      const OrcExpertLayout *lay, int B, float *states,
+                      const int *idx, const float *w);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,16 @@ int orc_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t *q, float 
 int orc_f8_gemm_digits(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, double *Y,
                        int R, int C, int N, int ND);
 
+/* One layer of the GPU batched prefill (prefill.cu / ds4f_gpu_moe_prefill),
+ * restated: the same quantisation points (3 E4M3 digits per routed
+ * activation and chain element, bf16 hi/lo digits in the shared expert),
+ * block sums in double, promotion, combine and residual in the GPU's fp32
+ * order. states [T][H] in/out; sel / w [T][K] (sel < 0: skipped). */
+struct OrcLayerW;
+struct OrcExpertLayout;
+int orc_prefill_layer(int H, int M, int K, const struct OrcLayerW *lw, const struct OrcExpertLayout *lay,
+                      int T, float *states, const int *sel, const float *w);
+
 #ifdef __cplusplus
 }
 #endif

@@ -112,6 +112,12 @@ def lib():
             C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_quant_f8_digits.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int,
                                           C.c_void_p, C.c_void_p]
+        L.orc_moe_batch_sel.argtypes = [C.c_int] * 4 + [
+            C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
+            C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_prefill_layer.argtypes = [C.c_int] * 3 + [
+            C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
+            C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_f8_gemm_digits.argtypes = [C.c_void_p] * 5 + [C.c_int] * 4
         _lib = L
     return _lib
@@ -310,6 +316,34 @@ class Layer:
                                ptr(w)) != 0:
             raise RuntimeError("orc_moe_batch failed")
         return st, idx, w
+
+
+def _layer_batch_sel(self, states, sel, w):
+    """The reference batched step with the routing given (fp32)."""
+    st = np.array(states, np.float32, copy=True)
+    sel = np.ascontiguousarray(sel, np.int32)
+    w = np.ascontiguousarray(w, np.float32)
+    lw = self.w()
+    if lib().orc_moe_batch_sel(self.fmt, self.H, self.M, sel.shape[1], C.byref(lw), C.byref(self.lay),
+                               st.shape[0], ptr(st), ptr(sel), ptr(w)) != 0:
+        raise RuntimeError("orc_moe_batch_sel failed")
+    return st
+
+
+def _layer_prefill(self, states, sel, w):
+    """The GPU prefill's own arithmetic (quantised activations) restated."""
+    st = np.array(states, np.float32, copy=True)
+    sel = np.ascontiguousarray(sel, np.int32)
+    w = np.ascontiguousarray(w, np.float32)
+    lw = self.w()
+    if lib().orc_prefill_layer(self.H, self.M, sel.shape[1], C.byref(lw), C.byref(self.lay), st.shape[0],
+                               ptr(st), ptr(sel), ptr(w)) != 0:
+        raise RuntimeError("orc_prefill_layer failed")
+    return st
+
+
+Layer.moe_batch_sel = _layer_batch_sel
+Layer.prefill = _layer_prefill
 
 
 def quant_f8_digits(x, nd=3):
