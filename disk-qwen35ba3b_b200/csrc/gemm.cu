@@ -117,7 +117,8 @@ __global__ void k_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t 
 // slot 0. Grouped mode: tile t = blockIdx.y < *ntiles names (slot, first B
 // row, valid rows) -- the experts' token groups of the batched prefill.
 constexpr int kStages = 4;
-constexpr int kGemmThreads = 192;          // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+constexpr int kEpiWarps = 8;               // two per TMEM lane quadrant, 32 columns each
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2.. epilogue
 
 template <int ND, bool BF>
 struct GemmSmem {
@@ -136,35 +137,33 @@ struct GemmSmem {
     static_assert(NM % 16 == 0 && NM <= 256 && 2 * NM <= 512, "MMA N and TMEM columns");
 };
 
-// Epilogue of one K block: combine the digit columns of column n (n, 64 + n,
-// 128 + n) and add into acc[n] with the block's scales.
+// Epilogue of one K block for columns [c0, c0 + 32): combine the digit
+// columns of column n (n, 64 + n, 128 + n) and add into acc[n - c0] with the
+// block's scales. The digit loads of 16 columns share one wait.
 template <int ND, bool BF>
-__device__ __forceinline__ void promote(uint32_t t, const float *sxt, int KB, int kb, float w,
-                                        float (&acc)[kGemmBN]) {
+__device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxt, int KB, int kb, float w,
+                                        float (&acc)[32]) {
     constexpr int BN = kGemmBN;
 #pragma unroll
-    for (int c = 0; c < BN / 16; c++) {
-        float v[16];
-        tc::tmem_ld16(t + c * 16, v);
-        if (ND > 1) {
-            float v1[16];
-            tc::tmem_ld16(t + BN + c * 16, v1);
+    for (int c = 0; c < 2; c++) {
+        const uint32_t col = c0 + c * 16;
+        uint32_t r[3][16];
+        tc::tmem_ld16_nowait(t + col, r[0]);
+        if (ND > 1) tc::tmem_ld16_nowait(t + BN + col, r[1]);
+        if (ND > 2) tc::tmem_ld16_nowait(t + 2 * BN + col, r[2]);
+        tc::tmem_wait_ld();
+        tc::tmem_regs_ready(r[0]);
+        if (ND > 1) tc::tmem_regs_ready(r[1]);
+        if (ND > 2) tc::tmem_regs_ready(r[2]);
 #pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = BF ? __fadd_rn(v[i], v1[i]) : __fadd_rn(v[i], __fmul_rn(v1[i], 0.0625f));
-        }
-        if (ND > 2) {
-            float v2[16];
-            tc::tmem_ld16(t + 2 * BN + c * 16, v2);
-#pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = __fadd_rn(v[i], __fmul_rn(v2[i], 0.00390625f));
-        }
-        if (BF) {
-#pragma unroll
-            for (int i = 0; i < 16; i++) acc[c * 16 + i] = __fadd_rn(acc[c * 16 + i], v[i]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; i++)
-                acc[c * 16 + i] = fmaf(v[i], __fmul_rn(w, sxt[(c * 16 + i) * KB + kb]), acc[c * 16 + i]);
+        for (int i = 0; i < 16; i++) {
+            float v = __uint_as_float(r[0][i]);
+            if (ND > 1) v = BF ? __fadd_rn(v, __uint_as_float(r[1][i])) : __fadd_rn(v, __fmul_rn(__uint_as_float(r[1][i]), 0.0625f));
+            if (ND > 2) v = __fadd_rn(v, __fmul_rn(__uint_as_float(r[2][i]), 0.00390625f));
+            if (BF)
+                acc[c * 16 + i] = __fadd_rn(acc[c * 16 + i], v);
+            else
+                acc[c * 16 + i] = fmaf(v, __fmul_rn(w, sxt[(col + i) * KB + kb]), acc[c * 16 + i]);
         }
     }
 }
@@ -199,14 +198,14 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
     if (warp == 1) tc::tmem_alloc(slot, L::NCOLS);
     if (tid == 0) {
         for (int s = 0; s < kStages; s++) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
-        for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, 4); }
+        for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, kEpiWarps); }
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
         tc::prefetch_tmap(&tW);
         tc::prefetch_tmap(&tX);
     }
     if (!BF)
-        for (int i = tid - 64; i >= 0 && i < BN * KB; i += 128)
+        for (int i = tid - 64; i >= 0 && i < BN * KB; i += 32 * kEpiWarps)
             sxt[i] = i / KB < nv ? g.sX[(int64_t)(n0 + i / KB) * KB + i % KB] : 0.f;
     tc::fence_before_sync();
     __syncthreads();
@@ -230,48 +229,60 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            // FP8: one TMEM buffer per K block (alternating), promoted by the
+            // epilogue; BF16: every K block accumulates into buffer 0, read
+            // once at the end
             for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % kStages, b = kb & 1;
+                const int s = kb % kStages, b = BF ? 0 : kb & 1;
                 if (!tc::mbar_wait(full + s, (kb / kStages) & 1, err, 3)) break;
-                if (kb >= 2 && !tc::mbar_wait(tempty + b, ((kb >> 1) - 1) & 1, err, 4)) break;
+                if (!BF && kb >= 2 && !tc::mbar_wait(tempty + b, ((kb >> 1) - 1) & 1, err, 4)) break;
                 tc::fence_after_sync();
                 const uint8_t *a = sm + s * L::STAGE;
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
                     if (BF)
-                        tc::mma_f16(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
-                                    tc::sdesc_sw128(a + L::A + 32 * k), L::ID, k > 0);
+                        tc::mma_f16(taddr, tc::sdesc_sw128(a + 32 * k), tc::sdesc_sw128(a + L::A + 32 * k), L::ID,
+                                    kb > 0 || k > 0);
                     else
                         tc::mma_f8f6f4(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
                                        tc::sdesc_sw128(a + L::A + 32 * k), L::ID, k > 0);
                 }
                 tc::commit(empty + s);
-                tc::commit(tfull + b);
+                if (!BF || kb == KB - 1) tc::commit(tfull + b);
             }
             tc::commit(done);
             tc::mbar_wait(done, 0, err, 5, true);      // every MMA finished
         }
     } else {
-        // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows
-        const int q = warp & 3, row = q * 32 + lane;
-        float acc[BN];
+        // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows;
+        // the two warps of a quadrant take columns [0, 32) and [32, 64)
+        const int q = warp & 3, c0 = ((warp - 2) >> 2) * 32, row = q * 32 + lane;
+        float acc[32];
 #pragma unroll
-        for (int j = 0; j < BN; j++) acc[j] = 0.f;
-        const float *swr = BF ? nullptr : g.sW + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
-        for (int kb = 0; kb < KB; kb++) {
-            const int b = kb & 1;
-            if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
-            tc::fence_after_sync();
-            promote<ND, BF>(taddr + ((uint32_t)(q * 32) << 16) + b * L::NM, sxt, KB, kb, BF ? 1.f : swr[kb], acc);
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(tempty + b);
+        for (int j = 0; j < 32; j++) acc[j] = 0.f;
+        const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
+        if (BF) {
+            if (tc::mbar_wait(tfull, 0, err, 6)) {
+                tc::fence_after_sync();
+                promote<ND, BF>(tq, c0, sxt, KB, 0, 1.f, acc);
+            }
+        } else {
+            const float *swr = g.sW + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
+            for (int kb = 0; kb < KB; kb++) {
+                const int b = kb & 1;
+                if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
+                tc::fence_after_sync();
+                promote<ND, BF>(tq + b * L::NM, c0, sxt, KB, kb, swr[kb], acc);
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tempty + b);
+            }
         }
         if (r0 + row < g.R) {
-            float *y = g.Y + (int64_t)n0 * g.ldy + g.ycol0 + r0 + row;
+            float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + g.ycol0 + r0 + row;
 #pragma unroll
-            for (int j = 0; j < BN; j++)
-                if (j < nv) y[(int64_t)j * g.ldy] = acc[j];
+            for (int j = 0; j < 32; j++)
+                if (c0 + j < nv) y[(int64_t)j * g.ldy] = acc[j];
         }
     }
     tc::fence_before_sync();

@@ -4,11 +4,11 @@
 //
 //  1. RMSNorm of every token (src/moe.c:841-851 arithmetic), then the
 //     activation digits (gemm.cu quantiser: 3 E4M3 digits per element).
-//  2. Group the (token, selection) pairs by expert: counts, offsets, a
-//     stable rank in (token, selection) order (the reference sorts with
+//  2. Group the (token, selection) pairs by expert: counts, offsets, the
+//     tile list (expert, first row, rows) of 64-row tiles, and each
+//     selection's row in its expert's range (the reference sorts with
 //     qsort, src/moe.c:1527, whose order within a group does not matter as
-//     each selection keeps its own output row, :1606-1607), and the tile
-//     list (expert, first row, rows) of 64-row tiles.
+//     each selection keeps its own output row, :1606-1607).
 //  3. Gather each selection's digit rows; grouped GEMMs: gate and up
 //     (tcgen05, per expert), SiLU-mul (src/moe.c:645-649) into the chain's
 //     digits, down.
@@ -94,20 +94,20 @@ __global__ void k_plan(const int *cnt, int count, int slot0, int *off, int *tile
     if (e == 0) { *ntiles = tiles_n; *nrows = rows; }
 }
 
-// Block e: the selections of expert first + e in (token, selection) order
-// get rows off[e], off[e] + 1, ...; pos[selection] = row, src[row] = selection.
-__global__ void k_rank(const int *sel, int n, int first, const int *off, int *pos, int *src) {
-    __shared__ int sh[33];
-    const int e = blockIdx.x;
-    int base = off[e];
-    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
-        const int i = i0 + threadIdx.x;
-        const int f = i < n && sel[i] - first == e;
-        int rank;
-        const int tot = block_excl_scan(f, &rank, sh);
-        if (f) { pos[i] = base + rank; src[base + rank] = i; }
-        base += tot;
-    }
+// Each in-shard selection takes the next row of its expert's range:
+// pos[selection] = row, src[row] = selection. The order of rows inside an
+// expert's range does not change any result (every output column of the
+// tensor-core GEMM depends on its own row only; the combine reads rows by
+// pos), as in the reference whose qsort leaves it open (src/moe.c:1527).
+__global__ void k_place(const int *sel, int n, int first, int count, const int *off, int *fill, int *pos,
+                        int *src) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int e = sel[i] - first;
+    if (e < 0 || e >= count) return;
+    const int p = off[e] + atomicAdd(fill + e, 1);
+    pos[i] = p;
+    src[p] = i;
 }
 
 // Row p of the gathered digit planes <- token src[p] / K; one warp per
@@ -180,19 +180,51 @@ __global__ void k_gate_logit(const float *xin, const uint16_t *gw, int H, float 
 }
 
 // ---- 5. combine ------------------------------------------------------------------------
+// One block per token: its in-shard selections (j order, zero weights
+// skipped) staged in shared memory, then 4 output columns per thread.
 __global__ void k_combine(float *states, const float *O, const float *OS, const float *sg, const int *sel,
                           const float *w, const int *pos, int first, int count, int K, int H) {
+    __shared__ int prow[16];
+    __shared__ float pw[16];
+    __shared__ int np;
     const int t = blockIdx.x;
-    const float sig = sigmoid_ref(sg[t]);
-    for (int r = threadIdx.x; r < H; r += blockDim.x) {
-        float acc = 0.f;
+    if (threadIdx.x == 0) {
+        int n = 0;
         for (int j = 0; j < K; j++) {
             const int i = t * K + j, e = sel[i] - first;
             if (e < 0 || e >= count || w[i] == 0.0f) continue;
-            acc = __fadd_rn(acc, __fmul_rn(w[i], O[(int64_t)pos[i] * H + r]));
+            prow[n] = pos[i];
+            pw[n] = w[i];
+            n++;
         }
-        acc = __fadd_rn(acc, __fmul_rn(sig, OS[(int64_t)t * H + r]));
-        states[(int64_t)t * H + r] = __fadd_rn(states[(int64_t)t * H + r], acc);
+        np = n;
+    }
+    __syncthreads();
+    const float sig = sigmoid_ref(sg[t]);
+    const int n = np;
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int k = 0; k < n; k++) {
+            const float4 o = *(const float4 *)(O + (int64_t)prow[k] * H + 4 * c);
+            const float wk = pw[k];
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wk, o.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wk, o.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wk, o.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wk, o.w));
+        }
+        const float4 so = *(const float4 *)(OS + (int64_t)t * H + 4 * c);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(sig, so.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(sig, so.y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(sig, so.z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(sig, so.w));
+        float4 *st = (float4 *)(states + (int64_t)t * H) + c;
+        float4 v = *st;
+        v.x = __fadd_rn(v.x, acc.x);
+        v.y = __fadd_rn(v.y, acc.y);
+        v.z = __fadd_rn(v.z, acc.z);
+        v.w = __fadd_rn(v.w, acc.w);
+        *st = v;
     }
 }
 
@@ -245,7 +277,8 @@ int pf_workspace(Model *m, int T, PfWs *w) {
 
 }  // namespace
 
-int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w, cudaStream_t st) {
+int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w, cudaStream_t st,
+                  bool first_layer, bool last_layer) {
     DS4F_REQUIRE(m->d.fmt == DS4F_FMT_FP8, "prefill: the tensor-core path takes FP8 pools");
     DS4F_REQUIRE(T > 0 && L >= 0 && L < m->d.n_layers, "prefill: layer %d / tokens %d", L, T);
     const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk;
@@ -262,11 +295,13 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     if (quant_f8_digits_launch(ws.xin, T, H, kND, ws.Xq, ws.sx, st)) return -1;
     // 2
     DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));
-    DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
+    if (first_layer) DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
     k_count<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.cnt);
     k_plan<<<1, ((count + 31) / 32) * 32, 0, st>>>(ws.cnt, count, L * count, ws.off, ws.tiles, ws.ntiles,
                                                    ws.nrows);
-    k_rank<<<count, 256, 0, st>>>(sel, (int)R, first, ws.off, ws.pos, ws.src);
+    DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));       // now the per-expert fill counters
+    k_place<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.off, ws.cnt, ws.pos,
+                                                        ws.src);
     k_gather<<<(unsigned)((R * kND * 32 + 255) / 256), 256, 0, st>>>(ws.Xq, ws.sx, ws.src, ws.nrows, K, T, H,
                                                                     ws.Xg, ws.sxg, (int)R);
     // 3: gate, up, SiLU digits, down
@@ -312,10 +347,13 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     // 5
     k_combine<<<T, 256, 0, st>>>(states, ws.O, ws.OS, ws.sg, sel, w, ws.pos, first, count, K, H);
     DS4F_CUDA(cudaGetLastError());
-    unsigned h = 0;
-    DS4F_CUDA(cudaMemcpyAsync(&h, ws.err, 4, cudaMemcpyDeviceToHost, st));
-    DS4F_CUDA(cudaStreamSynchronize(st));
-    DS4F_REQUIRE(h == 0, "prefill: a tensor-core pipeline wait gave up (code %u)", h);
+    if (last_layer) {
+        // the pipeline waits of every layer since first_layer report here
+        unsigned h = 0;
+        DS4F_CUDA(cudaMemcpyAsync(&h, ws.err, 4, cudaMemcpyDeviceToHost, st));
+        DS4F_CUDA(cudaStreamSynchronize(st));
+        DS4F_REQUIRE(h == 0, "prefill: a tensor-core pipeline wait gave up (code %u)", h);
+    }
     return 0;
 }
 
@@ -326,7 +364,7 @@ extern "C" {
 int ds4f_gpu_moe_prefill(Ds4fGpuModel *h, int layer, float *states_dev, int T, const int *sel_dev,
                          const float *w_dev, void *stream) {
     DS4F_REQUIRE(h && states_dev && sel_dev && w_dev, "moe_prefill: null argument");
-    return ds4f::prefill_layer(&h->m, layer, states_dev, T, sel_dev, w_dev, (cudaStream_t)stream);
+    return ds4f::prefill_layer(&h->m, layer, states_dev, T, sel_dev, w_dev, (cudaStream_t)stream, true, true);
 }
 
 int ds4f_gpu_prefill(Ds4fGpuModel *h, float *states_dev, int T, const int *sel_dev, const float *w_dev,
@@ -334,8 +372,10 @@ int ds4f_gpu_prefill(Ds4fGpuModel *h, float *states_dev, int T, const int *sel_d
     DS4F_REQUIRE(h && states_dev && sel_dev && w_dev, "prefill: null argument");
     const ds4f::Model &m = h->m;
     const int64_t per = (int64_t)T * m.d.topk;
+    // one synchronisation (and error check) for the whole stack
     for (int L = 0; L < m.d.n_layers; L++)
-        if (ds4f::prefill_layer(&h->m, L, states_dev, T, sel_dev + L * per, w_dev + L * per, (cudaStream_t)stream))
+        if (ds4f::prefill_layer(&h->m, L, states_dev, T, sel_dev + L * per, w_dev + L * per, (cudaStream_t)stream,
+                                L == 0, L == m.d.n_layers - 1))
             return -1;
     return 0;
 }
