@@ -643,6 +643,21 @@ int ds4f_gpu_moe_layer_dev(Ds4fGpuModel *h, int layer, float *state, int *idx, f
     });
 }
 
+int ds4f_gpu_moe_layer_partial_dev(Ds4fGpuModel *h, int layer, const float *state, int B, float *acc,
+                                   int add_shared, void *stream) {
+    DS4F_REQUIRE(h && state && acc && B > 0, "moe_layer_partial: bad arguments");
+    Model &m = h->m;
+    DS4F_REQUIRE(layer >= 0 && layer < m.d.n_layers, "moe_layer_partial: layer %d out of range", layer);
+    const int H = m.d.hidden;
+    return on_model_stream(m, stream, [&](cudaStream_t st) {
+        for (int b = 0; b < B; b++)
+            if (moe_layer_launch_ex(&m, layer, const_cast<float *>(state) + (int64_t)b * H, nullptr, nullptr,
+                                    acc + (int64_t)b * H, true, add_shared != 0, st))
+                return -1;
+        return 0;
+    });
+}
+
 int ds4f_gpu_moe_layer(Ds4fGpuModel *h, int layer, float *state, int *idx, float *w) {
     DS4F_REQUIRE(h && state, "moe_layer: null argument");
     Model &m = h->m;

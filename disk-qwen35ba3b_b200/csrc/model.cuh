@@ -81,6 +81,11 @@ int trunk_layout(int H, int M, int E, TrunkLayout *t);
 // (device, [K]) optional copies of the routing.
 int moe_layer_launch(Model *m, int L, float *state, int *idx_out,
                      float *w_out, cudaStream_t st);
+// The same with the expert-parallel options: partial = this model's shard
+// only, acc_out gets the partial sum and the state is not updated;
+// add_shared includes the shared expert.
+int moe_layer_launch_ex(Model *m, int L, float *state, int *idx_out, float *w_out, float *acc_out,
+                        bool partial, bool add_shared, cudaStream_t st);
 
 // Whole decode steps in one persistent cooperative launch (decode.cu).
 bool decode_eligible(const Model *m);

@@ -339,6 +339,10 @@ struct LayerArgs {
     float *sgate;
     float *state;                // [H] in/out
     float *acc_out;              // [H] or null
+    int partial;                 // 1: expert-parallel shard step -- only selections in
+                                 //    [efirst, efirst + ecount) count, acc_out gets the
+                                 //    shard's partial sum, the state is left alone
+    int add_shared;              // shared expert included (partial: on one rank only)
 };
 
 // ---------------------------------------------------------------------------
@@ -358,8 +362,19 @@ k_gateup(LayerArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = a.xin[i] * DS4F_X_PRESCALE;
     __syncthreads();
+    // the selections held here, in selection order (all of them unless
+    // this is an expert-parallel shard step)
+    __shared__ int loc[16];
+    __shared__ int nloc;
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int j = 0; j < a.K; j++)
+            if (a.idx[j] >= a.efirst && a.idx[j] < a.efirst + a.ecount) loc[n++] = j;
+        nloc = n;
+    }
+    __syncthreads();
     const int nb = gridDim.x, cb = blockIdx.x;
-    const int P = a.K * M;
+    const int P = nloc * M;
     const int p0 = (int)((int64_t)cb * P / nb), p1 = (int)((int64_t)(cb + 1) * P / nb);
     {
         float x[G::kch * G::ce];
@@ -371,7 +386,7 @@ k_gateup(LayerArgs a) {
 #pragma unroll
             for (int t = 0; t < 2; t++) {
                 int p = min(pp + t, p1 - 1);
-                jj[t] = p / M; ii[t] = p % M;
+                jj[t] = loc[p / M]; ii[t] = p % M;
                 base[t] = a.pool_l + (int64_t)(a.idx[jj[t]] - a.efirst) * a.slot_bytes;
                 load_row<FMT, H>(bg[t], base[t] + a.slot.rel_v[0] + (int64_t)ii[t] * G::bytes);
                 load_row<FMT, H>(bu[t], base[t] + a.slot.rel_v[1] + (int64_t)ii[t] * G::bytes);
@@ -396,7 +411,7 @@ k_gateup(LayerArgs a) {
             }
         }
     }
-    {
+    if (a.add_shared) {
         float x[GB::kch * GB::ce];
         load_x<kBF16, H>(x, xs);
         const int s0 = (int)((int64_t)cb * M / nb), s1 = (int)((int64_t)(cb + 1) * M / nb);
@@ -444,7 +459,10 @@ k_down(LayerArgs a) {
     const int nb = gridDim.x, cb = blockIdx.x;
     const int r0 = (int)((int64_t)cb * H / nb), r1 = (int)((int64_t)(cb + 1) * H / nb);
     const int nr = r1 - r0;
-    if (warp < K) {
+    const bool held = warp < K && a.idx[warp] >= a.efirst && a.idx[warp] < a.efirst + a.ecount;
+    if (warp < K && !held) {
+        for (int t = lane; t < nr; t += 32) outs[warp][t] = 0.0f;    // another rank's selection
+    } else if (warp < K) {
         float x[G::kch * G::ce];
         load_x<FMT, M>(x, cs[warp]);
         const uint8_t *base = a.pool_l + (int64_t)(a.idx[warp] - a.efirst) * a.slot_bytes;
@@ -473,6 +491,8 @@ k_down(LayerArgs a) {
                 if (lane % G::lpr == 0 && lr < nr) outs[warp][lr] = v;
             }
         }
+    } else if (warp == K && !a.add_shared) {
+        for (int t = lane; t < nr; t += 32) outs[K][t] = 0.0f;
     } else if (warp == K) {
         float x[GB::kch * GB::ce];
         load_x<kBF16, M>(x, cs[K]);
@@ -496,11 +516,12 @@ k_down(LayerArgs a) {
     if (threadIdx.x < nr) {
         const int t = threadIdx.x, r = r0 + t;
         float acc = 0.0f;
-        for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(a.w[j], outs[j][t]));
-        float sg = sigmoid_ref(*a.sgate);
-        acc = __fadd_rn(acc, __fmul_rn(sg, outs[K][t]));
+        for (int j = 0; j < K; j++)
+            if (a.idx[j] >= a.efirst && a.idx[j] < a.efirst + a.ecount)
+                acc = __fadd_rn(acc, __fmul_rn(a.w[j], outs[j][t]));
+        if (a.add_shared) acc = __fadd_rn(acc, __fmul_rn(sigmoid_ref(*a.sgate), outs[K][t]));
         if (a.acc_out) a.acc_out[r] = acc;
-        a.state[r] = __fadd_rn(a.state[r], acc);
+        if (!a.partial) a.state[r] = __fadd_rn(a.state[r], acc);
     }
 }
 
@@ -559,6 +580,11 @@ int trunk_layout(int H, int M, int E, TrunkLayout *t) {
 
 int moe_layer_launch(Model *m, int L, float *state, int *idx_out, float *w_out,
                      cudaStream_t st) {
+    return moe_layer_launch_ex(m, L, state, idx_out, w_out, nullptr, false, true, st);
+}
+
+int moe_layer_launch_ex(Model *m, int L, float *state, int *idx_out, float *w_out, float *acc_out,
+                        bool partial, bool add_shared, cudaStream_t st) {
     const ModelDesc &d = m->d;
     const int H = d.hidden, M = d.moe_inter, E = d.n_experts, K = d.topk;
     const uint16_t *trunk_l = m->trunk + (int64_t)L * m->tr.n;
@@ -578,7 +604,8 @@ int moe_layer_launch(Model *m, int L, float *state, int *idx_out, float *w_out,
     a.tr = m->tr;
     a.E = E; a.K = K; a.efirst = d.expert_first; a.ecount = d.expert_count;
     a.idx = w.idx; a.w = w.w; a.xin = w.xin; a.chain = w.chain; a.sgate = w.sgate;
-    a.state = state; a.acc_out = w.acc;
+    a.state = state; a.acc_out = acc_out ? acc_out : w.acc;
+    a.partial = partial ? 1 : 0; a.add_shared = add_shared ? 1 : 0;
     int rc;
     if (d.fmt == DS4F_FMT_FP8 && H == 2048 && M == 512) rc = launch_chain<DS4F_FMT_FP8, 2048, 512>(a, st);
     else if (d.fmt == DS4F_FMT_MXFP4 && H == 2048 && M == 512) rc = launch_chain<DS4F_FMT_MXFP4, 2048, 512>(a, st);
@@ -714,6 +741,7 @@ extern "C" int ds4f_gpu_moe_layer_static(const Ds4fLayerDev *ld, float *state, i
     a.E = E; a.K = K; a.efirst = 0; a.ecount = E;
     a.idx = wk.idx; a.w = wk.w; a.xin = wk.xin; a.chain = wk.chain; a.sgate = wk.sgate;
     a.state = state; a.acc_out = wk.acc;
+    a.partial = 0; a.add_shared = 1;
     int rc;
     if (ld->fmt == DS4F_FMT_FP8 && H == 2048) rc = launch_chain<DS4F_FMT_FP8, 2048, 512>(a, st);
     else if (ld->fmt == DS4F_FMT_MXFP4 && H == 2048) rc = launch_chain<DS4F_FMT_MXFP4, 2048, 512>(a, st);

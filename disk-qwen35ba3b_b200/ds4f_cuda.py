@@ -84,6 +84,7 @@ def lib():
             "ds4f_gpu_quant_f8_digits": [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_f8_gemm": [_vp] * 5 + [C.c_int] * 4 + [_vp],
             "ds4f_gpu_moe_prefill": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_moe_layer_partial_dev": [_vp, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp],
             "ds4f_gpu_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
         }
         for name, args in sig.items():
@@ -274,6 +275,13 @@ class Model:
 
     def stack_dev(self, state, n_steps, stream=None):
         check(lib().ds4f_gpu_moe_stack_dev(self.h, ptr(state), n_steps, stream))
+
+    def layer_partial_dev(self, L, states, acc, add_shared, stream=None):
+        """Expert-parallel shard step of layer L: states [B][H] -> acc [B][H]
+        (device); the state is not updated."""
+        B = states.shape[0] if states.dim() == 2 else 1
+        check(lib().ds4f_gpu_moe_layer_partial_dev(self.h, L, ptr(states), B, ptr(acc),
+                                                    1 if add_shared else 0, stream))
 
     def prefill_layer_dev(self, L, states, sel, w, stream=None):
         """Batched prefill of layer L: states [T][H], sel / w [T][K] (device)."""

@@ -172,6 +172,19 @@ int  ds4f_gpu_moe_layer_dev(Ds4fGpuModel *m, int layer, float *state,
 int  ds4f_gpu_moe_stack(Ds4fGpuModel *m, float *state, int n_steps);
 int  ds4f_gpu_moe_stack_dev(Ds4fGpuModel *m, float *state, int n_steps,
                             void *stream);
+/* Expert-parallel layer step (no reference counterpart: the reference runs
+ * on one host): the model holds the expert shard [expert_first,
+ * expert_first + expert_count) of every layer and the whole trunk. For each
+ * of B tokens (state [B][H], device, read only) the router and top-K run
+ * on the full state, as on every rank; acc [B][H] (device) receives the
+ * shard's part of the selection-order combine (ds4f_moe_step's
+ * acc, src/moe.c:1224-1225) plus, when add_shared, the shared expert
+ * (:1279-1282). Summing acc over the ranks of a full partition (NCCL
+ * all-reduce) and adding it to the state completes the step (src/moe.c:1424).
+ * Enqueued on `stream`. */
+int  ds4f_gpu_moe_layer_partial_dev(Ds4fGpuModel *m, int layer, const float *state, int B,
+                                    float *acc, int add_shared, void *stream);
+
 /* Decode-step implementation: DS4F_PATH_AUTO (persistent kernel where it
  * covers the model: top-8, (H, M) = (2048, 512) or (1024, 256), 64 or 256
  * experts, whole pool on this device), DS4F_PATH_LAYERED (four kernels per

