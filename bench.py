@@ -38,6 +38,8 @@ sys.path.insert(0, ROOT)
 
 H, M, E, K, LAYERS = 2048, 512, 256, 8, 40
 METRIC = "MoE-stack decode tok/s (40-layer FP8, 1 B200 per rank)"
+METRIC_MX = "MoE-stack decode tok/s (40-layer MXFP4, 1 B200 per rank)"
+METRIC_EP = "MoE-stack decode tok/s (40-layer, experts sharded over the GPUs)"
 
 
 def bytes_per_token(fmt_fp8=True):
@@ -268,7 +270,8 @@ def run_gpu(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    model = dc.Model(dc.FMT_FP8, LAYERS, H, M, E, K)
+    fp8 = args.fmt == "fp8"
+    model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, LAYERS, H, M, E, K)
     model.synth(0)
     model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
@@ -317,22 +320,24 @@ def run_gpu(args, rank, world, local_rank):
     if rank == 0:
         ms = t_ms / args.steps
         value = world * args.steps / (t_ms / 1e3)
-        bpt = bytes_per_token(True)
+        bpt = bytes_per_token(fp8)
         peak, src = peaks()
         achieved = bpt / (ms / 1e3) / 1e9
         res = {
-            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC if fp8 else METRIC_MX, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp8-e4m3 weights, fp32 accumulate", "data": "synthetic (seeded, device-generated)",
-            "config": {"workload": "config 2: 40-layer FP8 MoE decode, 1 token/step",
+            "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (e2m1 + e8m0/32)") + " weights, fp32 accumulate",
+            "data": "synthetic (seeded, device-generated)",
+            "config": {"workload": ("config 2: 40-layer FP8 MoE decode, 1 token/step" if fp8 else
+                                    "config 3 (1 GPU, batch 1): 40-layer MXFP4 MoE decode, 1 token/step"),
                        "hidden": H, "moe_inter": M, "experts": E, "topk": K,
-                       "layers": LAYERS, "pool_gb": round(LAYERS * E * 3146496 / 1e9, 2),
-                       "l2": "inputs larger than L2 (1.30 GB of weights per step)",
+                       "layers": LAYERS, "pool_gb": round(LAYERS * E * (3146496 if fp8 else 1671168) / 1e9, 2),
+                       "l2": f"inputs larger than L2 ({bpt / 1e9:.2f} GB of weights per step)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": (None if args.layered else TRAFFIC_PER_LAUNCH),
+                         "traffic": (TRAFFIC_PER_LAUNCH if fp8 and not args.layered else None),
                          "traffic_unit": "bytes per launch (ncu, 4-layer capture x 10)",
                          "peak_source": src,
                          "kernel": ("whole decode step: 4 kernels per layer in a CUDA graph" if args.layered
@@ -482,6 +487,99 @@ def run_gpu_prefill(args, rank, world, local_rank):
     return res
 
 
+# ---- config 3: expert-parallel decode ------------------------------------------
+
+def run_gpu_ep(args, rank, world, local_rank):
+    import importlib.util
+    import torch
+    import torch.distributed as dist
+    from tests._lib import ds4f_cuda
+    dc = ds4f_cuda()
+    torch.cuda.set_device(local_rank)
+    dc.init()
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        import tempfile
+        dist.init_process_group("gloo", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1)
+    spec = importlib.util.spec_from_file_location(
+        "ep", os.path.join(ROOT, "disk-qwen35ba3b_b200", "ep.py"))
+    ep = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ep)
+    fp8 = args.fmt == "fp8"
+    shard = ep.GpuShard(dc, dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, LAYERS, H, M, E, K, rank, world, seed=0)
+    dec = ep.ExpertParallelDecoder(shard)
+    Bt = args.batch
+    st = torch.empty((Bt, H), dtype=torch.float32, device="cuda")
+    dc.synth_f32_dev(st, Bt * H, 0, 0, 4, 0, 2, 1.0)            # the same tokens on every rank
+    sp = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.warmup):
+        dec.step(st, sp)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = Clocks(local_rank)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dec.step(st, sp)
+    e1.record()
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    clocks = clk.stop()
+    # e2e: host state in, host state out each step
+    hst = st.cpu().pin_memory()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        st.copy_(hst, non_blocking=True)
+        dec.step(st, sp)
+        hst.copy_(st, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    tt = torch.tensor([t_ms, e2e_s], dtype=torch.float64, device="cuda" if world > 1 else "cpu")
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_s = float(tt[0]), float(tt[1])
+    shard.close()
+    res = None
+    if rank == 0:
+        ms = t_ms / args.steps
+        slot = 3 * (M * H + (M // 128) * (H // 128) * 4) if fp8 else 3 * (M * H // 2 + M * H // 32)
+        # experts a layer touches for B distinct tokens (expected value; K at
+        # B = 1), each read once by the job, plus router and shared expert
+        uniq = K if Bt == 1 else E * (1 - (1 - K / E) ** Bt)
+        bytes_step = int(LAYERS * (uniq * slot + E * H * 2 + 3 * M * H * 2 + 2 * H * 2))
+        peak, src = peaks()
+        bw = bytes_step / (ms / 1e3) / 1e9
+        res = {
+            "metric": METRIC_EP, "value": round(Bt * args.steps / (t_ms / 1e3), 2), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (e2m1 + e8m0/32)") + " weights, fp32 accumulate",
+            "data": "synthetic (seeded, device-generated)",
+            "config": {"workload": f"config 3: 40-layer {'FP8' if fp8 else 'MXFP4'} decode, batch {Bt}, "
+                                   f"{E // world} experts per GPU",
+                       "batch": Bt, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
+                       "parallelism": f"expert-parallel x{world} (all-reduce of acc per layer)",
+                       "l2": "inputs larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": peak * world, "unit": "GB/s",
+                         "frac": round(bw / (peak * world), 4), "traffic": None, "peak_source": src,
+                         "algorithmic_bytes_per_step": bytes_step,
+                         "note": "expected unique experts per layer for the batch; peak = N x per-GPU"},
+            "e2e": {"value": round(Bt * args.steps / e2e_s, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": Bt * H * 4, "d2h_bytes_per_step": Bt * H * 4,
+                    "timer": "host clock, synchronous steps"},
+            "gpu_launches": args.steps * LAYERS * 4 * Bt,
+            "clocks": clocks,
+        }
+    dist.barrier()
+    dist.destroy_process_group()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -491,8 +589,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layered", action="store_true",
                     help="per-layer kernels (CUDA graph) instead of the persistent kernel")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: config 2 (the headline); prefill: config 4")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep-decode"],
+                    help="decode: config 2 (the headline); prefill: config 4; ep-decode: config 3 "
+                         "(experts sharded over the ranks)")
+    ap.add_argument("--fmt", default=None, choices=["fp8", "mxfp4"],
+                    help="expert format (decode default fp8; ep-decode default mxfp4)")
+    ap.add_argument("--batch", type=int, default=1, help="ep-decode: tokens per step")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -519,7 +621,10 @@ def main():
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}))
         return
-    res = (run_gpu_prefill if args.workload == "prefill" else run_gpu)(args, rank, world, local_rank)
+    if args.fmt is None:
+        args.fmt = "mxfp4" if args.workload == "ep-decode" else "fp8"
+    fn = {"prefill": run_gpu_prefill, "ep-decode": run_gpu_ep}.get(args.workload, run_gpu)
+    res = fn(args, rank, world, local_rank)
     if rank == 0:
         if world == 1:
             v, desc = cpu_reference_sample(args.cpu_seconds)
