@@ -82,6 +82,14 @@ __device__ __forceinline__ void st_tag(uint64_t *p, uint32_t tag, uint32_t bits)
     uint64_t w = ((uint64_t)tag << 32) | bits;
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// After a thread's last tagged store of a phase: push its stores out to L2
+// now (readers poll with bulk copies; a relaxed store may otherwise linger
+// in the SM's write path for microseconds). It blocks the storing thread
+// for ~0.5-1.5 us, so it is used where that thread waits anyway (the chain
+// and state publishes), not where it issues the next copies.
+__device__ __forceinline__ void publish_flush() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -125,7 +133,9 @@ struct Smem {
                                                    : PP * 2 * S::gsc_b;          // [mat][pair]
     static constexpr int DSC = FMT == DS4F_FMT_FP8 ? S::dsc_b : a16(RR * S::dsc_b + 48);
     static_assert(PP <= kGroups * kGroupPairs, "gate/up pairs exceed the copy groups");
-    static constexpr int o_bar = 0;                                   // 8 mbarriers
+    static_assert(4 * RT <= 8 && M < 4 * kGmin && 2 * ((M + kGmin - 1) / kGmin) <= 8,
+                  "warp roles: router rows in warps 0-7, shared rows in 8-15, gate logit in CTA 0 warp 15");
+    static constexpr int o_bar = 0;                                   // 9 mbarriers (of 16 slots)
     static constexpr int o_xin = 128;
     static constexpr int o_nw = o_xin + a16(H * 4);
     static constexpr int o_rt = o_nw + a16(H * 2);
@@ -138,7 +148,14 @@ struct Smem {
                                          ? (H > 4 * E ? H : 4 * E) : (K + 1) * M + 2);
     // + the chains unpacked to floats after the tagged words
     static constexpr int UNP = GATH + 4 * ((K + 1) * M + 4);
-    static constexpr int GU = 2 * PP * S::row_b > UNP ? 2 * PP * S::row_b : UNP;
+    // + the next layer's shared gate/up rows and the shared-gate row, past
+    // the gathers (they land during the down phase, are read in the router
+    // phase, and are overwritten by the gate/up copies after that)
+    static constexpr int NSG = (M + kGmin - 1) / kGmin;
+    static constexpr int SHO = a16(UNP);
+    static constexpr int SHB = 2 * NSG * H * 2 + H * 2;
+    static constexpr int GU0 = 2 * PP * S::row_b > UNP ? 2 * PP * S::row_b : UNP;
+    static constexpr int GU = GU0 > SHO + SHB ? GU0 : SHO + SHB;
     static constexpr int o_gu = o_dsc + a16(K * DSC);
     static constexpr int o_gsc = o_gu + a16(GU);
     static constexpr int o_srow = o_gsc + a16(GSC);
@@ -261,7 +278,7 @@ k_decode(DecodeArgs a) {
     bool ok = true;
 
     if (tid == 0) {
-        for (int i = 0; i < 8; i++) mbar_init(bar + i, 1);
+        for (int i = 0; i < 9; i++) mbar_init(bar + i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -277,6 +294,18 @@ k_decode(DecodeArgs a) {
         mbar_expect(bar + 0, b1 + H * 2);
         bulk(nw, t + a.tr.norm, H * 2, bar + 0);
         if (b1) bulk(rt, t + a.tr.router + (int64_t)rt0 * H, b1, bar + 0);
+    };
+    // one thread: shared gate rows, up rows of layer l (and the shared-gate
+    // row in CTA 0) into gu + SHO (bar 8)
+    auto prefetch_sh = [&](int l) {
+        const uint16_t *t = trunk_l(l);
+        const uint32_t b = nsg * H * 2;
+        mbar_expect(bar + 8, 2 * b + (c == 0 ? H * 2 : 0));
+        if (b) {
+            bulk(gu + L::SHO, t + a.tr.sh_gate + (int64_t)sg0 * H, b, bar + 8);
+            bulk(gu + L::SHO + L::NSG * H * 2, t + a.tr.sh_up + (int64_t)sg0 * H, b, bar + 8);
+        }
+        if (c == 0) bulk(gu + L::SHO + 2 * L::NSG * H * 2, t + a.tr.sh_gw, H * 2, bar + 8);
     };
     // one thread: shared down rows of layer l (bar 1)
     auto prefetch_sd = [&](int l) {
@@ -339,8 +368,9 @@ k_decode(DecodeArgs a) {
     if (tid == 0) {
         prefetch_rt(0);
         prefetch_sd(0);
+        prefetch_sh(0);
     }
-    pendb |= 3u;
+    pendb |= 3u | (1u << 8);
 
     const int T = a.n_layers * a.n_steps;
 #define DS4F_TRACE(k) \
@@ -400,19 +430,26 @@ k_decode(DecodeArgs a) {
             __syncthreads();
         }
         DS4F_TRACE(2);
-        // (C) router rows (warps 0 .. nrt-1); lane owns columns
-        //     [lane * cpl, (lane + 1) * cpl) so one warp scan gives prefixes
-        if (warp < nrt) {
-            const int e = rt0 + warp;
-            const uint16_t *row = rt + warp * H + lane * S::cpl;
-            constexpr int NCH = S::cpl / 8;
+        // (C) router rows: warps 4 r .. 4 r + 3 take row r (r < nrt), warp q
+        //     the columns [q H/4, (q+1) H/4), lane l CPL contiguous columns of
+        //     them. Pass 1: chunk sums and each warp's total; the totals of the
+        //     warps before give each lane its exact column-order prefix for the
+        //     bound in pass 2 (named barrier over the router warps only).
+        if (warp < 4 * nrt) {
+            constexpr int CQ = H / 4, CPL = CQ / 32, NCH = CPL / 8;
+            static_assert(CPL % 8 == 0, "router rows: whole 8-element chunks per lane");
+            const int rr = warp >> 2, q = warp & 3, e = rt0 + rr, nrw = 128 * nrt;
+            const int c0 = q * CQ + lane * CPL;
+            const uint16_t *row = rt + rr * H + c0;
             double Tq[NCH];
             float Aq[NCH];
 #pragma unroll
             for (int k = 0; k < NCH; k++) {
                 uint4 w = lds16(row + k * 8);
                 const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-                const float *x = xin + lane * S::cpl + k * 8;
+                const float4 x0 = *(const float4 *)(xin + c0 + k * 8);
+                const float4 x1 = *(const float4 *)(xin + c0 + k * 8 + 4);
+                const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                 double p8[8];
                 // the bound's |p| (8 - u) terms: positive, summed in fp32 (<= 64
                 // terms per lane, relative error < 4e-6, inside the 1.001 margin)
@@ -420,9 +457,9 @@ k_decode(DecodeArgs a) {
 #pragma unroll
                 for (int u = 0; u < 8; u++) {
                     uint32_t h = (u & 1) ? (ww[u >> 1] & 0xFFFF0000u) : (ww[u >> 1] << 16);
-                    float p = __fmul_rn(__uint_as_float(h), x[u]);   // the reference's product
-                    p8[u] = (double)p;
-                    ab = fmaf(fabsf(p), (float)(8 - u), ab);
+                    float pr = __fmul_rn(__uint_as_float(h), x[u]);   // the reference's product
+                    p8[u] = (double)pr;
+                    ab = fmaf(fabsf(pr), (float)(8 - u), ab);
                 }
                 Tq[k] = __dadd_rn(__dadd_rn(__dadd_rn(p8[0], p8[1]), __dadd_rn(p8[2], p8[3])),
                                   __dadd_rn(__dadd_rn(p8[4], p8[5]), __dadd_rn(p8[6], p8[7])));
@@ -437,47 +474,56 @@ k_decode(DecodeArgs a) {
                 double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
                 if (lane >= o) incl = __dadd_rn(incl, y);
             }
-            double P = __dsub_rn(incl, tot);            // prefix before this lane
+            double *rx = (double *)red + 32;      // [row][quarter] totals, then at +8 bound parts
+            if (lane == 31) rx[rr * 4 + q] = incl;
+            asm volatile("bar.sync 1, %0;" ::"r"(nrw) : "memory");
+            double P = __dsub_rn(incl, tot);      // prefix before this lane within the warp
+            for (int k = 0; k < q; k++) P = __dadd_rn(rx[rr * 4 + k], P);
             double bs = 0.0, loc = 0.0;
 #pragma unroll
             for (int k = 0; k < NCH; k++) {
                 bs = __dadd_rn(bs, __dadd_rn(8.0 * fabs(__dadd_rn(P, loc)), (double)Aq[k]));
                 loc = __dadd_rn(loc, Tq[k]);
             }
-            // the prefixes carry double rounding of their own: widen by 1e-12
-            bs = warp_sum_d(bs) * (1.0 + 1e-12);
-            const double Sv = __shfl_sync(0xFFFFFFFFu, incl, 31);
-            const double Bv = 1.001 * kU * bs + 1e-300;
-            if (lane < 4) {
+            bs = warp_sum_d(bs);
+            if (lane == 0) rx[8 + rr * 4 + q] = bs;
+            asm volatile("bar.sync 1, %0;" ::"r"(nrw) : "memory");
+            if (q == 0 && lane < 4) {
+                double Sv = 0.0, Bs = 0.0;
+                for (int k = 0; k < 4; k++) {
+                    Sv = __dadd_rn(Sv, rx[rr * 4 + k]);
+                    Bs = __dadd_rn(Bs, rx[8 + rr * 4 + k]);
+                }
+                // the prefixes carry double rounding of their own: widen by 1e-12
+                const double Bv = 1.001 * kU * (Bs * (1.0 + 1e-12)) + 1e-300;
                 const uint64_t sb = (uint64_t)__double_as_longlong(Sv);
                 const uint64_t bb = (uint64_t)__double_as_longlong(Bv);
                 const uint32_t word = lane == 0 ? (uint32_t)sb : lane == 1 ? (uint32_t)(sb >> 32)
                                     : lane == 2 ? (uint32_t)bb : (uint32_t)(bb >> 32);
                 st_tag(a.sb_ll + 4 * e + lane, tg, word);
             }
-        } else if (warp >= L::RT && warp < L::RT + 2 * nsg) {
-            // (D) shared gate (even) / up (odd) rows through registers
-            const int w2 = warp - L::RT, i = sg0 + (w2 >> 1), m = w2 & 1;
-            const uint16_t *row = trunk_l(l) + (m ? a.tr.sh_up : a.tr.sh_gate) + (int64_t)i * H;
-            uint4 b[H / 256];
-#pragma unroll
-            for (int k = 0; k < H / 256; k++) b[k] = ldg_stream(row + (lane + 32 * k) * 8);
+        } else if ((warp >= 8 && warp < 8 + 2 * nsg) || (warp == kWarps - 1 && c == 0)) {
+            // (D) shared gate (even) / up (odd) rows and, CTA 0 warp 15, the
+            // shared-gate row: prefetched into shared memory (bar 8)
+            const bool okd = mbar_wait(a, bar + 8, PH(8), 9);
+            const bool gl = warp == kWarps - 1 && c == 0;   // CTA 0 has < 4 shared rows
+            const int w2 = warp - 8, m = w2 & 1;
+            const uint16_t *row = (const uint16_t *)(gu + L::SHO) +
+                                  (gl ? 2 * L::NSG * H : (m * L::NSG + (w2 >> 1)) * H);
             float acc = 0.f;
+            if (okd) {
 #pragma unroll
-            for (int k = 0; k < H / 256; k++) acc += bf16_dot8(b[k], xin + (lane + 32 * k) * 8);
+                for (int k = 0; k < H / 256; k++)
+                    acc += bf16_dot8(lds16(row + (lane + 32 * k) * 8), xin + (lane + 32 * k) * 8);
+            }
             acc = warp_sum(acc);
-            if (lane == 0) red[192 + w2] = acc;     // bytes 768..: clear of rd[0..63]
-        } else if (warp == kWarps - 1 && c == G - 1) {
-            const uint16_t *gw = trunk_l(l) + a.tr.sh_gw;
-            uint4 b[H / 256];
-#pragma unroll
-            for (int k = 0; k < H / 256; k++) b[k] = ldg_stream(gw + (lane + 32 * k) * 8);
-            float acc = 0.f;
-#pragma unroll
-            for (int k = 0; k < H / 256; k++) acc += bf16_dot8(b[k], xin + (lane + 32 * k) * 8);
-            acc = warp_sum(acc);
-            if (lane == 0) st_tag(a.ch_ll + (K + 1) * M, tg, __float_as_uint(acc));
+            if (lane == 0 && okd) {
+                if (gl) st_tag(a.ch_ll + (K + 1) * M, tg, __float_as_uint(acc));
+                else red[192 + w2] = acc;       // bytes 768..: clear of rd[0..63]
+            }
         }
+        FLIP(8);
+        PEND(8, false);
         DS4F_TRACE(3);
         // (F) routing: gather every S/B word, then warp 0 takes the
         //     certified top-K
@@ -582,7 +628,7 @@ k_decode(DecodeArgs a) {
         __syncthreads();
         if (!ctl[3]) { ok = false; break; }
         DS4F_TRACE(4);
-        if (tid < nsg)
+        if (tid < nsg)          // needed in the down phase only: no flush
             st_tag(a.ch_ll + K * M + sg0 + tid, tg,
                    __float_as_uint(silu_mul(red[192 + 2 * tid], red[192 + 2 * tid + 1])));
         if (!ctl[1]) {
@@ -737,12 +783,17 @@ k_decode(DecodeArgs a) {
 #pragma unroll
             for (int g = 0; g < kGroups; g++)
                 if (g < ngroups) { FLIP(2 + g); PEND(2 + g, false); }
+            // the gate/up rows are consumed: the next layer's shared rows
+            // may land past the gathers' region of the buffer
+            if (tid == 0 && more) { fence_async(); prefetch_sh(ln); }
+            PEND(8, more);
             if (tid < np) {
                 constexpr int HALF = kGroups * kGroupPairs * 2;
                 const int q = p0 + tid;
                 st_tag(a.ch_ll + (q / M) * M + (q % M), tg,
                        __float_as_uint(silu_mul(red[2 * tid] + red[HALF + 2 * tid],
                                                 red[2 * tid + 1] + red[HALF + 2 * tid + 1])));
+                publish_flush();
             }
         }
         DS4F_TRACE(9);
@@ -865,6 +916,7 @@ k_decode(DecodeArgs a) {
                 acc = __fadd_rn(acc, __fmul_rn(red[0], outs[K * L::RR + tid]));
                 const float ns = __fadd_rn(srow[tid], acc);
                 st_tag(a.st_ll + r, tg, __float_as_uint(ns));
+                publish_flush();
                 if (!more) __stcg(a.state + r, ns);
             }
             __syncthreads();
@@ -874,7 +926,7 @@ k_decode(DecodeArgs a) {
         PEND(1, more);
     }
     // drain this CTA's copies before exit (bounded)
-    for (int i = 0; i < 8; i++)
+    for (int i = 0; i < 9; i++)
         if ((pendb >> i) & 1u) mbar_wait(a, bar + i, PH(i), 8);
 #undef DS4F_TRACE
 #undef DS4F_ROUNDS
