@@ -580,6 +580,108 @@ def run_gpu_ep(args, rank, world, local_rank):
     return res
 
 
+# ---- config 4 at N GPUs: expert-parallel prefill ----------------------------------
+
+def run_gpu_ep_prefill(args, rank, world, local_rank):
+    import importlib.util
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from tests._lib import ds4f_cuda
+    dc = ds4f_cuda()
+    torch.cuda.set_device(local_rank)
+    dc.init()
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    else:
+        import tempfile
+        dist.init_process_group("gloo", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1)
+    spec = importlib.util.spec_from_file_location(
+        "ep", os.path.join(ROOT, "disk-qwen35ba3b_b200", "ep.py"))
+    ep = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ep)
+    T = T_PREFILL
+    shard = ep.GpuShard(dc, dc.FMT_FP8, LAYERS, H, M, E, K, rank, world, seed=0)
+    pf = ep.ExpertParallelPrefill(shard)
+    sel, w = zipf_routing(LAYERS, T, E, K, seed=100)            # the same chunk on every rank
+    selg, wg = torch.from_numpy(sel).cuda(), torch.from_numpy(w).cuda()
+    x0 = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    dc.synth_f32_dev(x0, T * H, 0, 0, 4, 0, 1, 1.0)
+    x0 = x0.bfloat16().float()
+    st = torch.empty_like(x0)
+    sp = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.warmup):
+        st.copy_(x0)
+        pf.step(st, selg, wg, sp)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = Clocks(local_rank)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        st.copy_(x0)
+        pf.step(st, selg, wg, sp)
+    e1.record()
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    clocks = clk.stop()
+    hx = x0.cpu().pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        st.copy_(hx, non_blocking=True)
+        pf.step(st, selg, wg, sp)
+        hout.copy_(st, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    tt = torch.tensor([t_ms, e2e_s], dtype=torch.float64, device="cuda" if world > 1 else "cpu")
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_s = float(tt[0]), float(tt[1])
+    shard.close()
+    res = None
+    if rank == 0:
+        ms = t_ms / args.steps
+        uniq = [len(np.unique(sel[L])) for L in range(LAYERS)]
+        slot = 3 * (M * H + (M // 128) * (H // 128) * 4)
+        bytes_step = sum(u * slot + 3 * M * H * 2 + 2 * H * 2 for u in uniq)
+        flops_step = LAYERS * (2 * T * K * 3 * M * H + 2 * T * 3 * M * H)
+        peak, src = peaks()
+        bw = bytes_step / (ms / 1e3) / 1e9
+        tf = flops_step / (ms / 1e3) / 1e12
+        res = {
+            "metric": METRIC_PREFILL.replace("1 B200 per rank", "experts sharded over the GPUs"),
+            "value": round(T * args.steps / (t_ms / 1e3), 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp8-e4m3 weights x 3-digit e4m3 activations, fp32 accumulate (tcgen05)",
+            "data": "synthetic (seeded weights, bf16 N(0,1) activations, Zipf(1.1) routing)",
+            "config": {"workload": f"config 4: prefill of a 2048-token chunk, 40-layer FP8, "
+                                   f"{E // world} experts per GPU",
+                       "tokens": T, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
+                       "parallelism": f"expert-parallel x{world} (all-reduce of acc [T][H] per layer)",
+                       "l2": "inputs larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": peak * world, "unit": "GB/s",
+                         "frac": round(bw / (peak * world), 4), "traffic": None, "peak_source": src,
+                         "algorithmic_bytes_per_step": bytes_step,
+                         "tensor": {"achieved_tflops": round(tf, 1), "peak_tflops": 4500.0 * world,
+                                    "peak_source": "nominal dense FP8 x N", "frac": round(tf / 4500.0 / world, 4),
+                                    "flops_per_step": flops_step}},
+            "e2e": {"value": round(T * args.steps / e2e_s, 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+                    "timer": "host clock, synchronous steps"},
+            "gpu_launches": args.steps * LAYERS * 17,
+            "clocks": clocks,
+        }
+    dist.barrier()
+    dist.destroy_process_group()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -589,7 +691,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layered", action="store_true",
                     help="per-layer kernels (CUDA graph) instead of the persistent kernel")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep-decode"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep-decode", "ep-prefill"],
                     help="decode: config 2 (the headline); prefill: config 4; ep-decode: config 3 "
                          "(experts sharded over the ranks)")
     ap.add_argument("--fmt", default=None, choices=["fp8", "mxfp4"],
@@ -623,7 +725,8 @@ def main():
         return
     if args.fmt is None:
         args.fmt = "mxfp4" if args.workload == "ep-decode" else "fp8"
-    fn = {"prefill": run_gpu_prefill, "ep-decode": run_gpu_ep}.get(args.workload, run_gpu)
+    fn = {"prefill": run_gpu_prefill, "ep-decode": run_gpu_ep,
+          "ep-prefill": run_gpu_ep_prefill}.get(args.workload, run_gpu)
     res = fn(args, rank, world, local_rank)
     if rank == 0:
         if world == 1:

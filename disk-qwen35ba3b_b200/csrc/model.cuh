@@ -99,9 +99,11 @@ int synth_f32(float *dst, int64_t n, uint64_t key, double sigma, cudaStream_t st
 // Batched prefill of one layer (prefill.cu): states [T][H] in/out, routing
 // sel / w [T][K] (global expert ids; ids outside this shard are skipped).
 // first_layer resets the pipeline error word; last_layer synchronises and
-// reports it.
+// reports it. acc_out: expert-parallel partial -- the combine goes to
+// acc_out [T][H] and the states are left alone; add_shared: include the
+// shared expert (one rank of a partition).
 int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w,
-                  cudaStream_t st, bool first_layer, bool last_layer);
+                  cudaStream_t st, bool first_layer, bool last_layer, float *acc_out, bool add_shared);
 
 inline const uint8_t *expert_ptr(const Model *m, int L, int e) {
     return m->pool + ((int64_t)L * m->d.expert_count + (e - m->d.expert_first)) *

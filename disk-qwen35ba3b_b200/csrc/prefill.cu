@@ -182,8 +182,8 @@ __global__ void k_gate_logit(const float *xin, const uint16_t *gw, int H, float 
 // ---- 5. combine ------------------------------------------------------------------------
 // One block per token: its in-shard selections (j order, zero weights
 // skipped) staged in shared memory, then 4 output columns per thread.
-__global__ void k_combine(float *states, const float *O, const float *OS, const float *sg, const int *sel,
-                          const float *w, const int *pos, int first, int count, int K, int H) {
+__global__ void k_combine(float *states, float *acc_out, const float *O, const float *OS, const float *sg,
+                          const int *sel, const float *w, const int *pos, int first, int count, int K, int H) {
     __shared__ int prow[16];
     __shared__ float pw[16];
     __shared__ int np;
@@ -200,7 +200,7 @@ __global__ void k_combine(float *states, const float *O, const float *OS, const 
         np = n;
     }
     __syncthreads();
-    const float sig = sigmoid_ref(sg[t]);
+    const float sig = OS ? sigmoid_ref(sg[t]) : 0.f;
     const int n = np;
     for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -213,11 +213,17 @@ __global__ void k_combine(float *states, const float *O, const float *OS, const 
             acc.z = __fadd_rn(acc.z, __fmul_rn(wk, o.z));
             acc.w = __fadd_rn(acc.w, __fmul_rn(wk, o.w));
         }
-        const float4 so = *(const float4 *)(OS + (int64_t)t * H + 4 * c);
-        acc.x = __fadd_rn(acc.x, __fmul_rn(sig, so.x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(sig, so.y));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(sig, so.z));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(sig, so.w));
+        if (OS) {
+            const float4 so = *(const float4 *)(OS + (int64_t)t * H + 4 * c);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(sig, so.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(sig, so.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(sig, so.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(sig, so.w));
+        }
+        if (acc_out) {                       // expert-parallel partial: acc only
+            *((float4 *)(acc_out + (int64_t)t * H) + c) = acc;
+            continue;
+        }
         float4 *st = (float4 *)(states + (int64_t)t * H) + c;
         float4 v = *st;
         v.x = __fadd_rn(v.x, acc.x);
@@ -278,7 +284,7 @@ int pf_workspace(Model *m, int T, PfWs *w) {
 }  // namespace
 
 int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w, cudaStream_t st,
-                  bool first_layer, bool last_layer) {
+                  bool first_layer, bool last_layer, float *acc_out, bool add_shared) {
     DS4F_REQUIRE(m->d.fmt == DS4F_FMT_FP8, "prefill: the tensor-core path takes FP8 pools");
     DS4F_REQUIRE(T > 0 && L >= 0 && L < m->d.n_layers, "prefill: layer %d / tokens %d", L, T);
     const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk;
@@ -328,6 +334,7 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
             return -1;
     }
     // 4: shared expert
+    if (add_shared) {
     k_bf16_digits<<<(unsigned)(((int64_t)T * H + 255) / 256), 256, 0, st>>>(ws.xin, (int64_t)T * H, ws.Xb);
     const int ntd = (T + kGemmBN - 1) / kGemmBN;
     for (int mat = 0; mat < 2; mat++) {
@@ -344,8 +351,10 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
         if (gemm_launch<2, true>(tl + m->tr.sh_down, 1, (int64_t)H * M * 2, ws.Cb, T, g, ntd, st)) return -1;
     }
     k_gate_logit<<<T, 256, 0, st>>>(ws.xin, tl + m->tr.sh_gw, H, ws.sg);
+    }
     // 5
-    k_combine<<<T, 256, 0, st>>>(states, ws.O, ws.OS, ws.sg, sel, w, ws.pos, first, count, K, H);
+    k_combine<<<T, 256, 0, st>>>(states, acc_out, ws.O, add_shared ? ws.OS : nullptr, ws.sg, sel, w, ws.pos,
+                                 first, count, K, H);
     DS4F_CUDA(cudaGetLastError());
     if (last_layer) {
         // the pipeline waits of every layer since first_layer report here
@@ -364,7 +373,8 @@ extern "C" {
 int ds4f_gpu_moe_prefill(Ds4fGpuModel *h, int layer, float *states_dev, int T, const int *sel_dev,
                          const float *w_dev, void *stream) {
     DS4F_REQUIRE(h && states_dev && sel_dev && w_dev, "moe_prefill: null argument");
-    return ds4f::prefill_layer(&h->m, layer, states_dev, T, sel_dev, w_dev, (cudaStream_t)stream, true, true);
+    return ds4f::prefill_layer(&h->m, layer, states_dev, T, sel_dev, w_dev, (cudaStream_t)stream, true, true,
+                               nullptr, true);
 }
 
 int ds4f_gpu_prefill(Ds4fGpuModel *h, float *states_dev, int T, const int *sel_dev, const float *w_dev,
@@ -375,9 +385,16 @@ int ds4f_gpu_prefill(Ds4fGpuModel *h, float *states_dev, int T, const int *sel_d
     // one synchronisation (and error check) for the whole stack
     for (int L = 0; L < m.d.n_layers; L++)
         if (ds4f::prefill_layer(&h->m, L, states_dev, T, sel_dev + L * per, w_dev + L * per, (cudaStream_t)stream,
-                                L == 0, L == m.d.n_layers - 1))
+                                L == 0, L == m.d.n_layers - 1, nullptr, true))
             return -1;
     return 0;
+}
+
+int ds4f_gpu_moe_prefill_partial(Ds4fGpuModel *h, int layer, const float *states_dev, int T, const int *sel_dev,
+                                 const float *w_dev, float *acc_dev, int add_shared, void *stream) {
+    DS4F_REQUIRE(h && states_dev && sel_dev && w_dev && acc_dev, "moe_prefill_partial: null argument");
+    return ds4f::prefill_layer(&h->m, layer, const_cast<float *>(states_dev), T, sel_dev, w_dev,
+                               (cudaStream_t)stream, true, true, acc_dev, add_shared != 0);
 }
 
 }  // extern "C"

@@ -86,6 +86,7 @@ def lib():
             "ds4f_gpu_moe_prefill": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_moe_layer_partial_dev": [_vp, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp],
             "ds4f_gpu_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_moe_prefill_partial": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -286,6 +287,11 @@ class Model:
     def prefill_layer_dev(self, L, states, sel, w, stream=None):
         """Batched prefill of layer L: states [T][H], sel / w [T][K] (device)."""
         check(lib().ds4f_gpu_moe_prefill(self.h, L, ptr(states), states.shape[0], ptr(sel), ptr(w), stream))
+
+    def prefill_partial_dev(self, L, states, sel, w, acc, add_shared, stream=None):
+        """Expert-parallel partial prefill of layer L into acc [T][H]."""
+        check(lib().ds4f_gpu_moe_prefill_partial(self.h, L, ptr(states), states.shape[0], ptr(sel), ptr(w),
+                                                 ptr(acc), 1 if add_shared else 0, stream))
 
     def prefill_dev(self, states, sel, w, stream=None):
         """Every layer: sel / w [n_layers][T][K] (device)."""

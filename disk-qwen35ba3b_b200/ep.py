@@ -17,8 +17,12 @@ The reference runs on one host and has no counterpart; this is the
 partitioning the expert pool's layout invites (experts are independent
 slots, src/st.c:127-180).
 
+Batched prefill (ExpertParallelPrefill) follows the same pattern with
+the tensor-core grouped GEMMs of the selections each rank's experts
+received and one all-reduce of acc [T][H] per layer.
+
 The per-rank layer step is a backend: `GpuShard` wraps the library; tests
-drive the same decoder on CPU ranks (gloo) with an oracle backend.
+drive the same drivers on CPU ranks (gloo) with an oracle backend.
 """
 import torch
 import torch.distributed as dist
@@ -46,6 +50,9 @@ class GpuShard:
     def layer_partial(self, L, states, acc, add_shared, stream=None):
         self.model.layer_partial_dev(L, states, acc, add_shared, stream)
 
+    def prefill_partial(self, L, states, sel, w, acc, add_shared, stream=None):
+        self.model.prefill_partial_dev(L, states, sel, w, acc, add_shared, stream)
+
     def close(self):
         self.model.close()
 
@@ -57,6 +64,7 @@ class ExpertParallelDecoder:
         self.b = backend
         self.group = group
         self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
         self.acc = None
 
     def step(self, states, stream=None):
@@ -66,6 +74,33 @@ class ExpertParallelDecoder:
             self.acc = torch.empty_like(states)
         for L in range(self.b.n_layers):
             self.b.layer_partial(L, states, self.acc, self.rank == 0, stream)
-            dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
+            if self.world > 1:
+                dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
+            states.add_(self.acc)
+        return states
+
+
+class ExpertParallelPrefill:
+    """Batched prefill of a token chunk over an expert-sharded process
+    group: every rank holds the chunk's states and routing, runs the grouped
+    tensor-core GEMMs of the selections its experts received (the shared
+    expert on rank 0), and one all-reduce of acc [T][H] per layer completes
+    the combine before the residual."""
+
+    def __init__(self, backend, group=None):
+        self.b = backend
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.acc = None
+
+    def step(self, states, sel, w, stream=None):
+        """states [T][H]; sel / w [n_layers][T][K] (global expert ids)."""
+        if self.acc is None or self.acc.shape != states.shape:
+            self.acc = torch.empty_like(states)
+        for L in range(self.b.n_layers):
+            self.b.prefill_partial(L, states, sel[L], w[L], self.acc, self.rank == 0, stream)
+            if self.world > 1:
+                dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
             states.add_(self.acc)
         return states

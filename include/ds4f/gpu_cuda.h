@@ -279,6 +279,14 @@ int  ds4f_gpu_f8_gemm(const uint8_t *W, const float *sW, const uint8_t *X, const
  * routing weights. FP8 pools. Synchronous on `stream`. */
 int  ds4f_gpu_moe_prefill(Ds4fGpuModel *m, int layer, float *states_dev, int T,
                           const int *sel_dev, const float *w_dev, void *stream);
+/* Expert-parallel partial of ds4f_gpu_moe_prefill (no reference
+ * counterpart): the model's shard of the routed combine, plus the shared
+ * expert when add_shared, into acc_dev [T][H]; states_dev is read only.
+ * Summing acc over a partition of the experts and adding it to the states
+ * completes the layer. */
+int  ds4f_gpu_moe_prefill_partial(Ds4fGpuModel *m, int layer, const float *states_dev, int T,
+                                  const int *sel_dev, const float *w_dev, float *acc_dev,
+                                  int add_shared, void *stream);
 /* Every layer in order: sel_dev / w_dev [n_layers][T][K]. */
 int  ds4f_gpu_prefill(Ds4fGpuModel *m, float *states_dev, int T, const int *sel_dev,
                       const float *w_dev, void *stream);

@@ -100,3 +100,73 @@ def test_expert_parallel_decode_two_ranks_matches_single_host():
             want[b], _, _, _, _ = lay.moe(want[b], K)
     err = np.abs(got0 - want).max() / np.abs(want).max()
     assert err < TOL, err
+
+
+# ---- expert-parallel prefill ------------------------------------------------
+
+T_PF = 6
+
+
+class OraclePrefillShard:
+    """Per-rank partial of the batched step, from the oracle's reference
+    batched step (orc_moe_batch_sel): the shard's selections (others -1),
+    minus the shared expert's part on ranks other than 0."""
+
+    def __init__(self, layers, first, count):
+        self.layers, self.first, self.count = layers, first, count
+        self.n_layers, self.hidden = len(layers), H
+
+    def prefill_partial(self, L, states, sel, w, acc, add_shared, stream=None):
+        lay = self.layers[L]
+        st = states.numpy()
+        s = sel.numpy().copy()
+        s[(s < self.first) | (s >= self.first + self.count)] = -1
+        part = lay.moe_batch_sel(st, s, w.numpy()) - st
+        if not add_shared:
+            part = part - (lay.moe_batch_sel(st, np.full_like(s, -1), w.numpy()) - st)
+        acc.copy_(torch.from_numpy(part.astype(np.float32)))
+
+
+def _routing_pf():
+    rng = np.random.default_rng(5)
+    sel = np.stack([np.stack([rng.choice(E, K, replace=False) for _ in range(T_PF)]) for _ in range(NL)])
+    w = rng.random((NL, T_PF, K)).astype(np.float32)
+    w /= w.sum(-1, keepdims=True)
+    return sel.astype(np.int32), w.astype(np.float32)
+
+
+def _rank_pf(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ep = _ep_module()
+    first, count = ep.shard_of(rank, world, E)
+    pf = ep.ExpertParallelPrefill(OraclePrefillShard(_layers(), first, count))
+    st = torch.from_numpy(po.fill_f32(T_PF * H, po.key(4, 0, 4, 0, 0), 1.0).reshape(T_PF, H).copy())
+    sel, w = _routing_pf()
+    pf.step(st, torch.from_numpy(sel), torch.from_numpy(w))
+    out[rank] = st.numpy().copy()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_prefill_two_ranks_matches_single_host():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    procs = [ctx.Process(target=_rank_pf, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    assert np.array_equal(out[0], out[1])
+    want = po.fill_f32(T_PF * H, po.key(4, 0, 4, 0, 0), 1.0).reshape(T_PF, H).copy()
+    sel, w = _routing_pf()
+    for L, lay in enumerate(_layers()):
+        want = lay.moe_batch_sel(want, sel[L], w[L])
+    err = np.abs(out[0] - want).max() / np.abs(want).max()
+    assert err < TOL, err

@@ -91,3 +91,76 @@ def test_expert_parallel_two_gpus(fmt):
     m.close()
     err = np.abs(out[0] - want).max() / np.abs(want - x0).max()
     assert err < REASSOC_TOL, err
+
+
+# ---- expert-parallel prefill ------------------------------------------------
+
+T_PF = 96
+
+
+def _routing_pf():
+    rng = np.random.default_rng(7)
+    sel = np.stack([np.stack([rng.choice(E, K, replace=False) for _ in range(T_PF)]) for _ in range(NL)])
+    w = rng.random((NL, T_PF, K)).astype(np.float32)
+    w /= w.sum(-1, keepdims=True)
+    return sel.astype(np.int32), w.astype(np.float32)
+
+
+def _x0_pf():
+    return po.fill_f32(T_PF * H, po.key(23, 0, 4, 0, 0), 1.0).reshape(T_PF, H).copy()
+
+
+def _rank_pf(rank, world, port, out):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    dc = ds4f_cuda()
+    dc.init()
+    ep = _ep_module()
+    shard = ep.GpuShard(dc, 2, NL, H, M, E, K, rank, world, seed=23)
+    pf = ep.ExpertParallelPrefill(shard)
+    sel, w = _routing_pf()
+    st = torch.from_numpy(_x0_pf()).cuda()
+    pf.step(st, torch.from_numpy(sel).cuda(), torch.from_numpy(w).cuda(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    out[rank] = st.cpu().numpy()
+    shard.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_prefill_two_gpus():
+    import socket
+    import torch
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    procs = [ctx.Process(target=_rank_pf, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    assert np.array_equal(out[0], out[1])
+    dc = ds4f_cuda()
+    dc.init()
+    m = dc.Model(2, NL, H, M, E, K)
+    m.synth(23)
+    sel, w = _routing_pf()
+    x0 = _x0_pf()
+    st = torch.from_numpy(x0.copy()).cuda()
+    m.prefill_dev(st, torch.from_numpy(sel).cuda(), torch.from_numpy(w).cuda())
+    want = st.cpu().numpy()
+    m.close()
+    err = np.abs(out[0] - want).max() / np.abs(want - x0).max()
+    assert err < REASSOC_TOL, err
