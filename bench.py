@@ -256,6 +256,39 @@ def cpu_reference_sample(seconds=12.0, threads=8):
                    "nproc": os.cpu_count()}
 
 
+def cpu_matvec_sample(seconds=4.0):
+    """The reference's own ds4f_f8_matvec (oracle/_ref, AVX2; E8M0 block
+    scales, the reference's FP8 scale format, same work per element) over the
+    24 config-1 matvecs, one thread as the reference runs one matvec: GB/s."""
+    import numpy as np
+    from oracle import pyoracle as po
+    R_ = po.ref()
+    rng = np.random.default_rng(0)
+    canon = np.array([b for b in range(256) if (b >> 3) & 15 != 15], np.uint8)
+    mats = []
+    for e in range(8):
+        for (r, c) in ((M, H), (M, H), (H, M)):
+            w = canon[rng.integers(0, len(canon), r * c)].reshape(r, c)
+            sc = rng.integers(112, 120, (r // 128) * (c // 128), dtype=np.uint16).astype(np.uint8)
+            mats.append((w, sc, r, c, po.fill_f32(c, po.key(1, 0, 4, e, 0), 1.0), np.zeros(r, np.float32)))
+    if R_ is not None:
+        R_.ds4f_kernels_set_simd(1)
+    nbytes = sum(w.nbytes + sc.nbytes for w, sc, _, _, _, _ in mats)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 1:
+        for w, sc, r, c, x, y in mats:
+            if R_ is not None:
+                R_.ds4f_f8_matvec(po.ptr(w), po.ptr(sc), r, c, r // 128, c // 128, po.ptr(x), po.ptr(y))
+            else:
+                po.lib().orc_f8_matvec(po.ptr(w), 0, po.ptr(sc), r, c, r // 128, c // 128, po.ptr(x), po.ptr(y))
+        n += 1
+    dt = time.perf_counter() - t0
+    return n * nbytes / dt / 1e9, {"cores": 1, "kind": "reference" if R_ is not None else "port",
+                                   "sample": f"{n} passes over the 24 config-1 FP8 matvecs in {dt:.1f} s "
+                                             f"({'reference AVX2' if R_ is not None else 'scalar port'}, one thread)",
+                                   "nproc": os.cpu_count()}
+
+
 # ---- GPU arm ------------------------------------------------------------------
 
 def run_gpu(args, rank, world, local_rank):
@@ -682,6 +715,85 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
     return res
 
 
+# ---- config 1: dequant-matvec microbench ------------------------------------------
+
+def run_gpu_matvec(args, rank, world, local_rank):
+    """8 experts x (gate 512x2048, up 512x2048, down 2048x512) as one job list
+    per format (FP8 with fp32 128x128 scales; MXFP4), x ~ N(0, 1), batch 1.
+    Sixteen copies of the 24 matrices are rotated (a 16 x 38 MB working set,
+    larger than L2; a plain flush by copying 256 MB did not evict them here),
+    and each launch is timed alone with CUDA events."""
+    import numpy as np
+    import torch
+    from oracle import pyoracle as po
+    from tests._lib import ds4f_cuda
+    dc = ds4f_cuda()
+    torch.cuda.set_device(local_rank)
+    dc.init()
+    NSET = 16                     # distinct copies, rotated: 16 x 38 MB, every launch misses L2
+    keep, jobs = [], {"fp8": [[] for _ in range(NSET)], "mxfp4": [[] for _ in range(NSET)]}
+    bytes_fmt = {"fp8": 0, "mxfp4": 0}
+    for e in range(8):
+        for t, (R, Cc) in enumerate(((M, H), (M, H), (H, M))):
+            k = po.key(1, 0, 3, e, t)
+            x = po.fill_f32(Cc, po.key(1, 0, 4, e, t), 1.0)
+            W, s = po.quant_fp8(R, Cc, k, 0.02)
+            v, sm = po.quant_mxfp4(R, Cc, k, 0.02)
+            tx = torch.from_numpy(x).cuda()
+            y8 = torch.zeros(R, device="cuda")
+            ym = torch.zeros(R, device="cuda")
+            keep += [tx, y8, ym]
+            for c in range(NSET):
+                tW, ts, tv, tsm = (torch.from_numpy(a).cuda() for a in (W, s, v, sm))
+                keep += [tW, ts, tv, tsm]
+                jobs["fp8"][c].append(dc.Ds4fMvJob(tW.data_ptr(), ts.data_ptr(), tx.data_ptr(), y8.data_ptr(),
+                                                   R, Cc, R // 128, Cc // 128, dc.FMT_FP8, dc.SCALE_F32, 32, 1))
+                jobs["mxfp4"][c].append(dc.Ds4fMvJob(tv.data_ptr(), tsm.data_ptr(), tx.data_ptr(), ym.data_ptr(),
+                                                     R, Cc, 1, 1, dc.FMT_MXFP4, 0, 32, 0))
+            bytes_fmt["fp8"] += W.nbytes + s.nbytes
+            bytes_fmt["mxfp4"] += v.nbytes + sm.nbytes
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = {}
+    for fmt in ("fp8", "mxfp4"):
+        plans = [dc.MvPlan(j) for j in jobs[fmt]]
+        for i in range(max(args.warmup, NSET)):
+            plans[i % NSET].run(sp)
+        torch.cuda.synchronize()
+        clk = Clocks(local_rank) if fmt == "fp8" else None
+        ts = []
+        for i in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            plans[i % NSET].run(sp)
+            e1.record()
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        clocks = clk.stop() if clk else None
+        ms = sum(a.elapsed_time(b) for a, b in ts) / args.steps
+        out[fmt] = (ms, bytes_fmt[fmt] / (ms / 1e3) / 1e9, clocks)
+        del plans
+    # e2e: host vectors in (24 x), outputs out, through the per-matvec C calls
+    peak, src = peaks()
+    ms8, gbs8, clocks = out["fp8"]
+    msm, gbsm, _ = out["mxfp4"]
+    return {
+        "metric": "expert dequant-matvec HBM GB/s (8 experts x gate/up/down, FP8 128x128 fp32 scales)",
+        "value": round(gbs8, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms8, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8-e4m3 weights, fp32 x and accumulate", "data": "synthetic (seeded, N(0,0.02) weights)",
+        "config": {"workload": "config 1: 24 matvecs (8 x 512x2048, 8 x 512x2048, 8 x 2048x512), batch 1",
+                   "l2": "16 copies of the weights rotated (608 MB working set > 126 MB L2)",
+                   "mxfp4": {"gb_s": round(gbsm, 1), "ms_per_step": round(msm, 4),
+                             "frac": round(gbsm / peak, 4), "bytes": bytes_fmt["mxfp4"]}},
+        "roofline": {"bound": "hbm", "achieved": round(gbs8, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs8 / peak, 4), "traffic": None, "peak_source": src,
+                     "algorithmic_bytes_per_step": bytes_fmt["fp8"]},
+        "gpu_launches": args.steps * 1,
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -691,7 +803,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--layered", action="store_true",
                     help="per-layer kernels (CUDA graph) instead of the persistent kernel")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep-decode", "ep-prefill"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "ep-decode", "ep-prefill", "matvec"],
                     help="decode: config 2 (the headline); prefill: config 4; ep-decode: config 3 "
                          "(experts sharded over the ranks)")
     ap.add_argument("--fmt", default=None, choices=["fp8", "mxfp4"],
@@ -726,10 +839,13 @@ def main():
     if args.fmt is None:
         args.fmt = "mxfp4" if args.workload == "ep-decode" else "fp8"
     fn = {"prefill": run_gpu_prefill, "ep-decode": run_gpu_ep,
-          "ep-prefill": run_gpu_ep_prefill}.get(args.workload, run_gpu)
+          "ep-prefill": run_gpu_ep_prefill, "matvec": run_gpu_matvec}.get(args.workload, run_gpu)
     res = fn(args, rank, world, local_rank)
     if rank == 0:
-        if world == 1:
+        if world == 1 and args.workload == "matvec":
+            v, desc = cpu_matvec_sample(args.cpu_seconds)
+            res["cpu_baseline"] = dict(desc, value=round(v, 4), unit="GB/s")
+        elif world == 1:
             v, desc = cpu_reference_sample(args.cpu_seconds)
             res["cpu_baseline"] = dict(desc, value=round(v, 4), unit="tok/s")
         print(json.dumps(res))

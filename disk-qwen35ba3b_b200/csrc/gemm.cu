@@ -127,8 +127,9 @@ struct GemmSmem {
     static constexpr int B = NM * 128;
     static constexpr int STAGE = A + B;
     static constexpr int o_bar = kStages * STAGE;     // full[S], empty[S], tfull[2], tempty[2], done
-    static constexpr int o_slot = o_bar + (2 * kStages + 5) * 8;
-    static constexpr int o_sx = o_slot + 16;
+    static constexpr int o_slot = o_bar + ((2 * kStages + 5) * 8 + 127) / 128 * 128;
+    static_assert((2 * kStages + 5) * 8 <= 128, "barriers fit their 128 bytes");
+    static constexpr int o_sx = o_slot + 16;                           // 16-byte aligned: float4 reads
     static constexpr int bytes(int kb) { return o_sx + (BF ? 0 : kGemmBN * kb * 4) + 1024; }
     static constexpr uint32_t NCOLS = 2 * NM <= 32 ? 32 : 2 * NM <= 64 ? 64 : 2 * NM <= 128 ? 128
                                     : 2 * NM <= 256 ? 256 : 512;
@@ -138,11 +139,13 @@ struct GemmSmem {
 };
 
 // Epilogue of one K block for columns [c0, c0 + 32): combine the digit
-// columns of column n (n, 64 + n, 128 + n) and add into acc[n - c0] with the
-// block's scales. The digit loads of 16 columns share one wait.
+// columns of column n (n, 64 + n, 128 + n) as fma(D2, 2^-8, fma(D1, 2^-4,
+// D0)) -- the same roundings as adding the exactly scaled digits -- and add
+// into acc[n - c0] with the block's scales (sxk: the activation scales of
+// this block, [column]); packed fp32 (FFMA2) for the accumulation. The digit
+// loads of 16 columns share one wait.
 template <int ND, bool BF>
-__device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxt, int KB, int kb, float w,
-                                        float (&acc)[32]) {
+__device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxk, float w, float2 (&acc)[16]) {
     constexpr int BN = kGemmBN;
 #pragma unroll
     for (int c = 0; c < 2; c++) {
@@ -151,19 +154,33 @@ __device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxt, in
         tc::tmem_ld16_nowait(t + col, r[0]);
         if (ND > 1) tc::tmem_ld16_nowait(t + BN + col, r[1]);
         if (ND > 2) tc::tmem_ld16_nowait(t + 2 * BN + col, r[2]);
+        float sc[16];
+        if (!BF) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                const float4 s4 = *(const float4 *)(sxk + col + i);
+                sc[i] = __fmul_rn(w, s4.x); sc[i + 1] = __fmul_rn(w, s4.y);
+                sc[i + 2] = __fmul_rn(w, s4.z); sc[i + 3] = __fmul_rn(w, s4.w);
+            }
+        }
         tc::tmem_wait_ld();
         tc::tmem_regs_ready(r[0]);
         if (ND > 1) tc::tmem_regs_ready(r[1]);
         if (ND > 2) tc::tmem_regs_ready(r[2]);
+        float v[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-            float v = __uint_as_float(r[0][i]);
-            if (ND > 1) v = BF ? __fadd_rn(v, __uint_as_float(r[1][i])) : __fadd_rn(v, __fmul_rn(__uint_as_float(r[1][i]), 0.0625f));
-            if (ND > 2) v = __fadd_rn(v, __fmul_rn(__uint_as_float(r[2][i]), 0.00390625f));
+            v[i] = __uint_as_float(r[0][i]);
+            if (ND > 1) v[i] = BF ? __fadd_rn(v[i], __uint_as_float(r[1][i])) : fmaf(__uint_as_float(r[1][i]), 0.0625f, v[i]);
+            if (ND > 2) v[i] = fmaf(__uint_as_float(r[2][i]), 0.00390625f, v[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+            float2 &a2 = acc[(c * 16 + i) >> 1];
             if (BF)
-                acc[c * 16 + i] = __fadd_rn(acc[c * 16 + i], v);
+                a2 = __fadd2_rn(a2, make_float2(v[i], v[i + 1]));
             else
-                acc[c * 16 + i] = fmaf(v, __fmul_rn(w, sxt[(col + i) * KB + kb]), acc[c * 16 + i]);
+                a2 = __ffma2_rn(make_float2(v[i], v[i + 1]), make_float2(sc[i], sc[i + 1]), a2);
         }
     }
 }
@@ -204,9 +221,9 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         tc::prefetch_tmap(&tW);
         tc::prefetch_tmap(&tX);
     }
-    if (!BF)
+    if (!BF)      // the activation scales, stored [kb][column]
         for (int i = tid - 64; i >= 0 && i < BN * KB; i += 32 * kEpiWarps)
-            sxt[i] = i / KB < nv ? g.sX[(int64_t)(n0 + i / KB) * KB + i % KB] : 0.f;
+            sxt[(i % KB) * BN + i / KB] = i / KB < nv ? g.sX[(int64_t)(n0 + i / KB) * KB + i % KB] : 0.f;
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -257,14 +274,14 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows;
         // the two warps of a quadrant take columns [0, 32) and [32, 64)
         const int q = warp & 3, c0 = ((warp - 2) >> 2) * 32, row = q * 32 + lane;
-        float acc[32];
+        float2 acc[16];
 #pragma unroll
-        for (int j = 0; j < 32; j++) acc[j] = 0.f;
+        for (int j = 0; j < 16; j++) acc[j] = make_float2(0.f, 0.f);
         const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
         if (BF) {
             if (tc::mbar_wait(tfull, 0, err, 6)) {
                 tc::fence_after_sync();
-                promote<ND, BF>(tq, c0, sxt, KB, 0, 1.f, acc);
+                promote<ND, BF>(tq, c0, sxt, 1.f, acc);
             }
         } else {
             const float *swr = g.sW + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
@@ -272,7 +289,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
                 const int b = kb & 1;
                 if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
                 tc::fence_after_sync();
-                promote<ND, BF>(tq + b * L::NM, c0, sxt, KB, kb, swr[kb], acc);
+                promote<ND, BF>(tq + b * L::NM, c0, sxt + kb * BN, swr[kb], acc);
                 tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(tempty + b);
@@ -282,7 +299,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
             float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + g.ycol0 + r0 + row;
 #pragma unroll
             for (int j = 0; j < 32; j++)
-                if (c0 + j < nv) y[(int64_t)j * g.ldy] = acc[j];
+                if (c0 + j < nv) y[(int64_t)j * g.ldy] = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
         }
     }
     tc::fence_before_sync();
