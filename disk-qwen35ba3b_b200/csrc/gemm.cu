@@ -187,7 +187,8 @@ __device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxk, fl
 
 template <int ND, bool BF>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tX, GemmArgs g) {
+k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tW2,
+       const __grid_constant__ CUtensorMap tX, GemmArgs g) {
     using L = GemmSmem<ND, BF>;
     constexpr int BN = kGemmBN;
     extern __shared__ uint8_t smem_raw[];
@@ -209,7 +210,11 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         nv = min(BN, g.N - n0);
     }
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int r0 = blockIdx.x * 128, KB = g.KB;
+    // row tile: blockIdx.x over the first A matrix's R / 128 tiles, then the
+    // second's
+    const int MT = g.R / 128, mat = blockIdx.x / MT;
+    const int r0 = (blockIdx.x % MT) * 128, KB = g.KB;
+    const CUtensorMap *tA = mat ? &tW2 : &tW;
     unsigned *err = g.err;
 
     if (warp == 1) tc::tmem_alloc(slot, L::NCOLS);
@@ -218,7 +223,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, kEpiWarps); }
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
-        tc::prefetch_tmap(&tW);
+        tc::prefetch_tmap(tA);
         tc::prefetch_tmap(&tX);
     }
     if (!BF)      // the activation scales, stored [kb][column]
@@ -237,7 +242,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
                 if (kb >= kStages && !tc::mbar_wait(empty + s, ((kb / kStages) - 1) & 1, err, 1)) break;
                 uint8_t *a = sm + s * L::STAGE;
                 tc::mbar_expect(full + s, L::STAGE);
-                tc::tma_load_3d(a, &tW, kb * 128, r0, zs, full + s);
+                tc::tma_load_3d(a, tA, kb * 128, r0, zs, full + s);
                 tc::tma_load_3d(a + L::A, &tX, kb * 128, n0, 0, full + s);
             }
             // every issued load has landed before the CTA may exit
@@ -284,7 +289,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
                 promote<ND, BF>(tq, c0, sxt, 1.f, acc);
             }
         } else {
-            const float *swr = g.sW + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
+            const float *swr = (mat ? g.sW2 : g.sW) + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
             for (int kb = 0; kb < KB; kb++) {
                 const int b = kb & 1;
                 if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
@@ -296,7 +301,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
             }
         }
         if (r0 + row < g.R) {
-            float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + g.ycol0 + r0 + row;
+            float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + (mat ? g.ycol2 : g.ycol0) + r0 + row;
 #pragma unroll
             for (int j = 0; j < 32; j++)
                 if (c0 + j < nv) y[(int64_t)j * g.ldy] = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
@@ -317,15 +322,16 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
 // grouped mode's CTAs past *g.ntiles return at once).
 template <int ND, bool BF>
 int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
-                GemmArgs g, int ntiles_max, cudaStream_t st) {
+                GemmArgs g, int ntiles_max, cudaStream_t st, const void *A2) {
     using L = GemmSmem<ND, BF>;
     const int es = BF ? 2 : 1;
     if (g.R <= 0 || g.C <= 0 || g.R % 128 || (g.C * es) % 128 || ntiles_max <= 0) {
         set_error("gemm: R and C bytes must be positive multiples of 128");
         return -1;
     }
-    CUtensorMap tW, tX;
+    CUtensorMap tW, tW2, tX;
     if (tmap_u8_3d(&tW, A, (uint64_t)g.C * es, g.R, slots, (uint64_t)g.C * es, slot_stride, 128, 1) ||
+        tmap_u8_3d(&tW2, A2 ? A2 : A, (uint64_t)g.C * es, g.R, slots, (uint64_t)g.C * es, slot_stride, 128, 1) ||
         tmap_u8_3d(&tX, X, (uint64_t)g.C * es, xrows, ND, (uint64_t)g.C * es, (uint64_t)xrows * g.C * es,
                    kGemmBN, ND))
         return -1;
@@ -337,15 +343,15 @@ int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X
         DS4F_CUDA(cudaFuncSetAttribute(k_gemm<ND, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr = true;
     }
-    dim3 grid(g.R / 128, ntiles_max);
-    k_gemm<ND, BF><<<grid, kGemmThreads, smem, st>>>(tW, tX, g);
+    dim3 grid((g.R / 128) * (A2 ? 2 : 1), ntiles_max);
+    k_gemm<ND, BF><<<grid, kGemmThreads, smem, st>>>(tW, tW2, tX, g);
     DS4F_CUDA(cudaGetLastError());
     return 0;
 }
 template int gemm_launch<3, false>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
-                                   cudaStream_t);
+                                   cudaStream_t, const void *);
 template int gemm_launch<2, true>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
-                                  cudaStream_t);
+                                  cudaStream_t, const void *);
 
 int f8_gemm_launch(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
                    int R, int C, int N, int ND, unsigned *err, cudaStream_t st) {

@@ -12,6 +12,8 @@ constexpr int kGemmBN = 64;                // B columns (tokens) per tile
 
 struct GemmArgs {
     const float *sW;          // FP8: scales of slot 0, [R/128][KB] floats
+    const float *sW2;         // the second A matrix's (gemm_launch with A2)
+    int ycol2;                // the second A matrix's output column offset
     int64_t sw_slot;          // floats between consecutive slots' scales
     const float *sX;          // FP8: [rows][KB] activation scales
     float *Y;                 // Y[(first row + n) * ldy + ycol0 + r]
@@ -26,9 +28,12 @@ struct GemmArgs {
 // A: slots x [R][C] elements (FP8 bytes, or bf16 when BF), `slot_stride`
 // bytes apart; X: ND digit planes [xrows][C]. The grid has `ntiles_max` tile
 // rows (grouped: CTAs past *g.ntiles return at once).
+// A2 (optional): a second A matrix of the same shape and slots (the up
+// projection beside the gate), computed in the same launch into columns
+// ycol2 + r of Y with scales sW2.
 template <int ND, bool BF>
 int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
-                GemmArgs g, int ntiles_max, cudaStream_t st);
+                GemmArgs g, int ntiles_max, cudaStream_t st, const void *A2 = nullptr);
 
 int quant_f8_digits_launch(const float *x, int N, int C, int ND, uint8_t *q, float *s, cudaStream_t st);
 

@@ -311,14 +311,15 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     k_gather<<<(unsigned)((R * kND * 32 + 255) / 256), 256, 0, st>>>(ws.Xq, ws.sx, ws.src, ws.nrows, K, T, H,
                                                                     ws.Xg, ws.sxg, (int)R);
     // 3: gate, up, SiLU digits, down
-    for (int mat = 0; mat < 2; mat++) {
+    {   // gate and up in one launch
         GemmArgs g{};
-        g.sW = (const float *)(m->pool + m->slot.rel_s[mat]);
+        g.sW = (const float *)(m->pool + m->slot.rel_s[0]);
+        g.sW2 = (const float *)(m->pool + m->slot.rel_s[1]);
         g.sw_slot = m->slot.nbytes / 4;
-        g.sX = ws.sxg; g.Y = ws.GU; g.ldy = 2 * M; g.ycol0 = mat * M;
+        g.sX = ws.sxg; g.Y = ws.GU; g.ldy = 2 * M; g.ycol0 = 0; g.ycol2 = M;
         g.R = M; g.C = H; g.tiles = ws.tiles; g.ntiles = ws.ntiles; g.err = ws.err;
-        if (gemm_launch<kND, false>(m->pool + m->slot.rel_v[mat], total_slots, m->slot.nbytes, ws.Xg, R, g,
-                                    ws.tiles_max, st))
+        if (gemm_launch<kND, false>(m->pool + m->slot.rel_v[0], total_slots, m->slot.nbytes, ws.Xg, R, g,
+                                    ws.tiles_max, st, m->pool + m->slot.rel_v[1]))
             return -1;
     }
     k_silu_digits<<<(unsigned)((R * (M / 128) * 32 + 255) / 256), 256, 0, st>>>(ws.GU, M, ws.nrows, ws.Cq,
@@ -337,11 +338,11 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     if (add_shared) {
     k_bf16_digits<<<(unsigned)(((int64_t)T * H + 255) / 256), 256, 0, st>>>(ws.xin, (int64_t)T * H, ws.Xb);
     const int ntd = (T + kGemmBN - 1) / kGemmBN;
-    for (int mat = 0; mat < 2; mat++) {
+    {   // shared gate and up in one launch
         GemmArgs g{};
-        g.Y = ws.GS; g.ldy = 2 * M; g.ycol0 = mat * M; g.R = M; g.C = H; g.N = T; g.err = ws.err;
-        if (gemm_launch<2, true>(tl + (mat ? m->tr.sh_up : m->tr.sh_gate), 1, (int64_t)M * H * 2, ws.Xb, T, g,
-                                 ntd, st))
+        g.Y = ws.GS; g.ldy = 2 * M; g.ycol0 = 0; g.ycol2 = M; g.R = M; g.C = H; g.N = T; g.err = ws.err;
+        if (gemm_launch<2, true>(tl + m->tr.sh_gate, 1, (int64_t)M * H * 2, ws.Xb, T, g, ntd, st,
+                                 tl + m->tr.sh_up))
             return -1;
     }
     k_silu_bf16_digits<<<(unsigned)(((int64_t)T * M + 255) / 256), 256, 0, st>>>(ws.GS, M, T, ws.Cb);
