@@ -428,7 +428,8 @@ def run_gpu_prefill(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     T = T_PREFILL
-    model = dc.Model(dc.FMT_FP8, LAYERS, H, M, E, K)
+    fp8 = args.fmt != "mxfp4"
+    model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, LAYERS, H, M, E, K)
     model.synth(0)
     sel, w = zipf_routing(LAYERS, T, E, K, seed=100 + rank)
     selg = torch.from_numpy(sel).cuda()
@@ -483,7 +484,9 @@ def run_gpu_prefill(args, rank, world, local_rank):
         # algorithmic work: the weights of every expert a layer's tokens touch
         # (read once), the shared expert and norm, plus FLOPs 2 * rows * K * R
         uniq = [len(np.unique(sel[L])) for L in range(LAYERS)]
-        slot = 3 * (M * H + (M // 128) * (H // 128) * 4)
+        # algorithmic bytes: every touched expert once in the pool's own format
+        # (the MXFP4 path streams its exact FP8 copy: 2x these bytes)
+        slot = 3 * (M * H + (M // 128) * (H // 128) * 4) if fp8 else 3 * (M * H // 2 + M * H // 32)
         bytes_step = sum(u * slot + 3 * M * H * 2 + 2 * H * 2 for u in uniq)
         flops_step = LAYERS * (2 * T * K * 3 * M * H + 2 * T * 3 * M * H)
         peak, src = peaks()
@@ -491,12 +494,14 @@ def run_gpu_prefill(args, rank, world, local_rank):
         tf = flops_step / (ms / 1e3) / 1e12
         loads = np.bincount(sel[0].ravel(), minlength=E)
         res = {
-            "metric": METRIC_PREFILL, "value": round(world * T * args.steps / (t_ms / 1e3), 1),
+            "metric": METRIC_PREFILL if fp8 else METRIC_PREFILL.replace("FP8", "MXFP4"),
+            "value": round(world * T * args.steps / (t_ms / 1e3), 1),
             "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp8-e4m3 weights x 3-digit e4m3 activations, fp32 accumulate (tcgen05)",
+            "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (as its exact fp8 copy)") +
+                     " weights x 3-digit e4m3 activations, fp32 accumulate (tcgen05)",
             "data": "synthetic (seeded weights, bf16 N(0,1) activations, Zipf(1.1) routing)",
-            "config": {"workload": "config 4: prefill of a 2048-token chunk, 40-layer FP8",
+            "config": {"workload": f"config 4: prefill of a 2048-token chunk, 40-layer {'FP8' if fp8 else 'MXFP4'}",
                        "tokens": T, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
                        "max_tokens_per_expert_L0": int(loads.max()),
                        "median_tokens_per_expert_L0": float(np.median(loads)),

@@ -461,6 +461,7 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (m.graph) cudaGraphExecDestroy(m.graph);
     if (m.trace) cudaFree(m.trace);
     if (m.pf_ws) cudaFree(m.pf_ws);
+    if (m.pf8) cudaFree(m.pf8);
     cudaFree(m.pool);
     cudaFree(m.trunk);
     cudaFree(m.ws_base);

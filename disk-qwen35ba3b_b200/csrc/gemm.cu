@@ -289,7 +289,8 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
                 promote<ND, BF>(tq, c0, sxt, 1.f, acc);
             }
         } else {
-            const float *swr = (mat ? g.sW2 : g.sW) + zs * g.sw_slot + (int64_t)(r0 / 128) * KB;
+            const float *swr = (mat ? g.sW2 : g.sW) + zs * g.sw_slot +
+                               (g.row_scales ? (int64_t)(r0 + row) * KB : (int64_t)(r0 / 128) * KB);
             for (int kb = 0; kb < KB; kb++) {
                 const int b = kb & 1;
                 if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;

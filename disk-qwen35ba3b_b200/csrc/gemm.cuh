@@ -19,6 +19,8 @@ struct GemmArgs {
     float *Y;                 // Y[(first row + n) * ldy + ycol0 + r]
     int64_t ldy;
     int ycol0, R, C, KB;      // KB: K blocks of 128 bytes (set by gemm_launch)
+    int row_scales;           // 1: sW holds a scale per (row, K block) (an MXFP4
+                              //    pool's FP8 copy), [R][KB]; 0: per 128x128 block
     const int *tiles;         // grouped: [*ntiles][3] = slot, first B row, valid rows
     const int *ntiles;
     int N;                    // dense: B rows

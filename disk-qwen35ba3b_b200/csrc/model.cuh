@@ -72,6 +72,8 @@ struct Model {
     int epoch;                   // last persistent launch's tag epoch
     void *pf_ws;                 // batched-prefill workspace (prefill.cu), grown on demand
     size_t pf_bytes;
+    uint8_t *pf8;                // MXFP4 models: the pool's exact FP8 copy for the
+    SlotLayout slot8;            //   tensor-core prefill (row scales), built on first use
 };
 
 int slot_layout(int fmt, int H, int M, SlotLayout *s);

@@ -20,14 +20,19 @@ int orc_f8_gemm_digits(const uint8_t *W, const float *sW, const uint8_t *X, cons
                        int R, int C, int N, int ND);
 
 /* One layer of the GPU batched prefill (prefill.cu / ds4f_gpu_moe_prefill),
- * restated: the same quantisation points (3 E4M3 digits per routed
+ * restated (FP8 pools, or MXFP4 pools through their exact FP8 copy): the
+ * same quantisation points (3 E4M3 digits per routed
  * activation and chain element, bf16 hi/lo digits in the shared expert),
  * block sums in double, promotion, combine and residual in the GPU's fp32
  * order. states [T][H] in/out; sel / w [T][K] (sel < 0: skipped). */
 struct OrcLayerW;
 struct OrcExpertLayout;
-int orc_prefill_layer(int H, int M, int K, const struct OrcLayerW *lw, const struct OrcExpertLayout *lay,
-                      int T, float *states, const int *sel, const float *w);
+int orc_prefill_layer(int fmt, int H, int M, int K, const struct OrcLayerW *lw,
+                      const struct OrcExpertLayout *lay, int T, float *states, const int *sel, const float *w);
+
+/* An MXFP4 matrix as the GPU prefill's exact FP8 copy (bytes [R][C], row
+ * scales [R][C/128]); returns the count of elements not exact in E4M3. */
+int orc_mxfp4_to_f8rows(const uint8_t *vals, const uint8_t *sc, int R, int C, uint8_t *q, float *s);
 
 #ifdef __cplusplus
 }

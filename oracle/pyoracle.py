@@ -116,7 +116,8 @@ def lib():
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_shared_add.argtypes = [C.POINTER(OrcLayerW), C.c_int, C.c_int, C.c_void_p, C.c_void_p]
-        L.orc_prefill_layer.argtypes = [C.c_int] * 3 + [
+        L.orc_mxfp4_to_f8rows.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.orc_prefill_layer.argtypes = [C.c_int] * 4 + [
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_f8_gemm_digits.argtypes = [C.c_void_p] * 5 + [C.c_int] * 4
@@ -337,7 +338,7 @@ def _layer_prefill(self, states, sel, w):
     sel = np.ascontiguousarray(sel, np.int32)
     w = np.ascontiguousarray(w, np.float32)
     lw = self.w()
-    if lib().orc_prefill_layer(self.H, self.M, sel.shape[1], C.byref(lw), C.byref(self.lay), st.shape[0],
+    if lib().orc_prefill_layer(self.fmt, self.H, self.M, sel.shape[1], C.byref(lw), C.byref(self.lay), st.shape[0],
                                ptr(st), ptr(sel), ptr(w)) != 0:
         raise RuntimeError("orc_prefill_layer failed")
     return st
@@ -369,3 +370,13 @@ def f8_gemm_digits(W, sW, q, sx):
     Y = np.zeros((N, R), np.float64)
     assert lib().orc_f8_gemm_digits(ptr(W), ptr(sW), ptr(q), ptr(sx), ptr(Y), R, Cc, N, nd) == 0
     return Y
+
+
+def mxfp4_to_f8rows(vals, scales, R, Cc):
+    """An MXFP4 matrix as the GPU prefill's exact FP8 copy: (bytes [R][C],
+    row scales [R][C/128], count of inexact elements)."""
+    q = np.zeros((R, Cc), np.uint8)
+    s = np.zeros((R, Cc // 128), np.float32)
+    bad = lib().orc_mxfp4_to_f8rows(ptr(np.ascontiguousarray(vals, np.uint8)),
+                                    ptr(np.ascontiguousarray(scales, np.uint8)), R, Cc, ptr(q), ptr(s))
+    return q, s, bad
