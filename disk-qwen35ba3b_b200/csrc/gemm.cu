@@ -116,8 +116,9 @@ __global__ void k_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t 
 // [ND][rows][C]. Dense mode: tile = blockIdx.y, rows n0 = 64 blockIdx.y,
 // slot 0. Grouped mode: tile t = blockIdx.y < *ntiles names (slot, first B
 // row, valid rows) -- the experts' token groups of the batched prefill.
-constexpr int kStages = 4;
-constexpr int kEpiWarps = 8;               // two per TMEM lane quadrant, 32 columns each
+constexpr int kStages = 5;               // 5 x 40 KB in flight per SM (3 digits)
+constexpr int kEpiWarps = 16;              // four per TMEM lane quadrant, 16 columns each
+constexpr int kEpiCols = kGemmBN / (kEpiWarps / 4);
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2.. epilogue
 
 template <int ND, bool BF>
@@ -138,17 +139,18 @@ struct GemmSmem {
     static_assert(NM % 16 == 0 && NM <= 256 && 2 * NM <= 512, "MMA N and TMEM columns");
 };
 
-// Epilogue of one K block for columns [c0, c0 + 32): combine the digit
+// Epilogue of one K block for columns [c0, c0 + kEpiCols): combine the digit
 // columns of column n (n, 64 + n, 128 + n) as fma(D2, 2^-8, fma(D1, 2^-4,
 // D0)) -- the same roundings as adding the exactly scaled digits -- and add
 // into acc[n - c0] with the block's scales (sxk: the activation scales of
 // this block, [column]); packed fp32 (FFMA2) for the accumulation. The digit
 // loads of 16 columns share one wait.
 template <int ND, bool BF>
-__device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxk, float w, float2 (&acc)[16]) {
+__device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxk, float w,
+                                        float2 (&acc)[kEpiCols / 2]) {
     constexpr int BN = kGemmBN;
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
+    for (int c = 0; c < kEpiCols / 16; c++) {
         const uint32_t col = c0 + c * 16;
         uint32_t r[3][16];
         tc::tmem_ld16_nowait(t + col, r[0]);
@@ -277,11 +279,11 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         }
     } else {
         // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows;
-        // the two warps of a quadrant take columns [0, 32) and [32, 64)
-        const int q = warp & 3, c0 = ((warp - 2) >> 2) * 32, row = q * 32 + lane;
-        float2 acc[16];
+        // the four warps of a quadrant take 16 columns each
+        const int q = warp & 3, c0 = ((warp - 2) >> 2) * kEpiCols, row = q * 32 + lane;
+        float2 acc[kEpiCols / 2];
 #pragma unroll
-        for (int j = 0; j < 16; j++) acc[j] = make_float2(0.f, 0.f);
+        for (int j = 0; j < kEpiCols / 2; j++) acc[j] = make_float2(0.f, 0.f);
         const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
         if (BF) {
             if (tc::mbar_wait(tfull, 0, err, 6)) {
@@ -304,7 +306,7 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         if (r0 + row < g.R) {
             float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + (mat ? g.ycol2 : g.ycol0) + r0 + row;
 #pragma unroll
-            for (int j = 0; j < 32; j++)
+            for (int j = 0; j < kEpiCols; j++)
                 if (c0 + j < nv) y[(int64_t)j * g.ldy] = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
         }
     }

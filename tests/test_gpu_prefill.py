@@ -67,7 +67,7 @@ def run_layer(m, L, states, sel, w):
 
 
 @pytest.mark.parametrize("fmt", [dc.FMT_FP8, dc.FMT_MXFP4])
-@pytest.mark.parametrize("shape", [(1024, 256, 64, 150), (2048, 512, 256, 20)])
+@pytest.mark.parametrize("shape", [(1024, 256, 64, 80), (2048, 512, 256, 20)])
 def test_prefill_layer_matches_oracle(shape, fmt):
     H, M, E, T = shape
     K = 8
