@@ -116,7 +116,7 @@ __global__ void k_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t 
 // [ND][rows][C]. Dense mode: tile = blockIdx.y, rows n0 = 64 blockIdx.y,
 // slot 0. Grouped mode: tile t = blockIdx.y < *ntiles names (slot, first B
 // row, valid rows) -- the experts' token groups of the batched prefill.
-constexpr int kStages = 5;               // 5 x 40 KB in flight per SM (3 digits)
+constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;              // four per TMEM lane quadrant, 16 columns each
 constexpr int kEpiCols = kGemmBN / (kEpiWarps / 4);
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2.. epilogue
