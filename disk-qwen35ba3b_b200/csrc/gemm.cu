@@ -318,6 +318,253 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
     }
 }
 
+// ---- persistent FP8 GEMM ------------------------------------------------------------
+// One CTA per SM walks the items (B tile t, A row tile m), item i = t RT + m,
+// i = blockIdx.x, + gridDim.x, ...; the load ring and the two TMEM buffers run
+// on across item boundaries, so the next item's first K blocks land while the
+// tensor core and the epilogue finish the current one (a CTA per item pays the
+// pipeline fill every time: the down projection has only 4 K blocks). Each
+// item loads and multiplies only its valid B rows rounded up to 16 (one tensor
+// map per width), so narrow expert groups do not stream 64 digit rows.
+constexpr int kPStages = 5;
+
+template <int ND>
+struct PSmem {
+    static constexpr int NMX = kGemmBN * ND;          // widest MMA N (one TMEM buffer)
+    static constexpr int A = 128 * 128;
+    static constexpr int STAGE = A + NMX * 128;
+    static constexpr int o_bar = kPStages * STAGE;    // full[S], empty[S], tfull[2], tempty[2], done
+    static constexpr int o_slot = o_bar + ((2 * kPStages + 5) * 8 + 127) / 128 * 128;
+    static constexpr int o_sx = o_slot + 16;          // two [kb][64] activation-scale tiles
+    static constexpr int bytes(int kb) { return o_sx + 2 * kGemmBN * kb * 4 + 1024; }
+    static_assert(STAGE % 1024 == 0 && 2 * NMX <= 512, "stage alignment and TMEM columns");
+};
+
+struct PItem { int zs, n0, nv, w, mat, r0; };
+
+// Item i of RT row tiles per B tile (MT per A matrix); false past the end.
+__device__ __forceinline__ bool p_item(const GemmArgs &g, int i, int n_items, int RT, int MT, PItem &it) {
+    if (i >= n_items) return false;
+    const int t = i / RT, m = i % RT;
+    if (g.tiles) {
+        it.zs = g.tiles[3 * t]; it.n0 = g.tiles[3 * t + 1]; it.nv = g.tiles[3 * t + 2];
+    } else {
+        it.zs = 0; it.n0 = t * kGemmBN; it.nv = min(kGemmBN, g.N - it.n0);
+    }
+    it.w = (it.nv + 15) & ~15;
+    it.mat = m / MT;
+    it.r0 = (m % MT) * 128;
+    return true;
+}
+
+// Epilogue of one K block for columns [c0, c0 + kEpiCols) of a tile w rows
+// wide: digit d of column n sits at TMEM column d w + n; otherwise as promote().
+template <int ND>
+__device__ __forceinline__ void promote_w(uint32_t t, int w, int c0, const float *sxk, float sw,
+                                          float2 (&acc)[kEpiCols / 2]) {
+#pragma unroll
+    for (int c = 0; c < kEpiCols / 16; c++) {
+        const uint32_t col = c0 + c * 16;
+        uint32_t r[3][16];
+        tc::tmem_ld16_nowait(t + col, r[0]);
+        if (ND > 1) tc::tmem_ld16_nowait(t + w + col, r[1]);
+        if (ND > 2) tc::tmem_ld16_nowait(t + 2 * w + col, r[2]);
+        float sc[16];
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+            const float4 s4 = *(const float4 *)(sxk + col + i);
+            sc[i] = __fmul_rn(sw, s4.x); sc[i + 1] = __fmul_rn(sw, s4.y);
+            sc[i + 2] = __fmul_rn(sw, s4.z); sc[i + 3] = __fmul_rn(sw, s4.w);
+        }
+        tc::tmem_wait_ld();
+        tc::tmem_regs_ready(r[0]);
+        if (ND > 1) tc::tmem_regs_ready(r[1]);
+        if (ND > 2) tc::tmem_regs_ready(r[2]);
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+            float v0 = __uint_as_float(r[0][i]), v1 = __uint_as_float(r[0][i + 1]);
+            if (ND > 1) {
+                v0 = fmaf(__uint_as_float(r[1][i]), 0.0625f, v0);
+                v1 = fmaf(__uint_as_float(r[1][i + 1]), 0.0625f, v1);
+            }
+            if (ND > 2) {
+                v0 = fmaf(__uint_as_float(r[2][i]), 0.00390625f, v0);
+                v1 = fmaf(__uint_as_float(r[2][i + 1]), 0.00390625f, v1);
+            }
+            float2 &a2 = acc[(c * 16 + i) >> 1];
+            a2 = __ffma2_rn(make_float2(v0, v1), make_float2(sc[i], sc[i + 1]), a2);
+        }
+    }
+}
+
+// The activation scales of item `it` that thread e of the epilogue holds:
+// entries e + 32 kEpiWarps p of the tile's [kb][64] table (0 past nv).
+constexpr int kPSxRegs = 4;                // KB <= 32
+__device__ __forceinline__ void p_sx_load(const GemmArgs &g, const PItem &it, bool valid, int e,
+                                          float (&v)[kPSxRegs]) {
+    const int KB = g.KB;
+#pragma unroll
+    for (int p = 0; p < kPSxRegs; p++) {
+        const int i = e + p * 32 * kEpiWarps, kb = i / kGemmBN, col = i % kGemmBN;
+        v[p] = (valid && kb < KB && col < it.nv) ? __ldg(g.sX + (int64_t)(it.n0 + col) * KB + kb) : 0.f;
+    }
+}
+__device__ __forceinline__ void p_sx_store(float *sxt, int KB, int e, const float (&v)[kPSxRegs]) {
+#pragma unroll
+    for (int p = 0; p < kPSxRegs; p++) {
+        const int i = e + p * 32 * kEpiWarps;
+        if (i < kGemmBN * KB) sxt[i] = v[p];
+    }
+}
+
+template <int ND>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tW2,
+         const __grid_constant__ CUtensorMap tX16, const __grid_constant__ CUtensorMap tX32,
+         const __grid_constant__ CUtensorMap tX48, const __grid_constant__ CUtensorMap tX64, GemmArgs g) {
+    using L = PSmem<ND>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
+    uint64_t *full = (uint64_t *)(sm + L::o_bar), *empty = full + kPStages;
+    uint64_t *tfull = empty + kPStages, *tempty = tfull + 2, *done = tempty + 2;
+    uint32_t *slot = (uint32_t *)(sm + L::o_slot);
+    float *sxt = (float *)(sm + L::o_sx);
+
+    const int MT = g.R / 128, RT = MT * g.nmat, KB = g.KB;
+    const int n_items = (g.tiles ? *g.ntiles : (g.N + kGemmBN - 1) / kGemmBN) * RT;
+    if ((int)blockIdx.x >= n_items) return;                 // uniform: before any barrier
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    unsigned *err = g.err;
+
+    if (warp == 1) tc::tmem_alloc(slot, 2 * L::NMX <= 256 ? 256 : 512);
+    if (tid == 0) {
+        for (int s = 0; s < kPStages; s++) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+        for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, kEpiWarps); }
+        tc::mbar_init(done, 1);
+        tc::mbar_fence_init();
+        tc::prefetch_tmap(&tW);
+        if (g.nmat > 1) tc::prefetch_tmap(&tW2);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t taddr = *slot;
+    PItem it;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int k = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; ok && p_item(g, i, n_items, RT, MT, it); i += gridDim.x) {
+                const CUtensorMap *tA = it.mat ? &tW2 : &tW;
+                const CUtensorMap *tB = it.w == 16 ? &tX16 : it.w == 32 ? &tX32 : it.w == 48 ? &tX48 : &tX64;
+                const uint32_t bytes = L::A + ND * it.w * 128;
+                for (int kb = 0; kb < KB; kb++, k++) {
+                    const int s = k % kPStages;
+                    if (k >= kPStages && !tc::mbar_wait(empty + s, ((k / kPStages) - 1) & 1, err, 1)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *a = sm + s * L::STAGE;
+                    tc::mbar_expect(full + s, bytes);
+                    tc::tma_load_3d(a, tA, kb * 128, it.r0, it.zs, full + s);
+                    tc::tma_load_3d(a + L::A, tB, kb * 128, it.n0, 0, full + s);
+                }
+            }
+            // every issued load has landed before the CTA may exit
+            for (int j = k - 1; j >= 0 && j >= k - kPStages; j--)
+                tc::mbar_wait(full + j % kPStages, (j / kPStages) & 1, err, 2, true);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int k = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; ok && p_item(g, i, n_items, RT, MT, it); i += gridDim.x) {
+                const uint32_t id = tc::idesc(128, ND * it.w, 0, 0);
+                for (int kb = 0; kb < KB; kb++, k++) {
+                    const int s = k % kPStages, b = k & 1;
+                    if (!tc::mbar_wait(full + s, (k / kPStages) & 1, err, 3) ||
+                        (k >= 2 && !tc::mbar_wait(tempty + b, ((k >> 1) - 1) & 1, err, 4))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint8_t *a = sm + s * L::STAGE;
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        tc::mma_f8f6f4(taddr + b * L::NMX, tc::sdesc_sw128(a + 32 * q),
+                                       tc::sdesc_sw128(a + L::A + 32 * q), id, q > 0);
+                    tc::commit(empty + s);
+                    tc::commit(tfull + b);
+                }
+            }
+            tc::commit(done);
+            tc::mbar_wait(done, 0, err, 5, true);      // every MMA finished
+        }
+    } else {
+        // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows;
+        // the four warps of a quadrant take 16 columns each. After a failed
+        // wait the warps keep walking the items without waiting, so every
+        // one of them reaches each named barrier.
+        const int q = warp & 3, c0 = ((warp - 2) >> 2) * kEpiCols, row = q * 32 + lane, e = tid - 64;
+        const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
+        float pre[kPSxRegs];
+        bool ok = true;
+        int k = 0, j = 0;
+        p_item(g, blockIdx.x, n_items, RT, MT, it);
+        p_sx_load(g, it, true, e, pre);
+        p_sx_store(sxt, KB, e, pre);
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
+        for (int i = blockIdx.x; i < n_items; i += gridDim.x, j++) {
+            p_item(g, i, n_items, RT, MT, it);
+            PItem nx;
+            const bool has_next = p_item(g, i + gridDim.x, n_items, RT, MT, nx);
+            p_sx_load(g, nx, has_next, e, pre);
+            const float *sxi = sxt + (j & 1) * kGemmBN * KB;
+            const float *swr = (it.mat ? g.sW2 : g.sW) + it.zs * g.sw_slot +
+                               (g.row_scales ? (int64_t)(it.r0 + row) * KB : (int64_t)(it.r0 / 128) * KB);
+            float2 acc[kEpiCols / 2];
+#pragma unroll
+            for (int c = 0; c < kEpiCols / 2; c++) acc[c] = make_float2(0.f, 0.f);
+            for (int kb = 0; kb < KB; kb++, k++) {
+                const int b = k & 1;
+                if (ok) ok = tc::mbar_wait(tfull + b, (k >> 1) & 1, err, 6);
+                if (ok) {
+                    tc::fence_after_sync();
+                    if (c0 < it.w) promote_w<ND>(tq + b * L::NMX, it.w, c0, sxi + kb * kGemmBN, __ldg(swr + kb), acc);
+                    tc::fence_before_sync();
+                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(tempty + b);
+            }
+            if (ok && c0 < it.nv && it.r0 + row < g.R) {
+                float *y = g.Y + (int64_t)(it.n0 + c0) * g.ldy + (it.mat ? g.ycol2 : g.ycol0) + it.r0 + row;
+#pragma unroll
+                for (int c = 0; c < kEpiCols; c++)
+                    if (c0 + c < it.nv) y[(int64_t)c * g.ldy] = (c & 1) ? acc[c >> 1].y : acc[c >> 1].x;
+            }
+            p_sx_store(sxt + ((j + 1) & 1) * kGemmBN * KB, KB, e, pre);
+            asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(taddr, 2 * L::NMX <= 256 ? 256 : 512);
+    }
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    }
+    return n;
+}
+
 }  // namespace
 
 // A: slots x [R][C] elements of `esize` bytes, `slot_stride` bytes apart;
@@ -339,6 +586,31 @@ int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X
                    kGemmBN, ND))
         return -1;
     g.KB = g.C * es / 128;
+    if constexpr (!BF) {
+        // FP8: the persistent kernel, one B tensor map per tile width
+        using P = PSmem<ND>;
+        CUtensorMap tX16, tX32, tX48;
+        if (tmap_u8_3d(&tX16, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 16, ND) ||
+            tmap_u8_3d(&tX32, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 32, ND) ||
+            tmap_u8_3d(&tX48, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 48, ND))
+            return -1;
+        const int psmem = P::bytes(g.KB);
+        if (psmem > 227 * 1024 || kGemmBN * g.KB > kPSxRegs * 32 * kEpiWarps) {
+            set_error("gemm: C too large for the scale tiles");
+            return -1;
+        }
+        static bool pattr = false;
+        if (!pattr) {
+            DS4F_CUDA(cudaFuncSetAttribute(k_gemm_p<ND>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+            pattr = true;
+        }
+        g.nmat = A2 ? 2 : 1;
+        const int64_t items = (int64_t)ntiles_max * (g.R / 128) * (A2 ? 2 : 1);
+        const int grid = (int)std::min<int64_t>(items, sm_count());
+        k_gemm_p<ND><<<grid, kGemmThreads, psmem, st>>>(tW, tW2, tX16, tX32, tX48, tX, g);
+        DS4F_CUDA(cudaGetLastError());
+        return 0;
+    }
     const int smem = L::bytes(g.KB);
     if (smem > 227 * 1024) { set_error("gemm: C too large for the scale tile"); return -1; }
     static bool attr = false;

@@ -24,6 +24,7 @@ struct GemmArgs {
     const int *tiles;         // grouped: [*ntiles][3] = slot, first B row, valid rows
     const int *ntiles;
     int N;                    // dense: B rows
+    int nmat;                 // A matrices (2: A2 given; set by gemm_launch)
     unsigned *err;
 };
 
