@@ -51,22 +51,34 @@ __device__ __forceinline__ float e4m3_val(uint32_t b) {      // exact
     return __int_as_float(((int)(b << 24) >> 4) & (int)0x87F00000) * DS4F_F8_UNSCALE;
 }
 // A warp holds one 128-column block, 4 values per lane (columns 4 lane ..):
-// a = max |v|, r = 240 / a, y = v r, then ND E4M3 digits, each written to
-// its plane q + d * plane at byte offset `off`; returns the block scale.
-__device__ __forceinline__ float quant_block_digits(float4 v, int ND, uint8_t *q, int64_t plane,
-                                                    int64_t off) {
+// a = max |v|, r = 240 / a, y = v r, then ND (<= 3) E4M3 digits, the lane's
+// 4 bytes of digit d in wd[d]; returns the block scale.
+__device__ __forceinline__ float quant_block_words(float4 v, int ND, uint32_t (&wd)[3]) {
     float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
     const float r = a > 0.f ? __fdiv_rn(240.0f, a) : 0.f;
     float y[4] = {__fmul_rn(v.x, r), __fmul_rn(v.y, r), __fmul_rn(v.z, r), __fmul_rn(v.w, r)};
-    for (int d = 0; d < ND; d++) {
+#pragma unroll
+    for (int d = 0; d < 3; d++) {
+        wd[d] = 0;
+        if (d >= ND) continue;
         const uint32_t w = e4m3_2(y[0], y[1]) | (e4m3_2(y[2], y[3]) << 16);
-        *(uint32_t *)(q + (int64_t)d * plane + off) = w;
+        wd[d] = w;
 #pragma unroll
         for (int i = 0; i < 4; i++) y[i] = __fmul_rn(__fsub_rn(y[i], e4m3_val((w >> (8 * i)) & 0xFF)), 16.0f);
     }
     return a > 0.f ? __fdiv_rn(a, 240.0f) : 1.0f;
+}
+// The same, each digit written to its plane q + d * plane at byte offset `off`.
+__device__ __forceinline__ float quant_block_digits(float4 v, int ND, uint8_t *q, int64_t plane,
+                                                    int64_t off) {
+    uint32_t wd[3];
+    const float s = quant_block_words(v, ND, wd);
+#pragma unroll
+    for (int d = 0; d < 3; d++)
+        if (d < ND) *(uint32_t *)(q + (int64_t)d * plane + off) = wd[d];
+    return s;
 }
 
 }  // namespace ds4f

@@ -28,22 +28,6 @@ namespace {
 
 constexpr int kND = 3;           // E4M3 digits per routed activation
 
-// ---- 1. RMSNorm ------------------------------------------------------------------
-__global__ void k_rmsnorm_rows(const float *st, const uint16_t *nw, int H, float *xin) {
-    __shared__ double part[8];
-    const float *x = st + (int64_t)blockIdx.x * H;
-    double ss = 0.0;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = __dadd_rn(ss, __dmul_rn((double)x[i], (double)x[i]));
-    ss = warp_sum_d(ss);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    double tot = 0.0;
-    for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot = __dadd_rn(tot, part[k]);
-    const float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(tot, (double)H)), 1e-6f));
-    float *y = xin + (int64_t)blockIdx.x * H;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) y[i] = __fmul_rn(__fdiv_rn(x[i], r), bf16_to_f32(nw[i]));
-}
-
 // ---- 2. grouping -------------------------------------------------------------------
 __global__ void k_count(const int *sel, int n, int first, int count, int *cnt) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -95,35 +79,89 @@ __global__ void k_plan(const int *cnt, int count, int slot0, int *off, int *tile
 }
 
 // Each in-shard selection takes the next row of its expert's range:
-// pos[selection] = row, src[row] = selection. The order of rows inside an
-// expert's range does not change any result (every output column of the
-// tensor-core GEMM depends on its own row only; the combine reads rows by
-// pos), as in the reference whose qsort leaves it open (src/moe.c:1527).
-__global__ void k_place(const int *sel, int n, int first, int count, const int *off, int *fill, int *pos,
-                        int *src) {
+// pos[selection] = row. The order of rows inside an expert's range does not
+// change any result (every output column of the tensor-core GEMM depends on
+// its own row only; the combine reads rows by pos), as in the reference
+// whose qsort leaves it open (src/moe.c:1527).
+__global__ void k_place(const int *sel, int n, int first, int count, const int *off, int *fill, int *pos) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int e = sel[i] - first;
     if (e < 0 || e >= count) return;
-    const int p = off[e] + atomicAdd(fill + e, 1);
-    pos[i] = p;
-    src[p] = i;
+    pos[i] = off[e] + atomicAdd(fill + e, 1);
 }
 
-// Row p of the gathered digit planes <- token src[p] / K; one warp per
-// (row, plane); plus the row's scales.
-__global__ void k_gather(const uint8_t *Xq, const float *sx, const int *src, const int *nrows, int K, int T,
-                         int H, uint8_t *Xg, float *sxg, int rows_cap) {
-    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    const int p = (int)(w / kND), d = (int)(w % kND);
-    if (p >= *nrows) return;
-    const int t = src[p] / K;
-    const uint4 *s4 = (const uint4 *)(Xq + ((int64_t)d * T + t) * H);
-    uint4 *d4 = (uint4 *)(Xg + ((int64_t)d * rows_cap + p) * H);
-    for (int i = lane; i < H / 16; i += 32) d4[i] = s4[i];
-    if (d == 0)
-        for (int i = lane; i < H / 128; i += 32) sxg[(int64_t)p * (H / 128) + i] = sx[(int64_t)t * (H / 128) + i];
+// ---- 1. the token's front end ------------------------------------------------------
+// One block per token, one warp per 128-column block (4 columns per lane):
+// RMSNorm (src/moe.c:841-851: double sum of squares, x / r * w), the E4M3
+// digits and scale of every block written straight into the row of each of
+// the token's in-shard selections (its expert's range of the grouped B
+// planes), and, for the shared expert, the bf16 (hi, lo) digits and the
+// shared_expert_gate logit (fp32 products of the bf16 matvec,
+// src/kernels.c:84-103).
+__global__ void k_front(const float *st, const uint16_t *nw, int H, const int *sel, int K, int first, int count,
+                        const int *pos, uint8_t *Xg, float *sxg, int64_t rows_cap, uint16_t *Xb, int64_t xb_plane,
+                        const uint16_t *gw, float *sg) {
+    __shared__ double part[32];
+    __shared__ float gpart[32];
+    __shared__ int rows[16];
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwp = blockDim.x >> 5;
+    const int c = warp * 128 + 4 * lane;
+    const int64_t off = (int64_t)t * H + c;
+    if (threadIdx.x < K) {
+        const int i = t * K + threadIdx.x, e = sel[i] - first;
+        rows[threadIdx.x] = (e >= 0 && e < count) ? pos[i] : -1;
+    }
+    const float4 v = *(const float4 *)(st + off);
+    double ss = __dadd_rn(__dadd_rn(__dmul_rn((double)v.x, (double)v.x), __dmul_rn((double)v.y, (double)v.y)),
+                          __dadd_rn(__dmul_rn((double)v.z, (double)v.z), __dmul_rn((double)v.w, (double)v.w)));
+    ss = warp_sum_d(ss);
+    if (lane == 0) part[warp] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int k = 0; k < nwp; k++) tot = __dadd_rn(tot, part[k]);
+    const float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(tot, (double)H)), 1e-6f));
+    const uint2 nw4 = *(const uint2 *)(nw + c);
+    const float4 x = make_float4(__fmul_rn(__fdiv_rn(v.x, r), __uint_as_float(nw4.x << 16)),
+                                 __fmul_rn(__fdiv_rn(v.y, r), __uint_as_float(nw4.x & 0xFFFF0000u)),
+                                 __fmul_rn(__fdiv_rn(v.z, r), __uint_as_float(nw4.y << 16)),
+                                 __fmul_rn(__fdiv_rn(v.w, r), __uint_as_float(nw4.y & 0xFFFF0000u)));
+    uint32_t wd[3];
+    const float s = quant_block_words(x, kND, wd);
+    for (int j = 0; j < K; j++) {
+        const int p = rows[j];
+        if (p < 0) continue;
+#pragma unroll
+        for (int d = 0; d < kND; d++) *(uint32_t *)(Xg + ((int64_t)d * rows_cap + p) * H + c) = wd[d];
+        if (lane == 0) sxg[(int64_t)p * (H / 128) + warp] = s;
+    }
+    if (Xb) {
+        uint32_t hi[2], lo[2];
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(xs[i]), h1 = __float2bfloat16_rn(xs[i + 1]);
+            const __nv_bfloat16 l0 = __float2bfloat16_rn(__fsub_rn(xs[i], __bfloat162float(h0)));
+            const __nv_bfloat16 l1 = __float2bfloat16_rn(__fsub_rn(xs[i + 1], __bfloat162float(h1)));
+            hi[i >> 1] = __bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+            lo[i >> 1] = __bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+        }
+        *(uint2 *)(Xb + off) = make_uint2(hi[0], hi[1]);
+        *(uint2 *)(Xb + xb_plane + off) = make_uint2(lo[0], lo[1]);
+        const uint2 g4 = *(const uint2 *)(gw + c);
+        float a = __fmul_rn(__uint_as_float(g4.x << 16), x.x);
+        a = fmaf(__uint_as_float(g4.x & 0xFFFF0000u), x.y, a);
+        a = fmaf(__uint_as_float(g4.y << 16), x.z, a);
+        a = fmaf(__uint_as_float(g4.y & 0xFFFF0000u), x.w, a);
+        a = warp_sum(a);
+        if (lane == 0) gpart[warp] = a;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float sum = 0.f;
+            for (int k = 0; k < nwp; k++) sum += gpart[k];
+            sg[t] = sum;
+        }
+    }
 }
 
 // ---- 3. SiLU-mul into the chain's digits --------------------------------------------
@@ -151,10 +189,6 @@ __device__ __forceinline__ void bf16_digits(float x, uint16_t *q, int64_t n, int
     q[i] = __bfloat16_as_ushort(hi);
     q[n + i] = __bfloat16_as_ushort(lo);
 }
-__global__ void k_bf16_digits(const float *x, int64_t n, uint16_t *q) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) bf16_digits(x[i], q, n, i);
-}
 // GS [T][2M] -> chain digits [2][T][M]
 __global__ void k_silu_bf16_digits(const float *GS, int M, int64_t T, uint16_t *q) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -162,23 +196,6 @@ __global__ void k_silu_bf16_digits(const float *GS, int M, int64_t T, uint16_t *
     const int64_t t = i / M, m = i % M;
     bf16_digits(silu_mul(GS[t * 2 * M + m], GS[t * 2 * M + M + m]), q, T * M, i);
 }
-// shared_expert_gate logit per token (fp32, the reference's bf16 matvec
-// products, src/kernels.c:84-103)
-__global__ void k_gate_logit(const float *xin, const uint16_t *gw, int H, float *sg) {
-    __shared__ float part[8];
-    const float *x = xin + (int64_t)blockIdx.x * H;
-    float a = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) a = fmaf(bf16_to_f32(gw[i]), x[i], a);
-    a = warp_sum(a);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = a;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = 0.f;
-        for (int k = 0; k < (int)(blockDim.x >> 5); k++) s += part[k];
-        sg[blockIdx.x] = s;
-    }
-}
-
 // ---- 5. combine ------------------------------------------------------------------------
 // One block per token: its in-shard selections (j order, zero weights
 // skipped) staged in shared memory, then 4 output columns per thread.
@@ -312,8 +329,7 @@ int ensure_f8_copy(Model *m, cudaStream_t st) {
 
 // ---- workspace -----------------------------------------------------------------------
 struct PfWs {
-    float *xin; uint8_t *Xq; float *sx;
-    int *cnt, *off, *tiles, *ntiles, *nrows, *pos, *src;
+    int *cnt, *off, *tiles, *ntiles, *nrows, *pos;
     uint8_t *Xg; float *sxg; float *GU; uint8_t *Cq; float *sc; float *O;
     uint16_t *Xb; float *GS; uint16_t *Cb; float *OS; float *sg;
     unsigned *err;
@@ -327,8 +343,7 @@ int pf_workspace(Model *m, int T, PfWs *w) {
     const int64_t R = (int64_t)T * K;
     const int tiles_max = (int)(R / kGemmBN) + count;
     const size_t sizes[] = {
-        al((size_t)T * H * 4), al((size_t)kND * T * H), al((size_t)T * (H / 128) * 4),
-        al(count * 4), al(count * 4), al((size_t)tiles_max * 12), al(4), al(4), al(R * 4), al(R * 4),
+        al(count * 4), al(count * 4), al((size_t)tiles_max * 12), al(4), al(4), al(R * 4),
         al((size_t)kND * R * H), al((size_t)R * (H / 128) * 4), al((size_t)R * 2 * M * 4),
         al((size_t)kND * R * M), al((size_t)R * (M / 128) * 4), al((size_t)R * H * 4),
         al((size_t)2 * T * H * 2), al((size_t)T * 2 * M * 4), al((size_t)2 * T * M * 2),
@@ -347,9 +362,8 @@ int pf_workspace(Model *m, int T, PfWs *w) {
     uint8_t *p = (uint8_t *)m->pf_ws;
     int k = 0;
     auto take = [&]() { uint8_t *r = p; p += sizes[k++]; return r; };
-    w->xin = (float *)take(); w->Xq = take(); w->sx = (float *)take();
     w->cnt = (int *)take(); w->off = (int *)take(); w->tiles = (int *)take(); w->ntiles = (int *)take();
-    w->nrows = (int *)take(); w->pos = (int *)take(); w->src = (int *)take();
+    w->nrows = (int *)take(); w->pos = (int *)take();
     w->Xg = take(); w->sxg = (float *)take(); w->GU = (float *)take(); w->Cq = take(); w->sc = (float *)take();
     w->O = (float *)take(); w->Xb = (uint16_t *)take(); w->GS = (float *)take(); w->Cb = (uint16_t *)take();
     w->OS = (float *)take(); w->sg = (float *)take(); w->err = (unsigned *)take();
@@ -370,26 +384,26 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk;
     const int first = m->d.expert_first, count = m->d.expert_count;
     DS4F_REQUIRE(count <= 1024, "prefill: at most 1024 experts per shard");
+    DS4F_REQUIRE(H % 128 == 0 && H <= 4096 && M % 128 == 0 && K <= 16,
+                 "prefill: hidden %d / moe_inter %d must be multiples of 128 (hidden <= 4096), top-k %d <= 16", H, M, K);
     PfWs ws;
     if (pf_workspace(m, T, &ws)) return -1;
     const int64_t R = (int64_t)T * K;
     const uint16_t *tl = m->trunk + (int64_t)L * m->tr.n;
     const int64_t total_slots = (int64_t)m->d.n_layers * count;
 
-    // 1
-    k_rmsnorm_rows<<<T, 256, 0, st>>>(states, tl + m->tr.norm, H, ws.xin);
-    if (quant_f8_digits_launch(ws.xin, T, H, kND, ws.Xq, ws.sx, st)) return -1;
-    // 2
+    // 1: grouping (it depends on the routing only)
     DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));
     if (first_layer) DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
     k_count<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.cnt);
     k_plan<<<1, ((count + 31) / 32) * 32, 0, st>>>(ws.cnt, count, L * count, ws.off, ws.tiles, ws.ntiles,
                                                    ws.nrows);
     DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));       // now the per-expert fill counters
-    k_place<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.off, ws.cnt, ws.pos,
-                                                        ws.src);
-    k_gather<<<(unsigned)((R * kND * 32 + 255) / 256), 256, 0, st>>>(ws.Xq, ws.sx, ws.src, ws.nrows, K, T, H,
-                                                                    ws.Xg, ws.sxg, (int)R);
+    k_place<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.off, ws.cnt, ws.pos);
+    // 2: RMSNorm, digits into the grouped rows, the shared expert's inputs
+    k_front<<<T, 32 * (H / 128), 0, st>>>(states, tl + m->tr.norm, H, sel, K, first, count, ws.pos, ws.Xg, ws.sxg,
+                                           R, add_shared ? ws.Xb : nullptr, (int64_t)T * H, tl + m->tr.sh_gw,
+                                           ws.sg);
     // 3: gate, up, SiLU digits, down
     {   // gate and up in one launch
         GemmArgs g{};
@@ -417,7 +431,6 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     }
     // 4: shared expert
     if (add_shared) {
-    k_bf16_digits<<<(unsigned)(((int64_t)T * H + 255) / 256), 256, 0, st>>>(ws.xin, (int64_t)T * H, ws.Xb);
     const int ntd = (T + kGemmBN - 1) / kGemmBN;
     {   // shared gate and up in one launch
         GemmArgs g{};
@@ -432,7 +445,6 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
         g.Y = ws.OS; g.ldy = H; g.ycol0 = 0; g.R = H; g.C = M; g.N = T; g.err = ws.err;
         if (gemm_launch<2, true>(tl + m->tr.sh_down, 1, (int64_t)H * M * 2, ws.Cb, T, g, ntd, st)) return -1;
     }
-    k_gate_logit<<<T, 256, 0, st>>>(ws.xin, tl + m->tr.sh_gw, H, ws.sg);
     }
     // 5
     k_combine<<<T, 256, 0, st>>>(states, acc_out, ws.O, add_shared ? ws.OS : nullptr, ws.sg, sel, w, ws.pos,
