@@ -53,8 +53,12 @@ def bytes_per_token(fmt_fp8=True):
 
 # DRAM bytes (read + write) of one k_decode launch, from the ncu --set full
 # capture summarised in profiles/k_decode_fp8_4layer_full.md (4-layer case,
-# 135.33 MB) scaled to 40 layers: every layer reads its own weights.
-TRAFFIC_PER_LAUNCH = 10 * 135_330_000
+# 134.91 MB) scaled to 40 layers: every layer reads its own weights.
+TRAFFIC_PER_LAUNCH = 10 * 134_910_000
+# kernels of one batched-prefill layer (csrc/prefill.cu): count, plan, place,
+# front end, gate/up GEMM, SiLU digits, down GEMM, shared gate/up and down
+# GEMMs, shared SiLU digits, combine
+PREFILL_LAUNCHES_PER_LAYER = 11
 
 
 def peaks():
@@ -516,7 +520,7 @@ def run_gpu_prefill(args, rank, world, local_rank):
             "e2e": {"value": round(world * T * args.steps / e2e_s, 1), "unit": "tok/s",
                     "h2d_bytes_per_step": T * H * 4 + sel.nbytes + w.nbytes,
                     "d2h_bytes_per_step": T * H * 4, "timer": "host clock, synchronous steps"},
-            "gpu_launches": args.steps * LAYERS * 17,
+            "gpu_launches": args.steps * LAYERS * PREFILL_LAUNCHES_PER_LAYER,
             "clocks": clocks,
         }
     if dist:
@@ -712,7 +716,7 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
             "e2e": {"value": round(T * args.steps / e2e_s, 1), "unit": "tok/s",
                     "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
                     "timer": "host clock, synchronous steps"},
-            "gpu_launches": args.steps * LAYERS * 17,
+            "gpu_launches": args.steps * LAYERS * PREFILL_LAUNCHES_PER_LAYER,
             "clocks": clocks,
         }
     dist.barrier()
