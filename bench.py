@@ -557,16 +557,24 @@ def run_gpu_ep(args, rank, world, local_rank):
     st = torch.empty((Bt, H), dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(st, Bt * H, 0, 0, 4, 0, 2, 1.0)            # the same tokens on every rank
     sp = torch.cuda.current_stream().cuda_stream
-    for _ in range(args.warmup):
-        dec.step(st, sp)
+    # one GPU, a batch: the whole pool is here, so the batched stack (one
+    # captured graph per step) replaces the per-layer shard steps
+    stack = world == 1 and Bt > 1
+
+    def steps(n):
+        if stack:
+            shard.model.stack_batch_dev(st, n, sp)
+        else:
+            for _ in range(n):
+                dec.step(st, sp)
+    steps(args.warmup)
     torch.cuda.synchronize()
     dist.barrier()
     clk = Clocks(local_rank)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        dec.step(st, sp)
+    steps(args.steps)
     e1.record()
     torch.cuda.synchronize()
     t_ms = e0.elapsed_time(e1)
@@ -578,7 +586,7 @@ def run_gpu_ep(args, rank, world, local_rank):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         st.copy_(hst, non_blocking=True)
-        dec.step(st, sp)
+        steps(1)
         hst.copy_(st, non_blocking=True)
         torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
@@ -600,12 +608,15 @@ def run_gpu_ep(args, rank, world, local_rank):
             "metric": METRIC_EP, "value": round(Bt * args.steps / (t_ms / 1e3), 2), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (e2m1 + e8m0/32)") + " weights, fp32 accumulate",
+            "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (e2m1 + e8m0/32)") + " weights, " +
+                     ("fp32 accumulate" if Bt == 1 else
+                      "3-digit e4m3 activations, fp32 accumulate (tcgen05 grouped chain)"),
             "data": "synthetic (seeded, device-generated)",
             "config": {"workload": f"config 3: 40-layer {'FP8' if fp8 else 'MXFP4'} decode, batch {Bt}, "
                                    f"{E // world} experts per GPU",
                        "batch": Bt, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
-                       "parallelism": f"expert-parallel x{world} (all-reduce of acc per layer)",
+                       "parallelism": (f"expert-parallel x{world} (all-reduce of acc per layer)" if world > 1 else
+                                       "single GPU" + (" (batched stack, one CUDA graph per step)" if stack else "")),
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": peak * world, "unit": "GB/s",
                          "frac": round(bw / (peak * world), 4), "traffic": None, "peak_source": src,
@@ -614,7 +625,9 @@ def run_gpu_ep(args, rank, world, local_rank):
             "e2e": {"value": round(Bt * args.steps / e2e_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": Bt * H * 4, "d2h_bytes_per_step": Bt * H * 4,
                     "timer": "host clock, synchronous steps"},
-            "gpu_launches": args.steps * LAYERS * 4 * Bt,
+            # one token: route, top-K, gate/up, down; a batch: route, top-K
+            # and the grouped tensor-core layer
+            "gpu_launches": args.steps * LAYERS * (4 if Bt == 1 else 2 + PREFILL_LAUNCHES_PER_LAYER),
             "clocks": clocks,
         }
     dist.barrier()

@@ -131,24 +131,6 @@ struct Ds4fMvPlan {
 };
 
 namespace ds4f {
-// Enqueue `fn` on the model stream ordered after the caller's stream, and
-// make the caller's stream wait for it (timing on the caller's stream then
-// brackets the work).
-template <typename F>
-int on_model_stream(Model &m, void *stream, F fn) {
-    cudaStream_t cs = (cudaStream_t)stream;
-    cudaEvent_t e0, e1;
-    DS4F_CUDA(cudaEventCreateWithFlags(&e0, cudaEventDisableTiming));
-    DS4F_CUDA(cudaEventCreateWithFlags(&e1, cudaEventDisableTiming));
-    int rc = 0;
-    if (cudaEventRecord(e0, cs) != cudaSuccess || cudaStreamWaitEvent(m.stream, e0, 0) != cudaSuccess) rc = -1;
-    if (!rc) rc = fn(m.stream);
-    if (cudaEventRecord(e1, m.stream) != cudaSuccess || cudaStreamWaitEvent(cs, e1, 0) != cudaSuccess) rc = -1;
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    if (rc && !g_err[0]) set_error("stream ordering failed");
-    return rc;
-}
 
 }  // namespace ds4f
 
@@ -462,6 +444,8 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (m.trace) cudaFree(m.trace);
     if (m.pf_ws) cudaFree(m.pf_ws);
     if (m.pf8) cudaFree(m.pf8);
+    if (m.pf_err_h) cudaFreeHost(m.pf_err_h);
+    if (m.bgraph) cudaGraphExecDestroy(m.bgraph);
     cudaFree(m.pool);
     cudaFree(m.trunk);
     cudaFree(m.ws_base);

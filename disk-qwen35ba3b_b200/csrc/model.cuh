@@ -4,6 +4,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "../../include/ds4f/gpu_cuda.h"
 
 namespace ds4f {
 
@@ -74,6 +75,12 @@ struct Model {
     size_t pf_bytes;
     uint8_t *pf8;                // MXFP4 models: the pool's exact FP8 copy for the
     SlotLayout slot8;            //   tensor-core prefill (row scales), built on first use
+    unsigned *pf_err_h;          // pinned copy of the prefill pipeline error word,
+                                 //   written after each asynchronous step
+    cudaGraphExec_t bgraph;      // captured batched decode step (prefill.cu), valid for
+    float *bgraph_state;         //   these states, batch and workspace
+    int bgraph_B;
+    void *bgraph_ws;
 };
 
 int slot_layout(int fmt, int H, int M, SlotLayout *s);
@@ -88,6 +95,10 @@ int moe_layer_launch(Model *m, int L, float *state, int *idx_out,
 // add_shared includes the shared expert.
 int moe_layer_launch_ex(Model *m, int L, float *state, int *idx_out, float *w_out, float *acc_out,
                         bool partial, bool add_shared, cudaStream_t st);
+// The certified router and top-K of layer L for B tokens at once (moe.cu):
+// states [B][H] -> xin [B][H], S / Bnd [B][E], idx / w [B][K] (device).
+int route_batch_launch(Model *m, int L, const float *states, int B, float *xin, double *S, double *Bnd,
+                       int *idx, float *w, cudaStream_t st);
 
 // Whole decode steps in one persistent cooperative launch (decode.cu).
 bool decode_eligible(const Model *m);
@@ -106,6 +117,25 @@ int synth_f32(float *dst, int64_t n, uint64_t key, double sigma, cudaStream_t st
 // shared expert (one rank of a partition).
 int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w,
                   cudaStream_t st, bool first_layer, bool last_layer, float *acc_out, bool add_shared);
+
+// Enqueue `fn` on the model stream ordered after the caller's stream, and
+// make the caller's stream wait for it (timing on the caller's stream then
+// brackets the work).
+template <typename F>
+int on_model_stream(Model &m, void *stream, F fn) {
+    cudaStream_t cs = (cudaStream_t)stream;
+    cudaEvent_t e0, e1;
+    DS4F_CUDA(cudaEventCreateWithFlags(&e0, cudaEventDisableTiming));
+    DS4F_CUDA(cudaEventCreateWithFlags(&e1, cudaEventDisableTiming));
+    int rc = 0;
+    if (cudaEventRecord(e0, cs) != cudaSuccess || cudaStreamWaitEvent(m.stream, e0, 0) != cudaSuccess) rc = -1;
+    if (!rc) rc = fn(m.stream);
+    if (cudaEventRecord(e1, m.stream) != cudaSuccess || cudaStreamWaitEvent(cs, e1, 0) != cudaSuccess) rc = -1;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc && !ds4f_gpu_last_error()[0]) set_error("stream ordering failed");
+    return rc;
+}
 
 inline const uint8_t *expert_ptr(const Model *m, int L, int e) {
     return m->pool + ((int64_t)L * m->d.expert_count + (e - m->d.expert_first)) *

@@ -64,6 +64,7 @@ __device__ void rmsnorm_smem(const float *__restrict__ state,
 // Bnd = 1.001 u * that sum (the 1.001 covers 1/(1-nu) and double rounding).
 // k_topk decides the top-k from [S - Bnd, S + Bnd] and recomputes exact
 // fp32 sums only when two candidates' intervals overlap.
+// Token b = blockIdx.y of a batch: state [b][H], xin [b][H], S / Bnd [b][E].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 k_route(const float *__restrict__ state, const uint16_t *__restrict__ trunk_l,
@@ -71,6 +72,10 @@ k_route(const float *__restrict__ state, const uint16_t *__restrict__ trunk_l,
         double *__restrict__ S, double *__restrict__ Bnd) {
     extern __shared__ float xs[];
     __shared__ double red[33];
+    state += (int64_t)blockIdx.y * H;
+    xin_out += (int64_t)blockIdx.y * H;
+    S += (int64_t)blockIdx.y * E;
+    Bnd += (int64_t)blockIdx.y * E;
     rmsnorm_smem(state, trunk_l + tr.norm, H, xs, red, 1.0f);
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < H; i += blockDim.x) xin_out[i] = xs[i];
@@ -126,12 +131,18 @@ __device__ float exact_logit(const uint16_t *__restrict__ row,
 // Selection: descending, lower index first among equal values. Weights:
 // softmax over all E in double with the max subtracted, the selected
 // probabilities kept, then (renorm) divided by their fp32 sum in j order.
+// Token b = blockIdx.x of a batch: S / Bnd [b][E], xin [b][H], idx / w [b][K].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
        const float *__restrict__ xin, const uint16_t *__restrict__ router,
        int H, int E, int K, int renorm, int exact_all, int *__restrict__ idx_out,
        float *__restrict__ w_out, unsigned *__restrict__ diag) {
+    S += (int64_t)blockIdx.x * E;
+    Bnd += (int64_t)blockIdx.x * E;
+    xin += (int64_t)blockIdx.x * H;
+    idx_out += (int64_t)blockIdx.x * K;
+    w_out += (int64_t)blockIdx.x * K;
     extern __shared__ unsigned char sm[];
     double *lo = (double *)sm;
     double *hi = lo + E;
@@ -575,6 +586,22 @@ int trunk_layout(int H, int M, int E, TrunkLayout *t) {
     t->sh_down = o; o += al((int64_t)H * M);
     t->sh_gw = o; o += al(H);
     t->n = o;
+    return 0;
+}
+
+int route_batch_launch(Model *m, int L, const float *states, int B, float *xin, double *S, double *Bnd,
+                       int *idx, float *w, cudaStream_t st) {
+    const ModelDesc &d = m->d;
+    const int H = d.hidden, E = d.n_experts, K = d.topk;
+    DS4F_REQUIRE(B > 0 && B <= 65535, "route: batch %d out of range", B);
+    const uint16_t *trunk_l = m->trunk + (int64_t)L * m->tr.n;
+    k_route<<<dim3((E + kRouteWarps - 1) / kRouteWarps, B), 256, H * sizeof(float), st>>>(
+        states, trunk_l, m->tr, H, E, xin, S, Bnd);
+    DS4F_CUDA(cudaGetLastError());
+    const size_t tk_smem = (size_t)E * (8 + 8 + 4 + 4 + 4) + (size_t)H * 4;
+    k_topk<<<B, 256, tk_smem, st>>>(S, Bnd, xin, trunk_l + m->tr.router, H, E, K, d.renorm, d.router_exact,
+                                    idx, w, m->w.diag);
+    DS4F_CUDA(cudaGetLastError());
     return 0;
 }
 

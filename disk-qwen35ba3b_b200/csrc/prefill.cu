@@ -333,6 +333,8 @@ struct PfWs {
     uint8_t *Xg; float *sxg; float *GU; uint8_t *Cq; float *sc; float *O;
     uint16_t *Xb; float *GS; uint16_t *Cb; float *OS; float *sg;
     unsigned *err;
+    // batched decode: the routing computed on the device
+    float *rxin; double *rS, *rB; int *ridx; float *rw;
     int tiles_max;
 };
 
@@ -340,6 +342,7 @@ size_t al(size_t n) { return (n + 255) / 256 * 256; }
 
 int pf_workspace(Model *m, int T, PfWs *w) {
     const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk, count = m->d.expert_count;
+    const int E = m->d.n_experts;
     const int64_t R = (int64_t)T * K;
     const int tiles_max = (int)(R / kGemmBN) + count;
     const size_t sizes[] = {
@@ -347,8 +350,10 @@ int pf_workspace(Model *m, int T, PfWs *w) {
         al((size_t)kND * R * H), al((size_t)R * (H / 128) * 4), al((size_t)R * 2 * M * 4),
         al((size_t)kND * R * M), al((size_t)R * (M / 128) * 4), al((size_t)R * H * 4),
         al((size_t)2 * T * H * 2), al((size_t)T * 2 * M * 4), al((size_t)2 * T * M * 2),
-        al((size_t)T * H * 4), al((size_t)T * 4), al(4)};
+        al((size_t)T * H * 4), al((size_t)T * 4), al(4),
+        al((size_t)T * H * 4), al((size_t)T * E * 8), al((size_t)T * E * 8), al(R * 4), al(R * 4)};
     size_t total = 0;
+    bool fresh = false;
     for (size_t s : sizes) total += s;
     if (total > m->pf_bytes) {
         if (m->pf_ws) { DS4F_CUDA(cudaFree(m->pf_ws)); m->pf_ws = nullptr; m->pf_bytes = 0; }
@@ -358,6 +363,7 @@ int pf_workspace(Model *m, int T, PfWs *w) {
                      "prefill: workspace of %.2f GB for %d tokens, %.2f GB free", total / 1e9, T, fre / 1e9);
         DS4F_CUDA(cudaMalloc(&m->pf_ws, total));
         m->pf_bytes = total;
+        fresh = true;
     }
     uint8_t *p = (uint8_t *)m->pf_ws;
     int k = 0;
@@ -367,7 +373,33 @@ int pf_workspace(Model *m, int T, PfWs *w) {
     w->Xg = take(); w->sxg = (float *)take(); w->GU = (float *)take(); w->Cq = take(); w->sc = (float *)take();
     w->O = (float *)take(); w->Xb = (uint16_t *)take(); w->GS = (float *)take(); w->Cb = (uint16_t *)take();
     w->OS = (float *)take(); w->sg = (float *)take(); w->err = (unsigned *)take();
+    w->rxin = (float *)take(); w->rS = (double *)take(); w->rB = (double *)take(); w->ridx = (int *)take();
+    w->rw = (float *)take();
     w->tiles_max = tiles_max;
+    if (fresh) DS4F_CUDA(cudaMemset(w->err, 0, 4));
+    return 0;
+}
+
+// Asynchronous steps (the expert-parallel partial calls, made once per layer
+// between collectives) do not synchronise: each copies the pipeline error
+// word to pinned host memory after its kernels, and a later call reports
+// what an earlier step left there (then clears it).
+int async_begin(Model *m, const PfWs &ws, cudaStream_t st) {
+    if (!m->pf_err_h) {
+        DS4F_CUDA(cudaHostAlloc((void **)&m->pf_err_h, 4, cudaHostAllocDefault));
+        *m->pf_err_h = 0;
+    }
+    const unsigned h = *(volatile unsigned *)m->pf_err_h;
+    if (h) {
+        *m->pf_err_h = 0;
+        DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
+        set_error("prefill: a tensor-core pipeline wait gave up (code %u) in an earlier asynchronous step", h);
+        return -1;
+    }
+    return 0;
+}
+int async_end(Model *m, const PfWs &ws, cudaStream_t st) {
+    DS4F_CUDA(cudaMemcpyAsync(m->pf_err_h, ws.err, 4, cudaMemcpyDeviceToHost, st));
     return 0;
 }
 
@@ -460,9 +492,100 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     return 0;
 }
 
+// Batched decode of one layer: the certified router and top-K of every
+// token on the device (the per-token route of src/main.c:1014-1088 and
+// ds4f_topk, src/moe.c:531-561, B at once), then the grouped chain of the
+// batched step (ds4f_moe_step_batch, src/moe.c:1480-1707) on the tensor
+// cores with that routing. idx / w (device, may be null) receive the routing.
+// async: no synchronisation (errors reported by a later call, async_begin);
+// otherwise first_layer / last_layer as in prefill_layer.
+int decode_batch_layer(Model *m, int L, float *states, int B, int *idx, float *w, cudaStream_t st,
+                       bool first_layer, bool last_layer, float *acc_out, bool add_shared, bool async) {
+    DS4F_REQUIRE(B > 0 && L >= 0 && L < m->d.n_layers, "decode batch: layer %d / tokens %d", L, B);
+    const int K = m->d.topk;
+    PfWs ws;
+    if (pf_workspace(m, B, &ws)) return -1;
+    if (async && async_begin(m, ws, st)) return -1;
+    if (route_batch_launch(m, L, states, B, ws.rxin, ws.rS, ws.rB, ws.ridx, ws.rw, st)) return -1;
+    if (idx) DS4F_CUDA(cudaMemcpyAsync(idx, ws.ridx, (size_t)B * K * 4, cudaMemcpyDeviceToDevice, st));
+    if (w) DS4F_CUDA(cudaMemcpyAsync(w, ws.rw, (size_t)B * K * 4, cudaMemcpyDeviceToDevice, st));
+    if (prefill_layer(m, L, states, B, ws.ridx, ws.rw, st, async ? false : first_layer, async ? false : last_layer,
+                      acc_out, add_shared))
+        return -1;
+    return async ? async_end(m, ws, st) : 0;
+}
+
 }  // namespace ds4f
 
 extern "C" {
+
+int ds4f_gpu_moe_layer_batch_dev(Ds4fGpuModel *h, int layer, float *states_dev, int B, int *idx_dev,
+                                 float *w_dev, void *stream) {
+    DS4F_REQUIRE(h && states_dev, "moe_layer_batch: null argument");
+    return ds4f::decode_batch_layer(&h->m, layer, states_dev, B, idx_dev, w_dev, (cudaStream_t)stream, true, true,
+                                    nullptr, true, false);
+}
+
+int ds4f_gpu_moe_layer_batch_partial_dev(Ds4fGpuModel *h, int layer, const float *states_dev, int B,
+                                         float *acc_dev, int add_shared, void *stream) {
+    DS4F_REQUIRE(h && states_dev && acc_dev, "moe_layer_batch_partial: null argument");
+    return ds4f::decode_batch_layer(&h->m, layer, const_cast<float *>(states_dev), B, nullptr, nullptr,
+                                    (cudaStream_t)stream, false, false, acc_dev, add_shared != 0, true);
+}
+
+// The first step runs eagerly (it sizes the workspace, builds an MXFP4
+// pool's FP8 copy and sets the kernels' attributes); the later steps replay
+// one CUDA graph of a whole step (every layer's launches), kept while the
+// states buffer, the batch and the workspace stay the same. One pipeline
+// check after the last step.
+// The work runs on the model's own stream (a capture needs a stream of
+// its own), ordered after and before the caller's stream.
+static int stack_batch(ds4f::Model *m, float *states_dev, int B, int n_steps, cudaStream_t st) {
+    const int NL = m->d.n_layers;
+    ds4f::PfWs ws;
+    if (ds4f::pf_workspace(m, B, &ws)) return -1;
+    DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
+    int s = 0;
+    const bool fresh = !m->bgraph || m->bgraph_state != states_dev || m->bgraph_B != B || m->bgraph_ws != m->pf_ws;
+    if (fresh) {
+        for (int L = 0; L < NL; L++)
+            if (ds4f::decode_batch_layer(m, L, states_dev, B, nullptr, nullptr, st, false, false, nullptr, true,
+                                         false))
+                return -1;
+        s = 1;
+        if (s < n_steps) {
+            if (m->bgraph) { cudaGraphExecDestroy(m->bgraph); m->bgraph = nullptr; }
+            if (ds4f::pf_workspace(m, B, &ws)) return -1;     // the eager step left it sized
+            cudaGraph_t g;
+            DS4F_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            int rc = 0;
+            for (int L = 0; L < NL && !rc; L++)
+                rc = ds4f::decode_batch_layer(m, L, states_dev, B, nullptr, nullptr, st, false, false, nullptr, true,
+                                              false);
+            cudaError_t e = cudaStreamEndCapture(st, &g);
+            if (rc) { if (e == cudaSuccess) cudaGraphDestroy(g); return -1; }
+            DS4F_CUDA(e);
+            e = cudaGraphInstantiate(&m->bgraph, g, 0);
+            cudaGraphDestroy(g);
+            DS4F_CUDA(e);
+            m->bgraph_state = states_dev;
+            m->bgraph_B = B;
+            m->bgraph_ws = m->pf_ws;
+        }
+    }
+    for (; s < n_steps; s++) DS4F_CUDA(cudaGraphLaunch(m->bgraph, st));
+    unsigned e = 0;
+    DS4F_CUDA(cudaMemcpyAsync(&e, ws.err, 4, cudaMemcpyDeviceToHost, st));
+    DS4F_CUDA(cudaStreamSynchronize(st));
+    DS4F_REQUIRE(e == 0, "moe_stack_batch: a tensor-core pipeline wait gave up (code %u)", e);
+    return 0;
+}
+
+int ds4f_gpu_moe_stack_batch_dev(Ds4fGpuModel *h, float *states_dev, int B, int n_steps, void *stream) {
+    DS4F_REQUIRE(h && states_dev && n_steps > 0 && B > 0, "moe_stack_batch: bad arguments");
+    return ds4f::on_model_stream(h->m, stream,
+                                 [&](cudaStream_t st) { return stack_batch(&h->m, states_dev, B, n_steps, st); });
+}
 
 int ds4f_gpu_moe_prefill(Ds4fGpuModel *h, int layer, float *states_dev, int T, const int *sel_dev,
                          const float *w_dev, void *stream) {
@@ -486,9 +609,15 @@ int ds4f_gpu_prefill(Ds4fGpuModel *h, float *states_dev, int T, const int *sel_d
 
 int ds4f_gpu_moe_prefill_partial(Ds4fGpuModel *h, int layer, const float *states_dev, int T, const int *sel_dev,
                                  const float *w_dev, float *acc_dev, int add_shared, void *stream) {
-    DS4F_REQUIRE(h && states_dev && sel_dev && w_dev && acc_dev, "moe_prefill_partial: null argument");
-    return ds4f::prefill_layer(&h->m, layer, const_cast<float *>(states_dev), T, sel_dev, w_dev,
-                               (cudaStream_t)stream, true, true, acc_dev, add_shared != 0);
+    DS4F_REQUIRE(h && states_dev && sel_dev && w_dev && acc_dev && T > 0, "moe_prefill_partial: bad arguments");
+    ds4f::Model *m = &h->m;
+    cudaStream_t st = (cudaStream_t)stream;
+    ds4f::PfWs ws;
+    if (ds4f::pf_workspace(m, T, &ws) || ds4f::async_begin(m, ws, st)) return -1;
+    if (ds4f::prefill_layer(m, layer, const_cast<float *>(states_dev), T, sel_dev, w_dev, st, false, false, acc_dev,
+                            add_shared != 0))
+        return -1;
+    return ds4f::async_end(m, ws, st);
 }
 
 }  // extern "C"

@@ -87,6 +87,9 @@ def lib():
             "ds4f_gpu_moe_layer_partial_dev": [_vp, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp],
             "ds4f_gpu_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_moe_prefill_partial": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp],
+            "ds4f_gpu_moe_layer_batch_dev": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp],
+            "ds4f_gpu_moe_layer_batch_partial_dev": [_vp, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp],
+            "ds4f_gpu_moe_stack_batch_dev": [_vp, _vp, C.c_int, C.c_int, _vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -292,6 +295,23 @@ class Model:
         """Expert-parallel partial prefill of layer L into acc [T][H]."""
         check(lib().ds4f_gpu_moe_prefill_partial(self.h, L, ptr(states), states.shape[0], ptr(sel), ptr(w),
                                                  ptr(acc), 1 if add_shared else 0, stream))
+
+    def layer_batch_dev(self, L, states, idx=None, w=None, stream=None):
+        """Batched decode of layer L: states [B][H] (device) in/out, the
+        routing computed on the device into idx / w [B][K] (optional)."""
+        check(lib().ds4f_gpu_moe_layer_batch_dev(self.h, L, ptr(states), states.shape[0],
+                                                  ptr(idx) if idx is not None else None,
+                                                  ptr(w) if w is not None else None, stream))
+
+    def layer_batch_partial_dev(self, L, states, acc, add_shared, stream=None):
+        """Expert-parallel batched decode of layer L: this shard's part of
+        the combine into acc [B][H] (device); the states are not updated."""
+        check(lib().ds4f_gpu_moe_layer_batch_partial_dev(self.h, L, ptr(states), states.shape[0], ptr(acc),
+                                                          1 if add_shared else 0, stream))
+
+    def stack_batch_dev(self, states, n_steps, stream=None):
+        """n_steps batched decode steps of states [B][H] through every layer."""
+        check(lib().ds4f_gpu_moe_stack_batch_dev(self.h, ptr(states), states.shape[0], n_steps, stream))
 
     def prefill_dev(self, states, sel, w, stream=None):
         """Every layer: sel / w [n_layers][T][K] (device)."""

@@ -4,11 +4,12 @@ Rank r of N holds experts [r E/N, (r + 1) E/N) of every layer (the model's
 expert shard) and the whole bf16 trunk. One decode step of B tokens, per
 layer:
 
-  1. ds4f_gpu_moe_layer_partial_dev on every rank: RMSNorm, router and
-     certified top-K on the full state (the same result on every rank, the
-     state being identical), gate/up/SiLU/down of the selections this rank
-     holds, their part of the selection-order combine; the shared expert on
-     rank 0 only;
+  1. ds4f_gpu_moe_layer_partial_dev (one token) or
+     ds4f_gpu_moe_layer_batch_partial_dev (B > 1: the grouped tensor-core
+     chain) on every rank: RMSNorm, router and certified top-K on the full
+     state (the same result on every rank, the state being identical),
+     gate/up/SiLU/down of the selections this rank holds, their part of the
+     selection-order combine; the shared expert on rank 0 only;
   2. one all-reduce (sum) of acc [B][H] fp32 over the ranks (NCCL over
      NVLink on GPUs);
   3. state += acc on every rank (the residual, src/moe.c:1424).
@@ -48,7 +49,13 @@ class GpuShard:
         self.n_layers, self.hidden = n_layers, hidden
 
     def layer_partial(self, L, states, acc, add_shared, stream=None):
-        self.model.layer_partial_dev(L, states, acc, add_shared, stream)
+        # one token: the per-token kernels (fp32 chains); a batch: the
+        # routing of every token at once and the grouped tensor-core chain,
+        # each expert's weights streamed once for all its tokens
+        if states.dim() == 2 and states.shape[0] > 1:
+            self.model.layer_batch_partial_dev(L, states, acc, add_shared, stream)
+        else:
+            self.model.layer_partial_dev(L, states, acc, add_shared, stream)
 
     def prefill_partial(self, L, states, sel, w, acc, add_shared, stream=None):
         self.model.prefill_partial_dev(L, states, sel, w, acc, add_shared, stream)

@@ -283,13 +283,37 @@ int  ds4f_gpu_moe_prefill(Ds4fGpuModel *m, int layer, float *states_dev, int T,
  * counterpart): the model's shard of the routed combine, plus the shared
  * expert when add_shared, into acc_dev [T][H]; states_dev is read only.
  * Summing acc over a partition of the experts and adding it to the states
- * completes the layer. */
+ * completes the layer. Asynchronous on `stream` (it is called once per layer
+ * between collectives): a tensor-core pipeline wait that gave up is reported
+ * (-1) by a later partial call of this model. */
 int  ds4f_gpu_moe_prefill_partial(Ds4fGpuModel *m, int layer, const float *states_dev, int T,
                                   const int *sel_dev, const float *w_dev, float *acc_dev,
                                   int add_shared, void *stream);
 /* Every layer in order: sel_dev / w_dev [n_layers][T][K]. */
 int  ds4f_gpu_prefill(Ds4fGpuModel *m, float *states_dev, int T, const int *sel_dev,
                       const float *w_dev, void *stream);
+
+/* Batched decode of B tokens through one layer: the per-token router and
+ * top-K (src/main.c:1014-1088, ds4f_topk src/moe.c:531-561, certified as
+ * in ds4f_gpu_moe_layer: bit-exact indices) for all B tokens on the device,
+ * then the grouped expert chain of the batched step (ds4f_moe_step_batch,
+ * src/moe.c:1480-1707) on the tensor cores with that routing, as
+ * ds4f_gpu_moe_prefill computes it (3-digit E4M3 activations). states_dev
+ * [B][H] in/out; idx_dev / w_dev [B][K] receive the routing (may be NULL).
+ * Synchronous on `stream`. */
+int  ds4f_gpu_moe_layer_batch_dev(Ds4fGpuModel *m, int layer, float *states_dev, int B,
+                                  int *idx_dev, float *w_dev, void *stream);
+/* Expert-parallel form (no reference counterpart): routing on the full
+ * states as on every rank, this shard's part of the combine (plus the
+ * shared expert when add_shared) into acc_dev [B][H]; states unchanged.
+ * Asynchronous on `stream`, errors reported by a later partial call, as
+ * ds4f_gpu_moe_prefill_partial. */
+int  ds4f_gpu_moe_layer_batch_partial_dev(Ds4fGpuModel *m, int layer, const float *states_dev,
+                                          int B, float *acc_dev, int add_shared, void *stream);
+/* n_steps decode steps of B tokens through every layer (the batched
+ * counterpart of ds4f_gpu_moe_stack_dev); one pipeline check at the end. */
+int  ds4f_gpu_moe_stack_batch_dev(Ds4fGpuModel *m, float *states_dev, int B, int n_steps,
+                                  void *stream);
 
 #ifdef __cplusplus
 }

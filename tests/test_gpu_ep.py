@@ -1,8 +1,10 @@
 """Expert-parallel decode on 2 GPUs (one process per GPU, NCCL): each rank
 holds half of every layer's experts; after each step every rank's state
 equals the single-GPU full model's within fp32 reassociation of the combine
-(the partial sums meet in the all-reduce), and the oracle's within the
-chain tolerance. Skipped with fewer than 2 GPUs."""
+(the partial sums meet in the all-reduce): one token against the per-token
+layer steps, a batch against the batched (tensor-core) stack, which is in
+turn within the chain tolerance of the per-token fp32 path. Skipped with
+fewer than 2 GPUs."""
 import importlib.util
 import os
 
@@ -14,7 +16,7 @@ from tests._lib import ds4f_cuda, gpu_available
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-H, M, E, K, NL, B = 1024, 256, 64, 8, 3, 2
+H, M, E, K, NL = 1024, 256, 64, 8, 3
 REASSOC_TOL = 1e-5
 CHAIN_TOL = 2e-3
 
@@ -33,11 +35,11 @@ def _ep_module():
     return mod
 
 
-def _x0():
+def _x0(B):
     return po.fill_f32(B * H, po.key(21, 0, 4, 0, 0), 1.0).reshape(B, H).copy()
 
 
-def _rank(rank, world, port, fmt, out):
+def _rank(rank, world, port, fmt, B, out):
     import datetime
     import torch
     import torch.distributed as dist
@@ -52,7 +54,7 @@ def _rank(rank, world, port, fmt, out):
     ep = _ep_module()
     shard = ep.GpuShard(dc, fmt, NL, H, M, E, K, rank, world, seed=21)
     dec = ep.ExpertParallelDecoder(shard)
-    st = torch.from_numpy(_x0()).cuda()
+    st = torch.from_numpy(_x0(B)).cuda()
     for _ in range(2):
         dec.step(st, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
@@ -63,8 +65,9 @@ def _rank(rank, world, port, fmt, out):
 
 
 @pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("B", [1, 2])
 @pytest.mark.parametrize("fmt", [2, 0])            # FP8, MXFP4
-def test_expert_parallel_two_gpus(fmt):
+def test_expert_parallel_two_gpus(fmt, B):
     import socket
     import torch
     import torch.multiprocessing as mp
@@ -73,21 +76,28 @@ def test_expert_parallel_two_gpus(fmt):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, fmt, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, fmt, B, out)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(300)
         assert p.exitcode == 0
     assert np.array_equal(out[0], out[1])
-    # the single-GPU full model, layer by layer (two steps)
+    # the single-GPU full model (two steps): per-token layer steps, and for
+    # a batch the batched stack
     dc = ds4f_cuda()
     dc.init()
     m = dc.Model(fmt, NL, H, M, E, K)
     m.synth(21)
     m.set_path(dc.PATH_LAYERED)
-    x0 = _x0()
-    want = np.stack([m.stack(x0[b], 2) for b in range(B)])
+    x0 = _x0(B)
+    exact = np.stack([m.stack(x0[b], 2) for b in range(B)])
+    want = exact
+    if B > 1:
+        st = torch.from_numpy(x0.copy()).cuda()
+        m.stack_batch_dev(st, 2)
+        want = st.cpu().numpy()
+        assert np.abs(want - exact).max() / np.abs(exact - x0).max() < CHAIN_TOL
     m.close()
     err = np.abs(out[0] - want).max() / np.abs(want - x0).max()
     assert err < REASSOC_TOL, err
