@@ -208,29 +208,38 @@ __device__ bool mbar_wait(const DecodeArgs &a, uint64_t *b, uint32_t parity, uns
 // while any is still from an earlier layer); n is even (16-byte copies).
 // One bulk copy per round instead of per-thread polls. false (uniformly)
 // on timeout or abort.
+// The first copy of a gather, issued ahead so the block can work while it
+// is in flight (gather_ll with issued = true then waits for it).
+__device__ __forceinline__ void gather_issue(uint64_t *bar, uint32_t &pendb, uint64_t *dst, const uint64_t *src,
+                                             int n) {
+    if (threadIdx.x == 0) {
+        fence_async();
+        mbar_expect(bar, n * 8);
+        bulk(dst, src, n * 8, bar);
+    }
+    pendb |= 1u << 7;
+}
+
+// Copy n tagged words into dst until the first ncheck carry `tag`. Each
+// round is one bulk copy and two block barriers (the copy's round trip
+// spaces the polls); every 16th round also checks the limit and an abort.
 __device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uint32_t &pendb,
                           uint64_t *dst, const uint64_t *src, int n, int ncheck, uint32_t tag,
-                          unsigned code, unsigned long long *rounds = nullptr) {
+                          unsigned code, unsigned long long *rounds = nullptr, bool issued = false) {
     const int tid = threadIdx.x;
     for (long it = 0;; it++) {
         if (rounds && tid == 0) *rounds = (unsigned long long)(it + 1);
-        if (tid == 0) {
-            fence_async();
-            mbar_expect(bar, n * 8);
-            bulk(dst, src, n * 8, bar);
-        }
-        pendb |= 1u << 7;
+        if (it > 0 || !issued) gather_issue(bar, pendb, dst, src, n);
         if (!__syncthreads_and(mbar_wait(a, bar, (phb >> 7) & 1u, code))) return false;
         phb ^= 1u << 7;
         pendb &= ~(1u << 7);
         bool all = true;
         for (int i = tid; i < ncheck; i += kThreads) all = all && (uint32_t)(dst[i] >> 32) == tag;
         if (__syncthreads_and(all)) return true;
-        if (__syncthreads_or(it > (1L << 20) || aborted(a))) {
+        if ((it & 15) == 15 && __syncthreads_or(it > (1L << 20) || aborted(a))) {
             if (tid == 0 && !aborted(a)) give_up(a, code);
             return false;
         }
-        __nanosleep(128);
     }
 }
 
@@ -430,69 +439,57 @@ k_decode(DecodeArgs a) {
             __syncthreads();
         }
         DS4F_TRACE(2);
-        // (C) router rows: warps 4 r .. 4 r + 3 take row r (r < nrt), warp q
-        //     the columns [q H/4, (q+1) H/4), lane l CPL contiguous columns of
-        //     them. Pass 1: chunk sums and each warp's total; the totals of the
-        //     warps before give each lane its exact column-order prefix for the
-        //     bound in pass 2 (named barrier over the router warps only).
-        if (warp < 4 * nrt) {
-            constexpr int CQ = H / 4, CPL = CQ / 32, NCH = CPL / 8;
-            static_assert(CPL % 8 == 0, "router rows: whole 8-element chunks per lane");
-            const int rr = warp >> 2, q = warp & 3, e = rt0 + rr, nrw = 128 * nrt;
-            const int c0 = q * CQ + lane * CPL;
+        // (C) router rows: warps RW r .. RW r + RW - 1 take row r (r < nrt),
+        //     warp q the columns [q H/RW, (q+1) H/RW), lane l 8 contiguous
+        //     columns of them (RW = H / 256). The chunk sums and each warp's
+        //     total give each lane its exact column-order prefix for the
+        //     bound (named barrier over the router warps only).
+        constexpr int RW = H / 256;
+        static_assert(RW * 2 <= kWarps, "two router rows per CTA at most");
+        if (warp < RW * nrt) {
+            constexpr int CQ = H / RW;
+            static_assert(CQ == 256, "router rows: one 8-element chunk per lane");
+            const int rr = warp / RW, q = warp % RW, e = rt0 + rr, nrw = 32 * RW * nrt;
+            const int c0 = q * CQ + lane * 8;
             const uint16_t *row = rt + rr * H + c0;
-            double Tq[NCH];
-            float Aq[NCH];
+            uint4 w = lds16(row);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+            const float4 x0 = *(const float4 *)(xin + c0);
+            const float4 x1 = *(const float4 *)(xin + c0 + 4);
+            const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            double p8[8];
+            // the bound's |p| (8 - u) terms: positive, summed in fp32 (8 terms
+            // per lane, relative error < 1e-6, inside the 1.001 margin)
+            float ab = 0.f;
 #pragma unroll
-            for (int k = 0; k < NCH; k++) {
-                uint4 w = lds16(row + k * 8);
-                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-                const float4 x0 = *(const float4 *)(xin + c0 + k * 8);
-                const float4 x1 = *(const float4 *)(xin + c0 + k * 8 + 4);
-                const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                double p8[8];
-                // the bound's |p| (8 - u) terms: positive, summed in fp32 (<= 64
-                // terms per lane, relative error < 4e-6, inside the 1.001 margin)
-                float ab = 0.f;
-#pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    uint32_t h = (u & 1) ? (ww[u >> 1] & 0xFFFF0000u) : (ww[u >> 1] << 16);
-                    float pr = __fmul_rn(__uint_as_float(h), x[u]);   // the reference's product
-                    p8[u] = (double)pr;
-                    ab = fmaf(fabsf(pr), (float)(8 - u), ab);
-                }
-                Tq[k] = __dadd_rn(__dadd_rn(__dadd_rn(p8[0], p8[1]), __dadd_rn(p8[2], p8[3])),
-                                  __dadd_rn(__dadd_rn(p8[4], p8[5]), __dadd_rn(p8[6], p8[7])));
-                Aq[k] = ab;
+            for (int u = 0; u < 8; u++) {
+                uint32_t h = (u & 1) ? (ww[u >> 1] & 0xFFFF0000u) : (ww[u >> 1] << 16);
+                float pr = __fmul_rn(__uint_as_float(h), x[u]);   // the reference's product
+                p8[u] = (double)pr;
+                ab = fmaf(fabsf(pr), (float)(8 - u), ab);
             }
-            double tot = 0.0;
-#pragma unroll
-            for (int k = 0; k < NCH; k++) tot = __dadd_rn(tot, Tq[k]);
+            const double tot = __dadd_rn(__dadd_rn(__dadd_rn(p8[0], p8[1]), __dadd_rn(p8[2], p8[3])),
+                                         __dadd_rn(__dadd_rn(p8[4], p8[5]), __dadd_rn(p8[6], p8[7])));
             double incl = tot;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 double y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
                 if (lane >= o) incl = __dadd_rn(incl, y);
             }
-            double *rx = (double *)red + 32;      // [row][quarter] totals, then at +8 bound parts
-            if (lane == 31) rx[rr * 4 + q] = incl;
+            double *rx = (double *)red + 32;      // [row][warp] totals, then at +2 RW bound parts
+            if (lane == 31) rx[rr * RW + q] = incl;
             asm volatile("bar.sync 1, %0;" ::"r"(nrw) : "memory");
             double P = __dsub_rn(incl, tot);      // prefix before this lane within the warp
-            for (int k = 0; k < q; k++) P = __dadd_rn(rx[rr * 4 + k], P);
-            double bs = 0.0, loc = 0.0;
-#pragma unroll
-            for (int k = 0; k < NCH; k++) {
-                bs = __dadd_rn(bs, __dadd_rn(8.0 * fabs(__dadd_rn(P, loc)), (double)Aq[k]));
-                loc = __dadd_rn(loc, Tq[k]);
-            }
+            for (int k = 0; k < q; k++) P = __dadd_rn(rx[rr * RW + k], P);
+            double bs = __dadd_rn(8.0 * fabs(P), (double)ab);
             bs = warp_sum_d(bs);
-            if (lane == 0) rx[8 + rr * 4 + q] = bs;
+            if (lane == 0) rx[2 * RW + rr * RW + q] = bs;
             asm volatile("bar.sync 1, %0;" ::"r"(nrw) : "memory");
             if (q == 0 && lane < 4) {
                 double Sv = 0.0, Bs = 0.0;
-                for (int k = 0; k < 4; k++) {
-                    Sv = __dadd_rn(Sv, rx[rr * 4 + k]);
-                    Bs = __dadd_rn(Bs, rx[8 + rr * 4 + k]);
+                for (int k = 0; k < RW; k++) {
+                    Sv = __dadd_rn(Sv, rx[rr * RW + k]);
+                    Bs = __dadd_rn(Bs, rx[2 * RW + rr * RW + k]);
                 }
                 // the prefixes carry double rounding of their own: widen by 1e-12
                 const double Bv = 1.001 * kU * (Bs * (1.0 + 1e-12)) + 1e-300;
@@ -502,12 +499,20 @@ k_decode(DecodeArgs a) {
                                     : lane == 2 ? (uint32_t)bb : (uint32_t)(bb >> 32);
                 st_tag(a.sb_ll + 4 * e + lane, tg, word);
             }
-        } else if ((warp >= 8 && warp < 8 + 2 * nsg) || (warp == kWarps - 1 && c == 0)) {
-            // (D) shared gate (even) / up (odd) rows and, CTA 0 warp 15, the
-            // shared-gate row: prefetched into shared memory (bar 8)
+        }
+        DS4F_TRACE(3);
+        // the first copy of the router-logit gather flies while the shared
+        // expert's rows are computed (its words land in the gathers' region,
+        // clear of the shared rows; the last reads of that region, the state
+        // words, were ordered by the barriers of (B))
+        static_assert(E % 32 == 0 && (4 * E * 8) % 16 == 0, "router width: whole warps of experts");
+        gather_issue(bar + 7, pendb, (uint64_t *)gu, a.sb_ll, 4 * E);
+        // (D) shared gate (even) / up (odd) rows and, CTA 0 warp 15, the
+        //     shared-gate row: prefetched into shared memory (bar 8)
+        if (warp < 2 * nsg || (warp == kWarps - 1 && c == 0)) {
             const bool okd = mbar_wait(a, bar + 8, PH(8), 9);
             const bool gl = warp == kWarps - 1 && c == 0;   // CTA 0 has < 4 shared rows
-            const int w2 = warp - 8, m = w2 & 1;
+            const int w2 = warp, m = w2 & 1;
             const uint16_t *row = (const uint16_t *)(gu + L::SHO) +
                                   (gl ? 2 * L::NSG * H : (m * L::NSG + (w2 >> 1)) * H);
             float acc = 0.f;
@@ -524,12 +529,10 @@ k_decode(DecodeArgs a) {
         }
         FLIP(8);
         PEND(8, false);
-        DS4F_TRACE(3);
         // (F) routing: gather every S/B word, then warp 0 takes the
         //     certified top-K
-        static_assert(E % 32 == 0 && (4 * E * 8) % 16 == 0, "router width: whole warps of experts");
         if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.sb_ll, 4 * E, 4 * E, tg, 3,
-                       DS4F_ROUNDS(15))) {
+                       DS4F_ROUNDS(15), true)) {
             ok = false;
             break;
         }
