@@ -95,13 +95,59 @@ __device__ __forceinline__ unsigned long long gtimer() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// order-preserving 32-bit key of a float
-__device__ __forceinline__ uint32_t fkey(float f) {
-    uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+// ---- top-8 by a warp sorting network ------------------------------------------
+// Candidates for the selection are ordered by a 32-bit key: the logit's
+// order-preserving float key with its low 8 bits replaced by 255 - expert
+// (so the lower index comes first among equal keys, as in ds4f_topk,
+// src/moe.c:537-545). The key only proposes the 8 to certify: the
+// certificate itself compares the exact intervals, so two logits too close
+// for the key cannot pass it and go to the exact fallback instead.
+__device__ __forceinline__ uint32_t tk_key(double s, int e) {
+    const uint32_t u = __float_as_uint(__double2float_rn(s));
+    const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return (k & 0xFFFFFF00u) | (uint32_t)(255 - e);
 }
-__device__ __forceinline__ float fkey_inv(uint32_t k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+__device__ __forceinline__ int tk_expert(uint32_t key) { return 255 - (int)(key & 0xFFu); }
+// Bitonic sort of 8 keys, largest first.
+__device__ __forceinline__ void tk_sort8(uint32_t (&k8)[8]) {
+#pragma unroll
+    for (int k = 2; k <= 8; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint32_t hi = max(k8[i], k8[l]), lo = min(k8[i], k8[l]);
+                    k8[i] = (i & k) == 0 ? hi : lo;
+                    k8[l] = (i & k) == 0 ? lo : hi;
+                }
+            }
+}
+// Every lane holds its own sorted 8; after the five butterfly merges every
+// lane holds the warp's largest 8, sorted (the larger of each list against
+// the reverse of the other is the pair's largest 8 as a bitonic sequence,
+// sorted again by three half-cleaner rounds).
+__device__ __forceinline__ void tk_warp_top8(uint32_t (&k8)[8]) {
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        uint32_t p[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) p[j] = __shfl_xor_sync(0xFFFFFFFFu, k8[j], m);
+#pragma unroll
+        for (int j = 0; j < 8; j++) k8[j] = max(k8[j], p[7 - j]);
+#pragma unroll
+        for (int j = 4; j > 0; j >>= 1)
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const uint32_t hi = max(k8[i], k8[l]), lo = min(k8[i], k8[l]);
+                    k8[i] = hi;
+                    k8[l] = lo;
+                }
+            }
+    }
 }
 
 // ---- shapes -------------------------------------------------------------------
@@ -165,8 +211,7 @@ struct Smem {
     static constexpr int o_red = o_outs + a16((K + 1) * RR * 4);
     static constexpr int o_tk = o_red + 1024;                         // [E] doubles
     static constexpr int o_cand = o_tk + a16(E * 8);                  // [E] ints
-    static constexpr int o_cl = o_cand + a16(E * 4);                  // candidates: 4 x 32 doubles
-    static constexpr int o_sel = o_cl + 4 * 32 * 8;                   // sel[64], wsel[64], ctl[16]
+    static constexpr int o_sel = o_cand + a16(E * 4);                 // sel[64], wsel[64], ctl[16]
     static constexpr int bytes = o_sel + 64 * 4 + 64 * 4 + 16 * 4;
 };
 
@@ -265,7 +310,6 @@ k_decode(DecodeArgs a) {
     float *red = (float *)(sm + L::o_red);
     double *tk = (double *)(sm + L::o_tk);
     int *candf = (int *)(sm + L::o_cand);
-    double *cl = (double *)(sm + L::o_cl);          // [4][32]: S, lo, hi, e
     int *sel = (int *)(sm + L::o_sel);
     float *wsel = (float *)(sel + 64);
     int *ctl = (int *)(wsel + 64);
@@ -536,95 +580,65 @@ k_decode(DecodeArgs a) {
             ok = false;
             break;
         }
+        DS4F_TRACE(18);        // every router word visible; the top-K follows
         if (warp == 0) {
             constexpr int NE = E / 32;
-            double sv[NE], lo[NE], hi[NE];
-            // experts lane + 32 i, words 4e .. 4e+3 (S lo/hi, B lo/hi)
-            uint32_t wv[4 * NE];
+            static_assert(K == 8 && NE <= 8, "the sorting network selects 8");
+            // expert e's words 4e .. 4e+3: S (low, high half), its bound (low, high)
             const uint64_t *sbw = (const uint64_t *)gu;
+            auto word_d = [&](int w) {
+                return __longlong_as_double((long long)(((uint64_t)(uint32_t)sbw[w + 1] << 32) | (uint32_t)sbw[w]));
+            };
+            // the first 8 by key in selection order, in every lane (lane l
+            // starts from experts l + 32 i)
+            static_assert(E <= 256, "expert index in the key's low byte");
+            uint32_t k8[8];
 #pragma unroll
-            for (int i = 0; i < NE; i++)
+            for (int i = 0; i < 8; i++) {
+                k8[i] = 0u;
+                if (i < NE) {
+                    const int e = lane + 32 * i;
+                    const double sv = word_d(4 * e);
+                    k8[i] = tk_key(sv, e);
+                    tk[e] = (double)(float)sv;
+                }
+            }
+            if (lane == 0) { ctl[3] = 1; ctl[1] = 0; }
+            tk_sort8(k8);
+            tk_warp_top8(k8);
+            // lane r < 8: the r-th selection's interval
+            int er = 0;
 #pragma unroll
-                for (int h = 0; h < 4; h++) wv[4 * i + h] = (uint32_t)sbw[4 * (lane + 32 * i) + h];
-            bool got = true;
+            for (int j = 0; j < 8; j++) if (j == lane) er = tk_expert(k8[j]);
+            double lor = 1.0e308, hir = -1.0e308;
+            if (lane < K) {
+                const double b_ = a.exact_all ? 0.0 : word_d(4 * er + 2);
+                lor = word_d(4 * er) - b_;
+                hir = word_d(4 * er) + b_;
+            }
+            // certified when consecutive selections' intervals separate and
+            // only the 8 selections reach the last one's lower bound (then
+            // every reference-order logit ranks the same); otherwise the
+            // exact fallback recomputes every expert whose interval reaches
+            // the lowest lower bound among the 8 (a superset of the true 8)
+            const double hin = __shfl_down_sync(0xFFFFFFFFu, hir, 1);
+            const bool sep = lane >= K - 1 || lor > hin;
+            const double lo8 = __shfl_sync(0xFFFFFFFFu, lor, K - 1);
+            double lmin = lor;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) lmin = fmin(lmin, __shfl_xor_sync(0xFFFFFFFFu, lmin, o));
+            int nmine = 0;
 #pragma unroll
             for (int i = 0; i < NE; i++) {
-                const double s = __longlong_as_double((long long)(((uint64_t)wv[4 * i + 1] << 32) | wv[4 * i]));
-                const double b = a.exact_all ? 0.0
-                    : __longlong_as_double((long long)(((uint64_t)wv[4 * i + 3] << 32) | wv[4 * i + 2]));
-                sv[i] = s; lo[i] = s - b; hi[i] = s + b;
+                const int e = lane + 32 * i;
+                const double hi = word_d(4 * e) + (a.exact_all ? 0.0 : word_d(4 * e + 2));
+                nmine += hi >= lo8;
+                candf[e] = a.exact_all || hi >= lmin;
             }
-            got = __all_sync(0xFFFFFFFFu, got);
-            if (lane == 0) { ctl[3] = got; ctl[1] = 0; }
-            if (got) {
-                // K-th largest lower bound from float keys rounded down: a
-                // lower bound of the true one, so candidates can only grow
-                uint32_t key[NE];
-#pragma unroll
-                for (int i = 0; i < NE; i++)
-                    key[i] = (lane + 32 * i < E) ? fkey(__double2float_rd(lo[i])) : 0u;
-                uint32_t taken = 0, thr = 0;
-                int rem = K;
-                for (int it = 0; it < K; it++) {
-                    uint32_t mloc = 0;
-#pragma unroll
-                    for (int i = 0; i < NE; i++) if (!(taken >> i & 1)) mloc = max(mloc, key[i]);
-                    const uint32_t gmax = __reduce_max_sync(0xFFFFFFFFu, mloc);
-                    uint32_t cl_ = 0;
-#pragma unroll
-                    for (int i = 0; i < NE; i++)
-                        if (!(taken >> i & 1) && key[i] == gmax) { cl_++; taken |= 1u << i; }
-                    const int cnt = (int)__reduce_add_sync(0xFFFFFFFFu, cl_);
-                    thr = gmax;
-                    if (cnt >= rem) break;
-                    rem -= cnt;
-                }
-                const double lk = (double)fkey_inv(thr);
-                int nmine = 0;
-#pragma unroll
-                for (int i = 0; i < NE; i++) nmine += (lane + 32 * i < E) && hi[i] >= lk;
-                const int ncand = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
-                bool cert = !a.exact_all && ncand == K;
-                if (cert) {
-                    // compact the K candidates, rank them by S (lower index
-                    // first on equal S), check adjacent intervals separate
-                    int base = 0;
-#pragma unroll
-                    for (int i = 0; i < NE; i++) {
-                        const bool cf = (lane + 32 * i < E) && hi[i] >= lk;
-                        const unsigned msk = __ballot_sync(0xFFFFFFFFu, cf);
-                        if (cf) {
-                            const int pos = base + __popc(msk & ((1u << lane) - 1));
-                            cl[pos] = sv[i]; cl[32 + pos] = lo[i]; cl[64 + pos] = hi[i];
-                            cl[96 + pos] = (double)(lane + 32 * i);
-                        }
-                        base += __popc(msk);
-                    }
-                    __syncwarp();
-                    double *rd = (double *)red;
-                    if (lane < K) {
-                        const double s = cl[lane], ex = cl[96 + lane];
-                        int rk = 0;
-                        for (int q = 0; q < K; q++)
-                            rk += (cl[q] > s) || (cl[q] == s && cl[96 + q] < ex);
-                        sel[rk] = (int)ex;
-                        rd[rk] = cl[32 + lane];            // lo by rank
-                        rd[16 + rk] = cl[64 + lane];       // hi by rank
-                    }
-                    __syncwarp();
-                    const bool sep = lane >= K - 1 || rd[lane] > rd[16 + lane + 1];
-                    cert = __all_sync(0xFFFFFFFFu, sep);
-                }
-#pragma unroll
-                for (int i = 0; i < NE; i++) {
-                    const int e = lane + 32 * i;
-                    if (e < E) {
-                        tk[e] = (double)(float)sv[i];
-                        candf[e] = a.exact_all || hi[i] >= lk;
-                    }
-                }
-                if (lane == 0) ctl[1] = cert ? 1 : 0;
-            }
+            const int nreach = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
+            const bool cert = !a.exact_all && __all_sync(0xFFFFFFFFu, sep) && nreach == K;
+            if (cert && lane < K) sel[lane] = er;
+            if (lane == 0) ctl[1] = cert ? 1 : 0;
         }
         // ctl[] is read after the barrier (a __syncthreads_and predicate
         // would be evaluated before warp 0 wrote it)

@@ -50,6 +50,11 @@ def phase_table(tr):
     for k, name in enumerate(["down: chain gather", "down: row-dots", "down: combine"]):
         rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
                      float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
+    # slot 18: every router word visible (between rows_done and routes_vis)
+    inner = np.diff(tr[:, :, [3, 18, 4]], axis=2)
+    for k, name in enumerate(["routes: gather", "routes: top-K"]):
+        rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
+                     float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
     out["phases_us"] = rows
     # slots 14-16: copy rounds of the state, router and chain gathers
     rounds = tr[:, :, 14:17].astype(np.float64)

@@ -200,7 +200,10 @@ int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
  * 0..13 are used: start, state ready, normed, router rows done, routes
  * visible, top-k done, copies issued, softmax done, first gate/up group
  * landed, chains done, down rows landed, state written (11), chains
- * gathered (12), row-dots done (13).
+ * gathered (12), row-dots done (13); 14..16 hold the copy rounds of the
+ * state, router-logit and chain gathers, 17 a bitmask of the gate/up copy
+ * groups that had landed before their compute, 18 the time every router
+ * word was visible (before the top-k).
  * n_stamps = 0 turns it off. */
 int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
 int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
