@@ -95,6 +95,7 @@ __device__ __forceinline__ float e2m1_raw(uint32_t nib) {
 #define DS4F_X_PRESCALE 1.8446744073709552e+19f    // 2^64
 #define DS4F_E2M1_POST 4.611686018427388e+18f      // 2^126 / 2^64 = 2^62
 #define DS4F_BF16_POST 5.421010862427522e-20f      // 2^-64
+#define DS4F_X_UNSCALE 5.421010862427522e-20f      // 2^-64: undoes DS4F_X_PRESCALE
 
 // ---- reductions ----------------------------------------------------------
 
@@ -142,22 +143,24 @@ __device__ __forceinline__ float f8_dot4(uint32_t w, const float *x) {
     return a + b;
 }
 
-// E4M3 bytes (0, 1) and (2, 3) of a canonical word -> fp32 x 2^-120, the
-// same bits as f8_raw: an arithmetic shift by 4 puts e and m at bits 20..26
-// and copies the sign into bits 27..31, of which the mask keeps bit 31.
-__device__ __forceinline__ float2 f8_lo2(uint32_t w) {
-    return make_float2(__int_as_float(((int)(w << 24) >> 4) & (int)0x87F00000),
-                       __int_as_float(((int)(w << 16) >> 4) & (int)0x87F00000));
-}
-__device__ __forceinline__ float2 f8_hi2(uint32_t w) {
-    return make_float2(__int_as_float(((int)(w << 8) >> 4) & (int)0x87F00000),
-                       __int_as_float(((int)w >> 4) & (int)0x87F00000));
+// Two canonical E4M3 bytes (the low 16 bits of w16) -> their fp32 values,
+// exactly: the hardware conversion to f16x2 (every E4M3 value, subnormals
+// included, is an f16; canonical bytes hold no NaN code), then to fp32.
+// Four instructions for two bytes, against three per byte by shifts.
+__device__ __forceinline__ float2 f8_cvt2(uint32_t w16) {
+    uint32_t h;
+    asm("{ .reg .b16 t; cvt.u16.u32 t, %1; cvt.rn.f16x2.e4m3x2 %0, t; }" : "=r"(h) : "r"(w16));
+    float lo, hi;
+    asm("{ .reg .b16 a, b; mov.b32 {a, b}, %2; cvt.f32.f16 %0, a; cvt.f32.f16 %1, b; }"
+        : "=f"(lo), "=f"(hi) : "r"(h));
+    return make_float2(lo, hi);
 }
 // acc + (Σ of the 4 products of w's bytes with x01, x23) * s, as two lanes
-// of packed fp32 (sm_100 FFMA2).
+// of packed fp32 (sm_100 FFMA2). With x pre-scaled by 2^64 the result is
+// in units of 2^-64 (DS4F_X_UNSCALE brings it back).
 __device__ __forceinline__ float2 f8_fma4(uint32_t w, float2 x01, float2 x23, float s, float2 acc) {
-    float2 p = __fmul2_rn(f8_lo2(w), x01);
-    p = __ffma2_rn(f8_hi2(w), x23, p);
+    float2 p = __fmul2_rn(f8_cvt2(w & 0xFFFFu), x01);
+    p = __ffma2_rn(f8_cvt2(w >> 16), x23, p);
     return __ffma2_rn(p, make_float2(s, s), acc);
 }
 

@@ -771,8 +771,8 @@ k_decode(DecodeArgs a) {
                         g2 = f8_fma4(*(const uint32_t *)(rg + off), x01, x23, sg[j], g2);
                         u2 = f8_fma4(*(const uint32_t *)(ru + off), x01, x23, su[j], u2);
                     }
-                    ag = (g2.x + g2.y) * DS4F_F8_POST;
-                    au = (u2.x + u2.y) * DS4F_F8_POST;
+                    ag = (g2.x + g2.y) * DS4F_X_UNSCALE;
+                    au = (u2.x + u2.y) * DS4F_X_UNSCALE;
                 } else {
                     const uint8_t *s4g = gsc + slot * S::gsc_b, *s4u = gsc + (L::PP + slot) * S::gsc_b;
                     float eg = 0.f, eu = 0.f;
@@ -862,7 +862,7 @@ k_decode(DecodeArgs a) {
                             a2 = f8_fma4(*(const uint32_t *)(row + 4 * (32 * g + lane)),
                                          make_float2(xc[4 * g], xc[4 * g + 1]),
                                          make_float2(xc[4 * g + 2], xc[4 * g + 3]), sc[g], a2);
-                        return (a2.x + a2.y) * DS4F_F8_POST;
+                        return (a2.x + a2.y) * DS4F_X_UNSCALE;
                     } else {
                         const uint8_t *s4 = dsc + j * L::DSC + (r0 + rr) * S::dsc_b - sa0;
                         float v = 0.f;
