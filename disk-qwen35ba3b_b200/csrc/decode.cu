@@ -639,6 +639,14 @@ k_decode(DecodeArgs a) {
             const bool cert = !a.exact_all && __all_sync(0xFFFFFFFFu, sep) && nreach == K;
             if (cert && lane < K) sel[lane] = er;
             if (lane == 0) ctl[1] = cert ? 1 : 0;
+            if (cert) {
+                // the routing is final: the gate/up copies start now (their
+                // buffers' last readers, the previous layer's gate/up and this
+                // warp's look at the router words, are done)
+                __syncwarp();
+                fence_async();
+                issue_group_lane(l, lane);
+            }
         }
         // ctl[] is read after the barrier (a __syncthreads_and predicate
         // would be evaluated before warp 0 wrote it)
@@ -673,14 +681,17 @@ k_decode(DecodeArgs a) {
         }
         DS4F_TRACE(5);
         // (G) every routed byte of this CTA in flight, one copy per lane:
-        //     warp 0 the gate/up groups, warp 1 the down rows, warp 2 the next
+        //     warp 0 the gate/up groups (already at the top-8 when it
+        //     certified), warp 1 the down rows, warp 2 the next
         //     layer's router rows + norm weights (buffers (B) and (C) are
         //     done with). Meanwhile the other warps load their x registers
         //     and the last warp takes the softmax alone.
         static_assert(kGroups * 8 <= 32 && 2 * K <= 32, "one copy per lane");
         if (warp == 0) {
-            fence_async();
-            issue_group_lane(l, lane);
+            if (!ctl[1]) {           // after the exact fallback (certified: issued above)
+                fence_async();
+                issue_group_lane(l, lane);
+            }
         } else if (warp == 1) {
             fence_async();
             if (lane == 0) mbar_expect(bar + 6, dn_total);
