@@ -102,8 +102,8 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // src/moe.c:537-545). The key only proposes the 8 to certify: the
 // certificate itself compares the exact intervals, so two logits too close
 // for the key cannot pass it and go to the exact fallback instead.
-__device__ __forceinline__ uint32_t tk_key(double s, int e) {
-    const uint32_t u = __float_as_uint(__double2float_rn(s));
+__device__ __forceinline__ uint32_t tk_key(float s, int e) {
+    const uint32_t u = __float_as_uint(s);
     const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     return (k & 0xFFFFFF00u) | (uint32_t)(255 - e);
 }
@@ -226,7 +226,7 @@ struct DecodeArgs {
     uint32_t epoch;             // 1..65535, distinct from the previous launch's
     float *state;               // [H] in (read at layer 0) / out (last layer)
     uint64_t *st_ll;            // [H] tagged state words
-    uint64_t *sb_ll;            // [E][4] tagged S (lo, hi) and B (lo, hi) words
+    uint64_t *sb_ll;            // [E][4] tagged words: S, its interval's ends (fp32), 0
     uint64_t *ch_ll;            // [(K+1) M + 1] tagged chains, then the shared-gate logit
     unsigned *diag;             // [4]: layers, fallbacks, error code, failing CTA
     unsigned long long *trace;  // optional [T][G][kTracePts] %globaltimer stamps
@@ -537,10 +537,14 @@ k_decode(DecodeArgs a) {
                 }
                 // the prefixes carry double rounding of their own: widen by 1e-12
                 const double Bv = 1.001 * kU * (Bs * (1.0 + 1e-12)) + 1e-300;
-                const uint64_t sb = (uint64_t)__double_as_longlong(Sv);
-                const uint64_t bb = (uint64_t)__double_as_longlong(Bv);
-                const uint32_t word = lane == 0 ? (uint32_t)sb : lane == 1 ? (uint32_t)(sb >> 32)
-                                    : lane == 2 ? (uint32_t)bb : (uint32_t)(bb >> 32);
+                // published as fp32: S rounded to nearest (the softmax input and
+                // the selection key), the interval [S - B, S + B] rounded
+                // outward (still a certificate, wider by at most an ulp)
+                const float sf = __double2float_rn(Sv);
+                const float lf = __double2float_rd(__dsub_rd(Sv, Bv));
+                const float hf = __double2float_ru(__dadd_ru(Sv, Bv));
+                const uint32_t word = lane == 0 ? __float_as_uint(sf) : lane == 1 ? __float_as_uint(lf)
+                                    : lane == 2 ? __float_as_uint(hf) : 0u;
                 st_tag(a.sb_ll + 4 * e + lane, tg, word);
             }
         }
@@ -584,11 +588,9 @@ k_decode(DecodeArgs a) {
         if (warp == 0) {
             constexpr int NE = E / 32;
             static_assert(K == 8 && NE <= 8, "the sorting network selects 8");
-            // expert e's words 4e .. 4e+3: S (low, high half), its bound (low, high)
+            // expert e's words 4e .. 4e+2: S, and its interval's ends (fp32)
             const uint64_t *sbw = (const uint64_t *)gu;
-            auto word_d = [&](int w) {
-                return __longlong_as_double((long long)(((uint64_t)(uint32_t)sbw[w + 1] << 32) | (uint32_t)sbw[w]));
-            };
+            auto word_f = [&](int w) { return __uint_as_float((uint32_t)sbw[w]); };
             // the first 8 by key in selection order, in every lane (lane l
             // starts from experts l + 32 i)
             static_assert(E <= 256, "expert index in the key's low byte");
@@ -598,9 +600,9 @@ k_decode(DecodeArgs a) {
                 k8[i] = 0u;
                 if (i < NE) {
                     const int e = lane + 32 * i;
-                    const double sv = word_d(4 * e);
+                    const float sv = word_f(4 * e);
                     k8[i] = tk_key(sv, e);
-                    tk[e] = (double)(float)sv;
+                    tk[e] = (double)sv;
                 }
             }
             if (lane == 0) { ctl[3] = 1; ctl[1] = 0; }
@@ -610,28 +612,27 @@ k_decode(DecodeArgs a) {
             int er = 0;
 #pragma unroll
             for (int j = 0; j < 8; j++) if (j == lane) er = tk_expert(k8[j]);
-            double lor = 1.0e308, hir = -1.0e308;
+            float lor = 3.0e38f, hir = -3.0e38f;
             if (lane < K) {
-                const double b_ = a.exact_all ? 0.0 : word_d(4 * er + 2);
-                lor = word_d(4 * er) - b_;
-                hir = word_d(4 * er) + b_;
+                lor = word_f(4 * er + 1);
+                hir = word_f(4 * er + 2);
             }
             // certified when consecutive selections' intervals separate and
             // only the 8 selections reach the last one's lower bound (then
             // every reference-order logit ranks the same); otherwise the
             // exact fallback recomputes every expert whose interval reaches
             // the lowest lower bound among the 8 (a superset of the true 8)
-            const double hin = __shfl_down_sync(0xFFFFFFFFu, hir, 1);
+            const float hin = __shfl_down_sync(0xFFFFFFFFu, hir, 1);
             const bool sep = lane >= K - 1 || lor > hin;
-            const double lo8 = __shfl_sync(0xFFFFFFFFu, lor, K - 1);
-            double lmin = lor;
+            const float lo8 = __shfl_sync(0xFFFFFFFFu, lor, K - 1);
+            float lmin = lor;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) lmin = fmin(lmin, __shfl_xor_sync(0xFFFFFFFFu, lmin, o));
+            for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xFFFFFFFFu, lmin, o));
             int nmine = 0;
 #pragma unroll
             for (int i = 0; i < NE; i++) {
                 const int e = lane + 32 * i;
-                const double hi = word_d(4 * e) + (a.exact_all ? 0.0 : word_d(4 * e + 2));
+                const float hi = word_f(4 * e + 2);
                 nmine += hi >= lo8;
                 candf[e] = a.exact_all || hi >= lmin;
             }

@@ -46,7 +46,7 @@ struct Work {
     unsigned *diag;       // [4] 0: layers routed, 1: exact fallbacks, 2: error
                           //     code of the persistent kernel, 3: its CTA
     uint64_t *st_ll;      // [H] persistent kernel: tagged state words
-    uint64_t *sb_ll;      // [E][4] tagged router logits and bounds
+    uint64_t *sb_ll;      // [E][4] tagged router logits and interval ends (fp32)
     uint64_t *ch_ll;      // [(K+1) M + 1] tagged chains + shared-gate logit
 };
 
