@@ -53,8 +53,8 @@ def bytes_per_token(fmt_fp8=True):
 
 # DRAM bytes (read + write) of one k_decode launch, from the ncu --set full
 # capture summarised in profiles/k_decode_fp8_4layer_full.md (4-layer case,
-# 134.91 MB) scaled to 40 layers: every layer reads its own weights.
-TRAFFIC_PER_LAUNCH = 10 * 134_910_000
+# 133.95 MB) scaled to 40 layers: every layer reads its own weights.
+TRAFFIC_PER_LAUNCH = 10 * 133_950_000
 # kernels of one batched-prefill layer (csrc/prefill.cu): count, plan, place,
 # front end, gate/up GEMM, SiLU digits, down GEMM, shared gate/up and down
 # GEMMs, shared SiLU digits, combine
