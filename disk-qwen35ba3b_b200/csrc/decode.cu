@@ -95,61 +95,6 @@ __device__ __forceinline__ unsigned long long gtimer() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// ---- top-8 by a warp sorting network ------------------------------------------
-// Candidates for the selection are ordered by a 32-bit key: the logit's
-// order-preserving float key with its low 8 bits replaced by 255 - expert
-// (so the lower index comes first among equal keys, as in ds4f_topk,
-// src/moe.c:537-545). The key only proposes the 8 to certify: the
-// certificate itself compares the exact intervals, so two logits too close
-// for the key cannot pass it and go to the exact fallback instead.
-__device__ __forceinline__ uint32_t tk_key(float s, int e) {
-    const uint32_t u = __float_as_uint(s);
-    const uint32_t k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return (k & 0xFFFFFF00u) | (uint32_t)(255 - e);
-}
-__device__ __forceinline__ int tk_expert(uint32_t key) { return 255 - (int)(key & 0xFFu); }
-// Bitonic sort of 8 keys, largest first.
-__device__ __forceinline__ void tk_sort8(uint32_t (&k8)[8]) {
-#pragma unroll
-    for (int k = 2; k <= 8; k <<= 1)
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1)
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int l = i ^ j;
-                if (l > i) {
-                    const uint32_t hi = max(k8[i], k8[l]), lo = min(k8[i], k8[l]);
-                    k8[i] = (i & k) == 0 ? hi : lo;
-                    k8[l] = (i & k) == 0 ? lo : hi;
-                }
-            }
-}
-// Every lane holds its own sorted 8; after the five butterfly merges every
-// lane holds the warp's largest 8, sorted (the larger of each list against
-// the reverse of the other is the pair's largest 8 as a bitonic sequence,
-// sorted again by three half-cleaner rounds).
-__device__ __forceinline__ void tk_warp_top8(uint32_t (&k8)[8]) {
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-        uint32_t p[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) p[j] = __shfl_xor_sync(0xFFFFFFFFu, k8[j], m);
-#pragma unroll
-        for (int j = 0; j < 8; j++) k8[j] = max(k8[j], p[7 - j]);
-#pragma unroll
-        for (int j = 4; j > 0; j >>= 1)
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int l = i ^ j;
-                if (l > i) {
-                    const uint32_t hi = max(k8[i], k8[l]), lo = min(k8[i], k8[l]);
-                    k8[i] = hi;
-                    k8[l] = lo;
-                }
-            }
-    }
-}
-
 // ---- shapes -------------------------------------------------------------------
 template <int FMT, int H, int M>
 struct Shape {

@@ -151,7 +151,7 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
     int *rk = cand + E;
     float *xs = (float *)(rk + E);
     __shared__ double lk_s, red[8];
-    __shared__ int ncand_s, cert_s, sel_s[64];
+    __shared__ int ncand_s, cert_s, fast_s, sel_s[64];
     const int tid = threadIdx.x;
     for (int e = tid; e < E; e += blockDim.x) {
         double b = exact_all ? 0.0 : Bnd[e];
@@ -159,9 +159,45 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
         hi[e] = S[e] + b;
         v[e] = (float)S[e];
     }
-    if (tid == 0) { ncand_s = 0; cert_s = 1; }
+    if (tid == 0) { ncand_s = 0; cert_s = 1; fast_s = 0; }
     __syncthreads();
-    if (!exact_all) {
+    // Fast path (top-8 of at most 256): warp 0 proposes the 8 by a sorting
+    // network on 32-bit keys of the logits and certifies them on the
+    // intervals rounded outward to fp32 (consecutive selections separate,
+    // and only the 8 reach the last one's lower bound); the general path
+    // below runs only when that fails. Both select by the same rule, so a
+    // certified proposal is the general path's selection.
+    if (K == 8 && E % 32 == 0 && E <= 256 && !exact_all) {
+        if (tid < 32) {
+            const int lane = tid, NE = E / 32;
+            uint32_t k8[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                k8[i] = i < NE ? tk_key(__double2float_rn(S[lane + 32 * i]), lane + 32 * i) : 0u;
+            tk_sort8(k8);
+            tk_warp_top8(k8);
+            int er = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) if (j == lane) er = tk_expert(k8[j]);
+            float lor = 3.0e38f, hir = -3.0e38f;
+            if (lane < 8) {
+                lor = __double2float_rd(__dsub_rd(S[er], Bnd[er]));
+                hir = __double2float_ru(__dadd_ru(S[er], Bnd[er]));
+            }
+            const float hin = __shfl_down_sync(0xFFFFFFFFu, hir, 1);
+            const bool sep = lane >= 7 || lor > hin;
+            const float lo8 = __shfl_sync(0xFFFFFFFFu, lor, 7);
+            int nmine = 0;
+            for (int i = 0; i < NE; i++)
+                nmine += __double2float_ru(__dadd_ru(S[lane + 32 * i], Bnd[lane + 32 * i])) >= lo8;
+            const int nreach = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
+            const bool cert = __all_sync(0xFFFFFFFFu, sep) && nreach == 8;
+            if (cert && lane < 8) sel_s[lane] = er;
+            if (lane == 0) fast_s = cert ? 1 : 0;
+        }
+        __syncthreads();
+    }
+    if (!exact_all && !fast_s) {
         // K-th largest lower bound
         for (int e = tid; e < E; e += blockDim.x) {
             int r = 0;
@@ -195,7 +231,7 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
             __syncthreads();
         }
     }
-    if (exact_all || !cert_s) {
+    if (!fast_s && (exact_all || !cert_s)) {
         // exact reference-order logits for every candidate (all experts in
         // exact mode), then select on them
         for (int i = tid; i < H; i += blockDim.x) xs[i] = xin[i];
@@ -215,27 +251,36 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
         if (tid == 0 && !exact_all) atomicAdd(diag + 1, 1u);
         __syncthreads();
     }
-    // softmax over all E in double, max subtracted
+    // softmax over all E in double, max subtracted (the max as a block
+    // reduction: the same value in any order)
     double mx = -1e300;
-    for (int e = 0; e < E; e++) mx = fmax(mx, (double)v[e]);
+    for (int e = tid; e < E; e += blockDim.x) mx = fmax(mx, (double)v[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int k = 1; k < (int)(blockDim.x >> 5); k++) mx = fmax(mx, red[k]);
+    __syncthreads();
     double part = 0.0;
     for (int e = tid; e < E; e += blockDim.x) part += exp((double)v[e] - mx);
     part = warp_sum_d(part);
     if ((tid & 31) == 0) red[tid >> 5] = part;
     __syncthreads();
-    if (tid == 0) {
+    // the K selected probabilities in parallel, their fp32 sum in j order
+    __shared__ float wj_s[64];
+    if (tid < K) {
         double sw = 0.0;
         for (int k = 0; k < (int)(blockDim.x >> 5); k++) sw += red[k];
-        float wj[64];
+        wj_s[tid] = (float)(exp((double)v[sel_s[tid]] - mx) / sw);
+    }
+    __syncthreads();
+    if (tid == 0) {
         float s = 0.0f;
-        for (int j = 0; j < K; j++) {
-            int e = sel_s[j];
-            wj[j] = (float)(exp((double)v[e] - mx) / sw);
-            s = __fadd_rn(s, wj[j]);
-        }
+        for (int j = 0; j < K; j++) s = __fadd_rn(s, wj_s[j]);
         for (int j = 0; j < K; j++) {
             idx_out[j] = sel_s[j];
-            w_out[j] = (renorm && s > 0.0f) ? __fdiv_rn(wj[j], s) : wj[j];
+            w_out[j] = (renorm && s > 0.0f) ? __fdiv_rn(wj_s[j], s) : wj_s[j];
         }
         atomicAdd(diag, 1u);
     }
