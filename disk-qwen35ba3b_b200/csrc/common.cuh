@@ -219,6 +219,26 @@ __device__ __forceinline__ float2 f8_fma4(uint32_t w, float2 x01, float2 x23, fl
     return __ffma2_rn(p, make_float2(s, s), acc);
 }
 
+// Two E2M1 nibbles (the low byte of w8, the even element in the low nibble)
+// -> their fp32 values, exactly, by the hardware conversion to f16x2.
+__device__ __forceinline__ float2 e2m1_cvt2(uint32_t w8) {
+    uint32_t h;
+    asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(h) : "r"(w8));
+    float lo, hi;
+    asm("{ .reg .b16 a, b; mov.b32 {a, b}, %2; cvt.f32.f16 %0, a; cvt.f32.f16 %1, b; }"
+        : "=f"(lo), "=f"(hi) : "r"(h));
+    return make_float2(lo, hi);
+}
+// e2m1_dot8 by the hardware conversion: the same even / odd partial sums in
+// packed fp32, scaled to units of 2^-126 once at the end (the products are
+// the same up to that power of two).
+__device__ __forceinline__ float e2m1_dot8c(uint32_t w, const float *x) {
+    float2 p = __fmul2_rn(e2m1_cvt2(w & 0xFFu), make_float2(x[0], x[1]));
+    p = __ffma2_rn(e2m1_cvt2((w >> 8) & 0xFFu), make_float2(x[2], x[3]), p);
+    p = __ffma2_rn(e2m1_cvt2((w >> 16) & 0xFFu), make_float2(x[4], x[5]), p);
+    p = __ffma2_rn(e2m1_cvt2(w >> 24), make_float2(x[6], x[7]), p);
+    return (p.x + p.y) * 1.1754943508222875e-38f;      // 2^-126
+}
 // Dot of the 8 E2M1 nibbles of w (even index low nibble) with x[0..7], in
 // units of 2^-126.
 __device__ __forceinline__ float e2m1_dot8(uint32_t w, const float *x) {

@@ -736,8 +736,8 @@ k_decode(DecodeArgs a) {
 #pragma unroll
                     for (int j = 0; j < NGH; j++) {
                         const int gi = 32 * (hcol * NGH + j) + lane;
-                        eg = fmaf(e2m1_dot8(*(const uint32_t *)(rg + 4 * gi), xr + 8 * j), e8m0_to_f32(s4g[gi >> 2]), eg);
-                        eu = fmaf(e2m1_dot8(*(const uint32_t *)(ru + 4 * gi), xr + 8 * j), e8m0_to_f32(s4u[gi >> 2]), eu);
+                        eg = fmaf(e2m1_dot8c(*(const uint32_t *)(rg + 4 * gi), xr + 8 * j), e8m0_to_f32(s4g[gi >> 2]), eg);
+                        eu = fmaf(e2m1_dot8c(*(const uint32_t *)(ru + 4 * gi), xr + 8 * j), e8m0_to_f32(s4u[gi >> 2]), eu);
                     }
                     ag = eg * DS4F_E2M1_POST;
                     au = eu * DS4F_E2M1_POST;
@@ -826,7 +826,7 @@ k_decode(DecodeArgs a) {
 #pragma unroll
                         for (int g = 0; g < S::dg; g++) {
                             const int q = 32 * g + lane;
-                            v = fmaf(e2m1_dot8(*(const uint32_t *)(row + 4 * q), xc + 8 * g),
+                            v = fmaf(e2m1_dot8c(*(const uint32_t *)(row + 4 * q), xc + 8 * g),
                                      e8m0_to_f32(s4[q >> 2]), v);
                         }
                         return v * DS4F_E2M1_POST;
