@@ -20,7 +20,9 @@
 // the block's two scales differ per output element, so each block's partial
 // sums are read back from TMEM, the digits combined, and added into fp32
 // registers with the scales ("promotion") while the tensor core already
-// works on the next block in the other TMEM buffer.
+// works on the next block in the other TMEM buffer. The FP8 GEMMs run on
+// one persistent kernel (k_gemm_p); the shared expert's bf16 GEMMs
+// (k_gemm_bf16) accumulate their whole K in TMEM instead.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -105,132 +107,55 @@ __global__ void k_quant_f8_digits(const float *x, int N, int C, int ND, uint8_t 
     if (lane == 0) s[blk] = sc;
 }
 
-// ---- block-scaled GEMM ------------------------------------------------------------
-// Two element kinds share the kernel:
-//   FP8  (BF = false): tcgen05 kind::f8f6f4, 128-column K blocks (4 MMAs of
-//        K = 32), W's fp32 block scales and X's row scales promoted per block;
-//        ND digits combined as D0 + D1 / 16 + D2 / 256.
-//   BF16 (BF = true):  tcgen05 kind::f16 on bf16, 64-column K blocks (4 MMAs
-//        of K = 16), no scales; 2 digits (hi, lo) combined as D0 + D1.
-// A is [slots][R][C] (3-D tensor map; slot = the expert), B the digit planes
-// [ND][rows][C]. Dense mode: tile = blockIdx.y, rows n0 = 64 blockIdx.y,
-// slot 0. Grouped mode: tile t = blockIdx.y < *ntiles names (slot, first B
-// row, valid rows) -- the experts' token groups of the batched prefill.
-constexpr int kStages = 4;
 constexpr int kEpiWarps = 16;              // four per TMEM lane quadrant, 16 columns each
 constexpr int kEpiCols = kGemmBN / (kEpiWarps / 4);
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2.. epilogue
+static_assert(kEpiCols == 16, "one 16-column TMEM load per warp");
 
-template <int ND, bool BF>
-struct GemmSmem {
-    static constexpr int NM = kGemmBN * ND;           // MMA N: the digit rows of 64 columns
-    static constexpr int A = 128 * 128;               // one 128-row x 128-byte tile
-    static constexpr int B = NM * 128;
-    static constexpr int STAGE = A + B;
-    static constexpr int o_bar = kStages * STAGE;     // full[S], empty[S], tfull[2], tempty[2], done
-    static constexpr int o_slot = o_bar + ((2 * kStages + 5) * 8 + 127) / 128 * 128;
-    static_assert((2 * kStages + 5) * 8 <= 128, "barriers fit their 128 bytes");
-    static constexpr int o_sx = o_slot + 16;                           // 16-byte aligned: float4 reads
-    static constexpr int bytes(int kb) { return o_sx + (BF ? 0 : kGemmBN * kb * 4) + 1024; }
-    static constexpr uint32_t NCOLS = 2 * NM <= 32 ? 32 : 2 * NM <= 64 ? 64 : 2 * NM <= 128 ? 128
-                                    : 2 * NM <= 256 ? 256 : 512;
-    static constexpr uint32_t ID = BF ? tc::idesc(128, NM, 1, 1) : tc::idesc(128, NM, 0, 0);
-    static_assert(B % 1024 == 0, "B tiles keep 1024-byte alignment");
-    static_assert(NM % 16 == 0 && NM <= 256 && 2 * NM <= 512, "MMA N and TMEM columns");
+// ---- bf16 GEMM (the shared expert) ------------------------------------------------
+// tcgen05 kind::f16 on bf16, 64-column K blocks (4 MMAs of K = 16), no
+// scales, 2 digits (hi, lo) as 2 x 64 MMA columns; the whole K sum stays
+// in TMEM and is read once. A is [R][C] bf16 (A2: a second matrix of the
+// same shape into columns ycol2 + r), B the digit planes [2][N][C]; one CTA
+// per (row tile, 64-row B tile): tile = blockIdx.y, rows 64 blockIdx.y.
+constexpr int kBStages = 4;
+struct BfSmem {
+    static constexpr int NM = 2 * kGemmBN;            // MMA N: the two digit planes
+    static constexpr int A = 128 * 128;
+    static constexpr int STAGE = A + NM * 128;
+    static constexpr int o_bar = kBStages * STAGE;    // full[S], empty[S], tfull, done
+    static constexpr int o_slot = o_bar + ((2 * kBStages + 2) * 8 + 127) / 128 * 128;
+    static constexpr int bytes = o_slot + 16 + 1024;
+    static constexpr uint32_t ID = tc::idesc(128, NM, 1, 1);
 };
 
-// Epilogue of one K block for columns [c0, c0 + kEpiCols): combine the digit
-// columns of column n (n, 64 + n, 128 + n) as fma(D2, 2^-8, fma(D1, 2^-4,
-// D0)) -- the same roundings as adding the exactly scaled digits -- and add
-// into acc[n - c0] with the block's scales (sxk: the activation scales of
-// this block, [column]); packed fp32 (FFMA2) for the accumulation. The digit
-// loads of 16 columns share one wait.
-template <int ND, bool BF>
-__device__ __forceinline__ void promote(uint32_t t, int c0, const float *sxk, float w,
-                                        float2 (&acc)[kEpiCols / 2]) {
-    constexpr int BN = kGemmBN;
-#pragma unroll
-    for (int c = 0; c < kEpiCols / 16; c++) {
-        const uint32_t col = c0 + c * 16;
-        uint32_t r[3][16];
-        tc::tmem_ld16_nowait(t + col, r[0]);
-        if (ND > 1) tc::tmem_ld16_nowait(t + BN + col, r[1]);
-        if (ND > 2) tc::tmem_ld16_nowait(t + 2 * BN + col, r[2]);
-        float sc[16];
-        if (!BF) {
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-                const float4 s4 = *(const float4 *)(sxk + col + i);
-                sc[i] = __fmul_rn(w, s4.x); sc[i + 1] = __fmul_rn(w, s4.y);
-                sc[i + 2] = __fmul_rn(w, s4.z); sc[i + 3] = __fmul_rn(w, s4.w);
-            }
-        }
-        tc::tmem_wait_ld();
-        tc::tmem_regs_ready(r[0]);
-        if (ND > 1) tc::tmem_regs_ready(r[1]);
-        if (ND > 2) tc::tmem_regs_ready(r[2]);
-        float v[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            v[i] = __uint_as_float(r[0][i]);
-            if (ND > 1) v[i] = BF ? __fadd_rn(v[i], __uint_as_float(r[1][i])) : fmaf(__uint_as_float(r[1][i]), 0.0625f, v[i]);
-            if (ND > 2) v[i] = fmaf(__uint_as_float(r[2][i]), 0.00390625f, v[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-            float2 &a2 = acc[(c * 16 + i) >> 1];
-            if (BF)
-                a2 = __fadd2_rn(a2, make_float2(v[i], v[i + 1]));
-            else
-                a2 = __ffma2_rn(make_float2(v[i], v[i + 1]), make_float2(sc[i], sc[i + 1]), a2);
-        }
-    }
-}
-
-template <int ND, bool BF>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tW2,
-       const __grid_constant__ CUtensorMap tX, GemmArgs g) {
-    using L = GemmSmem<ND, BF>;
+k_gemm_bf16(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tW2,
+            const __grid_constant__ CUtensorMap tX, GemmArgs g) {
+    using L = BfSmem;
     constexpr int BN = kGemmBN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
-    uint64_t *full = (uint64_t *)(sm + L::o_bar), *empty = full + kStages;
-    uint64_t *tfull = empty + kStages, *tempty = tfull + 2, *done = tempty + 2;
+    uint64_t *full = (uint64_t *)(sm + L::o_bar), *empty = full + kBStages;
+    uint64_t *tfull = empty + kBStages, *done = tfull + 1;
     uint32_t *slot = (uint32_t *)(sm + L::o_slot);
-    float *sxt = (float *)(sm + L::o_sx);
 
-    // this CTA's tile
-    int zs = 0, n0, nv;
-    if (g.tiles) {
-        if ((int)blockIdx.y >= *g.ntiles) return;               // uniform: before any barrier
-        zs = g.tiles[3 * blockIdx.y];
-        n0 = g.tiles[3 * blockIdx.y + 1];
-        nv = g.tiles[3 * blockIdx.y + 2];
-    } else {
-        n0 = blockIdx.y * BN;
-        nv = min(BN, g.N - n0);
-    }
+    const int n0 = blockIdx.y * BN, nv = min(BN, g.N - n0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // row tile: blockIdx.x over the first A matrix's R / 128 tiles, then the
-    // second's
     const int MT = g.R / 128, mat = blockIdx.x / MT;
     const int r0 = (blockIdx.x % MT) * 128, KB = g.KB;
     const CUtensorMap *tA = mat ? &tW2 : &tW;
     unsigned *err = g.err;
 
-    if (warp == 1) tc::tmem_alloc(slot, L::NCOLS);
+    if (warp == 1) tc::tmem_alloc(slot, 128);
     if (tid == 0) {
-        for (int s = 0; s < kStages; s++) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
-        for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, kEpiWarps); }
+        for (int s = 0; s < kBStages; s++) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+        tc::mbar_init(tfull, 1);
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
         tc::prefetch_tmap(tA);
         tc::prefetch_tmap(&tX);
     }
-    if (!BF)      // the activation scales, stored [kb][column]
-        for (int i = tid - 64; i >= 0 && i < BN * KB; i += 32 * kEpiWarps)
-            sxt[(i % KB) * BN + i / KB] = i / KB < nv ? g.sX[(int64_t)(n0 + i / KB) * KB + i % KB] : 0.f;
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -240,81 +165,60 @@ k_gemm(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorM
         if (lane == 0) {
             int kb = 0;
             for (; kb < KB; kb++) {
-                const int s = kb % kStages;
-                if (kb >= kStages && !tc::mbar_wait(empty + s, ((kb / kStages) - 1) & 1, err, 1)) break;
+                const int s = kb % kBStages;
+                if (kb >= kBStages && !tc::mbar_wait(empty + s, ((kb / kBStages) - 1) & 1, err, 1)) break;
                 uint8_t *a = sm + s * L::STAGE;
                 tc::mbar_expect(full + s, L::STAGE);
-                tc::tma_load_3d(a, tA, kb * 128, r0, zs, full + s);
+                tc::tma_load_3d(a, tA, kb * 128, r0, 0, full + s);
                 tc::tma_load_3d(a + L::A, &tX, kb * 128, n0, 0, full + s);
             }
             // every issued load has landed before the CTA may exit
-            for (int k = kb - 1; k >= 0 && k >= kb - kStages; k--)
-                tc::mbar_wait(full + k % kStages, (k / kStages) & 1, err, 2, true);
+            for (int k = kb - 1; k >= 0 && k >= kb - kBStages; k--)
+                tc::mbar_wait(full + k % kBStages, (k / kBStages) & 1, err, 2, true);
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // FP8: one TMEM buffer per K block (alternating), promoted by the
-            // epilogue; BF16: every K block accumulates into buffer 0, read
-            // once at the end
             for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % kStages, b = BF ? 0 : kb & 1;
-                if (!tc::mbar_wait(full + s, (kb / kStages) & 1, err, 3)) break;
-                if (!BF && kb >= 2 && !tc::mbar_wait(tempty + b, ((kb >> 1) - 1) & 1, err, 4)) break;
+                const int s = kb % kBStages;
+                if (!tc::mbar_wait(full + s, (kb / kBStages) & 1, err, 3)) break;
                 tc::fence_after_sync();
                 const uint8_t *a = sm + s * L::STAGE;
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    if (BF)
-                        tc::mma_f16(taddr, tc::sdesc_sw128(a + 32 * k), tc::sdesc_sw128(a + L::A + 32 * k), L::ID,
-                                    kb > 0 || k > 0);
-                    else
-                        tc::mma_f8f6f4(taddr + b * L::NM, tc::sdesc_sw128(a + 32 * k),
-                                       tc::sdesc_sw128(a + L::A + 32 * k), L::ID, k > 0);
-                }
+                for (int k = 0; k < 4; k++)
+                    tc::mma_f16(taddr, tc::sdesc_sw128(a + 32 * k), tc::sdesc_sw128(a + L::A + 32 * k), L::ID,
+                                kb > 0 || k > 0);
                 tc::commit(empty + s);
-                if (!BF || kb == KB - 1) tc::commit(tfull + b);
+                if (kb == KB - 1) tc::commit(tfull);
             }
             tc::commit(done);
             tc::mbar_wait(done, 0, err, 5, true);      // every MMA finished
         }
     } else {
-        // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows;
-        // the four warps of a quadrant take 16 columns each
+        // warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows; the four
+        // warps of a quadrant take 16 columns each: D0 + D1 per column
         const int q = warp & 3, c0 = ((warp - 2) >> 2) * kEpiCols, row = q * 32 + lane;
-        float2 acc[kEpiCols / 2];
+        if (tc::mbar_wait(tfull, 0, err, 6)) {
+            tc::fence_after_sync();
+            const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
+            uint32_t r[2][16];
+            tc::tmem_ld16_nowait(tq + c0, r[0]);
+            tc::tmem_ld16_nowait(tq + BN + c0, r[1]);
+            tc::tmem_wait_ld();
+            tc::tmem_regs_ready(r[0]);
+            tc::tmem_regs_ready(r[1]);
+            if (r0 + row < g.R) {
+                float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + (mat ? g.ycol2 : g.ycol0) + r0 + row;
 #pragma unroll
-        for (int j = 0; j < kEpiCols / 2; j++) acc[j] = make_float2(0.f, 0.f);
-        const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
-        if (BF) {
-            if (tc::mbar_wait(tfull, 0, err, 6)) {
-                tc::fence_after_sync();
-                promote<ND, BF>(tq, c0, sxt, 1.f, acc);
+                for (int j = 0; j < kEpiCols; j++)
+                    if (c0 + j < nv) y[(int64_t)j * g.ldy] = __fadd_rn(__uint_as_float(r[0][j]), __uint_as_float(r[1][j]));
             }
-        } else {
-            const float *swr = (mat ? g.sW2 : g.sW) + zs * g.sw_slot +
-                               (g.row_scales ? (int64_t)(r0 + row) * KB : (int64_t)(r0 / 128) * KB);
-            for (int kb = 0; kb < KB; kb++) {
-                const int b = kb & 1;
-                if (!tc::mbar_wait(tfull + b, (kb >> 1) & 1, err, 6)) break;
-                tc::fence_after_sync();
-                promote<ND, BF>(tq + b * L::NM, c0, sxt + kb * BN, swr[kb], acc);
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(tempty + b);
-            }
-        }
-        if (r0 + row < g.R) {
-            float *y = g.Y + (int64_t)(n0 + c0) * g.ldy + (mat ? g.ycol2 : g.ycol0) + r0 + row;
-#pragma unroll
-            for (int j = 0; j < kEpiCols; j++)
-                if (c0 + j < nv) y[(int64_t)j * g.ldy] = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
         }
     }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 1) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(taddr, L::NCOLS);
+        tc::tmem_dealloc(taddr, 128);
     }
 }
 
@@ -567,66 +471,72 @@ int sm_count() {
 
 }  // namespace
 
-// A: slots x [R][C] elements of `esize` bytes, `slot_stride` bytes apart;
-// B: ND planes [rows][C]. Launches `ntiles_max` tile rows of the grid (the
-// grouped mode's CTAs past *g.ntiles return at once).
+// A: slots x [R][C] E4M3 bytes, `slot_stride` bytes apart; B: ND digit
+// planes [xrows][C]. At most `ntiles_max` B tiles (the grouped mode reads the
+// count from *g.ntiles). The persistent kernel, one B tensor map per tile width.
 template <int ND, bool BF>
 int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
                 GemmArgs g, int ntiles_max, cudaStream_t st, const void *A2) {
-    using L = GemmSmem<ND, BF>;
-    const int es = BF ? 2 : 1;
-    if (g.R <= 0 || g.C <= 0 || g.R % 128 || (g.C * es) % 128 || ntiles_max <= 0) {
-        set_error("gemm: R and C bytes must be positive multiples of 128");
+    static_assert(!BF, "bf16 GEMMs: bf16_gemm_launch");
+    if (g.R <= 0 || g.C <= 0 || g.R % 128 || g.C % 128 || ntiles_max <= 0) {
+        set_error("gemm: R and C must be positive multiples of 128");
         return -1;
     }
     CUtensorMap tW, tW2, tX;
-    if (tmap_u8_3d(&tW, A, (uint64_t)g.C * es, g.R, slots, (uint64_t)g.C * es, slot_stride, 128, 1) ||
-        tmap_u8_3d(&tW2, A2 ? A2 : A, (uint64_t)g.C * es, g.R, slots, (uint64_t)g.C * es, slot_stride, 128, 1) ||
-        tmap_u8_3d(&tX, X, (uint64_t)g.C * es, xrows, ND, (uint64_t)g.C * es, (uint64_t)xrows * g.C * es,
-                   kGemmBN, ND))
+    if (tmap_u8_3d(&tW, A, (uint64_t)g.C, g.R, slots, (uint64_t)g.C, slot_stride, 128, 1) ||
+        tmap_u8_3d(&tW2, A2 ? A2 : A, (uint64_t)g.C, g.R, slots, (uint64_t)g.C, slot_stride, 128, 1) ||
+        tmap_u8_3d(&tX, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, kGemmBN, ND))
         return -1;
-    g.KB = g.C * es / 128;
-    if constexpr (!BF) {
-        // FP8: the persistent kernel, one B tensor map per tile width
-        using P = PSmem<ND>;
-        CUtensorMap tX16, tX32, tX48;
-        if (tmap_u8_3d(&tX16, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 16, ND) ||
-            tmap_u8_3d(&tX32, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 32, ND) ||
-            tmap_u8_3d(&tX48, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 48, ND))
-            return -1;
-        const int psmem = P::bytes(g.KB);
-        if (psmem > 227 * 1024 || kGemmBN * g.KB > kPSxRegs * 32 * kEpiWarps) {
-            set_error("gemm: C too large for the scale tiles");
-            return -1;
-        }
-        static bool pattr = false;
-        if (!pattr) {
-            DS4F_CUDA(cudaFuncSetAttribute(k_gemm_p<ND>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-            pattr = true;
-        }
-        g.nmat = A2 ? 2 : 1;
-        const int64_t items = (int64_t)ntiles_max * (g.R / 128) * (A2 ? 2 : 1);
-        const int grid = (int)std::min<int64_t>(items, sm_count());
-        k_gemm_p<ND><<<grid, kGemmThreads, psmem, st>>>(tW, tW2, tX16, tX32, tX48, tX, g);
-        DS4F_CUDA(cudaGetLastError());
-        return 0;
+    g.KB = g.C / 128;
+    using P = PSmem<ND>;
+    CUtensorMap tX16, tX32, tX48;
+    if (tmap_u8_3d(&tX16, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 16, ND) ||
+        tmap_u8_3d(&tX32, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 32, ND) ||
+        tmap_u8_3d(&tX48, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 48, ND))
+        return -1;
+    const int psmem = P::bytes(g.KB);
+    if (psmem > 227 * 1024 || kGemmBN * g.KB > kPSxRegs * 32 * kEpiWarps) {
+        set_error("gemm: C too large for the scale tiles");
+        return -1;
     }
-    const int smem = L::bytes(g.KB);
-    if (smem > 227 * 1024) { set_error("gemm: C too large for the scale tile"); return -1; }
-    static bool attr = false;
-    if (!attr) {
-        DS4F_CUDA(cudaFuncSetAttribute(k_gemm<ND, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        attr = true;
+    static bool pattr = false;
+    if (!pattr) {
+        DS4F_CUDA(cudaFuncSetAttribute(k_gemm_p<ND>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        pattr = true;
     }
-    dim3 grid((g.R / 128) * (A2 ? 2 : 1), ntiles_max);
-    k_gemm<ND, BF><<<grid, kGemmThreads, smem, st>>>(tW, tW2, tX, g);
+    g.nmat = A2 ? 2 : 1;
+    const int64_t items = (int64_t)ntiles_max * (g.R / 128) * (A2 ? 2 : 1);
+    const int grid = (int)std::min<int64_t>(items, sm_count());
+    k_gemm_p<ND><<<grid, kGemmThreads, psmem, st>>>(tW, tW2, tX16, tX32, tX48, tX, g);
     DS4F_CUDA(cudaGetLastError());
     return 0;
 }
 template int gemm_launch<3, false>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
                                    cudaStream_t, const void *);
-template int gemm_launch<2, true>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
-                                  cudaStream_t, const void *);
+
+int bf16_gemm_launch(const uint16_t *A, const uint16_t *X, GemmArgs g, cudaStream_t st, const uint16_t *A2) {
+    using L = BfSmem;
+    if (g.R <= 0 || g.C <= 0 || g.R % 128 || g.C % 64 || g.N <= 0) {
+        set_error("bf16 gemm: R must be a positive multiple of 128, C of 64");
+        return -1;
+    }
+    const uint64_t cb = (uint64_t)g.C * 2;
+    CUtensorMap tW, tW2, tX;
+    if (tmap_u8_3d(&tW, A, cb, g.R, 1, cb, (uint64_t)g.R * cb, 128, 1) ||
+        tmap_u8_3d(&tW2, A2 ? A2 : A, cb, g.R, 1, cb, (uint64_t)g.R * cb, 128, 1) ||
+        tmap_u8_3d(&tX, X, cb, g.N, 2, cb, (uint64_t)g.N * cb, kGemmBN, 2))
+        return -1;
+    g.KB = (int)(cb / 128);
+    static bool attr = false;
+    if (!attr) {
+        DS4F_CUDA(cudaFuncSetAttribute(k_gemm_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, L::bytes));
+        attr = true;
+    }
+    dim3 grid((g.R / 128) * (A2 ? 2 : 1), (g.N + kGemmBN - 1) / kGemmBN);
+    k_gemm_bf16<<<grid, kGemmThreads, L::bytes, st>>>(tW, tW2, tX, g);
+    DS4F_CUDA(cudaGetLastError());
+    return 0;
+}
 
 int f8_gemm_launch(const uint8_t *W, const float *sW, const uint8_t *X, const float *sX, float *Y,
                    int R, int C, int N, int ND, unsigned *err, cudaStream_t st) {

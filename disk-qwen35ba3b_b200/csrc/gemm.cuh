@@ -28,15 +28,19 @@ struct GemmArgs {
     unsigned *err;
 };
 
-// A: slots x [R][C] elements (FP8 bytes, or bf16 when BF), `slot_stride`
-// bytes apart; X: ND digit planes [xrows][C]. The grid has `ntiles_max` tile
-// rows (grouped: CTAs past *g.ntiles return at once).
-// A2 (optional): a second A matrix of the same shape and slots (the up
-// projection beside the gate), computed in the same launch into columns
-// ycol2 + r of Y with scales sW2.
+// FP8 digit GEMM (persistent, tcgen05): A = slots x [R][C] E4M3 bytes,
+// `slot_stride` bytes apart (A2: a second matrix of the same shape and
+// slots, the up projection beside the gate: scales sW2, output columns
+// ycol2 + r); X = ND digit planes [xrows][C]. At most `ntiles_max` B tiles
+// (the grouped mode reads the count from *g.ntiles). BF must be false.
 template <int ND, bool BF>
 int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
                 GemmArgs g, int ntiles_max, cudaStream_t st, const void *A2 = nullptr);
+
+// bf16 GEMM (tcgen05 kind::f16): Y = A . X~, A [R][C] bf16 (A2 as above),
+// X~ = hi + lo, two bf16 planes [N][C]; dense over g.N rows.
+int bf16_gemm_launch(const uint16_t *A, const uint16_t *X, GemmArgs g, cudaStream_t st,
+                     const uint16_t *A2 = nullptr);
 
 int quant_f8_digits_launch(const float *x, int N, int C, int ND, uint8_t *q, float *s, cudaStream_t st);
 

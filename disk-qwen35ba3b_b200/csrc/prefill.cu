@@ -463,19 +463,16 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     }
     // 4: shared expert
     if (add_shared) {
-    const int ntd = (T + kGemmBN - 1) / kGemmBN;
     {   // shared gate and up in one launch
         GemmArgs g{};
         g.Y = ws.GS; g.ldy = 2 * M; g.ycol0 = 0; g.ycol2 = M; g.R = M; g.C = H; g.N = T; g.err = ws.err;
-        if (gemm_launch<2, true>(tl + m->tr.sh_gate, 1, (int64_t)M * H * 2, ws.Xb, T, g, ntd, st,
-                                 tl + m->tr.sh_up))
-            return -1;
+        if (bf16_gemm_launch(tl + m->tr.sh_gate, ws.Xb, g, st, tl + m->tr.sh_up)) return -1;
     }
     k_silu_bf16_digits<<<(unsigned)(((int64_t)T * M + 255) / 256), 256, 0, st>>>(ws.GS, M, T, ws.Cb);
     {
         GemmArgs g{};
         g.Y = ws.OS; g.ldy = H; g.ycol0 = 0; g.R = H; g.C = M; g.N = T; g.err = ws.err;
-        if (gemm_launch<2, true>(tl + m->tr.sh_down, 1, (int64_t)H * M * 2, ws.Cb, T, g, ntd, st)) return -1;
+        if (bf16_gemm_launch(tl + m->tr.sh_down, ws.Cb, g, st)) return -1;
     }
     }
     // 5
