@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define DS4F_FMT_MXFP4 0
 #define DS4F_FMT_FP8 2
 #define DS4F_SCALE_E8M0 0
@@ -29,6 +31,23 @@ int cuda_fail(cudaError_t e, const char *what, const char *file, int line);
         if (_e != cudaSuccess)                                              \
             return ::ds4f::cuda_fail(_e, #call, __FILE__, __LINE__);        \
     } while (0)
+
+// A kernel's opt-in to more than 48 KB of dynamic shared memory, made once
+// per device: the attribute belongs to the current device, and one process
+// may drive several GPUs (devices past 64 set it on every launch).
+struct SmemOptIn {
+    std::atomic<uint64_t> done{0};
+    template <class F>
+    int set(F *kernel, int bytes) {
+        int dev = 0;
+        DS4F_CUDA(cudaGetDevice(&dev));
+        const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+        if (bit && (done.load(std::memory_order_acquire) & bit)) return 0;
+        DS4F_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        done.fetch_or(bit, std::memory_order_release);
+        return 0;
+    }
+};
 
 #define DS4F_REQUIRE(cond, ...)                                             \
     do {                                                                    \

@@ -913,12 +913,9 @@ template <int FMT, int H, int M, int E, int K>
 int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     using L = Smem<FMT, H, M, E, K>;
     static_assert(L::bytes <= 227 * 1024, "decode kernel shared memory over budget");
-    static bool attr = false;
+    static SmemOptIn opt;
     auto kern = k_decode<FMT, H, M, E, K>;
-    if (!attr) {
-        DS4F_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::bytes));
-        attr = true;
-    }
+    if (opt.set(kern, L::bytes)) return -1;
     int dev = 0, sms = 0;
     DS4F_CUDA(cudaGetDevice(&dev));
     DS4F_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

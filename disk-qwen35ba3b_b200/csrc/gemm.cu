@@ -459,12 +459,15 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
     }
 }
 
+// SMs of the current device (cached per device).
 int sm_count() {
-    static int n = 0;
-    if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    int n = dev < 64 ? cache[dev].load() : 0;
+    if (n <= 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        if (dev < 64) cache[dev].store(n);
     }
     return n;
 }
@@ -499,11 +502,8 @@ int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X
         set_error("gemm: C too large for the scale tiles");
         return -1;
     }
-    static bool pattr = false;
-    if (!pattr) {
-        DS4F_CUDA(cudaFuncSetAttribute(k_gemm_p<ND>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        pattr = true;
-    }
+    static SmemOptIn opt;
+    if (opt.set(k_gemm_p<ND>, 227 * 1024)) return -1;
     g.nmat = A2 ? 2 : 1;
     const int64_t items = (int64_t)ntiles_max * (g.R / 128) * (A2 ? 2 : 1);
     const int grid = (int)std::min<int64_t>(items, sm_count());
@@ -527,11 +527,8 @@ int bf16_gemm_launch(const uint16_t *A, const uint16_t *X, GemmArgs g, cudaStrea
         tmap_u8_3d(&tX, X, cb, g.N, 2, cb, (uint64_t)g.N * cb, kGemmBN, 2))
         return -1;
     g.KB = (int)(cb / 128);
-    static bool attr = false;
-    if (!attr) {
-        DS4F_CUDA(cudaFuncSetAttribute(k_gemm_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, L::bytes));
-        attr = true;
-    }
+    static SmemOptIn opt;
+    if (opt.set(k_gemm_bf16, L::bytes)) return -1;
     dim3 grid((g.R / 128) * (A2 ? 2 : 1), (g.N + kGemmBN - 1) / kGemmBN);
     k_gemm_bf16<<<grid, kGemmThreads, L::bytes, st>>>(tW, tW2, tX, g);
     DS4F_CUDA(cudaGetLastError());

@@ -249,12 +249,8 @@ int synth_f32(float *dst, int64_t n, uint64_t key, double sigma, cudaStream_t st
 int synth_model(Model *m, uint64_t seed, double sigma, cudaStream_t st) {
     const ModelDesc &d = m->d;
     const int H = d.hidden, M = d.moe_inter, E = d.n_experts;
-    static bool attr = false;
-    if (!attr) {
-        DS4F_CUDA(cudaFuncSetAttribute(k_synth_fp8, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       128 * 128 * 4));
-        attr = true;
-    }
+    static SmemOptIn opt;
+    if (opt.set(k_synth_fp8, 128 * 128 * 4)) return -1;
     for (int L = 0; L < d.n_layers; L++) {
         uint16_t *t = m->trunk + (int64_t)L * m->tr.n;
         k_fill_u16<<<grid1d(H), 256, 0, st>>>(t + m->tr.norm, H, 0x3F80);   // 1.0
