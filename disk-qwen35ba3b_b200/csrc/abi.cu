@@ -353,7 +353,9 @@ void ds4f_gpu_mv_plan_free(Ds4fMvPlan *plan) {
 
 // ---- model --------------------------------------------------------------
 
-int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
+// pool_slots < 0: the whole shard resident; else an arena of that many slots
+// (a streaming model)
+static int model_create_impl(const Ds4fGpuModelDesc *desc, int64_t pool_slots, Ds4fGpuModel **out) {
     DS4F_REQUIRE(desc && out, "model_create: null argument");
     *out = nullptr;
     ModelDesc d;
@@ -383,7 +385,8 @@ int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
     DS4F_CUDA(cudaGetDevice(&m.device));
     const int H = d.hidden, M = d.moe_inter, E = d.n_experts, K = d.topk;
     // + 4 KB: bulk copies of small scale runs round up to 16 bytes
-    size_t pool_b = (size_t)d.n_layers * d.expert_count * m.slot.nbytes + 4096;
+    size_t pool_b = (size_t)(pool_slots < 0 ? (int64_t)d.n_layers * d.expert_count : pool_slots) * m.slot.nbytes +
+                    4096;
     size_t trunk_b = (size_t)d.n_layers * m.tr.n * 2;
     m.bmax = 64;
     size_t ws_b = al256(H * 4) + al256(E * 8) * 2 + al256(K * 4) * 2 +
@@ -433,6 +436,51 @@ int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
     return 0;
 }
 
+int ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out) {
+    return model_create_impl(desc, -1, out);
+}
+
+int ds4f_gpu_model_create_streaming(const Ds4fGpuModelDesc *desc, const uint8_t *host_pool, int n_slots,
+                                    Ds4fGpuModel **out) {
+    DS4F_REQUIRE(desc && host_pool && out, "model_create_streaming: null argument");
+    *out = nullptr;
+    DS4F_REQUIRE(desc->expert_first == 0 && desc->expert_count == desc->n_experts,
+                 "model_create_streaming: the host pool holds every expert (no shard)");
+    DS4F_REQUIRE(n_slots >= desc->topk, "model_create_streaming: %d slots, at least top-k = %d needed", n_slots,
+                 desc->topk);
+    Ds4fGpuModel *h = nullptr;
+    if (model_create_impl(desc, n_slots, &h)) return -1;
+    Model &m = h->m;
+    const size_t host_b = (size_t)m.d.n_layers * m.d.n_experts * m.slot.nbytes;
+    cudaError_t e = cudaHostRegister(const_cast<uint8_t *>(host_pool), host_b, cudaHostRegisterReadOnly);
+    if (e != cudaSuccess) e = cudaHostRegister(const_cast<uint8_t *>(host_pool), host_b, cudaHostRegisterDefault);
+    if (e != cudaSuccess) {
+        ds4f_gpu_model_destroy(h);
+        set_error("model_create_streaming: pinning the %.2f GB host pool failed (%s)", host_b / 1e9,
+                  cudaGetErrorString(e));
+        return -1;
+    }
+    m.host_pool = host_pool;
+    m.stream_slots = n_slots;
+    m.cache = slot_cache_new(n_slots);
+    const int K = m.d.topk;
+    if (!m.cache || cudaMalloc(&m.slot_dev, K * 4) != cudaSuccess ||
+        cudaHostAlloc((void **)&m.idx_h, K * 4, cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc((void **)&m.slot_h, K * 4, cudaHostAllocDefault) != cudaSuccess) {
+        ds4f_gpu_model_destroy(h);
+        set_error("model_create_streaming: allocation failed");
+        return -1;
+    }
+    *out = h;
+    return 0;
+}
+
+int ds4f_gpu_stream_stats(const Ds4fGpuModel *h, int64_t *requests, int64_t *hits, int64_t *fetched) {
+    DS4F_REQUIRE(h && h->m.cache, "stream_stats: not a streaming model");
+    slot_cache_stats(h->m.cache, requests, hits, nullptr, fetched);
+    return 0;
+}
+
 void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (!h) return;
     Model &m = h->m;
@@ -446,6 +494,11 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (m.pf8) cudaFree(m.pf8);
     if (m.pf_err_h) cudaFreeHost(m.pf_err_h);
     if (m.bgraph) cudaGraphExecDestroy(m.bgraph);
+    if (m.host_pool) cudaHostUnregister(const_cast<uint8_t *>(m.host_pool));
+    if (m.cache) slot_cache_delete(m.cache);
+    if (m.slot_dev) cudaFree(m.slot_dev);
+    if (m.idx_h) cudaFreeHost(m.idx_h);
+    if (m.slot_h) cudaFreeHost(m.slot_h);
     cudaFree(m.pool);
     cudaFree(m.trunk);
     cudaFree(m.ws_base);
@@ -467,6 +520,7 @@ int ds4f_gpu_model_slot(const Ds4fGpuModel *h, int64_t rel_v[3], int64_t rel_s[3
 
 int ds4f_gpu_model_synth(Ds4fGpuModel *h, uint64_t seed) {
     DS4F_REQUIRE(h, "model_synth: null model");
+    DS4F_REQUIRE(!h->m.cache, "model_synth: a streaming model's experts are the caller's host pool");
     if (synth_model(&h->m, seed, 0.02, h->m.stream)) return -1;
     DS4F_CUDA(cudaStreamSynchronize(h->m.stream));
     return 0;
@@ -520,6 +574,7 @@ static int canon_slot(Model &m, uint8_t *slot_dev) {
 int ds4f_gpu_model_set_expert(Ds4fGpuModel *h, int layer, int expert, const uint8_t *slot) {
     DS4F_REQUIRE(h && slot, "set_expert: null argument");
     Model &m = h->m;
+    DS4F_REQUIRE(!m.cache, "set_expert: a streaming model's experts are the caller's host pool");
     DS4F_REQUIRE(layer >= 0 && layer < m.d.n_layers, "set_expert: layer %d out of range", layer);
     DS4F_REQUIRE(expert >= m.d.expert_first && expert < m.d.expert_first + m.d.expert_count,
                  "set_expert: expert %d not in this shard", expert);
@@ -533,6 +588,7 @@ int ds4f_gpu_model_set_expert(Ds4fGpuModel *h, int layer, int expert, const uint
 int ds4f_gpu_model_get_expert(const Ds4fGpuModel *h, int layer, int expert, uint8_t *slot) {
     DS4F_REQUIRE(h && slot, "get_expert: null argument");
     const Model &m = h->m;
+    DS4F_REQUIRE(!m.cache, "get_expert: a streaming model's experts are the caller's host pool");
     DS4F_REQUIRE(layer >= 0 && layer < m.d.n_layers, "get_expert: layer %d out of range", layer);
     DS4F_REQUIRE(expert >= m.d.expert_first && expert < m.d.expert_first + m.d.expert_count,
                  "get_expert: expert %d not in this shard", expert);
@@ -545,6 +601,7 @@ int ds4f_gpu_model_get_expert(const Ds4fGpuModel *h, int layer, int expert, uint
 int ds4f_gpu_pool_load(Ds4fGpuModel *h, const char *path) {
     DS4F_REQUIRE(h && path, "pool_load: null argument");
     Model &m = h->m;
+    DS4F_REQUIRE(!m.cache, "pool_load: a streaming model reads its experts from the caller's host pool");
     int fd = open(path, O_RDONLY);
     DS4F_REQUIRE(fd >= 0, "pool_load: cannot open %s", path);
     uint8_t hdr[24];
@@ -661,6 +718,11 @@ int ds4f_gpu_moe_layer(Ds4fGpuModel *h, int layer, float *state, int *idx, float
 static int stack_step(Model &m, float *state, cudaStream_t st) {
     if (m.path != 1 && decode_eligible(&m)) return decode_launch(&m, state, 1, st);
     DS4F_REQUIRE(m.path != 2, "moe_stack: the persistent decode kernel does not cover this model");
+    if (m.cache) {              // streaming: every layer waits for its routing on the host
+        for (int L = 0; L < m.d.n_layers; L++)
+            if (moe_layer_launch(&m, L, state, nullptr, nullptr, st)) return -1;
+        return 0;
+    }
     if (!m.graph || m.graph_state != state) {
         if (m.graph) { cudaGraphExecDestroy(m.graph); m.graph = nullptr; }
         cudaGraph_t g;

@@ -965,7 +965,7 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
 
 bool decode_eligible(const Model *m) {
     const ModelDesc &d = m->d;
-    if (d.expert_count != d.n_experts || d.topk != 8) return false;
+    if (d.expert_count != d.n_experts || d.topk != 8 || m->cache) return false;
     if (!((d.hidden == 2048 && d.moe_inter == 512) || (d.hidden == 1024 && d.moe_inter == 256)))
         return false;
     return d.n_experts == 256 || d.n_experts == 64;

@@ -8,6 +8,8 @@
 
 namespace ds4f {
 
+struct SlotCache;                // stream.cu: the expert-cache policy
+
 struct ModelDesc {
     int fmt;              // DS4F_FMT_FP8 or DS4F_FMT_MXFP4 (routed experts)
     int n_layers;
@@ -77,6 +79,14 @@ struct Model {
     SlotLayout slot8;            //   tensor-core prefill (row scales), built on first use
     unsigned *pf_err_h;          // pinned copy of the prefill pipeline error word,
                                  //   written after each asynchronous step
+    // streaming pool (ds4f_gpu_model_create_streaming): the experts live in
+    // a pinned host copy of the packed pool; `pool` is an arena of
+    // stream_slots slots managed by `cache`
+    const uint8_t *host_pool;
+    int stream_slots;
+    SlotCache *cache;
+    int *slot_dev;               // [K] arena slots of the current selections
+    int *idx_h, *slot_h;         // [K] pinned host copies
     cudaGraphExec_t bgraph;      // captured batched decode step (prefill.cu), valid for
     float *bgraph_state;         //   these states, batch and workspace
     int bgraph_B;
@@ -108,6 +118,14 @@ int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st);
 // model's trunk and expert shard.
 int synth_model(Model *m, uint64_t seed, double sigma, cudaStream_t st);
 int synth_f32(float *dst, int64_t n, uint64_t key, double sigma, cudaStream_t st);
+
+// Streaming models (stream.cu): the current layer's selections (m->w.idx)
+// looked up in the slot cache, misses copied in from the host pool, their
+// slots uploaded to m->slot_dev; ordered on st.
+int stream_fetch(Model *m, int L, cudaStream_t st);
+SlotCache *slot_cache_new(int n);
+void slot_cache_delete(SlotCache *c);
+void slot_cache_stats(const SlotCache *c, int64_t *req, int64_t *hit, int64_t *drop, int64_t *fetched);
 
 // Batched prefill of one layer (prefill.cu): states [T][H] in/out, routing
 // sel / w [T][K] (global expert ids; ids outside this shard are skipped).

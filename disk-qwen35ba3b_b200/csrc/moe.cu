@@ -395,6 +395,8 @@ struct LayerArgs {
     float *sgate;
     float *state;                // [H] in/out
     float *acc_out;              // [H] or null
+    const int *slot_of;          // streaming: selection j's arena slot (pool_l = the arena);
+                                 //   null: expert idx[j] at pool_l + (idx[j] - efirst) slots
     int partial;                 // 1: expert-parallel shard step -- only selections in
                                  //    [efirst, efirst + ecount) count, acc_out gets the
                                  //    shard's partial sum, the state is left alone
@@ -443,7 +445,7 @@ k_gateup(LayerArgs a) {
             for (int t = 0; t < 2; t++) {
                 int p = min(pp + t, p1 - 1);
                 jj[t] = loc[p / M]; ii[t] = p % M;
-                base[t] = a.pool_l + (int64_t)(a.idx[jj[t]] - a.efirst) * a.slot_bytes;
+                base[t] = a.pool_l + (int64_t)(a.slot_of ? a.slot_of[jj[t]] : a.idx[jj[t]] - a.efirst) * a.slot_bytes;
                 load_row<FMT, H>(bg[t], base[t] + a.slot.rel_v[0] + (int64_t)ii[t] * G::bytes);
                 load_row<FMT, H>(bu[t], base[t] + a.slot.rel_v[1] + (int64_t)ii[t] * G::bytes);
             }
@@ -521,7 +523,7 @@ k_down(LayerArgs a) {
     } else if (warp < K) {
         float x[G::kch * G::ce];
         load_x<FMT, M>(x, cs[warp]);
-        const uint8_t *base = a.pool_l + (int64_t)(a.idx[warp] - a.efirst) * a.slot_bytes;
+        const uint8_t *base = a.pool_l + (int64_t)(a.slot_of ? a.slot_of[warp] : a.idx[warp] - a.efirst) * a.slot_bytes;
         const uint8_t *dv = base + a.slot.rel_v[2];
         const int sub = lane / G::lpr;
         for (int rr = 0; rr < nr; rr += 4 * G::rps) {
@@ -678,6 +680,12 @@ int moe_layer_launch_ex(Model *m, int L, float *state, int *idx_out, float *w_ou
     a.idx = w.idx; a.w = w.w; a.xin = w.xin; a.chain = w.chain; a.sgate = w.sgate;
     a.state = state; a.acc_out = acc_out ? acc_out : w.acc;
     a.partial = partial ? 1 : 0; a.add_shared = add_shared ? 1 : 0;
+    a.slot_of = nullptr;
+    if (m->cache) {             // streaming: the selections come through the slot cache
+        if (stream_fetch(m, L, st)) return -1;
+        a.pool_l = m->pool;
+        a.slot_of = m->slot_dev;
+    }
     int rc;
     if (d.fmt == DS4F_FMT_FP8 && H == 2048 && M == 512) rc = launch_chain<DS4F_FMT_FP8, 2048, 512>(a, st);
     else if (d.fmt == DS4F_FMT_MXFP4 && H == 2048 && M == 512) rc = launch_chain<DS4F_FMT_MXFP4, 2048, 512>(a, st);
@@ -813,7 +821,7 @@ extern "C" int ds4f_gpu_moe_layer_static(const Ds4fLayerDev *ld, float *state, i
     a.E = E; a.K = K; a.efirst = 0; a.ecount = E;
     a.idx = wk.idx; a.w = wk.w; a.xin = wk.xin; a.chain = wk.chain; a.sgate = wk.sgate;
     a.state = state; a.acc_out = wk.acc;
-    a.partial = 0; a.add_shared = 1;
+    a.partial = 0; a.add_shared = 1; a.slot_of = nullptr;
     int rc;
     if (ld->fmt == DS4F_FMT_FP8 && H == 2048) rc = launch_chain<DS4F_FMT_FP8, 2048, 512>(a, st);
     else if (ld->fmt == DS4F_FMT_MXFP4 && H == 2048) rc = launch_chain<DS4F_FMT_MXFP4, 2048, 512>(a, st);

@@ -408,6 +408,7 @@ int async_end(Model *m, const PfWs &ws, cudaStream_t st) {
 int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w, cudaStream_t st,
                   bool first_layer, bool last_layer, float *acc_out, bool add_shared) {
     DS4F_REQUIRE(T > 0 && L >= 0 && L < m->d.n_layers, "prefill: layer %d / tokens %d", L, T);
+    DS4F_REQUIRE(!m->cache, "prefill: not available for a streaming model (its experts are not resident)");
     const bool mx = m->d.fmt == DS4F_FMT_MXFP4;
     if (mx && ensure_f8_copy(m, st)) return -1;
     // the tensor core reads FP8: the pool itself, or an MXFP4 pool's exact copy
@@ -519,6 +520,7 @@ extern "C" {
 int ds4f_gpu_moe_layer_batch_dev(Ds4fGpuModel *h, int layer, float *states_dev, int B, int *idx_dev,
                                  float *w_dev, void *stream) {
     DS4F_REQUIRE(h && states_dev, "moe_layer_batch: null argument");
+    DS4F_REQUIRE(!h->m.cache, "moe_layer_batch: not available for a streaming model (its experts are not resident)");
     return ds4f::decode_batch_layer(&h->m, layer, states_dev, B, idx_dev, w_dev, (cudaStream_t)stream, true, true,
                                     nullptr, true, false);
 }
@@ -526,6 +528,7 @@ int ds4f_gpu_moe_layer_batch_dev(Ds4fGpuModel *h, int layer, float *states_dev, 
 int ds4f_gpu_moe_layer_batch_partial_dev(Ds4fGpuModel *h, int layer, const float *states_dev, int B,
                                          float *acc_dev, int add_shared, void *stream) {
     DS4F_REQUIRE(h && states_dev && acc_dev, "moe_layer_batch_partial: null argument");
+    DS4F_REQUIRE(!h->m.cache, "moe_layer_batch_partial: not available for a streaming model (its experts are not resident)");
     return ds4f::decode_batch_layer(&h->m, layer, const_cast<float *>(states_dev), B, nullptr, nullptr,
                                     (cudaStream_t)stream, false, false, acc_dev, add_shared != 0, true);
 }
@@ -580,6 +583,7 @@ static int stack_batch(ds4f::Model *m, float *states_dev, int B, int n_steps, cu
 
 int ds4f_gpu_moe_stack_batch_dev(Ds4fGpuModel *h, float *states_dev, int B, int n_steps, void *stream) {
     DS4F_REQUIRE(h && states_dev && n_steps > 0 && B > 0, "moe_stack_batch: bad arguments");
+    DS4F_REQUIRE(!h->m.cache, "moe_stack_batch: not available for a streaming model (its experts are not resident)");
     return ds4f::on_model_stream(h->m, stream,
                                  [&](cudaStream_t st) { return stack_batch(&h->m, states_dev, B, n_steps, st); });
 }

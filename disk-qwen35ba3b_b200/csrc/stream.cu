@@ -1,0 +1,191 @@
+// stream.cu -- pools larger than HBM: the reference's routed-expert cache
+// (src/cache.c:140-214, include/ds4f/ds4f.h:181-232) over an HBM slot
+// arena, filled from a pinned host copy of the packed pool instead of by
+// pread from disk. Host code only.
+//
+// Policy (as the reference's, so a streamed run fetches exactly what the
+// reference's cache would read): a slot holds EMPTY, INFLIGHT or the key
+// (layer + 1, expert + 1). A request for n experts
+//   1. reserves serially: a resident key is a hit; otherwise the victim is
+//      the first EMPTY slot, else the non-pinned, non-INFLIGHT slot fetched
+//      longest ago (hits do not refresh it); none left: a drop (slot -1);
+//   2. fetches the reserved slots in pool-offset order;
+//   3. publishes them in that order, each taking the next clock value.
+// One departure, behind `guard` (the streaming model sets it): in the
+// reference a slot answered as a hit in step 1 stays a victim candidate for
+// the request's later misses, so two selections can end up on one slot and
+// the earlier one reads the other expert's bytes (src/cache.c:150-170 with
+// src/main.c:729-733). Guarded, the request's hits are not evicted and an
+// expert named twice shares one slot; every other decision is the
+// reference's.
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "matvec.cuh"
+#include "model.cuh"
+#include "../../include/ds4f/gpu_cuda.h"
+
+namespace ds4f {
+
+struct SlotCache {
+    static constexpr uint64_t kEmpty = 0, kInflight = 1;
+    static constexpr int kMaxReq = 64;           // DS4F_MAX_TOPK
+    int nslot = 0;
+    std::vector<uint64_t> key, used_at;
+    std::vector<uint8_t> pinned;
+    std::unordered_map<uint64_t, int> where;     // live key -> slot
+    std::vector<uint8_t> held;                   // guard: this request's hits
+    uint64_t clock = 0;
+    int64_t nreq = 0, nhit = 0, ndrop = 0, nfetch = 0;
+    bool guard = false;
+
+    SlotCache(int n, bool g) : nslot(n), key(n, kEmpty), used_at(n, 0), pinned(n, 0), held(n, 0), guard(g) {}
+
+    static uint64_t expert_key(int layer, int expert) {
+        return ((uint64_t)(uint32_t)(layer + 1) << 32) | (uint32_t)(expert + 1);
+    }
+    int victim() const {
+        int best = -1;
+        uint64_t oldest = ~(uint64_t)0;
+        for (int i = 0; i < nslot; i++) {
+            if (key[i] == kInflight) continue;
+            if (key[i] == kEmpty) return i;
+            if (pinned[i] || held[i]) continue;
+            if (used_at[i] < oldest) { oldest = used_at[i]; best = i; }
+        }
+        return best;
+    }
+    // A request that names one expert twice fills two slots with one key; a
+    // lookup answers the lowest such slot, as a linear scan would.
+    void forget(int s) {
+        const uint64_t k = key[s];
+        auto it = where.find(k);
+        if (it == where.end() || it->second != s) return;
+        where.erase(it);
+        for (int i = 0; i < nslot; i++)
+            if (i != s && key[i] == k) { where[k] = i; break; }
+    }
+    // out_slot[j]: the slot of experts[j] (-1: dropped); fetch[] receives the
+    // (slot, expert) pairs to copy in, in pool-offset order, already
+    // published. Returns their count.
+    int getmany(int layer, const int *experts, int n, int *out_slot, std::vector<std::pair<int, int>> &fetch) {
+        if (n > kMaxReq) n = kMaxReq;
+        fetch.clear();
+        nreq += n;
+        for (int j = 0; j < n; j++) {
+            const uint64_t k = expert_key(layer, experts[j]);
+            auto it = where.find(k);
+            if (it != where.end()) {
+                out_slot[j] = it->second;
+                nhit++;
+                if (guard) held[it->second] = 1;
+                continue;
+            }
+            if (guard) {                         // named earlier in this request
+                int prev = -1;
+                for (int q = 0; q < j && prev < 0; q++)
+                    if (experts[q] == experts[j] && out_slot[q] >= 0) prev = out_slot[q];
+                if (prev >= 0) { out_slot[j] = prev; nhit++; continue; }
+            }
+            const int s = victim();
+            if (s < 0) { out_slot[j] = -1; ndrop++; continue; }
+            if (key[s] != kEmpty) forget(s);
+            key[s] = kInflight;
+            fetch.emplace_back(s, experts[j]);
+            out_slot[j] = s;
+        }
+        // pool offsets grow with the expert index within a layer; stable, as
+        // the reference's insertion sort
+        std::stable_sort(fetch.begin(), fetch.end(),
+                         [](const std::pair<int, int> &a, const std::pair<int, int> &b) { return a.second < b.second; });
+        for (const auto &f : fetch) {
+            const uint64_t k = expert_key(layer, f.second);
+            key[f.first] = k;
+            used_at[f.first] = ++clock;
+            auto it = where.find(k);
+            if (it == where.end() || f.first < it->second) where[k] = f.first;
+        }
+        if (guard)
+            for (int j = 0; j < n; j++)
+                if (out_slot[j] >= 0) held[out_slot[j]] = 0;
+        nfetch += (int64_t)fetch.size();
+        return (int)fetch.size();
+    }
+};
+
+// The streaming layer step's fetch: the K selections' routing (device,
+// m->w.idx) read back, the cache consulted, the misses copied from the pinned
+// host pool into their arena slots, and the selections' slots uploaded to
+// m->slot_dev -- all ordered on `st` before the chain kernels.
+int stream_fetch(Model *m, int L, cudaStream_t st) {
+    const int K = m->d.topk, E = m->d.n_experts;
+    const int64_t sb = m->slot.nbytes;
+    DS4F_CUDA(cudaMemcpyAsync(m->idx_h, m->w.idx, K * 4, cudaMemcpyDeviceToHost, st));
+    DS4F_CUDA(cudaStreamSynchronize(st));
+    std::vector<std::pair<int, int>> fetch;
+    m->cache->getmany(L, m->idx_h, K, m->slot_h, fetch);
+    for (int j = 0; j < K; j++)
+        DS4F_REQUIRE(m->slot_h[j] >= 0, "stream: no free slot for expert %d of layer %d (every slot pinned or "
+                     "in flight)", m->idx_h[j], L);
+    for (const auto &f : fetch) {
+        uint8_t *dst = m->pool + (int64_t)f.first * sb;
+        DS4F_CUDA(cudaMemcpyAsync(dst, m->host_pool + ((int64_t)L * E + f.second) * sb, sb, cudaMemcpyHostToDevice,
+                                  st));
+        if (m->d.fmt == DS4F_FMT_FP8)    // e=15 bytes -> +-448, as on every upload
+            for (int t = 0; t < 3; t++)
+                if (launch_f8_canon(dst + m->slot.rel_v[t], m->slot.rel_s[t] - m->slot.rel_v[t], st)) return -1;
+    }
+    DS4F_CUDA(cudaMemcpyAsync(m->slot_dev, m->slot_h, K * 4, cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
+SlotCache *slot_cache_new(int n) { return new (std::nothrow) SlotCache(n, true); }
+void slot_cache_delete(SlotCache *c) { delete c; }
+void slot_cache_stats(const SlotCache *c, int64_t *req, int64_t *hit, int64_t *drop, int64_t *fetched) {
+    if (req) *req = c->nreq;
+    if (hit) *hit = c->nhit;
+    if (drop) *drop = c->ndrop;
+    if (fetched) *fetched = c->nfetch;
+}
+
+}  // namespace ds4f
+
+// ---- the policy on its own (no device): for hosts that manage their own
+// ---- arena, and for checking it against the reference's cache -----------
+struct Ds4fSlotCache { ds4f::SlotCache c; Ds4fSlotCache(int n, bool g) : c(n, g) {} };
+
+extern "C" {
+
+int ds4f_slotcache_create(int n_slots, int flags, Ds4fSlotCache **out) {
+    DS4F_REQUIRE(out && n_slots > 0 && !(flags & ~DS4F_SLOTCACHE_GUARD), "slotcache_create: bad arguments");
+    *out = new (std::nothrow) Ds4fSlotCache(n_slots, (flags & DS4F_SLOTCACHE_GUARD) != 0);
+    DS4F_REQUIRE(*out, "slotcache_create: out of host memory");
+    return 0;
+}
+
+void ds4f_slotcache_free(Ds4fSlotCache *c) { delete c; }
+
+int ds4f_slotcache_getmany(Ds4fSlotCache *c, int layer, const int *experts, int n, int *out_slot) {
+    DS4F_REQUIRE(c && experts && out_slot && n >= 0, "slotcache_getmany: bad arguments");
+    std::vector<std::pair<int, int>> fetch;
+    return c->c.getmany(layer, experts, n, out_slot, fetch);
+}
+
+int ds4f_slotcache_pin(Ds4fSlotCache *c, int slot, int pin) {
+    DS4F_REQUIRE(c, "slotcache_pin: null cache");
+    if (slot >= 0 && slot < c->c.nslot) c->c.pinned[slot] = (uint8_t)(pin != 0);
+    return 0;
+}
+
+int ds4f_slotcache_stats(const Ds4fSlotCache *c, int64_t *requests, int64_t *hits, int64_t *drops,
+                         int64_t *fetched) {
+    DS4F_REQUIRE(c, "slotcache_stats: null cache");
+    ds4f::slot_cache_stats(&c->c, requests, hits, drops, fetched);
+    return 0;
+}
+
+}  // extern "C"

@@ -90,12 +90,20 @@ def lib():
             "ds4f_gpu_moe_layer_batch_dev": [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_moe_layer_batch_partial_dev": [_vp, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp],
             "ds4f_gpu_moe_stack_batch_dev": [_vp, _vp, C.c_int, C.c_int, _vp],
+            "ds4f_slotcache_create": [C.c_int, C.c_int, _vp],
+            "ds4f_slotcache_getmany": [_vp, C.c_int, _vp, C.c_int, _vp],
+            "ds4f_slotcache_pin": [_vp, C.c_int, C.c_int],
+            "ds4f_slotcache_stats": [_vp] * 5,
+            "ds4f_gpu_model_create_streaming": [_vp, _vp, C.c_int, _vp],
+            "ds4f_gpu_stream_stats": [_vp] * 4,
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
             if name not in ("ds4f_gpu_mv_plan_free", "ds4f_gpu_model_destroy"):
                 fn.restype = C.c_int
+        L.ds4f_slotcache_free.restype = None
+        L.ds4f_slotcache_free.argtypes = [_vp]
         _lib = L
     return _lib
 
@@ -105,7 +113,7 @@ def header_symbols():
     import re
     txt = open(HEADER).read()
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    return sorted(set(re.findall(r"\b(ds4f_gpu_\w+)\s*\(", txt)))
+    return sorted(set(re.findall(r"\b(ds4f_(?:gpu|slotcache)_\w+)\s*\(", txt)))
 
 
 def check(rc):
@@ -204,16 +212,60 @@ class MvPlan:
 
 # ---- model -----------------------------------------------------------
 
+class SlotCache:
+    """The reference's expert-cache policy (host only, no device); guard=True
+    keeps a request's hits from being evicted by its own misses."""
+
+    def __init__(self, n_slots, guard=False):
+        self.h = None
+        h = C.c_void_p()
+        check(lib().ds4f_slotcache_create(n_slots, 1 if guard else 0, C.byref(h)))
+        self.h = h
+
+    def getmany(self, layer, experts):
+        """-> (slot per expert, -1 = dropped; number of slots to fill)."""
+        e = np.ascontiguousarray(experts, np.int32)
+        out = np.zeros(len(e), np.int32)
+        n = lib().ds4f_slotcache_getmany(self.h, layer, ptr(e), len(e), ptr(out))
+        if n < 0:
+            raise GpuError(lib().ds4f_gpu_last_error().decode())
+        return out, n
+
+    def pin(self, slot, on=True):
+        check(lib().ds4f_slotcache_pin(self.h, slot, 1 if on else 0))
+
+    def stats(self):
+        v = [C.c_int64() for _ in range(4)]
+        check(lib().ds4f_slotcache_stats(self.h, *[C.byref(x) for x in v]))
+        return [x.value for x in v]
+
+    def close(self):
+        if self.h and _lib is not None:
+            _lib.ds4f_slotcache_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
+
+
 class Model:
     def __init__(self, fmt, n_layers, hidden=2048, moe_inter=512, n_experts=256, topk=8,
-                 renorm=True, expert_first=0, expert_count=None, router_exact=False):
+                 renorm=True, expert_first=0, expert_count=None, router_exact=False,
+                 host_pool=None, stream_slots=0):
+        """host_pool (uint8 array of every expert, packed) with stream_slots > 0:
+        a streaming model (ds4f_gpu_model_create_streaming); the array must
+        outlive the model."""
         self.h = None
         d = Ds4fGpuModelDesc(fmt, n_layers, hidden, moe_inter, n_experts, topk,
                              1 if renorm else 0, expert_first,
                              n_experts if expert_count is None else expert_count,
                              1 if router_exact else 0)
         h = C.c_void_p()
-        check(lib().ds4f_gpu_model_create(C.byref(d), C.byref(h)))
+        if host_pool is not None:
+            self.host_pool = host_pool
+            check(lib().ds4f_gpu_model_create_streaming(C.byref(d), ptr(host_pool), stream_slots, C.byref(h)))
+        else:
+            check(lib().ds4f_gpu_model_create(C.byref(d), C.byref(h)))
         self.h, self.d = h, d
         self.H, self.M, self.E, self.K, self.L = hidden, moe_inter, n_experts, topk, n_layers
         rv = (C.c_int64 * 3)()
@@ -333,6 +385,12 @@ class Model:
         out = (C.c_uint64 * 2)()
         check(lib().ds4f_gpu_model_stats(self.h, out))
         return list(out)
+
+    def stream_stats(self):
+        """Streaming model: [experts requested, hits, slots copied in]."""
+        v = [C.c_int64() for _ in range(3)]
+        check(lib().ds4f_gpu_stream_stats(self.h, *[C.byref(x) for x in v]))
+        return [x.value for x in v]
 
 
 def synth_f32_dev(dst, n, seed, layer, kind, x, t, sigma, stream=None):

@@ -158,6 +158,50 @@ int  ds4f_gpu_model_get_expert(const Ds4fGpuModel *m, int layer, int expert,
  * 24 + (L*E + N)*nbytes (ds4f_pool_open_packed, src/st.c:127-180). */
 int  ds4f_gpu_pool_load(Ds4fGpuModel *m, const char *path);
 
+/* ---- pools larger than HBM: the expert cache ------------------------ */
+
+/* The reference's routed-expert cache policy (ds4f_cache_init /
+ * ds4f_cache_getmany / ds4f_cache_pin, include/ds4f/ds4f.h:221-232,
+ * src/cache.c:140-223), host only: a slot holds nothing, an expert being
+ * fetched, or (layer, expert). A request for n experts reserves serially (a
+ * resident expert is a hit; else the first empty slot, else the non-pinned
+ * slot fetched longest ago -- hits do not refresh it; none left: slot -1, a
+ * drop), then marks the reserved slots fetched in pool-offset order, each
+ * taking the next clock value. getmany fills out_slot[n] and returns the
+ * number of slots to fill (the caller copies them in). No device needed. */
+typedef struct Ds4fSlotCache Ds4fSlotCache;
+/* flags: 0 = the reference's policy exactly. DS4F_SLOTCACHE_GUARD = a
+ * request's own hits are not evicted by its later misses and an expert named
+ * twice shares one slot (in the reference a hit slot can be re-reserved in
+ * the same request, src/cache.c:150-170, leaving an earlier selection on
+ * another expert's bytes); the streaming model runs guarded. */
+#define DS4F_SLOTCACHE_GUARD 1
+int  ds4f_slotcache_create(int n_slots, int flags, Ds4fSlotCache **out);
+void ds4f_slotcache_free(Ds4fSlotCache *c);
+int  ds4f_slotcache_getmany(Ds4fSlotCache *c, int layer, const int *experts, int n,
+                            int *out_slot);
+int  ds4f_slotcache_pin(Ds4fSlotCache *c, int slot, int pin);
+int  ds4f_slotcache_stats(const Ds4fSlotCache *c, int64_t *requests, int64_t *hits,
+                          int64_t *drops, int64_t *fetched);
+
+/* A model whose experts stay in host memory (the reference's disk-backed
+ * pool + cache, src/cache.c:140-214, for pools that do not fit in HBM):
+ * host_pool holds every expert in the packed layout, expert (L, X) at
+ * (L * n_experts + X) * slot bytes (ds4f_gpu_model_slot), and stays owned by
+ * the caller (the library pins it for the model's lifetime). The HBM holds
+ * the trunk and an arena of n_slots (>= top-k) expert slots run by the
+ * policy above, guarded; per layer the routing is read back, the misses are copied in
+ * (host to device) and the layer runs on the arena. Layer and stack calls
+ * work as for a resident model (each layer waits on the host for its
+ * routing, so none of them can be captured in a CUDA graph); synth,
+ * set/get_expert, pool_load, prefill and the batched calls refuse it. */
+int  ds4f_gpu_model_create_streaming(const Ds4fGpuModelDesc *desc, const uint8_t *host_pool,
+                                     int n_slots, Ds4fGpuModel **out);
+/* The streaming model's cache counters: experts requested, hits, slots
+ * copied in. */
+int  ds4f_gpu_stream_stats(const Ds4fGpuModel *m, int64_t *requests, int64_t *hits,
+                           int64_t *fetched);
+
 /* One token through one layer (host buffers): state[H] in/out; idx[K],
  * w[K] receive the routing (may be NULL). Replaces the reference's
  * per-layer route (src/main.c:1014-1088) + ds4f_moe_step
