@@ -96,6 +96,8 @@ def lib():
             "ds4f_slotcache_stats": [_vp] * 5,
             "ds4f_gpu_model_create_streaming": [_vp, _vp, C.c_int, _vp],
             "ds4f_gpu_stream_stats": [_vp] * 4,
+            "ds4f_pool_layout_plan": [C.c_char_p] + [C.c_int] * 5 + [_vp, _vp],
+            "ds4f_gpu_pool_load_json": [_vp, C.c_char_p, C.c_char_p],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -113,7 +115,7 @@ def header_symbols():
     import re
     txt = open(HEADER).read()
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    return sorted(set(re.findall(r"\b(ds4f_(?:gpu|slotcache)_\w+)\s*\(", txt)))
+    return sorted(set(re.findall(r"\b(ds4f_(?:gpu|slotcache|pool)_\w+)\s*\(", txt)))
 
 
 def check(rc):
@@ -310,6 +312,11 @@ class Model:
     def pool_load(self, path):
         check(lib().ds4f_gpu_pool_load(self.h, path.encode()))
 
+    def pool_load_json(self, pool_path, json_path):
+        """A packed pool with the converter's layout file beside it."""
+        check(lib().ds4f_gpu_pool_load_json(self.h, str(pool_path).encode(),
+                                            str(json_path).encode()))
+
     def layer(self, L, state):
         st = np.array(state, np.float32, copy=True)
         idx = np.zeros(self.K, np.int32)
@@ -391,6 +398,16 @@ class Model:
         v = [C.c_int64() for _ in range(3)]
         check(lib().ds4f_gpu_stream_stats(self.h, *[C.byref(x) for x in v]))
         return [x.value for x in v]
+
+
+def pool_layout_plan(json_path, fmt, hidden, moe_inter, n_layers, n_experts):
+    """-> (offsets [n_layers, n_experts, 3 roles, 2 (values, scales)] int64
+    absolute file offsets, roles gate/up/down; expert_nbytes). Host only."""
+    off = np.zeros((n_layers, n_experts, 3, 2), np.int64)
+    nb = C.c_int64()
+    check(lib().ds4f_pool_layout_plan(str(json_path).encode(), fmt, hidden, moe_inter,
+                                      n_layers, n_experts, ptr(off), C.byref(nb)))
+    return off, nb.value
 
 
 def synth_f32_dev(dst, n, seed, layer, kind, x, t, sigma, stream=None):

@@ -158,6 +158,28 @@ int  ds4f_gpu_model_get_expert(const Ds4fGpuModel *m, int layer, int expert,
  * 24 + (L*E + N)*nbytes (ds4f_pool_open_packed, src/st.c:127-180). */
 int  ds4f_gpu_pool_load(Ds4fGpuModel *m, const char *path);
 
+/* The converter's layout file beside a packed pool (pool-mxfp4.json,
+ * tools/convert-ds4f.py:1321-1393; read by ds4f_pool_layout_load,
+ * src/moe.c:51-160): per tensor its name, layer, expert, shape and absolute
+ * v_off / s_off / v_nbytes / s_nbytes. The converter writes each expert's
+ * tensors in sorted-name order (down, gate, up for Qwen names); these calls
+ * place each by its name (".gate_proj.weight", ".up_proj.weight",
+ * ".down_proj.weight"), or by entry order gate, up, down where entries carry
+ * no name, as the engine reads them (src/moe.c:598-605). Format
+ * "mxfp4-pool-v1" (e2m1 + E8M0 per 32) for MXFP4 models, "fp8-pool-v1"
+ * (E4M3 bytes + fp32 scale per 128x128 block, row-major) for FP8 ones.
+ * Refused as in the engine: missing keys, other layer/expert counts, a tensor
+ * outside its slot; and here also: a shape or byte count other than the
+ * model's, a role given twice or missing. */
+/* Host only: offsets[(L * n_experts + X) * 6 + 2 * role (+1 for scales)] =
+ * absolute file offsets, roles gate, up, down; may be NULL to validate. */
+int  ds4f_pool_layout_plan(const char *json_path, int fmt, int hidden, int moe_inter,
+                           int n_layers, int n_experts, int64_t *offsets,
+                           int64_t *expert_nbytes);
+/* Load this shard from the packed pool and its layout file (header and size
+ * checked against the layout). */
+int  ds4f_gpu_pool_load_json(Ds4fGpuModel *m, const char *pool_path, const char *json_path);
+
 /* ---- pools larger than HBM: the expert cache ------------------------ */
 
 /* The reference's routed-expert cache policy (ds4f_cache_init /
