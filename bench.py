@@ -816,6 +816,189 @@ def run_gpu_matvec(args, rank, world, local_rank):
     }
 
 
+def mem_available_bytes():
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def run_gpu_stream(args, rank, world, local_rank):
+    """Pools larger than HBM (the reference's disk-streaming configuration,
+    src/cache.c:140-214 over pool-mxfp4.bin): the 40-layer pool stays in
+    pinned host memory, the HBM holds the trunk and an arena of --slots
+    expert slots run by the reference's cache policy; every layer reads its
+    routing back and copies its misses in before the chain runs. One step =
+    one token through all layers. The host link is the bound: achieved =
+    bytes copied in per second against a pinned host-to-device copy measured
+    in the same run."""
+    import numpy as np
+    import torch
+    from tests._lib import ds4f_cuda
+    dc = ds4f_cuda()
+    torch.cuda.set_device(local_rank)
+    dc.init()
+    fp8 = args.fmt == "fp8"
+    fmt = dc.FMT_FP8 if fp8 else dc.FMT_MXFP4
+    slot_b = 3146496 if fp8 else 1671168
+    pool_b = LAYERS * E * slot_b
+    if mem_available_bytes() < pool_b * 1.5:
+        return {"workload": "stream-decode", "unavailable":
+                f"needs {pool_b * 1.5 / 1e9:.1f} GB of host memory for the pinned pool, "
+                f"{mem_available_bytes() / 1e9:.1f} GB available"}
+    # the pool: the device generator's bytes, read back once into host memory
+    r = dc.Model(fmt, LAYERS, H, M, E, K)
+    r.synth(0)
+    host = np.empty(pool_b, np.uint8)
+    L_ = dc.lib()
+    for l in range(LAYERS):
+        for x in range(E):
+            o = (l * E + x) * slot_b
+            dc.check(L_.ds4f_gpu_model_get_expert(r.h, l, x, dc.ptr(host[o:o + slot_b])))
+    trunks = [r.get_trunk(l) for l in range(LAYERS)]
+    r.close()
+    torch.cuda.empty_cache()
+    n_slots = args.slots or LAYERS * E // 4
+    try:
+        s = dc.Model(fmt, LAYERS, H, M, E, K, host_pool=host, stream_slots=n_slots)
+    except dc.GpuError as ex:
+        return {"workload": "stream-decode", "unavailable": str(ex)}
+    for l in range(LAYERS):
+        s.set_trunk(l, *trunks[l])
+    state = torch.empty(H, dtype=torch.float32, device="cuda")
+    dc.synth_f32_dev(state, H, 0, 0, 4, rank, 0, 1.0)
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(args.warmup):
+        s.stack_dev(state, 1, sp)
+    torch.cuda.synchronize()
+    req0, hit0, fet0 = s.stream_stats()
+    clk = Clocks(local_rank)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        s.stack_dev(state, 1, sp)
+    e1.record()
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    clocks = clk.stop()
+    req, hit, fet = (a - b for a, b in zip(s.stream_stats(), (req0, hit0, fet0)))
+    # e2e through the host-buffer call
+    hst = torch.empty(H, dtype=torch.float32).pin_memory()
+    hst.copy_(state.cpu())
+    hnp = hst.numpy()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s.stack_host_inplace(hnp, 1)
+    e2e_s = time.perf_counter() - t0
+    s.close()
+    # the host link's measured copy rate: 1 GiB pinned -> device, event-timed
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(4):
+        dst.copy_(src, non_blocking=True)
+    c1.record()
+    torch.cuda.synchronize()
+    link_gbs = 4 * (1 << 30) / (c0.elapsed_time(c1) / 1e3) / 1e9
+    del src, dst
+    ms = t_ms / args.steps
+    moved = fet * slot_b / args.steps
+    achieved = moved / (ms / 1e3) / 1e9
+    return {
+        "metric": f"MoE-stack decode tok/s, experts streamed from host memory (40-layer "
+                  f"{'FP8' if fp8 else 'MXFP4'}, 1 B200)",
+        "value": round(args.steps / (t_ms / 1e3), 2), "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (e2m1 + e8m0/32)") + " weights, fp32 accumulate",
+        "data": "synthetic (seeded, device-generated, read back into host memory)",
+        "config": {"workload": f"stream-decode: 40-layer {'FP8' if fp8 else 'MXFP4'} decode, pool "
+                               f"{pool_b / 1e9:.1f} GB in pinned host memory, {n_slots} HBM slots",
+                   "slots": n_slots, "pool_experts": LAYERS * E,
+                   "hit_rate": round(hit / max(req, 1), 4),
+                   "fetched_per_step": round(fet / args.steps, 2),
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "host link", "achieved": round(achieved, 2), "peak": round(link_gbs, 2),
+                     "unit": "GB/s", "frac": round(achieved / link_gbs, 4), "traffic": None,
+                     "peak_source": "pinned host-to-device copy of 1 GiB, measured in this run",
+                     "bytes_copied_per_step": round(moved)},
+        "e2e": {"value": round(args.steps / e2e_s, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": H * 4 + round(moved), "d2h_bytes_per_step": H * 4,
+                "timer": "host clock around the synchronous C-ABI call"},
+        "gpu_launches": 4 * LAYERS * args.steps,   # route, top-K, gate/up, down per layer
+        "clocks": clocks,
+    }
+
+
+def run_gpu_head(args, rank, world, local_rank):
+    """The output head after the MoE stack (ds4f_head_logits + ds4f_argmax,
+    src/head.c:243-309): Qwen3.5's 248,320 x 2048 vocabulary matrix in BF16,
+    logits and the greedy pick per step. Bytes per step = the weights
+    (1.02 GB, larger than L2) + x + logits."""
+    import numpy as np
+    import torch
+    from tests._lib import ds4f_cuda
+    dc = ds4f_cuda()
+    torch.cuda.set_device(local_rank)
+    dc.init()
+    V, Hh = 248_320, H
+    w = torch.empty(V * Hh, dtype=torch.bfloat16).normal_(0, 0.02, generator=torch.Generator().manual_seed(0))
+    hd = dc.Head(dc.HEAD_BF16, w.view(torch.int16).numpy(), V=V, H=Hh)
+    del w
+    x = torch.randn(Hh, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+    logits = torch.empty(V, device="cuda")
+    best = torch.empty(1, dtype=torch.int32, device="cuda")
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(args.warmup):
+        hd.logits_dev(x, logits, best, sp)
+    torch.cuda.synchronize()
+    clk = Clocks(local_rank)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        hd.logits_dev(x, logits, best, sp)
+    e1.record()
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+    clocks = clk.stop()
+    xh = x.cpu().numpy()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, b = hd.logits(xh, want_logits=False)
+    e2e_s = time.perf_counter() - t0
+    hd.close()
+    ms = t_ms / args.steps
+    algo = V * Hh * 2 + Hh * 4 + V * 4
+    peak, src = peaks()
+    gbs = algo / (ms / 1e3) / 1e9
+    return {
+        "metric": "output head tokens/s (248,320 x 2048 BF16 logits + argmax, 1 B200)",
+        "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 weights, fp32 accumulate", "data": "synthetic (seeded N(0, 0.02) weights)",
+        "config": {"workload": "head: Qwen3.5 vocabulary head, 248,320 x 2048 BF16, batch 1",
+                   "l2": "inputs larger than L2 (1.02 GB of weights per step)", "parallelism": "single GPU"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "traffic": None, "peak_source": src,
+                     "algorithmic_bytes_per_step": algo},
+        "e2e": {"value": round(args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": Hh * 4,
+                "d2h_bytes_per_step": 4, "timer": "host clock around ds4f_gpu_head_logits"},
+        "gpu_launches": 3 * args.steps,           # matvec, argmax partials, argmax final
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -826,12 +1009,14 @@ def main():
     ap.add_argument("--layered", action="store_true",
                     help="per-layer kernels (CUDA graph) instead of the persistent kernel")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "ep-decode", "ep-prefill", "matvec"],
+                    choices=["decode", "prefill", "ep-decode", "ep-prefill", "matvec", "stream-decode", "head"],
                     help="decode: config 2 (the headline); prefill: config 4; ep-decode: config 3 "
-                         "(experts sharded over the ranks)")
+                         "(experts sharded over the ranks); stream-decode: the pool in host memory")
     ap.add_argument("--fmt", default=None, choices=["fp8", "mxfp4"],
                     help="expert format (decode default fp8; ep-decode default mxfp4)")
     ap.add_argument("--batch", type=int, default=1, help="ep-decode: tokens per step")
+    ap.add_argument("--slots", type=int, default=0,
+                    help="stream-decode: HBM expert slots (default a quarter of the pool)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -859,12 +1044,15 @@ def main():
                     "d2h_bytes_per_step": 0}}))
         return
     if args.fmt is None:
-        args.fmt = "mxfp4" if args.workload == "ep-decode" else "fp8"
+        args.fmt = "mxfp4" if args.workload in ("ep-decode", "stream-decode") else "fp8"
     fn = {"prefill": run_gpu_prefill, "ep-decode": run_gpu_ep,
-          "ep-prefill": run_gpu_ep_prefill, "matvec": run_gpu_matvec}.get(args.workload, run_gpu)
+          "ep-prefill": run_gpu_ep_prefill, "matvec": run_gpu_matvec,
+          "stream-decode": run_gpu_stream, "head": run_gpu_head}.get(args.workload, run_gpu)
     res = fn(args, rank, world, local_rank)
     if rank == 0:
-        if world == 1 and args.workload == "matvec":
+        if "unavailable" in res or args.workload in ("stream-decode", "head"):
+            pass
+        elif world == 1 and args.workload == "matvec":
             v, desc = cpu_matvec_sample(args.cpu_seconds)
             res["cpu_baseline"] = dict(desc, value=round(v, 4), unit="GB/s")
         elif world == 1:

@@ -98,6 +98,10 @@ def lib():
             "ds4f_gpu_stream_stats": [_vp] * 4,
             "ds4f_pool_layout_plan": [C.c_char_p] + [C.c_int] * 5 + [_vp, _vp],
             "ds4f_gpu_pool_load_json": [_vp, C.c_char_p, C.c_char_p],
+            "ds4f_gpu_head_create": [C.c_int, _vp, _vp, _vp] + [C.c_int] * 4 + [_vp],
+            "ds4f_gpu_head_logits": [_vp] * 4,
+            "ds4f_gpu_head_logits_dev": [_vp] * 5,
+            "ds4f_gpu_argmax_dev": [_vp, C.c_int, _vp, _vp],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -105,6 +109,8 @@ def lib():
             if name not in ("ds4f_gpu_mv_plan_free", "ds4f_gpu_model_destroy"):
                 fn.restype = C.c_int
         L.ds4f_slotcache_free.restype = None
+        L.ds4f_gpu_head_free.restype = None
+        L.ds4f_gpu_head_free.argtypes = [_vp]
         L.ds4f_slotcache_free.argtypes = [_vp]
         _lib = L
     return _lib
@@ -398,6 +404,44 @@ class Model:
         v = [C.c_int64() for _ in range(3)]
         check(lib().ds4f_gpu_stream_stats(self.h, *[C.byref(x) for x in v]))
         return [x.value for x in v]
+
+
+HEAD_F8, HEAD_BF16, HEAD_MLX4 = 2, 4, 6
+
+
+class Head:
+    """The output head (ds4f_gpu_head_*): weights resident, logits + argmax."""
+
+    def __init__(self, dtype, w, scales=None, biases=None, V=None, H=None, SR=1, SC=1):
+        self.h = None
+        self._keep = [np.ascontiguousarray(a) if a is not None else None for a in (w, scales, biases)]
+        h = C.c_void_p()
+        check(lib().ds4f_gpu_head_create(dtype, *[ptr(a) for a in self._keep], V, H, SR, SC,
+                                         C.byref(h)))
+        self.h, self.V, self.H = h, V, H
+        self._keep = None
+
+    def logits(self, state, want_logits=True):
+        x = np.ascontiguousarray(state, np.float32)
+        y = np.zeros(self.V, np.float32) if want_logits else None
+        best = C.c_int(-1)
+        check(lib().ds4f_gpu_head_logits(self.h, ptr(x), ptr(y), C.byref(best)))
+        return y, best.value
+
+    def logits_dev(self, state, logits=None, best=None, stream=None):
+        check(lib().ds4f_gpu_head_logits_dev(self.h, ptr(state), ptr(logits), ptr(best), stream))
+
+    def close(self):
+        if self.h and _lib is not None:
+            _lib.ds4f_gpu_head_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def argmax_dev(logits, out, stream=None):
+    check(lib().ds4f_gpu_argmax_dev(ptr(logits), int(logits.numel()), ptr(out), stream))
 
 
 def pool_layout_plan(json_path, fmt, hidden, moe_inter, n_layers, n_experts):

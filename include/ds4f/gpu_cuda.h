@@ -180,6 +180,30 @@ int  ds4f_pool_layout_plan(const char *json_path, int fmt, int hidden, int moe_i
  * checked against the layout). */
 int  ds4f_gpu_pool_load_json(Ds4fGpuModel *m, const char *pool_path, const char *json_path);
 
+/* ---- the output head (the step after the MoE path) ----------------- */
+
+/* Logits over the vocabulary and the greedy pick: ds4f_head_logits
+ * (src/head.c:243-299) with the weights resident in HBM, and ds4f_argmax
+ * (src/head.c:303-309: the first index whose logit is strictly greater than
+ * every earlier one, starting from logits[0] -- so ties go to the lower
+ * index, NaN logits are never picked, and a NaN logits[0] gives 0). dtype is
+ * the reference head's w_dtype: 2 = F8_E4M3 with E8M0 block scales
+ * [SR x SC] (scales may be NULL: 1.0), 4 (or 3) = BF16, 6 = MLX 4-bit (U32
+ * words of 8 nibbles, BF16 scale and optional bias per 64; H is the decoded
+ * width, 8 x the packed columns). F32 (0), I8 (1) and F16 (5) heads are
+ * refused. The weights are copied at create. */
+typedef struct Ds4fGpuHead Ds4fGpuHead;
+int  ds4f_gpu_head_create(int dtype, const void *w, const void *scales, const void *biases,
+                          int V, int H, int SR, int SC, Ds4fGpuHead **out);
+void ds4f_gpu_head_free(Ds4fGpuHead *h);
+/* Host buffers: state[H] in; logits[V] and *argmax out (either may be NULL). */
+int  ds4f_gpu_head_logits(Ds4fGpuHead *h, const float *state, float *logits, int *argmax);
+/* Device pointers on `stream` (NULL: the head's own stream); no sync. */
+int  ds4f_gpu_head_logits_dev(Ds4fGpuHead *h, const float *state_dev, float *logits_dev,
+                              int *argmax_dev, void *stream);
+/* The pick alone over n device logits -> *out_dev. */
+int  ds4f_gpu_argmax_dev(const float *logits_dev, int n, int *out_dev, void *stream);
+
 /* ---- pools larger than HBM: the expert cache ------------------------ */
 
 /* The reference's routed-expert cache policy (ds4f_cache_init /

@@ -154,6 +154,16 @@ def ref():
     return _ref
 
 
+def argmax(logits):
+    """ds4f_argmax (src/head.c:303-309): start from logits[0]; an index is
+    taken only if its logit is strictly greater than the best so far."""
+    best, bv = 0, logits[0]
+    for i in range(1, len(logits)):
+        if logits[i] > bv:
+            bv, best = logits[i], i
+    return best
+
+
 def ptr(a):
     return a.ctypes.data_as(C.c_void_p) if a is not None else None
 
