@@ -196,7 +196,7 @@ int ds4f_gpu_head_logits_dev(Ds4fGpuHead *h, const float *state_dev, float *logi
                              void *stream) {
     using namespace ds4f;
     DS4F_REQUIRE(h && state_dev, "head_logits: null argument");
-    cudaStream_t st = stream ? (cudaStream_t)stream : h->stream;
+    cudaStream_t st = (cudaStream_t)stream;           // NULL: the default stream, as every _dev call
     DS4F_CUDA(cudaMemcpyAsync(h->x, state_dev, (size_t)h->H * 4, cudaMemcpyDeviceToDevice, st));
     if (launch_jobs(h->job, 1, h->nitems, st)) return -1;
     if (argmax_dev && argmax_launch(h->y, h->V, h->pv, h->pi, argmax_dev, st)) return -1;

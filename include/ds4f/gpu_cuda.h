@@ -198,7 +198,7 @@ int  ds4f_gpu_head_create(int dtype, const void *w, const void *scales, const vo
 void ds4f_gpu_head_free(Ds4fGpuHead *h);
 /* Host buffers: state[H] in; logits[V] and *argmax out (either may be NULL). */
 int  ds4f_gpu_head_logits(Ds4fGpuHead *h, const float *state, float *logits, int *argmax);
-/* Device pointers on `stream` (NULL: the head's own stream); no sync. */
+/* Device pointers on `stream` (NULL: the default stream); no sync. */
 int  ds4f_gpu_head_logits_dev(Ds4fGpuHead *h, const float *state_dev, float *logits_dev,
                               int *argmax_dev, void *stream);
 /* The pick alone over n device logits -> *out_dev. */

@@ -43,6 +43,14 @@ def test_bf16_head(V):
     assert best == po.argmax(y)                 # the pick of the logits it returned
     _, best2 = hd.logits(x, want_logits=False)
     assert best2 == best
+    # the device-pointer call on torch's stream: same logits, same pick
+    import torch
+    tx = torch.from_numpy(x).cuda()
+    ty = torch.zeros(V, device="cuda")
+    tb = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    hd.logits_dev(tx, ty, tb, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert np.array_equal(ty.cpu().numpy(), y) and int(tb.item()) == best
     hd.close()
 
 
