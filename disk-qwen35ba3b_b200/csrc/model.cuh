@@ -24,8 +24,10 @@ struct ModelDesc {
                           //    sequential fp32 order (slow, bit-exact weights)
 };
 
-// Expert slot layout: gate, up, down, each values then scales, in the
-// reference converter's manifest order (tools/convert-ds4f.py:1321-1356).
+// Expert slot layout: gate, up, down, each values then scales -- the order
+// in which the engine reads an expert's tensor entries (src/moe.c:598-605).
+// The converter writes sorted-name order (down, gate, up) into its pool file;
+// poolfile.cu places those by name.
 struct SlotLayout {
     int64_t rel_v[3], rel_s[3], nbytes;
 };

@@ -129,7 +129,8 @@ typedef struct Ds4fGpuModel Ds4fGpuModel;
 int  ds4f_gpu_model_create(const Ds4fGpuModelDesc *desc, Ds4fGpuModel **out);
 void ds4f_gpu_model_destroy(Ds4fGpuModel *m);
 /* Bytes of one expert slot (gate, up, down; values then scales each, the
- * converter's order, tools/convert-ds4f.py:1321-1356) and its offsets. */
+ * order in which the engine reads an expert's tensors, src/moe.c:598-605)
+ * and its offsets. */
 int  ds4f_gpu_model_slot(const Ds4fGpuModel *m, int64_t rel_v[3],
                          int64_t rel_s[3], int64_t *nbytes);
 /* Fill the whole shard with the seeded synthetic weights (sigma 0.02). */
@@ -155,7 +156,9 @@ int  ds4f_gpu_model_get_expert(const Ds4fGpuModel *m, int layer, int expert,
                                uint8_t *slot);
 /* Load this shard from a packed pool file: [u64 expert_nbytes][u64
  * n_layers][u64 n_experts] then slots layer-major, expert N of layer L at
- * 24 + (L*E + N)*nbytes (ds4f_pool_open_packed, src/st.c:127-180). */
+ * 24 + (L*E + N)*nbytes (ds4f_pool_open_packed, src/st.c:127-180), each slot
+ * already in this library's slot layout. A pool written by the converter
+ * (tensors in sorted-name order) loads with ds4f_gpu_pool_load_json. */
 int  ds4f_gpu_pool_load(Ds4fGpuModel *m, const char *path);
 
 /* The converter's layout file beside a packed pool (pool-mxfp4.json,
