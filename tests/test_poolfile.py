@@ -7,6 +7,7 @@ Pinned on a pool written by the reference's own converter
 the plan places as gate, up or down decodes to that tensor's source
 weights."""
 import copy
+import ctypes as C
 import importlib.util
 import json
 import os
@@ -177,3 +178,108 @@ def test_json_reader_corner_cases(tmp_path):
     off, nb = dc.pool_layout_plan(p, dc.FMT_MXFP4, 64, 32, 2, 3)
     ref, _ = dc.pool_layout_plan(j, dc.FMT_MXFP4, 64, 32, 2, 3)
     assert np.array_equal(off, ref)
+
+
+# ---- against the reference's own layout loader ------------------------------
+# ds4f_pool_layout_load (src/moe.c:51-160) is compiled into oracle/_ref with
+# the rest of moe.c; the structures below mirror include/ds4f/moe.h:20-44 and
+# include/ds4f/ds4f.h:56-75 (x86-64, LP64).
+
+class _MoETensor(C.Structure):
+    _fields_ = [("dims", C.c_long * 4), ("rank", C.c_int), ("rel_v", C.c_long),
+                ("rel_s", C.c_long), ("rel_b", C.c_long), ("v_nbytes", C.c_long),
+                ("s_nbytes", C.c_long), ("bsize", C.c_int), ("fmt", C.c_int)]
+
+
+class _ExpertLayout(C.Structure):
+    _fields_ = [("n", C.c_int), ("chain", C.c_int), ("t", _MoETensor * 8)]
+
+
+class _PoolLayout(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("n_experts", C.c_int),
+                ("expert_nbytes", C.c_int64), ("max_rc", C.c_int64),
+                ("exp", C.POINTER(_ExpertLayout))]
+
+
+class _Cfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "n_experts", "topk", "n_shared", "hidden",
+                                       "latent", "moe_inter", "n_heads", "n_kv_heads", "qk_rope")] + \
+               [(n, C.c_double) for n in ("rope_factor", "rope_beta_fast", "rope_beta_slow",
+                                          "rope_max_pos", "rope_theta")] + \
+               [("expert_nbytes", C.c_int64), ("n_shards", C.c_int), ("seed", C.c_uint64)]
+
+
+def _ref_layout(path, L, E):
+    """-> (rc, [[(rel_v, rel_s, dims) per entry] per expert]) from the
+    reference's loader, or None when oracle/_ref is absent."""
+    so = os.path.join(ROOT, "oracle", "_ref", "libds4f_ref.so")
+    if not os.path.exists(so):
+        return None
+    R = C.CDLL(so)
+    R.ds4f_pool_layout_load.argtypes = [C.POINTER(_PoolLayout), C.c_char_p, C.POINTER(_Cfg)]
+    pl, cfg = _PoolLayout(), _Cfg()
+    cfg.n_layers, cfg.n_experts = L, E
+    rc = R.ds4f_pool_layout_load(C.byref(pl), str(path).encode(), C.byref(cfg))
+    if rc != 0:
+        return rc, None
+    out = []
+    for i in range(L * E):
+        el = pl.exp[i]
+        out.append([(el.t[k].rel_v, el.t[k].rel_s, list(el.t[k].dims[:el.t[k].rank]))
+                    for k in range(el.n)])
+    C.CDLL(None).free(C.cast(pl.exp, C.c_void_p))
+    return rc, out
+
+
+def _compare_with_reference(json_path, fmt, H, M, L, E):
+    got = _ref_layout(json_path, L, E)
+    if got is None:
+        pytest.skip("oracle/_ref not built")
+    rc, ref = got
+    assert rc == 0
+    off, nb = dc.pool_layout_plan(json_path, fmt, H, M, L, E)
+    meta = json.load(open(json_path))
+    entries = {}
+    for t in meta["tensors"]:
+        entries.setdefault((t["layer"], t["expert"]), []).append(t)
+    for l in range(L):
+        for x in range(E):
+            base = 24 + (l * E + x) * nb
+            ents = entries[(l, x)]
+            assert len(ref[l * E + x]) == len(ents) == 3
+            for k, t in enumerate(ents):
+                role = (ROLES.index(t["n"].rsplit(".", 2)[-2]) if "n" in t else k)
+                rv, rs, dims = ref[l * E + x][k]
+                assert (rv, rs) == (off[l, x, role, 0] - base, off[l, x, role, 1] - base)
+                assert dims == t["shape"]
+
+
+def test_plan_agrees_with_reference_loader_on_converter_pool():
+    _compare_with_reference(os.path.join(REF, "pool-mxfp4.json"), dc.FMT_MXFP4, 64, 32, 2, 4)
+
+
+@pytest.mark.parametrize("order,names", [(pf.CONVERTER_ORDER, True), (pf.ROLES, False),
+                                         (("up", "gate", "down"), True)])
+def test_plan_agrees_with_reference_loader_on_written_pools(tmp_path, order, names):
+    L, E, H, M = 3, 5, 64, 32
+    slots = _slots(dc.FMT_MXFP4, L, E, H, M, 9)
+    b, j = tmp_path / "pool.bin", tmp_path / "pool.json"
+    pf.write_pool(b, j, dc.FMT_MXFP4, L, E, H, M, lambda l, x: slots[l, x], order=order, names=names)
+    _compare_with_reference(j, dc.FMT_MXFP4, H, M, L, E)
+
+
+def test_refusals_shared_with_reference_loader(tmp_path):
+    meta, _ = _base(tmp_path)
+    for mutate in (lambda m: m.__setitem__("n_layers", 5),
+                   lambda m: m["tensors"][4].__setitem__("v_off", 5),
+                   lambda m: m.pop("expert_nbytes")):
+        m = copy.deepcopy(meta)
+        mutate(m)
+        p = tmp_path / "bad.json"
+        p.write_text(json.dumps(m))
+        got = _ref_layout(p, 2, 3)
+        if got is None:
+            pytest.skip("oracle/_ref not built")
+        assert got[0] != 0
+        with pytest.raises(dc.GpuError):
+            dc.pool_layout_plan(p, dc.FMT_MXFP4, 64, 32, 2, 3)
