@@ -3,6 +3,7 @@
 #include "matvec.cuh"
 #include "model.cuh"
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -448,6 +449,7 @@ int ds4f_gpu_model_create_streaming(const Ds4fGpuModelDesc *desc, const uint8_t 
                  "model_create_streaming: the host pool holds every expert (no shard)");
     DS4F_REQUIRE(n_slots >= desc->topk, "model_create_streaming: %d slots, at least top-k = %d needed", n_slots,
                  desc->topk);
+    n_slots = (int)std::min<int64_t>(n_slots, (int64_t)desc->n_layers * desc->n_experts);   // no unused slots
     Ds4fGpuModel *h = nullptr;
     if (model_create_impl(desc, n_slots, &h)) return -1;
     Model &m = h->m;
