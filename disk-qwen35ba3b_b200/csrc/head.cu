@@ -2,8 +2,9 @@
 // vocabulary and the greedy pick (ds4f_head_logits, src/head.c:243-299;
 // ds4f_argmax, src/head.c:303-309), the head's weights resident in HBM.
 //
-// The matvec is the job kernel of matvec.cu on one job of R = vocabulary
-// rows (HBM-bound: the weight bytes are read once per call). The pick is a
+// The matvec is k_head_bf16 below for BF16 heads of width 1024, 2048 or 4096,
+// else the job kernel of matvec.cu on one job of R = vocabulary rows
+// (HBM-bound: the weight bytes are read once per call). The pick is a
 // two-stage reduction with the reference's rule: start from logits[0], take
 // an index only if its logit is strictly greater -- so the lowest index wins
 // ties, NaN logits are never taken, and a NaN logits[0] is the answer.
@@ -76,6 +77,42 @@ __global__ void __launch_bounds__(kArgThreads) k_argmax_final(const float *__res
     }
 }
 
+// BF16 head rows: one warp per row, the row's H/256 16-byte chunks per lane
+// loaded together (lane-contiguous, so each load instruction of a warp covers
+// 512 contiguous bytes), x staged once per block in shared memory. About 50
+// registers a thread: four 256-thread blocks per SM, 32 warps streaming.
+template <int CPL>
+__global__ void __launch_bounds__(256, 4) k_head_bf16(const uint16_t *__restrict__ W, const float *__restrict__ x,
+                                                      float *__restrict__ y, int V) {
+    constexpr int H = CPL * 256;
+    __shared__ __align__(16) float xs[H];
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < V; r += warps) {
+        const uint8_t *row = (const uint8_t *)W + (int64_t)r * H * 2;
+        uint4 c[CPL];
+#pragma unroll
+        for (int k = 0; k < CPL; k++) c[k] = ldg_stream(row + (size_t)(lane + 32 * k) * 16);
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < CPL; k++) {
+            const float4 *xv = (const float4 *)(xs + (lane + 32 * k) * 8);
+            const float4 x0 = xv[0], x1 = xv[1];
+            const uint32_t w[4] = {c[k].x, c[k].y, c[k].z, c[k].w};
+            const float xx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                acc = fmaf(__uint_as_float(w[j] << 16), xx[2 * j], acc);
+                acc = fmaf(__uint_as_float(w[j] & 0xFFFF0000u), xx[2 * j + 1], acc);
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+        if (lane == 0) y[r] = acc;
+    }
+}
+
 int argmax_launch(const float *y, int n, float *pv, int *pi, int *out, cudaStream_t st) {
     const int nb = std::max(1, std::min(kArgBlocks, (n + kArgThreads - 1) / kArgThreads));
     k_argmax_part<<<nb, kArgThreads, 0, st>>>(y, n, pv, pi);
@@ -90,6 +127,9 @@ int argmax_launch(const float *y, int n, float *pv, int *pi, int *out, cudaStrea
 
 struct Ds4fGpuHead {
     int dtype = 0, V = 0, H = 0, device = 0, nitems = 0;
+    int rows_kernel = 0;                // BF16 with H = 1024 / 2048 / 4096: k_head_bf16
+    int grid = 0;
+    const void *wdev = nullptr;
     void *wbuf = nullptr;               // weights, scales, biases, x, logits, job, partials
     float *x = nullptr, *y = nullptr, *pv = nullptr;
     int *pi = nullptr, *best = nullptr;
@@ -170,6 +210,13 @@ int ds4f_gpu_head_create(int dtype, const void *w, const void *scales, const voi
     J.b = bb ? base + ob : nullptr;
     J.x = h->x;
     J.y = h->y;
+    h->wdev = base + ow;
+    if (fmt == DS4F_FMT_BF16 && (H == 1024 || H == 2048 || H == 4096)) {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, h->device);
+        h->rows_kernel = 1;
+        h->grid = std::max(1, std::min(4 * sms, (V + 7) / 8));   // every block resident
+    }
     h->nitems = plan_jobs(&J, 1);
     if (h->nitems < 0) { ds4f_gpu_head_free(h); return -1; }
     if (cudaMemcpy(h->job, &J, sizeof J, cudaMemcpyHostToDevice) != cudaSuccess) return fail("job upload");
@@ -192,13 +239,24 @@ void ds4f_gpu_head_free(Ds4fGpuHead *h) {
     delete h;
 }
 
+static int head_matvec(Ds4fGpuHead *h, cudaStream_t st) {
+    using namespace ds4f;
+    if (!h->rows_kernel) return launch_jobs(h->job, 1, h->nitems, st);
+    const uint16_t *w = (const uint16_t *)h->wdev;
+    if (h->H == 1024) k_head_bf16<4><<<h->grid, 256, 0, st>>>(w, h->x, h->y, h->V);
+    else if (h->H == 2048) k_head_bf16<8><<<h->grid, 256, 0, st>>>(w, h->x, h->y, h->V);
+    else k_head_bf16<16><<<h->grid, 256, 0, st>>>(w, h->x, h->y, h->V);
+    DS4F_CUDA(cudaGetLastError());
+    return 0;
+}
+
 int ds4f_gpu_head_logits_dev(Ds4fGpuHead *h, const float *state_dev, float *logits_dev, int *argmax_dev,
                              void *stream) {
     using namespace ds4f;
     DS4F_REQUIRE(h && state_dev, "head_logits: null argument");
     cudaStream_t st = (cudaStream_t)stream;           // NULL: the default stream, as every _dev call
     DS4F_CUDA(cudaMemcpyAsync(h->x, state_dev, (size_t)h->H * 4, cudaMemcpyDeviceToDevice, st));
-    if (launch_jobs(h->job, 1, h->nitems, st)) return -1;
+    if (head_matvec(h, st)) return -1;
     if (argmax_dev && argmax_launch(h->y, h->V, h->pv, h->pi, argmax_dev, st)) return -1;
     if (logits_dev)
         DS4F_CUDA(cudaMemcpyAsync(logits_dev, h->y, (size_t)h->V * 4, cudaMemcpyDeviceToDevice, st));
@@ -211,7 +269,7 @@ int ds4f_gpu_head_logits(Ds4fGpuHead *h, const float *state, float *logits, int 
     cudaStream_t st = h->stream;
     memcpy(h->host_x, state, (size_t)h->H * 4);
     DS4F_CUDA(cudaMemcpyAsync(h->x, h->host_x, (size_t)h->H * 4, cudaMemcpyHostToDevice, st));
-    if (launch_jobs(h->job, 1, h->nitems, st)) return -1;
+    if (head_matvec(h, st)) return -1;
     if (argmax) {
         if (argmax_launch(h->y, h->V, h->pv, h->pi, h->best, st)) return -1;
         DS4F_CUDA(cudaMemcpyAsync(h->host_best, h->best, 4, cudaMemcpyDeviceToHost, st));
