@@ -940,8 +940,8 @@ def run_gpu_stream(args, rank, world, local_rank):
     }
 
 
-# DRAM bytes (read + write) of the head's matvec launch, from the ncu --set full
-# capture in profiles/k_mv_jobs_head_bf16_full.md
+# DRAM bytes (read + write) of the job-kernel launch that served the head before
+# k_head_bf16, from the ncu --set full capture in profiles/k_mv_jobs_head_bf16_full.md
 HEAD_TRAFFIC_PER_LAUNCH = 1_017_247_000 + 3_999_744
 
 
@@ -995,8 +995,10 @@ def run_gpu_head(args, rank, world, local_rank):
         "config": {"workload": "head: Qwen3.5 vocabulary head, 248,320 x 2048 BF16, batch 1",
                    "l2": "inputs larger than L2 (1.02 GB of weights per step)", "parallelism": "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(gbs / peak, 4), "traffic": HEAD_TRAFFIC_PER_LAUNCH,
-                     "traffic_unit": "bytes per k_mv_jobs launch (ncu, profiles/k_mv_jobs_head_bf16_full.md)",
+                     "frac": round(gbs / peak, 4), "traffic": None,
+                     "traffic_note": "k_head_bf16 not yet captured; the job kernel it replaced read "
+                                     f"{HEAD_TRAFFIC_PER_LAUNCH} B per launch (profiles/k_mv_jobs_head_bf16_full.md)",
+                     "kernel": "k_head_bf16 (one warp per row, 4 blocks per SM) + argmax",
                      "peak_source": src, "algorithmic_bytes_per_step": algo},
         "e2e": {"value": round(args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": Hh * 4,
                 "d2h_bytes_per_step": 4, "timer": "host clock around ds4f_gpu_head_logits"},
