@@ -14,8 +14,10 @@
  * (per host thread). Unlike the reference there is NO CPU fallback behind
  * these calls: a caller that gets -1 reports the message and stops.
  * Host-buffer calls are synchronous on return. `_dev` calls take device
- * pointers and enqueue on the given stream (NULL = the library's stream).
- * One host thread per model; calls are not re-entrant.
+ * pointers and enqueue on the given stream; NULL is the default stream,
+ * except for ds4f_gpu_mv_run and ds4f_gpu_synth_f32, which take NULL as the
+ * library's own stream. One host thread per model, head or cache; calls are
+ * not re-entrant.
  */
 #ifndef DS4F_GPU_CUDA_H
 #define DS4F_GPU_CUDA_H
@@ -217,7 +219,9 @@ int  ds4f_gpu_argmax_dev(const float *logits_dev, int n, int *out_dev, void *str
  * slot fetched longest ago -- hits do not refresh it; none left: slot -1, a
  * drop), then marks the reserved slots fetched in pool-offset order, each
  * taking the next clock value. getmany fills out_slot[n] and returns the
- * number of slots to fill (the caller copies them in). No device needed. */
+ * number of slots to fill (the caller copies them in); a request above 64
+ * experts is cut to its first 64, as the reference's DS4F_MAX_TOPK cuts it.
+ * No device needed. */
 typedef struct Ds4fSlotCache Ds4fSlotCache;
 /* flags: 0 = the reference's policy exactly. DS4F_SLOTCACHE_GUARD = a
  * request's own hits are not evicted by its later misses and an expert named
