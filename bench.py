@@ -956,7 +956,7 @@ def run_gpu_head(args, rank, world, local_rank):
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
-    V, Hh = 248_320, H
+    V, Hh = args.head_rows, H
     w = torch.empty(V * Hh, dtype=torch.bfloat16).normal_(0, 0.02, generator=torch.Generator().manual_seed(0))
     hd = dc.Head(dc.HEAD_BF16, w.view(torch.int16).numpy(), V=V, H=Hh)
     del w
@@ -992,7 +992,7 @@ def run_gpu_head(args, rank, world, local_rank):
         "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 weights, fp32 accumulate", "data": "synthetic (seeded N(0, 0.02) weights)",
-        "config": {"workload": "head: Qwen3.5 vocabulary head, 248,320 x 2048 BF16, batch 1",
+        "config": {"workload": f"head: vocabulary head, {V:,} x 2048 BF16, batch 1",
                    "l2": "inputs larger than L2 (1.02 GB of weights per step)", "parallelism": "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "traffic": None,
@@ -1023,6 +1023,8 @@ def main():
     ap.add_argument("--fmt", default=None, choices=["fp8", "mxfp4"],
                     help="expert format (decode default fp8; ep-decode default mxfp4)")
     ap.add_argument("--batch", type=int, default=1, help="ep-decode: tokens per step")
+    ap.add_argument("--head-rows", type=int, default=248_320,
+                    help="head: vocabulary rows (default Qwen3.5's 248,320; smaller for profiling)")
     ap.add_argument("--slots", type=int, default=0,
                     help="stream-decode: HBM expert slots (default a quarter of the pool)")
     args = ap.parse_args()
