@@ -940,9 +940,10 @@ def run_gpu_stream(args, rank, world, local_rank):
     }
 
 
-# DRAM bytes (read + write) of the job-kernel launch that served the head before
-# k_head_bf16, from the ncu --set full capture in profiles/k_mv_jobs_head_bf16_full.md
-HEAD_TRAFFIC_PER_LAUNCH = 1_017_247_000 + 3_999_744
+# DRAM bytes (read + write) of one k_head_bf16 launch over the 248,320-row head:
+# the ncu capture of a 62,080-row head (profiles/k_head_bf16_quarter_launch.md),
+# 254,331,904 + 2,894,848 bytes, times 4 (a launch reads its weights once)
+HEAD_TRAFFIC_PER_LAUNCH = 4 * (254_331_904 + 2_894_848)
 
 
 def run_gpu_head(args, rank, world, local_rank):
@@ -995,9 +996,9 @@ def run_gpu_head(args, rank, world, local_rank):
         "config": {"workload": f"head: vocabulary head, {V:,} x 2048 BF16, batch 1",
                    "l2": "inputs larger than L2 (1.02 GB of weights per step)", "parallelism": "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(gbs / peak, 4), "traffic": None,
-                     "traffic_note": "k_head_bf16 not yet captured; the job kernel it replaced read "
-                                     f"{HEAD_TRAFFIC_PER_LAUNCH} B per launch (profiles/k_mv_jobs_head_bf16_full.md)",
+                     "frac": round(gbs / peak, 4), "traffic": round(HEAD_TRAFFIC_PER_LAUNCH * V / 248_320),
+                     "traffic_unit": "bytes per k_head_bf16 launch (ncu of a 62,080-row head scaled by rows, "
+                                     "profiles/k_head_bf16_quarter_launch.md)",
                      "kernel": "k_head_bf16 (one warp per row, 4 blocks per SM) + argmax",
                      "peak_source": src, "algorithmic_bytes_per_step": algo},
         "e2e": {"value": round(args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": Hh * 4,
