@@ -989,7 +989,7 @@ def run_gpu_head(args, rank, world, local_rank):
     peak, src = peaks()
     gbs = algo / (ms / 1e3) / 1e9
     return {
-        "metric": "output head tokens/s (248,320 x 2048 BF16 logits + argmax, 1 B200)",
+        "metric": f"output head tokens/s ({V:,} x 2048 BF16 logits + argmax, 1 B200)",
         "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 weights, fp32 accumulate", "data": "synthetic (seeded N(0, 0.02) weights)",
