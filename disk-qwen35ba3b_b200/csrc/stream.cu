@@ -20,6 +20,7 @@
 // reference's.
 #include <algorithm>
 #include <cstring>
+#include <set>
 #include <new>
 #include <unordered_map>
 #include <vector>
@@ -39,25 +40,40 @@ struct SlotCache {
     std::vector<uint8_t> pinned;
     std::unordered_map<uint64_t, int> where;     // live key -> slot
     std::vector<uint8_t> held;                   // guard: this request's hits
+    // The victim order kept sorted instead of scanned: free slots by index,
+    // and the live slots that may be evicted (not pinned, not held) by their
+    // fetch clock, which is unique per slot -- so the first of each is the
+    // slot the reference's linear scan picks, in O(log n).
+    std::set<int> empty_slots;
+    std::set<std::pair<uint64_t, int>> lru;
     uint64_t clock = 0;
     int64_t nreq = 0, nhit = 0, ndrop = 0, nfetch = 0;
     bool guard = false;
 
-    SlotCache(int n, bool g) : nslot(n), key(n, kEmpty), used_at(n, 0), pinned(n, 0), held(n, 0), guard(g) {}
+    SlotCache(int n, bool g) : nslot(n), key(n, kEmpty), used_at(n, 0), pinned(n, 0), held(n, 0), guard(g) {
+        for (int i = 0; i < n; i++) empty_slots.insert(empty_slots.end(), i);
+    }
 
     static uint64_t expert_key(int layer, int expert) {
         return ((uint64_t)(uint32_t)(layer + 1) << 32) | (uint32_t)(expert + 1);
     }
+    bool evictable(int s) const { return key[s] > kInflight && !pinned[s] && !held[s]; }
+    // the first EMPTY slot, else the evictable slot fetched longest ago
     int victim() const {
-        int best = -1;
-        uint64_t oldest = ~(uint64_t)0;
-        for (int i = 0; i < nslot; i++) {
-            if (key[i] == kInflight) continue;
-            if (key[i] == kEmpty) return i;
-            if (pinned[i] || held[i]) continue;
-            if (used_at[i] < oldest) { oldest = used_at[i]; best = i; }
-        }
-        return best;
+        if (!empty_slots.empty()) return *empty_slots.begin();
+        return lru.empty() ? -1 : lru.begin()->second;
+    }
+    void set_pin(int s, bool on) {
+        const bool was = evictable(s);
+        pinned[s] = on;
+        const bool now = evictable(s);
+        if (was && !now) lru.erase({used_at[s], s});
+        if (!was && now) lru.insert({used_at[s], s});
+    }
+    void hold(int s) {
+        if (held[s]) return;
+        if (evictable(s)) lru.erase({used_at[s], s});
+        held[s] = 1;
     }
     // A request that names one expert twice fills two slots with one key; a
     // lookup answers the lowest such slot, as a linear scan would.
@@ -82,7 +98,7 @@ struct SlotCache {
             if (it != where.end()) {
                 out_slot[j] = it->second;
                 nhit++;
-                if (guard) held[it->second] = 1;
+                if (guard) hold(it->second);
                 continue;
             }
             if (guard) {                         // named earlier in this request
@@ -93,7 +109,12 @@ struct SlotCache {
             }
             const int s = victim();
             if (s < 0) { out_slot[j] = -1; ndrop++; continue; }
-            if (key[s] != kEmpty) forget(s);
+            if (key[s] == kEmpty) {
+                empty_slots.erase(s);
+            } else {
+                lru.erase({used_at[s], s});
+                forget(s);
+            }
             key[s] = kInflight;
             fetch.emplace_back(s, experts[j]);
             out_slot[j] = s;
@@ -106,12 +127,18 @@ struct SlotCache {
             const uint64_t k = expert_key(layer, f.second);
             key[f.first] = k;
             used_at[f.first] = ++clock;
+            if (evictable(f.first)) lru.insert({used_at[f.first], f.first});
             auto it = where.find(k);
             if (it == where.end() || f.first < it->second) where[k] = f.first;
         }
         if (guard)
-            for (int j = 0; j < n; j++)
-                if (out_slot[j] >= 0) held[out_slot[j]] = 0;
+            for (int j = 0; j < n; j++) {
+                const int h = out_slot[j];
+                if (h >= 0 && held[h]) {
+                    held[h] = 0;
+                    if (evictable(h)) lru.insert({used_at[h], h});
+                }
+            }
         nfetch += (int64_t)fetch.size();
         return (int)fetch.size();
     }
@@ -177,7 +204,7 @@ int ds4f_slotcache_getmany(Ds4fSlotCache *c, int layer, const int *experts, int 
 
 int ds4f_slotcache_pin(Ds4fSlotCache *c, int slot, int pin) {
     DS4F_REQUIRE(c, "slotcache_pin: null cache");
-    if (slot >= 0 && slot < c->c.nslot) c->c.pinned[slot] = (uint8_t)(pin != 0);
+    if (slot >= 0 && slot < c->c.nslot) c->c.set_pin(slot, pin != 0);
     return 0;
 }
 
