@@ -158,9 +158,11 @@ class Clocks:
 
 # ---- CPU baseline: the reference's own kernels on the host cores -------------
 
-def cpu_reference_sample(seconds=12.0, threads=8):
-    """Time layer-tokens of the reference CPU path (its own compiled
-    kernels) and return tok/s for the 40-layer stack plus a description.
+def cpu_reference_sampler(threads=8):
+    """Build the reference CPU path once and return (sample, close):
+    sample(seconds) times layer-tokens of it (its own compiled kernels) and
+    returns tok/s for the 40-layer stack plus a description; the state
+    restarts from the input every 40 layers, one token.
     Per layer: RMSNorm, bf16 router matvec (ds4f_bf16_matvec), ds4f_topk,
     8 expert chains (3 x ds4f_f8_matvec each, E8M0 128x128 block scales --
     the reference's FP8 scale format, same work per element as fp32 scales)
@@ -243,21 +245,34 @@ def cpu_reference_sample(seconds=12.0, threads=8):
         acc += (1.0 / (1.0 + np.exp(-sgt))) * so
         return state + acc
 
-    st = x.copy()
-    st = layer(st)                          # warm
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds or n < 2:
-        st = layer(st)
-        n += 1
-    dt = time.perf_counter() - t0
-    pool.shutdown()
-    tok_s = (n / LAYERS) / dt
-    return tok_s, {"cores": threads, "kind": kind,
-                   "sample": f"{n} layer-tokens of the 40-layer FP8 stack in {dt:.1f} s "
-                             f"(reference {'AVX2' if R is not None else 'scalar port'} "
-                             f"kernels, expert chains on {threads} threads), "
-                             f"extrapolated x{LAYERS} layers",
-                   "nproc": os.cpu_count()}
+    run = {"st": layer(x.copy()), "done": 1}            # warm
+
+    def sample(seconds):
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n < 2:
+            if run["done"] % LAYERS == 0:
+                run["st"] = x.copy()
+            run["st"] = layer(run["st"])
+            run["done"] += 1
+            n += 1
+        dt = time.perf_counter() - t0
+        return (n / LAYERS) / dt, {"cores": threads, "kind": kind,
+                                   "sample": f"{n} layer-tokens of the 40-layer FP8 stack in {dt:.1f} s "
+                                             f"(reference {'AVX2' if R is not None else 'scalar port'} "
+                                             f"kernels, expert chains on {threads} threads), "
+                                             f"extrapolated x{LAYERS} layers",
+                                   "nproc": os.cpu_count()}
+
+    return sample, pool.shutdown
+
+
+def cpu_reference_sample(seconds=12.0, threads=8):
+    """One bounded sample of the reference CPU path (cpu_reference_sampler)."""
+    sample, close = cpu_reference_sampler(threads)
+    try:
+        return sample(seconds)
+    finally:
+        close()
 
 
 def cpu_matvec_sample(seconds=4.0):
@@ -1036,14 +1051,17 @@ def main():
         if rank != 0:
             return
         n = max(1, args.steps)
-        per = max(2.0, min(20.0, 120.0 / (n + args.warmup)))
+        # built once; K samples sized so that warm-up and timing take ~2 minutes
+        per = max(0.25, min(20.0, 120.0 / (n + args.warmup / 4)))
+        sample, close = cpu_reference_sampler(threads=min(8, os.cpu_count() or 1))
         for _ in range(args.warmup):
-            cpu_reference_sample(per / 4, threads=min(8, os.cpu_count() or 1))
+            sample(per / 4)
         vals = []
         desc = None
         for _ in range(n):
-            v, desc = cpu_reference_sample(per, threads=min(8, os.cpu_count() or 1))
+            v, desc = sample(per)
             vals.append(v)
+        close()
         value = statistics.median(vals)
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
