@@ -126,7 +126,7 @@ def header_symbols():
 
 def check(rc):
     if rc != 0:
-        raise GpuError(lib().ds4f_gpu_last_error().decode())
+        raise GpuError(lib().ds4f_gpu_last_error().decode(errors="replace"))
 
 
 def ptr(a):
@@ -236,7 +236,7 @@ class SlotCache:
         out = np.zeros(len(e), np.int32)
         n = lib().ds4f_slotcache_getmany(self.h, layer, ptr(e), len(e), ptr(out))
         if n < 0:
-            raise GpuError(lib().ds4f_gpu_last_error().decode())
+            raise GpuError(lib().ds4f_gpu_last_error().decode(errors="replace"))
         return out, n
 
     def pin(self, slot, on=True):

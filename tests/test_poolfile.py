@@ -283,3 +283,36 @@ def test_refusals_shared_with_reference_loader(tmp_path):
         assert got[0] != 0
         with pytest.raises(dc.GpuError):
             dc.pool_layout_plan(p, dc.FMT_MXFP4, 64, 32, 2, 3)
+
+
+def test_reader_survives_mutated_files(tmp_path):
+    """Seeded byte flips, truncations, insertions and deletions of a valid
+    layout file: every one either plans or is refused with an error -- none
+    may crash the host process."""
+    _, j = _base(tmp_path)
+    good = j.read_bytes()
+    rng = np.random.default_rng(11)
+    p = tmp_path / "m.json"
+    planned = refused = 0
+    for i in range(1500):
+        b = bytearray(good)
+        for _ in range(int(rng.integers(1, 4))):
+            kind = int(rng.integers(0, 4))
+            at = int(rng.integers(0, len(b)))
+            if kind == 0:
+                b[at] = int(rng.integers(0, 256))
+            elif kind == 1:
+                del b[at:]
+            elif kind == 2:
+                b[at:at] = bytes(rng.choice(list(b'{}[]",:-0123456789.eE \\u'), int(rng.integers(1, 6))))
+            else:
+                del b[at:at + int(rng.integers(1, 8))]
+            if not b:
+                b = bytearray(b"{")
+        p.write_bytes(bytes(b))
+        try:
+            dc.pool_layout_plan(p, dc.FMT_MXFP4, 64, 32, 2, 3)
+            planned += 1
+        except dc.GpuError:
+            refused += 1
+    assert planned + refused == 1500 and refused > 0
