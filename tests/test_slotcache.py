@@ -130,6 +130,7 @@ def _requests(rng, n_layers, n_experts, count):
     (3, 16, 48, 1, 1),       # the whole pool fits: hits only after warm-up
     (2, 64, 5, 4, 2),        # fewer slots than a request: drops inside one
     (6, 256, 64, 2, 3),      # model-sized expert count
+    (8, 256, 2000, 2, 4),    # a large arena: long eviction order, many free slots
 ])
 def test_slot_policy_matches_reference_cache(tmp_path, n_layers, n_experts,
                                              nslot, nthreads, seed):
@@ -245,3 +246,29 @@ def test_slot_cache_arguments():
     c.close()
     with pytest.raises(dc.GpuError):
         dc.SlotCache(0)
+
+
+def test_host_entry_points_reject_bad_arguments():
+    """NULL pointers, bad sizes and unknown flags return -1 with a message
+    (no device involved); a pin outside the arena is ignored, as the
+    reference's ds4f_cache_pin ignores it (src/cache.c:221-223)."""
+    L = dc.lib()
+    h = C.c_void_p()
+    assert L.ds4f_slotcache_create(0, 0, C.byref(h)) == -1
+    assert L.ds4f_slotcache_create(4, 8, C.byref(h)) == -1          # unknown flag
+    assert L.ds4f_slotcache_create(4, 0, None) == -1
+    assert L.ds4f_slotcache_create(4, 0, C.byref(h)) == 0
+    out = np.zeros(2, np.int32)
+    ex = np.array([1, 2], np.int32)
+    assert L.ds4f_slotcache_getmany(None, 0, ex.ctypes.data, 2, out.ctypes.data) == -1
+    assert L.ds4f_slotcache_getmany(h, 0, None, 2, out.ctypes.data) == -1
+    assert L.ds4f_slotcache_getmany(h, 0, ex.ctypes.data, -1, out.ctypes.data) == -1
+    assert "slotcache_getmany" in L.ds4f_gpu_last_error().decode()
+    assert L.ds4f_slotcache_pin(h, 99, 1) == 0 and L.ds4f_slotcache_pin(h, -1, 1) == 0
+    assert L.ds4f_slotcache_getmany(h, 0, ex.ctypes.data, 2, out.ctypes.data) == 2
+    assert L.ds4f_slotcache_stats(None, None, None, None, None) == -1
+    L.ds4f_slotcache_free(h)
+    L.ds4f_slotcache_free(None)                                      # a no-op
+    assert L.ds4f_pool_layout_plan(None, dc.FMT_MXFP4, 64, 32, 2, 3, None, None) == -1
+    assert L.ds4f_pool_layout_plan(b"x.json", dc.FMT_MXFP4, 64, 32, 0, 3, None, None) == -1
+    assert L.ds4f_pool_layout_plan(b"x.json", 7, 64, 32, 2, 3, None, None) == -1
