@@ -34,7 +34,18 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "disk-qwen35ba3b_b200")
 sys.path.insert(0, ROOT)
+
+
+def ds4f_cuda():
+    """The product's ctypes binding (the package directory name is not a
+    Python identifier, so it is loaded by path)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ds4f_cuda", os.path.join(PKG, "ds4f_cuda.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 H, M, E, K, LAYERS = 2048, 512, 256, 8, 40
 METRIC = "MoE-stack decode tok/s (40-layer FP8, 1 B200 per rank)"
@@ -51,9 +62,12 @@ def bytes_per_token(fmt_fp8=True):
     return LAYERS * per_layer
 
 
-# DRAM bytes (read + write) of one k_decode launch, from the ncu --set full
-# capture summarised in profiles/k_decode_fp8_4layer_full.md (4-layer case,
-# 133.95 MB) scaled to 40 layers: every layer reads its own weights.
+# DRAM bytes (read + write) of one 40-layer k_decode launch: an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of the 4-layer case of this
+# script (--layers 4, 3.2 GB pool, 130 MB of weights per launch, larger than
+# L2), scaled by 10: every layer reads its own weights. Re-measured whenever
+# k_decode changes; KERNEL_REV names the kernel revision it belongs to.
+KERNEL_REV = "k_decode r1"
 TRAFFIC_PER_LAUNCH = 10 * 133_950_000
 # kernels of one batched-prefill layer (csrc/prefill.cu): count, plan, place,
 # front end, gate/up GEMM, SiLU digits, down GEMM, shared gate/up and down
@@ -158,6 +172,9 @@ class Clocks:
 
 # ---- CPU baseline: the reference's own kernels on the host cores -------------
 
+CPU_POOL_SLOTS = 128          # distinct FP8 expert slots of the CPU working set
+
+
 def cpu_reference_sampler(threads=8):
     """Build the reference CPU path once and return (sample, close):
     sample(seconds) times layer-tokens of it (its own compiled kernels) and
@@ -167,42 +184,45 @@ def cpu_reference_sampler(threads=8):
     8 expert chains (3 x ds4f_f8_matvec each, E8M0 128x128 block scales --
     the reference's FP8 scale format, same work per element as fp32 scales)
     on one thread per expert as ds4f_moe_step does (src/moe.c:1162-1192),
-    selection-order combine, bf16 shared expert with its sigmoid gate."""
+    selection-order combine, bf16 shared expert with its sigmoid gate.
+    Working set: 40 layers, each with its own router, shared expert and
+    gate (293 MB of bf16), and 128 distinct FP8 expert slots (403 MB);
+    expert e of layer L reads slot (L E + e) mod 128. That is ~700 MB, far
+    beyond the host's caches, so a token streams its 1.3 GB of weights from
+    DRAM as config 2's 32 GB pool would make it (the full pool is not built
+    on the host)."""
     import numpy as np
     from concurrent.futures import ThreadPoolExecutor
     from oracle import pyoracle as po
     R = po.ref()
-    kind = "reference"
-    if R is None:
-        kind = "port"
+    kind = "reference" if R is not None else "port"
     rng = np.random.default_rng(0)
     canon = np.array([b for b in range(256) if (b >> 3) & 15 != 15], np.uint8)
-    NX = 16                                 # distinct expert slots, reused
     ex = []
-    for _ in range(NX):
+    for _ in range(CPU_POOL_SLOTS):
         mats = []
         for (r, c) in ((M, H), (M, H), (H, M)):
-            w = canon[rng.integers(0, len(canon), r * c)].reshape(r, c)
-            s = rng.integers(112, 120, (r // 128) * (c // 128), dtype=np.uint16).astype(np.uint8)
-            mats.append((w, s, r, c))
+            w = canon[rng.integers(0, len(canon), r * c, dtype=np.uint8)].reshape(r, c)
+            sc = rng.integers(112, 120, (r // 128) * (c // 128), dtype=np.uint8)
+            mats.append((w, sc, r, c))
         ex.append(mats)
-    router = po.fill_bf16(E * H, po.key(0, 0, 1, 0, 0), 0.02).reshape(E, H)
-    shg = po.fill_bf16(M * H, po.key(0, 0, 2, 0, 0), 0.02).reshape(M, H)
-    shu = po.fill_bf16(M * H, po.key(0, 0, 2, 0, 1), 0.02).reshape(M, H)
-    shd = po.fill_bf16(H * M, po.key(0, 0, 2, 0, 2), 0.02).reshape(H, M)
-    shw = po.fill_bf16(H, po.key(0, 0, 2, 0, 3), 0.02).reshape(1, H)
+
+    def bf16(shape):
+        f = (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).view(np.uint32)
+        return (f >> 16).astype(np.uint16)
+    trunks = [(bf16((E, H)), bf16((M, H)), bf16((M, H)), bf16((H, M)), bf16((1, H))) for _ in range(LAYERS)]
     norm = np.full(H, 0x3F80, np.uint16)
     x = po.fill_f32(H, po.key(0, 0, 4, 0, 0), 1.0)
     ptr = po.ptr
     if R is not None:
         R.ds4f_kernels_set_simd(1)
 
-    def f8mv(w, s, r, c, xin):
+    def f8mv(w, sc, r, c, xin):
         y = np.zeros(r, np.float32)
         if R is not None:
-            R.ds4f_f8_matvec(ptr(w), ptr(s), r, c, r // 128, c // 128, ptr(xin), ptr(y))
+            R.ds4f_f8_matvec(ptr(w), ptr(sc), r, c, r // 128, c // 128, ptr(xin), ptr(y))
         else:
-            po.lib().orc_f8_matvec(ptr(w), 0, ptr(s), r, c, r // 128, c // 128, ptr(xin), ptr(y))
+            po.lib().orc_f8_matvec(ptr(w), 0, ptr(sc), r, c, r // 128, c // 128, ptr(xin), ptr(y))
         return y
 
     def bfmv(w, xin):
@@ -214,8 +234,8 @@ def cpu_reference_sampler(threads=8):
             po.lib().orc_bf16_matvec(ptr(w), r, c, ptr(xin), None, ptr(y))
         return y
 
-    def chain(e, xin):
-        (wg, sg, r, c), (wu, su, _, _), (wd, sd, rd, cd) = ex[e % NX]
+    def chain(slot, xin):
+        (wg, sg, r, c), (wu, su, _, _), (wd, sd, rd, cd) = ex[slot]
         g = f8mv(wg, sg, r, c, xin)
         u = f8mv(wu, su, r, c, xin)
         ch = (g * (1.0 / (1.0 + np.exp(-g))) * u).astype(np.float32)
@@ -223,7 +243,8 @@ def cpu_reference_sampler(threads=8):
 
     pool = ThreadPoolExecutor(threads)
 
-    def layer(state):
+    def layer(L, state):
+        router, shg, shu, shd, shw = trunks[L]
         xin = state.copy()
         po.lib().orc_rmsnorm(ptr(norm), H, ptr(xin))
         sc = bfmv(router, xin)
@@ -234,7 +255,7 @@ def cpu_reference_sampler(threads=8):
         else:
             po.lib().orc_topk(ptr(sc), E, K, ptr(idx), ptr(w))
         w = w / w.sum()
-        outs = list(pool.map(lambda e: chain(int(e), xin), idx))
+        outs = list(pool.map(lambda e: chain((L * E + int(e)) % CPU_POOL_SLOTS, xin), idx))
         acc = np.zeros(H, np.float32)
         for j in range(K):
             acc += w[j] * outs[j]
@@ -245,34 +266,44 @@ def cpu_reference_sampler(threads=8):
         acc += (1.0 / (1.0 + np.exp(-sgt))) * so
         return state + acc
 
-    run = {"st": layer(x.copy()), "done": 1}            # warm
+    run = {"st": x.copy(), "done": 0}
 
     def sample(seconds):
         n, t0 = 0, time.perf_counter()
         while time.perf_counter() - t0 < seconds or n < 2:
-            if run["done"] % LAYERS == 0:
+            L = run["done"] % LAYERS
+            if L == 0:
                 run["st"] = x.copy()
-            run["st"] = layer(run["st"])
+            run["st"] = layer(L, run["st"])
             run["done"] += 1
             n += 1
         dt = time.perf_counter() - t0
-        return (n / LAYERS) / dt, {"cores": threads, "kind": kind,
-                                   "sample": f"{n} layer-tokens of the 40-layer FP8 stack in {dt:.1f} s "
-                                             f"(reference {'AVX2' if R is not None else 'scalar port'} "
-                                             f"kernels, expert chains on {threads} threads), "
-                                             f"extrapolated x{LAYERS} layers",
-                                   "nproc": os.cpu_count()}
+        return (n / LAYERS) / dt, n, dt
 
-    return sample, pool.shutdown
+    desc = {"cores": threads, "kind": kind, "nproc": os.cpu_count(),
+            "working_set": f"40 distinct layers of router + shared expert (293 MB bf16) and "
+                           f"{CPU_POOL_SLOTS} distinct FP8 expert slots (403 MB): beyond the host caches"}
+    return sample, pool.shutdown, desc
 
 
-def cpu_reference_sample(seconds=12.0, threads=8):
-    """One bounded sample of the reference CPU path (cpu_reference_sampler)."""
-    sample, close = cpu_reference_sampler(threads)
+def cpu_reference_median(n_samples, seconds_each, warm_seconds, threads=8):
+    """The reference CPU path timed the same way in both bench arms: one
+    warm-up sample, then the median tok/s of n_samples samples."""
+    sample, close, desc = cpu_reference_sampler(threads)
     try:
-        return sample(seconds)
+        sample(warm_seconds)
+        runs = [sample(seconds_each) for _ in range(n_samples)]
     finally:
         close()
+    vals = sorted(r[0] for r in runs)
+    value = statistics.median(vals)
+    layers = sum(r[1] for r in runs)
+    secs = sum(r[2] for r in runs)
+    return value, dict(desc, sample=f"median of {n_samples} warmed samples ({layers} layer-tokens of the "
+                                    f"40-layer FP8 stack in {secs:.1f} s; reference "
+                                    f"{'AVX2' if desc['kind'] == 'reference' else 'scalar port'} kernels, "
+                                    f"expert chains on {threads} threads), tok/s = layer-tokens / 40 / s",
+                       spread=[round(vals[0], 4), round(vals[-1], 4)])
 
 
 def cpu_matvec_sample(seconds=4.0):
@@ -310,9 +341,63 @@ def cpu_matvec_sample(seconds=4.0):
 
 # ---- GPU arm ------------------------------------------------------------------
 
+def decode_config(fp8, world, layers=LAYERS, parallelism=None):
+    """The `config` of a decode line: the same dict in both bench arms."""
+    bpt = bytes_per_token(fp8) * layers // LAYERS
+    return {"workload": ("config 2: 40-layer FP8 MoE decode, 1 token/step" if fp8 else
+                         "config 3 (1 GPU, batch 1): 40-layer MXFP4 MoE decode, 1 token/step")
+            if layers == LAYERS else f"profiling case: {layers}-layer {'FP8' if fp8 else 'MXFP4'} decode",
+            "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": layers,
+            "pool_gb": round(layers * E * (3146496 if fp8 else 1671168) / 1e9, 2),
+            "l2": f"inputs larger than L2 ({bpt / 1e9:.2f} GB of weights per step)",
+            "parallelism": parallelism or ("single GPU" if world == 1 else f"replicas x{world}")}
+
+
+N_STAMPS = 20          # phase-trace stamp slots per (layer-step, CTA) in k_decode
+PHASES = ["start", "state", "norm", "rows_done", "routes_vis", "topk", "issued",
+          "softmax", "grp0", "chains", "down_in", "written"]
+
+
+def phase_table(tr):
+    """k_decode's %globaltimer phase trace of one step (the counterpart of
+    the reference's per-phase timers, src/main.c:253-258, 1522-1546):
+    tr int64 [L, G, N_STAMPS] -> per phase the median over layers of the
+    median and of the max over CTAs (us), gather rounds, layer period."""
+    import numpy as np
+    L = tr.shape[0]
+    out = {}
+    d = np.diff(tr[:, :, :12], axis=2)
+    rows = []
+    for k in range(11):
+        rows.append((f"{PHASES[k]} -> {PHASES[k + 1]}",
+                     float(np.median(np.median(d[:, :, k], axis=1)) / 1e3),
+                     float(np.median(np.max(d[:, :, k], axis=1)) / 1e3)))
+    inner = np.diff(tr[:, :, [10, 12, 13, 11]], axis=2)
+    for k, name in enumerate(["down: chain gather", "down: row-dots", "down: combine"]):
+        rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
+                     float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
+    inner = np.diff(tr[:, :, [3, 18, 4]], axis=2)
+    for k, name in enumerate(["routes: gather", "routes: top-K"]):
+        rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
+                     float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
+    out["phases_us"] = rows
+    rounds = tr[:, :, 14:17].astype(np.float64)
+    if L > 1:
+        rounds = rounds[1:]          # layer 0 reads the state directly
+    out["gather_rounds_mean"] = {n: round(float(rounds[:, :, k].mean()), 2)
+                                 for k, n in enumerate(["state", "router", "chains"])}
+    landed = tr[:, :, 17]
+    out["group_landed_early"] = [round(float(((landed >> g) & 1).mean()), 3) for g in range(4)]
+    if L > 1:
+        lay = (tr[1:, :, 0].min(axis=1) - tr[:-1, :, 0].min(axis=1)) / 1e3
+        out["layer_period_us"] = {"median": float(np.median(lay)), "min": float(lay.min()),
+                                  "max": float(lay.max())}
+    out["step_us"] = float((tr[-1, :, 11].max() - tr[0, :, 0].min()) / 1e3)
+    return out
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -323,7 +408,8 @@ def run_gpu(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     fp8 = args.fmt == "fp8"
-    model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, LAYERS, H, M, E, K)
+    layers = args.layers
+    model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K)
     model.synth(0)
     model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
@@ -362,6 +448,16 @@ def run_gpu(args, rank, world, local_rank):
         model.stack_host_inplace(hnp, 1)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
+    trace = None
+    if args.trace and not args.layered:
+        import numpy as np
+        G = torch.cuda.get_device_properties(local_rank).multi_processor_count
+        n = layers * G * N_STAMPS
+        model.trace(n)
+        model.stack_dev(state, 1, sp)
+        torch.cuda.synchronize()
+        trace = phase_table(model.trace_read(n).astype(np.int64).reshape(layers, G, N_STAMPS))
+        model.trace(0)
     fallbacks = model.stats()[1]
     if dist:
         t = torch.tensor([t_ms, e2e_s], device="cuda", dtype=torch.float64)
@@ -372,7 +468,7 @@ def run_gpu(args, rank, world, local_rank):
     if rank == 0:
         ms = t_ms / args.steps
         value = world * args.steps / (t_ms / 1e3)
-        bpt = bytes_per_token(fp8)
+        bpt = bytes_per_token(fp8) * layers // LAYERS
         peak, src = peaks()
         achieved = bpt / (ms / 1e3) / 1e9
         res = {
@@ -381,16 +477,12 @@ def run_gpu(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (e2m1 + e8m0/32)") + " weights, fp32 accumulate",
             "data": "synthetic (seeded, device-generated)",
-            "config": {"workload": ("config 2: 40-layer FP8 MoE decode, 1 token/step" if fp8 else
-                                    "config 3 (1 GPU, batch 1): 40-layer MXFP4 MoE decode, 1 token/step"),
-                       "hidden": H, "moe_inter": M, "experts": E, "topk": K,
-                       "layers": LAYERS, "pool_gb": round(LAYERS * E * (3146496 if fp8 else 1671168) / 1e9, 2),
-                       "l2": f"inputs larger than L2 ({bpt / 1e9:.2f} GB of weights per step)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "config": decode_config(fp8, world, layers),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": (TRAFFIC_PER_LAUNCH if fp8 and not args.layered else None),
-                         "traffic_unit": "bytes per launch (ncu, 4-layer capture x 10)",
+                         "traffic": (TRAFFIC_PER_LAUNCH * layers // LAYERS
+                                     if fp8 and not args.layered else None),
+                         "traffic_unit": f"bytes per launch (ncu of the 4-layer case x 10; {KERNEL_REV})",
                          "peak_source": src,
                          "kernel": ("whole decode step: 4 kernels per layer in a CUDA graph" if args.layered
                                     else "k_decode: the whole 40-layer step in one persistent launch"),
@@ -398,10 +490,14 @@ def run_gpu(args, rank, world, local_rank):
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4,
                     "timer": "host clock around the synchronous C-ABI call"},
-            "gpu_launches": (4 * LAYERS if args.layered else 1) * args.steps,
+            "gpu_launches": (4 * layers if args.layered else 1) * args.steps,
             "router_exact_fallbacks": int(fallbacks),
             "clocks": clocks,
         }
+        if trace is not None:
+            for name, med, mx in trace.pop("phases_us"):
+                print(f"  {name:<24s} {med:8.2f} {mx:8.2f}   (us: median, max over CTAs)", file=sys.stderr)
+            res["trace"] = trace
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -436,7 +532,6 @@ def zipf_routing(n_layers, T, E, K, seed):
 def run_gpu_prefill(args, rank, world, local_rank):
     import numpy as np
     import torch
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -446,11 +541,12 @@ def run_gpu_prefill(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    T = T_PREFILL
+    T = args.tokens
+    NL = args.layers
     fp8 = args.fmt != "mxfp4"
-    model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, LAYERS, H, M, E, K)
+    model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, NL, H, M, E, K)
     model.synth(0)
-    sel, w = zipf_routing(LAYERS, T, E, K, seed=100 + rank)
+    sel, w = zipf_routing(NL, T, E, K, seed=100 + rank)
     selg = torch.from_numpy(sel).cuda()
     wg = torch.from_numpy(w).cuda()
     x0 = torch.empty((T, H), dtype=torch.float32, device="cuda")
@@ -502,12 +598,12 @@ def run_gpu_prefill(args, rank, world, local_rank):
         ms = t_ms / args.steps
         # algorithmic work: the weights of every expert a layer's tokens touch
         # (read once), the shared expert and norm, plus FLOPs 2 * rows * K * R
-        uniq = [len(np.unique(sel[L])) for L in range(LAYERS)]
+        uniq = [len(np.unique(sel[L])) for L in range(NL)]
         # algorithmic bytes: every touched expert once in the pool's own format
         # (the MXFP4 path streams its exact FP8 copy: 2x these bytes)
         slot = 3 * (M * H + (M // 128) * (H // 128) * 4) if fp8 else 3 * (M * H // 2 + M * H // 32)
         bytes_step = sum(u * slot + 3 * M * H * 2 + 2 * H * 2 for u in uniq)
-        flops_step = LAYERS * (2 * T * K * 3 * M * H + 2 * T * 3 * M * H)
+        flops_step = NL * (2 * T * K * 3 * M * H + 2 * T * 3 * M * H)
         peak, src = peaks()
         bw = bytes_step / (ms / 1e3) / 1e9
         tf = flops_step / (ms / 1e3) / 1e12
@@ -520,8 +616,10 @@ def run_gpu_prefill(args, rank, world, local_rank):
             "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (as its exact fp8 copy)") +
                      " weights x 3-digit e4m3 activations, fp32 accumulate (tcgen05)",
             "data": "synthetic (seeded weights, bf16 N(0,1) activations, Zipf(1.1) routing)",
-            "config": {"workload": f"config 4: prefill of a 2048-token chunk, 40-layer {'FP8' if fp8 else 'MXFP4'}",
-                       "tokens": T, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
+            "config": {"workload": (f"config 4: prefill of a 2048-token chunk, 40-layer {'FP8' if fp8 else 'MXFP4'}"
+                                    if (NL, T) == (LAYERS, T_PREFILL) else
+                                    f"profiling case: {T}-token chunk, {NL}-layer {'FP8' if fp8 else 'MXFP4'}"),
+                       "tokens": T, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": NL,
                        "max_tokens_per_expert_L0": int(loads.max()),
                        "median_tokens_per_expert_L0": float(np.median(loads)),
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
@@ -535,7 +633,7 @@ def run_gpu_prefill(args, rank, world, local_rank):
             "e2e": {"value": round(world * T * args.steps / e2e_s, 1), "unit": "tok/s",
                     "h2d_bytes_per_step": T * H * 4 + sel.nbytes + w.nbytes,
                     "d2h_bytes_per_step": T * H * 4, "timer": "host clock, synchronous steps"},
-            "gpu_launches": args.steps * LAYERS * PREFILL_LAUNCHES_PER_LAYER,
+            "gpu_launches": args.steps * NL * PREFILL_LAUNCHES_PER_LAYER,
             "clocks": clocks,
         }
     if dist:
@@ -550,7 +648,6 @@ def run_gpu_ep(args, rank, world, local_rank):
     import importlib.util
     import torch
     import torch.distributed as dist
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -657,7 +754,6 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
     import numpy as np
     import torch
     import torch.distributed as dist
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -763,7 +859,6 @@ def run_gpu_matvec(args, rank, world, local_rank):
     import numpy as np
     import torch
     from oracle import pyoracle as po
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -852,7 +947,6 @@ def run_gpu_stream(args, rank, world, local_rank):
     in the same run."""
     import numpy as np
     import torch
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -956,7 +1050,7 @@ def run_gpu_stream(args, rank, world, local_rank):
 
 
 # DRAM bytes (read + write) of one k_head_bf16 launch over the 248,320-row head:
-# the ncu capture of a 62,080-row head (profiles/k_head_bf16_quarter_launch.md),
+# the ncu capture of a 62,080-row head (--workload head --head-rows 62080),
 # 254,331,904 + 2,894,848 bytes, times 4 (a launch reads its weights once)
 HEAD_TRAFFIC_PER_LAUNCH = 4 * (254_331_904 + 2_894_848)
 
@@ -968,7 +1062,6 @@ def run_gpu_head(args, rank, world, local_rank):
     (1.02 GB, larger than L2) + x + logits."""
     import numpy as np
     import torch
-    from tests._lib import ds4f_cuda
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
@@ -1012,8 +1105,7 @@ def run_gpu_head(args, rank, world, local_rank):
                    "l2": "inputs larger than L2 (1.02 GB of weights per step)", "parallelism": "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "traffic": round(HEAD_TRAFFIC_PER_LAUNCH * V / 248_320),
-                     "traffic_unit": "bytes per k_head_bf16 launch (ncu of a 62,080-row head scaled by rows, "
-                                     "profiles/k_head_bf16_quarter_launch.md)",
+                     "traffic_unit": "bytes per k_head_bf16 launch (ncu of a 62,080-row head scaled by rows)",
                      "kernel": "k_head_bf16 (one warp per row, 4 blocks per SM) + argmax",
                      "peak_source": src, "algorithmic_bytes_per_step": algo},
         "e2e": {"value": round(args.steps / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": Hh * 4,
@@ -1041,6 +1133,11 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="ep-decode: tokens per step")
     ap.add_argument("--head-rows", type=int, default=248_320,
                     help="head: vocabulary rows (default Qwen3.5's 248,320; smaller for profiling)")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decode / prefill: layers of the stack (fewer: a profiling case, not a bench line)")
+    ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per chunk")
+    ap.add_argument("--trace", action="store_true",
+                    help="decode: print k_decode's per-phase trace (stderr) and add it to the line")
     ap.add_argument("--slots", type=int, default=0,
                     help="stream-decode: HBM expert slots (default a quarter of the pool)")
     args = ap.parse_args()
@@ -1052,22 +1149,12 @@ def main():
             return
         n = max(1, args.steps)
         # built once; K samples sized so that warm-up and timing take ~2 minutes
-        per = max(0.25, min(20.0, 120.0 / (n + args.warmup / 4)))
-        sample, close = cpu_reference_sampler(threads=min(8, os.cpu_count() or 1))
-        for _ in range(args.warmup):
-            sample(per / 4)
-        vals = []
-        desc = None
-        for _ in range(n):
-            v, desc = sample(per)
-            vals.append(v)
-        close()
-        value = statistics.median(vals)
+        per = max(0.25, min(20.0, 120.0 / (n + 0.25)))
+        value, desc = cpu_reference_median(n, per, per / 4, threads=min(8, os.cpu_count() or 1))
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
             "n_gpus": 0, "steps": n, "warmup": args.warmup, "higher_is_better": True,
-            "config": {"workload": "config 2: 40-layer FP8 MoE decode, 1 token/step",
-                       "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS},
+            "config": decode_config(True, 1),
             "cpu_baseline": dict(desc, value=round(value, 4), unit="tok/s"),
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}))
@@ -1084,8 +1171,11 @@ def main():
         elif world == 1 and args.workload == "matvec":
             v, desc = cpu_matvec_sample(args.cpu_seconds)
             res["cpu_baseline"] = dict(desc, value=round(v, 4), unit="GB/s")
-        elif world == 1:
-            v, desc = cpu_reference_sample(args.cpu_seconds)
+        elif world == 1 and args.workload == "decode":
+            # the reference arm's procedure on a smaller budget: one warm-up
+            # sample, the median of five
+            per = max(0.2, args.cpu_seconds / 6)
+            v, desc = cpu_reference_median(5, per, per, threads=min(8, os.cpu_count() or 1))
             res["cpu_baseline"] = dict(desc, value=round(v, 4), unit="tok/s")
         print(json.dumps(res))
 

@@ -381,6 +381,7 @@ static int model_create_impl(const Ds4fGpuModelDesc *desc, int64_t pool_slots, D
     Model m;
     memset(&m, 0, sizeof m);
     m.d = d;
+    m.stall_cta = m.stall_t = -1;
     if (slot_layout(d.fmt, d.hidden, d.moe_inter, &m.slot)) return -1;
     trunk_layout(d.hidden, d.moe_inter, d.n_experts, &m.tr);
     DS4F_CUDA(cudaGetDevice(&m.device));
@@ -492,6 +493,7 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (m.stream) cudaStreamSynchronize(m.stream);
     if (m.graph) cudaGraphExecDestroy(m.graph);
     if (m.trace) cudaFree(m.trace);
+    if (m.log_base) cudaFree(m.log_base);
     if (m.pf_ws) cudaFree(m.pf_ws);
     if (m.pf8) cudaFree(m.pf8);
     if (m.pf_err_h) cudaFreeHost(m.pf_err_h);
@@ -779,10 +781,53 @@ int ds4f_gpu_model_trace(Ds4fGpuModel *h, int64_t n_stamps) {
     return 0;
 }
 
+int ds4f_gpu_model_route_log(Ds4fGpuModel *h, int n_layer_steps) {
+    DS4F_REQUIRE(h && n_layer_steps >= 0, "model_route_log: bad arguments");
+    Model &m = h->m;
+    DS4F_CUDA(cudaStreamSynchronize(m.stream));
+    if (m.log_base) { cudaFree(m.log_base); m.log_base = nullptr; }
+    m.log_idx = nullptr; m.log_w = m.log_state = nullptr; m.log_n = 0;
+    if (n_layer_steps == 0) return 0;
+    const size_t n = (size_t)n_layer_steps, K = m.d.topk, H = m.d.hidden;
+    const size_t b0 = al256(n * K * 4), b1 = al256(n * K * 4), b2 = al256(n * H * 4);
+    DS4F_CUDA(cudaMalloc(&m.log_base, b0 + b1 + b2));
+    DS4F_CUDA(cudaMemset(m.log_base, 0xFF, b0 + b1 + b2));      // -1 / NaN: not written
+    m.log_idx = (int *)m.log_base;
+    m.log_w = (float *)((char *)m.log_base + b0);
+    m.log_state = (float *)((char *)m.log_base + b0 + b1);
+    m.log_n = n_layer_steps;
+    return 0;
+}
+
+int ds4f_gpu_model_route_log_read(const Ds4fGpuModel *h, int *idx, float *w, float *states, int n_layer_steps) {
+    DS4F_REQUIRE(h && h->m.log_base && n_layer_steps >= 0 && n_layer_steps <= h->m.log_n,
+                 "model_route_log_read: bad arguments (log of %d layer-steps)", h ? h->m.log_n : 0);
+    const Model &m = h->m;
+    const size_t n = (size_t)n_layer_steps, K = m.d.topk, H = m.d.hidden;
+    DS4F_CUDA(cudaStreamSynchronize(m.stream));
+    if (idx) DS4F_CUDA(cudaMemcpy(idx, m.log_idx, n * K * 4, cudaMemcpyDeviceToHost));
+    if (w) DS4F_CUDA(cudaMemcpy(w, m.log_w, n * K * 4, cudaMemcpyDeviceToHost));
+    if (states) DS4F_CUDA(cudaMemcpy(states, m.log_state, n * H * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
 int ds4f_gpu_model_trace_read(const Ds4fGpuModel *h, uint64_t *out, int64_t n_stamps) {
     DS4F_REQUIRE(h && out && h->m.trace && n_stamps <= h->m.trace_n, "model_trace_read: bad arguments");
     DS4F_CUDA(cudaStreamSynchronize(h->m.stream));
     DS4F_CUDA(cudaMemcpy(out, h->m.trace, (size_t)n_stamps * 8, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *h, int64_t polls) {
+    DS4F_REQUIRE(h && polls >= 0, "model_set_wait_limit: bad arguments");
+    h->m.wait_limit = polls;
+    return 0;
+}
+
+int ds4f_gpu_model_inject_stall(Ds4fGpuModel *h, int cta, int layer_step) {
+    DS4F_REQUIRE(h && (cta < 0 || layer_step >= 0), "model_inject_stall: bad arguments");
+    h->m.stall_cta = cta < 0 ? -1 : cta;
+    h->m.stall_t = cta < 0 ? -1 : layer_step;
     return 0;
 }
 

@@ -129,6 +129,28 @@ __device__ __forceinline__ uint32_t tk_key(float s, int e) {
     return (k & 0xFFFFFF00u) | (uint32_t)(255 - e);
 }
 __device__ __forceinline__ int tk_expert(uint32_t key) { return 255 - (int)(key & 0xFFu); }
+// The reference's insertion top-k (ds4f_topk, src/moe.c:531-546), one
+// thread, on fp32 logits v[e] (held as float or double): a slot is passed
+// over while it is empty or the new logit is strictly greater. Used when a
+// logit is not finite: NaN never passes a filled slot and an all-NaN row
+// selects experts 0..K-1, exactly as the reference does; every sel[j] < K
+// then holds a valid expert whenever E >= K.
+template <typename V>
+__device__ void tk_insertion(const V *v, int E, int K, int *sel) {
+    float wk[64];
+    if (K > E) K = E;
+    for (int j = 0; j < K; j++) { sel[j] = -1; wk[j] = 0.0f; }
+    for (int e = 0; e < E; e++) {
+        const float s = (float)v[e];
+        int j = K - 1;
+        while (j >= 0 && (sel[j] < 0 || s > wk[j])) j--;
+        if (j < K - 1) {
+            for (int q = K - 2; q > j; q--) { sel[q + 1] = sel[q]; wk[q + 1] = wk[q]; }
+            sel[j + 1] = e;
+            wk[j + 1] = s;
+        }
+    }
+}
 // Bitonic sort of 8 keys, largest first.
 __device__ __forceinline__ void tk_sort8(uint32_t (&k8)[8]) {
 #pragma unroll

@@ -41,7 +41,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kGmin = 144;                 // shared memory is sized for G >= this
 constexpr int kGroupPairs = 8;             // gate/up pairs per copy group
 constexpr int kGroups = 4;
-constexpr long kSpin = 1L << 24;           // polls (with backoff) before giving up
+constexpr long kSpin = 1L << 24;           // default polls (with backoff) before giving up
 constexpr double kU = 5.9604644775390625e-08;
 constexpr int kTracePts = 20;
 
@@ -169,12 +169,20 @@ struct DecodeArgs {
     TrunkLayout tr;
     int n_layers, n_steps, E, renorm, exact_all;
     uint32_t epoch;             // 1..65535, distinct from the previous launch's
+    long spin;                  // polls of a copy barrier before giving up
+    long rounds;                // copy rounds of a tagged-word gather before giving up
+    int stall_cta, stall_t;     // test hook: this CTA withholds its state words
+                                // at this layer-step (-1: off)
     float *state;               // [H] in (read at layer 0) / out (last layer)
     uint64_t *st_ll;            // [H] tagged state words
     uint64_t *sb_ll;            // [E][4] tagged words: S, its interval's ends (fp32), 0
     uint64_t *ch_ll;            // [(K+1) M + 1] tagged chains, then the shared-gate logit
     unsigned *diag;             // [4]: layers, fallbacks, error code, failing CTA
     unsigned long long *trace;  // optional [T][G][kTracePts] %globaltimer stamps
+    int *log_idx;               // optional route log, layer-steps t < log_n:
+    float *log_w;               //   selections [t][K], weights [t][K],
+    float *log_state;           //   the layer's output state [t][H]
+    int log_n;
 };
 
 __device__ __forceinline__ bool aborted(const DecodeArgs &a) {
@@ -187,7 +195,7 @@ __device__ void give_up(const DecodeArgs &a, unsigned code) {
 __device__ bool mbar_wait(const DecodeArgs &a, uint64_t *b, uint32_t parity, unsigned code) {
     long it = 0;
     while (!mbar_test(b, parity)) {
-        if (++it > kSpin) { give_up(a, code); return false; }
+        if (++it > a.spin) { give_up(a, code); return false; }
         if (it > 16) __nanosleep(32);
     }
     return true;
@@ -226,7 +234,7 @@ __device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uin
         bool all = true;
         for (int i = tid; i < ncheck; i += kThreads) all = all && (uint32_t)(dst[i] >> 32) == tag;
         if (__syncthreads_and(all)) return true;
-        if ((it & 15) == 15 && __syncthreads_or(it > (1L << 20) || aborted(a))) {
+        if ((it & 15) == 15 && __syncthreads_or(it > a.rounds || aborted(a))) {
             if (tid == 0 && !aborted(a)) give_up(a, code);
             return false;
         }
@@ -540,6 +548,7 @@ k_decode(DecodeArgs a) {
             // starts from experts l + 32 i)
             static_assert(E <= 256, "expert index in the key's low byte");
             uint32_t k8[8];
+            bool fin = true;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 k8[i] = 0u;
@@ -548,9 +557,14 @@ k_decode(DecodeArgs a) {
                     const float sv = word_f(4 * e);
                     k8[i] = tk_key(sv, e);
                     tk[e] = (double)sv;
+                    fin = fin && isfinite(sv) && isfinite(word_f(4 * e + 1)) && isfinite(word_f(4 * e + 2));
                 }
             }
-            if (lane == 0) { ctl[3] = 1; ctl[1] = 0; }
+            // a logit that is not finite: no interval orders it; every
+            // expert's exact logit then goes through the reference's own
+            // insertion rule (tk_insertion) in the fallback below
+            const bool nonfin = !__all_sync(0xFFFFFFFFu, fin);
+            if (lane == 0) { ctl[3] = 1; ctl[1] = 0; ctl[2] = nonfin ? 1 : 0; }
             tk_sort8(k8);
             tk_warp_top8(k8);
             // lane r < 8: the r-th selection's interval
@@ -579,10 +593,10 @@ k_decode(DecodeArgs a) {
                 const int e = lane + 32 * i;
                 const float hi = word_f(4 * e + 2);
                 nmine += hi >= lo8;
-                candf[e] = a.exact_all || hi >= lmin;
+                candf[e] = a.exact_all || nonfin || hi >= lmin;
             }
             const int nreach = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
-            const bool cert = !a.exact_all && __all_sync(0xFFFFFFFFu, sep) && nreach == K;
+            const bool cert = !a.exact_all && !nonfin && __all_sync(0xFFFFFFFFu, sep) && nreach == K;
             if (cert && lane < K) sel[lane] = er;
             if (lane == 0) ctl[1] = cert ? 1 : 0;
             if (cert) {
@@ -615,12 +629,16 @@ k_decode(DecodeArgs a) {
                 tk[e] = (double)acc;
             }
             __syncthreads();
-            for (int e = tid; e < E; e += kThreads) {
-                if (!candf[e]) continue;
-                int r = 0;
-                const double ve = tk[e];
-                for (int f = 0; f < E; f++) r += candf[f] && (tk[f] > ve || (tk[f] == ve && f < e));
-                if (r < K) sel[r] = e;
+            if (ctl[2]) {
+                if (tid == 0) tk_insertion(tk, E, K, sel);
+            } else {
+                for (int e = tid; e < E; e += kThreads) {
+                    if (!candf[e]) continue;
+                    int r = 0;
+                    const double ve = tk[e];
+                    for (int f = 0; f < E; f++) r += candf[f] && (tk[f] > ve || (tk[f] == ve && f < e));
+                    if (r < K) sel[r] = e;
+                }
             }
             if (tid == 0 && !a.exact_all && c == 0) atomicAdd(a.diag + 1, 1u);
             __syncthreads();
@@ -689,6 +707,10 @@ k_decode(DecodeArgs a) {
             for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, wj, j));
             if (lane < K) wsel[lane] = (a.renorm && s > 0.0f) ? __fdiv_rn(wj, s) : wj;
             if (lane == 0 && c == 0) atomicAdd(a.diag, 1u);
+            if (a.log_idx && c == 0 && t < a.log_n && lane < K) {
+                a.log_idx[(int64_t)t * K + lane] = sel[lane];
+                a.log_w[(int64_t)t * K + lane] = wsel[lane];
+            }
         }
         DS4F_TRACE(7);
         // (H) gate/up: warp w -> pair w % 8 of every group, gate and up
@@ -889,9 +911,12 @@ k_decode(DecodeArgs a) {
                 for (int j = 0; j < K; j++) acc = __fadd_rn(acc, __fmul_rn(wsel[j], outs[j * L::RR + tid]));
                 acc = __fadd_rn(acc, __fmul_rn(red[0], outs[K * L::RR + tid]));
                 const float ns = __fadd_rn(srow[tid], acc);
-                st_tag(a.st_ll + r, tg, __float_as_uint(ns));
-                publish_flush();
+                if (c != a.stall_cta || t != a.stall_t) {
+                    st_tag(a.st_ll + r, tg, __float_as_uint(ns));
+                    publish_flush();
+                }
                 if (!more) __stcg(a.state + r, ns);
+                if (a.log_state && t < a.log_n) __stcg(a.log_state + (int64_t)t * H + r, ns);
             }
             __syncthreads();
         }
@@ -935,6 +960,10 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     a.sb_ll = m->w.sb_ll;
     a.ch_ll = m->w.ch_ll;
     a.diag = m->w.diag;
+    a.spin = m->wait_limit > 0 ? (long)m->wait_limit : kSpin;
+    a.rounds = std::max(16L, a.spin / 16);
+    a.stall_cta = m->stall_cta;
+    a.stall_t = m->stall_t;
     DS4F_CUDA(cudaMemsetAsync(m->w.diag + 2, 0, 2 * sizeof(unsigned), st));
     // tags carry 16 bits of layer-step: split long runs into launches
     const int per = std::max(1, 65000 / m->d.n_layers);
@@ -945,6 +974,10 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
         a.n_steps = ns;
         a.state = state;
         a.trace = nullptr;
+        a.log_n = m->log_n > 0 ? std::max(0, m->log_n - s0 * m->d.n_layers) : 0;
+        a.log_idx = a.log_n ? m->log_idx + (int64_t)s0 * m->d.n_layers * K : nullptr;
+        a.log_w = a.log_n ? m->log_w + (int64_t)s0 * m->d.n_layers * K : nullptr;
+        a.log_state = a.log_n ? m->log_state + (int64_t)s0 * m->d.n_layers * H : nullptr;
         if (m->trace && (int64_t)m->d.n_layers * ns * sms * kTracePts <= m->trace_n) a.trace = m->trace;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(sms);

@@ -75,6 +75,12 @@ struct Model {
     unsigned long long *trace;   // optional phase stamps of the persistent kernel
     int64_t trace_n;
     int epoch;                   // last persistent launch's tag epoch
+    int64_t wait_limit;          // persistent kernel: polls before a wait gives up (0: default)
+    int stall_cta, stall_t;      // test hook of the persistent kernel (-1: off)
+    int *log_idx;                // route log of the persistent kernel (log_n layer-steps
+    float *log_w, *log_state;    //   of the next launch): selections, weights, output state
+    int log_n;
+    void *log_base;
     void *pf_ws;                 // batched-prefill workspace (prefill.cu), grown on demand
     size_t pf_bytes;
     uint8_t *pf8;                // MXFP4 models: the pool's exact FP8 copy for the

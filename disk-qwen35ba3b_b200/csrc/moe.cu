@@ -151,23 +151,29 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
     int *rk = cand + E;
     float *xs = (float *)(rk + E);
     __shared__ double lk_s, red[8];
-    __shared__ int ncand_s, cert_s, fast_s, sel_s[64];
+    __shared__ int ncand_s, cert_s, fast_s, nonfin_s, sel_s[64];
     const int tid = threadIdx.x;
+    if (tid == 0) { ncand_s = 0; cert_s = 1; fast_s = 0; nonfin_s = 0; }
+    __syncthreads();
     for (int e = tid; e < E; e += blockDim.x) {
         double b = exact_all ? 0.0 : Bnd[e];
         lo[e] = S[e] - b;
         hi[e] = S[e] + b;
         v[e] = (float)S[e];
+        if (!isfinite(S[e]) || !isfinite(b)) nonfin_s = 1;
     }
-    if (tid == 0) { ncand_s = 0; cert_s = 1; fast_s = 0; }
     __syncthreads();
+    // a logit that is not finite (NaN or inf state): no interval orders it,
+    // so every expert's exact logit goes through the reference's own
+    // insertion rule below
+    const bool nonfin = nonfin_s != 0;
     // Fast path (top-8 of at most 256): warp 0 proposes the 8 by a sorting
     // network on 32-bit keys of the logits and certifies them on the
     // intervals rounded outward to fp32 (consecutive selections separate,
     // and only the 8 reach the last one's lower bound); the general path
     // below runs only when that fails. Both select by the same rule, so a
     // certified proposal is the general path's selection.
-    if (K == 8 && E % 32 == 0 && E <= 256 && !exact_all) {
+    if (K == 8 && E % 32 == 0 && E <= 256 && !exact_all && !nonfin) {
         if (tid < 32) {
             const int lane = tid, NE = E / 32;
             uint32_t k8[8];
@@ -197,7 +203,7 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
         }
         __syncthreads();
     }
-    if (!exact_all && !fast_s) {
+    if (!exact_all && !fast_s && !nonfin) {
         // K-th largest lower bound
         for (int e = tid; e < E; e += blockDim.x) {
             int r = 0;
@@ -231,22 +237,26 @@ k_topk(const double *__restrict__ S, const double *__restrict__ Bnd,
             __syncthreads();
         }
     }
-    if (!fast_s && (exact_all || !cert_s)) {
+    if (nonfin || (!fast_s && (exact_all || !cert_s))) {
         // exact reference-order logits for every candidate (all experts in
-        // exact mode), then select on them
+        // exact mode or with a non-finite logit), then select on them
         for (int i = tid; i < H; i += blockDim.x) xs[i] = xin[i];
         __syncthreads();
         for (int e = tid; e < E; e += blockDim.x) {
-            if (exact_all) cand[e] = 1;
+            if (exact_all || nonfin) cand[e] = 1;
             if (cand[e]) v[e] = exact_logit(router + (int64_t)e * H, xs, H);
         }
         __syncthreads();
-        for (int e = tid; e < E; e += blockDim.x) {
-            if (!cand[e]) continue;
-            int r = 0;
-            for (int f = 0; f < E; f++)
-                r += cand[f] && (v[f] > v[e] || (v[f] == v[e] && f < e));
-            if (r < K) sel_s[r] = e;
+        if (nonfin) {
+            if (tid == 0) tk_insertion(v, E, K, sel_s);
+        } else {
+            for (int e = tid; e < E; e += blockDim.x) {
+                if (!cand[e]) continue;
+                int r = 0;
+                for (int f = 0; f < E; f++)
+                    r += cand[f] && (v[f] > v[e] || (v[f] == v[e] && f < e));
+                if (r < K) sel_s[r] = e;
+            }
         }
         if (tid == 0 && !exact_all) atomicAdd(diag + 1, 1u);
         __syncthreads();
@@ -793,15 +803,21 @@ extern "C" int ds4f_gpu_moe_layer_static(const Ds4fLayerDev *ld, float *state, i
     wk.acc = (float *)take(kStaticMaxH * 4);
     wk.diag = (unsigned *)take(16);
 
-    // the bf16 trunk tensors as element offsets from the norm pointer
+    // the bf16 trunk tensors as element offsets from the norm pointer: the
+    // caller's buffers may be separate allocations, so the distance is taken
+    // between addresses (CUDA's unified virtual address space), not by
+    // subtracting pointers into different objects
     const uint16_t *tb = ld->norm;
+    auto elems_from_norm = [&](const uint16_t *p) {
+        return (int64_t)((intptr_t)(uintptr_t)p - (intptr_t)(uintptr_t)tb) / (int64_t)sizeof(uint16_t);
+    };
     TrunkLayout tr;
     tr.norm = 0;
-    tr.router = ld->router - tb;
-    tr.sh_gate = ld->sh_gate - tb;
-    tr.sh_up = ld->sh_up - tb;
-    tr.sh_down = ld->sh_down - tb;
-    tr.sh_gw = ld->sh_gw - tb;
+    tr.router = elems_from_norm(ld->router);
+    tr.sh_gate = elems_from_norm(ld->sh_gate);
+    tr.sh_up = elems_from_norm(ld->sh_up);
+    tr.sh_down = elems_from_norm(ld->sh_down);
+    tr.sh_gw = elems_from_norm(ld->sh_gw);
     tr.n = 0;
     cudaStream_t st = (cudaStream_t)stream;
 

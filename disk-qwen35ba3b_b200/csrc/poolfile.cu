@@ -249,6 +249,7 @@ const char *kRoleName[3] = {"gate_proj", "up_proj", "down_proj"};
 int pool_plan(const char *json_path, int fmt, int H, int M, int L, int E, std::vector<int64_t> &off,
               int64_t *nbytes) {
     SlotLayout sl;
+    DS4F_REQUIRE(L > 0 && E > 0, "pool layout: %d layers x %d experts", L, E);
     if (slot_layout(fmt, H, M, &sl)) return -1;
     const int64_t vb = sl.rel_s[0] - sl.rel_v[0], sb = sl.rel_v[1] - sl.rel_s[0];
     FILE *f = fopen(json_path, "rb");
@@ -271,7 +272,9 @@ int pool_plan(const char *json_path, int fmt, int H, int M, int L, int E, std::v
                      get_int(root, "expert_nbytes", &nb) && ts && ts->kind == JVal::kArr,
                  "pool layout: %s missing keys (n_layers, n_experts, expert_nbytes, tensors)", json_path);
     DS4F_REQUIRE(nl == L && ne == E, "pool layout: %lldx%lld vs model %dx%d", (long long)nl, (long long)ne, L, E);
-    DS4F_REQUIRE(nb > 0, "pool layout: expert_nbytes %lld", (long long)nb);
+    // every slot offset 24 + (L E) nb below must stay inside int64
+    DS4F_REQUIRE(nb > 0 && nb <= (INT64_MAX - 24) / ((int64_t)L * E), "pool layout: expert_nbytes %lld",
+                 (long long)nb);
     if (const JVal *fm = root.get("format")) {
         const char *want = fmt == DS4F_FMT_FP8 ? "fp8-pool-v1" : "mxfp4-pool-v1";
         DS4F_REQUIRE(fm->kind == JVal::kStr && fm->s == want, "pool layout: format \"%s\", this model reads \"%s\"",
@@ -322,6 +325,8 @@ int pool_plan(const char *json_path, int fmt, int H, int M, int L, int E, std::v
                      "has %lld + %lld",
                      (long long)l, (long long)x, kRoleName[role], (long long)vn, (long long)sn, (long long)vb,
                      (long long)sb);
+        DS4F_REQUIRE(vo >= 0 && so >= 0, "pool layout: tensor L%lld E%lld at a negative offset", (long long)l,
+                     (long long)x);
         const int64_t slot_off = 24 + (int64_t)ex * nb;
         const int64_t rv = vo - slot_off, rs = so - slot_off;
         DS4F_REQUIRE(rv >= 0 && rs >= 0 && rv + vn <= nb && rs + sn <= nb,

@@ -38,7 +38,10 @@ struct SlotCache {
     int nslot = 0;
     std::vector<uint64_t> key, used_at;
     std::vector<uint8_t> pinned;
-    std::unordered_map<uint64_t, int> where;     // live key -> slot
+    // live key -> the slots holding it (more than one only when a request
+    // of the unguarded policy names an expert twice); a lookup answers the
+    // lowest, as the reference's linear scan does
+    std::unordered_map<uint64_t, std::set<int>> where;
     std::vector<uint8_t> held;                   // guard: this request's hits
     // The victim order kept sorted instead of scanned: free slots by index,
     // and the live slots that may be evicted (not pinned, not held) by their
@@ -75,15 +78,12 @@ struct SlotCache {
         if (evictable(s)) lru.erase({used_at[s], s});
         held[s] = 1;
     }
-    // A request that names one expert twice fills two slots with one key; a
-    // lookup answers the lowest such slot, as a linear scan would.
+    // Slot s stops holding its key: O(log n).
     void forget(int s) {
-        const uint64_t k = key[s];
-        auto it = where.find(k);
-        if (it == where.end() || it->second != s) return;
-        where.erase(it);
-        for (int i = 0; i < nslot; i++)
-            if (i != s && key[i] == k) { where[k] = i; break; }
+        auto it = where.find(key[s]);
+        if (it == where.end()) return;
+        it->second.erase(s);
+        if (it->second.empty()) where.erase(it);
     }
     // out_slot[j]: the slot of experts[j] (-1: dropped); fetch[] receives the
     // (slot, expert) pairs to copy in, in pool-offset order, already
@@ -96,9 +96,10 @@ struct SlotCache {
             const uint64_t k = expert_key(layer, experts[j]);
             auto it = where.find(k);
             if (it != where.end()) {
-                out_slot[j] = it->second;
+                const int hs = *it->second.begin();
+                out_slot[j] = hs;
                 nhit++;
-                if (guard) hold(it->second);
+                if (guard) hold(hs);
                 continue;
             }
             if (guard) {                         // named earlier in this request
@@ -128,8 +129,7 @@ struct SlotCache {
             key[f.first] = k;
             used_at[f.first] = ++clock;
             if (evictable(f.first)) lru.insert({used_at[f.first], f.first});
-            auto it = where.find(k);
-            if (it == where.end() || f.first < it->second) where[k] = f.first;
+            where[k].insert(f.first);
         }
         if (guard)
             for (int j = 0; j < n; j++) {
@@ -153,6 +153,11 @@ int stream_fetch(Model *m, int L, cudaStream_t st) {
     const int64_t sb = m->slot.nbytes;
     DS4F_CUDA(cudaMemcpyAsync(m->idx_h, m->w.idx, K * 4, cudaMemcpyDeviceToHost, st));
     DS4F_CUDA(cudaStreamSynchronize(st));
+    // the routing indexes the host pool: a value outside [0, E) (the top-K
+    // always writes valid experts; this guards the host read) stops here
+    for (int j = 0; j < K; j++)
+        DS4F_REQUIRE(m->idx_h[j] >= 0 && m->idx_h[j] < E, "stream: selection %d of layer %d is expert %d, "
+                     "outside [0, %d)", j, L, m->idx_h[j], E);
     std::vector<std::pair<int, int>> fetch;
     m->cache->getmany(L, m->idx_h, K, m->slot_h, fetch);
     for (int j = 0; j < K; j++)
@@ -198,6 +203,12 @@ void ds4f_slotcache_free(Ds4fSlotCache *c) { delete c; }
 
 int ds4f_slotcache_getmany(Ds4fSlotCache *c, int layer, const int *experts, int n, int *out_slot) {
     DS4F_REQUIRE(c && experts && out_slot && n >= 0, "slotcache_getmany: bad arguments");
+    // the policy knows no pool, so the upper bound of an expert index is the
+    // caller's to check against its own; a negative one (the reference's key
+    // would then collide with the empty slot's) is refused
+    for (int j = 0; j < n && j < ds4f::SlotCache::kMaxReq; j++)
+        DS4F_REQUIRE(experts[j] >= 0 && layer >= 0, "slotcache_getmany: negative layer %d or expert %d (entry %d)",
+                     layer, experts[j], j);
     std::vector<std::pair<int, int>> fetch;
     return c->c.getmany(layer, experts, n, out_slot, fetch);
 }

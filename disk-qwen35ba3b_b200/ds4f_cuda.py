@@ -79,6 +79,10 @@ def lib():
             "ds4f_gpu_model_set_path": [_vp, C.c_int],
             "ds4f_gpu_model_trace": [_vp, C.c_int64],
             "ds4f_gpu_model_trace_read": [_vp, _vp, C.c_int64],
+            "ds4f_gpu_model_set_wait_limit": [_vp, C.c_int64],
+            "ds4f_gpu_model_inject_stall": [_vp, C.c_int, C.c_int],
+            "ds4f_gpu_model_route_log": [_vp, C.c_int],
+            "ds4f_gpu_model_route_log_read": [_vp, _vp, _vp, _vp, C.c_int],
             "ds4f_gpu_synth_f32": [_vp, C.c_int64, C.c_uint64, C.c_uint32, C.c_uint32,
                                    C.c_uint32, C.c_uint32, C.c_double, _vp],
             "ds4f_gpu_quant_f8_digits": [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
@@ -393,6 +397,25 @@ class Model:
         out = np.zeros(n_stamps, np.uint64)
         check(lib().ds4f_gpu_model_trace_read(self.h, ptr(out), n_stamps))
         return out
+
+    def set_wait_limit(self, polls):
+        """Persistent kernel: polls before a bounded wait gives up (0: default)."""
+        check(lib().ds4f_gpu_model_set_wait_limit(self.h, polls))
+
+    def inject_stall(self, cta, layer_step):
+        """Test hook: CTA `cta` withholds its state words at `layer_step` (cta < 0: off)."""
+        check(lib().ds4f_gpu_model_inject_stall(self.h, cta, layer_step))
+
+    def route_log(self, n_layer_steps):
+        check(lib().ds4f_gpu_model_route_log(self.h, n_layer_steps))
+
+    def route_log_read(self, n_layer_steps):
+        """(idx [n][K], w [n][K], states [n][H]) of the last persistent call."""
+        idx = np.zeros((n_layer_steps, self.K), np.int32)
+        w = np.zeros((n_layer_steps, self.K), np.float32)
+        st = np.zeros((n_layer_steps, self.H), np.float32)
+        check(lib().ds4f_gpu_model_route_log_read(self.h, ptr(idx), ptr(w), ptr(st), n_layer_steps))
+        return idx, w, st
 
     def stats(self):
         out = (C.c_uint64 * 2)()

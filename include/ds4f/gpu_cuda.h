@@ -304,9 +304,37 @@ int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
  * n_stamps = 0 turns it off. */
 int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
 int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
+/* Route log of the persistent decode kernel: the counterpart of the
+ * reference's routing and state probes (src/main.c:1089-1094 prints each
+ * layer's selections and weights, :1095-1110 checksums the state). With
+ * n_layer_steps > 0 every later persistent call records, for its layer-steps
+ * t < n_layer_steps (t = step * n_layers + layer, counted from the call's
+ * first layer), the K selections, their weights and the layer's output
+ * state; entries not written read as -1 / NaN. 0 turns it off. */
+int  ds4f_gpu_model_route_log(Ds4fGpuModel *m, int n_layer_steps);
+/* idx [n][K], w [n][K], states [n][H] (host; any may be NULL). */
+int  ds4f_gpu_model_route_log_read(const Ds4fGpuModel *m, int *idx, float *w, float *states,
+                                   int n_layer_steps);
 /* Counters: [0] layers routed, [1] router exact-fallbacks taken. Also
  * reports (-1) a persistent-kernel wait that gave up. */
 int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
+/* Bounded waits of the persistent decode kernel (no reference counterpart:
+ * the reference's waits are pthread joins, src/moe.c:1185-1192, and its
+ * failures are exit codes, src/main.c:1-7). A wait on a weight copy gives up
+ * after `polls` polls, a gather of another CTA's words after polls / 16 copy
+ * rounds; the CTA then records an error code and its index, drains its own
+ * copies and returns, every other CTA follows, and the call reports -1
+ * ("decode kernel gave up waiting (code C at CTA N)"); the model stays
+ * usable. 0 restores the default, 2^24 polls (about a second). */
+int  ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *m, int64_t polls);
+/* Failure injection for tests (no reference counterpart): in the following
+ * persistent launches CTA `cta` does not publish its rows of the state at
+ * layer-step `layer_step` of a launch (0 = the first layer of its first
+ * step), as a CTA that stalled would not; the other CTAs' bounded waits for
+ * those rows run out and the call returns -1 with code 1 (the state gather).
+ * cta < 0 turns it off. Nothing faults: the missing words are never
+ * written, and every wait for them is bounded. */
+int  ds4f_gpu_model_inject_stall(Ds4fGpuModel *m, int cta, int layer_step);
 
 /* ---- allocation-free layer step ------------------------------------- */
 

@@ -146,6 +146,13 @@ def test_plan_refusals(tmp_path):
     _refused(tmp_path, m, "lacks")
     m = copy.deepcopy(meta); m["tensors"][0]["n"] = "layers.0.ffn.experts.0.w1.weight"
     _refused(tmp_path, m, "not a gate_proj")
+    # sizes whose slot offsets 24 + (L E) nb would leave int64, and a
+    # negative tensor offset: refused before any arithmetic on them
+    for nb in (2 ** 62, 2 ** 63 - 1, (2 ** 63 - 24) // 6 + 1):
+        m = copy.deepcopy(meta); m["expert_nbytes"] = nb
+        _refused(tmp_path, m, "expert_nbytes")
+    m = copy.deepcopy(meta); m["tensors"][3]["v_off"] = -(2 ** 63) + 5
+    _refused(tmp_path, m, "negative offset")
     _refused(tmp_path, None, "not parseable", text=json.dumps(meta)[:-40])
     _refused(tmp_path, None, "not parseable", text='{"n_layers": 01}')
     with pytest.raises(dc.GpuError, match="cannot read"):

@@ -264,6 +264,10 @@ def test_host_entry_points_reject_bad_arguments():
     assert L.ds4f_slotcache_getmany(h, 0, None, 2, out.ctypes.data) == -1
     assert L.ds4f_slotcache_getmany(h, 0, ex.ctypes.data, -1, out.ctypes.data) == -1
     assert "slotcache_getmany" in L.ds4f_gpu_last_error().decode()
+    neg = np.array([3, -1], np.int32)                  # the key of -1 would be the empty slot's
+    assert L.ds4f_slotcache_getmany(h, 0, neg.ctypes.data, 2, out.ctypes.data) == -1
+    assert "negative" in L.ds4f_gpu_last_error().decode()
+    assert L.ds4f_slotcache_getmany(h, -2, ex.ctypes.data, 2, out.ctypes.data) == -1
     assert L.ds4f_slotcache_pin(h, 99, 1) == 0 and L.ds4f_slotcache_pin(h, -1, 1) == 0
     assert L.ds4f_slotcache_getmany(h, 0, ex.ctypes.data, 2, out.ctypes.data) == 2
     assert L.ds4f_slotcache_stats(None, None, None, None, None) == -1
