@@ -18,9 +18,10 @@ roofline   algorithmic bytes per token / time per token vs the measured
 cpu_baseline  the reference's own kernels (oracle/_ref: ds4f_f8_matvec AVX2,
            ds4f_bf16_matvec, ds4f_topk; expert chains on 8 threads as
            ds4f_moe_step does) on a bounded sample of layer-tokens.
-N > 1      weak scaling: every rank holds the full pool and decodes its own
-           token stream; no collective on the data path (barrier and a max
-           reduction of the timings only).
+N > 1      the same 40-layer FP8 decode with the experts partitioned E / N
+           per GPU (config 3's partition; ds4f_gpu_ep_stack_dev: per layer
+           each GPU's partial chains and one NCCL all-reduce of acc);
+           strong scaling: one token per step, the same on every rank.
 """
 import argparse
 import ctypes as C
@@ -644,49 +645,55 @@ def run_gpu_prefill(args, rank, world, local_rank):
 
 # ---- config 3: expert-parallel decode ------------------------------------------
 
-def run_gpu_ep(args, rank, world, local_rank):
+def _ep_module():
     import importlib.util
+    spec = importlib.util.spec_from_file_location("ep", os.path.join(PKG, "ep.py"))
+    ep = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ep)
+    return ep
+
+
+def _init_group(world, local_rank):
+    """torch.distributed for the barriers, the timing max over ranks and the
+    communicator id; the data plane is the library's own NCCL."""
+    import datetime
     import torch
     import torch.distributed as dist
-    dc = ds4f_cuda()
-    torch.cuda.set_device(local_rank)
-    dc.init()
     if world > 1:
-        import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     else:
         import tempfile
         dist.init_process_group("gloo", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1)
-    spec = importlib.util.spec_from_file_location(
-        "ep", os.path.join(ROOT, "disk-qwen35ba3b_b200", "ep.py"))
-    ep = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(ep)
+    return dist
+
+
+def run_gpu_ep(args, rank, world, local_rank):
+    """Config 3 (and the N > 1 default): decode with E / N experts per GPU
+    through ds4f_gpu_ep_stack_dev. Strong scaling: every rank works on the
+    same B tokens, the experts (and their bytes) are partitioned."""
+    import torch
+    dc = ds4f_cuda()
+    torch.cuda.set_device(local_rank)
+    dc.init()
+    dist = _init_group(world, local_rank)
+    ep = _ep_module()
     fp8 = args.fmt == "fp8"
-    shard = ep.GpuShard(dc, dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, LAYERS, H, M, E, K, rank, world, seed=0)
-    dec = ep.ExpertParallelDecoder(shard)
+    layers = args.layers
+    shard = ep.GpuShard(dc, dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K, rank, world, seed=0)
+    shard.attach()
     Bt = args.batch
     st = torch.empty((Bt, H), dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(st, Bt * H, 0, 0, 4, 0, 2, 1.0)            # the same tokens on every rank
     sp = torch.cuda.current_stream().cuda_stream
-    # one GPU, a batch: the whole pool is here, so the batched stack (one
-    # captured graph per step) replaces the per-layer shard steps
-    stack = world == 1 and Bt > 1
-
-    def steps(n):
-        if stack:
-            shard.model.stack_batch_dev(st, n, sp)
-        else:
-            for _ in range(n):
-                dec.step(st, sp)
-    steps(args.warmup)
+    shard.decode(st, max(1, args.warmup), sp)
     torch.cuda.synchronize()
     dist.barrier()
     clk = Clocks(local_rank)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    steps(args.steps)
+    shard.decode(st, args.steps, sp)
     e1.record()
     torch.cuda.synchronize()
     t_ms = e0.elapsed_time(e1)
@@ -698,7 +705,7 @@ def run_gpu_ep(args, rank, world, local_rank):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         st.copy_(hst, non_blocking=True)
-        steps(1)
+        shard.decode(st, 1, sp)
         hst.copy_(st, non_blocking=True)
         torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
@@ -713,9 +720,10 @@ def run_gpu_ep(args, rank, world, local_rank):
         # experts a layer touches for B distinct tokens (expected value; K at
         # B = 1), each read once by the job, plus router and shared expert
         uniq = K if Bt == 1 else E * (1 - (1 - K / E) ** Bt)
-        bytes_step = int(LAYERS * (uniq * slot + E * H * 2 + 3 * M * H * 2 + 2 * H * 2))
+        bytes_step = int(layers * (uniq * slot + E * H * 2 + 3 * M * H * 2 + 2 * H * 2))
         peak, src = peaks()
         bw = bytes_step / (ms / 1e3) / 1e9
+        headline = world > 1 and args.workload == "decode"
         res = {
             "metric": METRIC_EP, "value": round(Bt * args.steps / (t_ms / 1e3), 2), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -724,11 +732,12 @@ def run_gpu_ep(args, rank, world, local_rank):
                      ("fp32 accumulate" if Bt == 1 else
                       "3-digit e4m3 activations, fp32 accumulate (tcgen05 grouped chain)"),
             "data": "synthetic (seeded, device-generated)",
-            "config": {"workload": f"config 3: 40-layer {'FP8' if fp8 else 'MXFP4'} decode, batch {Bt}, "
-                                   f"{E // world} experts per GPU",
-                       "batch": Bt, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
-                       "parallelism": (f"expert-parallel x{world} (all-reduce of acc per layer)" if world > 1 else
-                                       "single GPU" + (" (batched stack, one CUDA graph per step)" if stack else "")),
+            "config": {"workload": (f"config {'2' if fp8 else '3'} sharded: {layers}-layer {'FP8' if fp8 else 'MXFP4'} "
+                                    f"decode, batch {Bt}, {E // world} experts per GPU"),
+                       "batch": Bt, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": layers,
+                       "parallelism": (f"expert-parallel x{world}: per layer the partial chains of each GPU's "
+                                       f"experts, one NCCL all-reduce of acc [{Bt}][{H}] fp32, residual; "
+                                       f"one CUDA graph per step"),
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": peak * world, "unit": "GB/s",
                          "frac": round(bw / (peak * world), 4), "traffic": None, "peak_source": src,
@@ -737,50 +746,49 @@ def run_gpu_ep(args, rank, world, local_rank):
             "e2e": {"value": round(Bt * args.steps / e2e_s, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": Bt * H * 4, "d2h_bytes_per_step": Bt * H * 4,
                     "timer": "host clock, synchronous steps"},
-            # one token: route, top-K, gate/up, down; a batch: route, top-K
-            # and the grouped tensor-core layer
-            "gpu_launches": args.steps * LAYERS * (4 if Bt == 1 else 2 + PREFILL_LAUNCHES_PER_LAYER),
+            # per layer: route, top-K, gate/up, down (B = 1; a batch: route,
+            # top-K and the grouped tensor-core layer), the all-reduce, the add
+            "gpu_launches": args.steps * layers * ((4 if Bt == 1 else 2 + PREFILL_LAUNCHES_PER_LAYER) + 2),
             "clocks": clocks,
         }
+        if headline:
+            res["metric"] = METRIC
+            res["note"] = ("N > 1: the 40-layer FP8 decode of config 2 with its experts sharded over the GPUs "
+                           "(config 3's partition); 1 token per step, the same token on every rank")
     dist.barrier()
     dist.destroy_process_group()
     return res
 
 
-# ---- config 4 at N GPUs: expert-parallel prefill ----------------------------------
+# ---- config 4 at N GPUs: token-parallel prefill with all-to-all dispatch ----------
 
 def run_gpu_ep_prefill(args, rank, world, local_rank):
-    import importlib.util
+    """Config 4 at N GPUs: the 2048-token chunk partitioned T / N per rank,
+    E / N experts per rank, rows dispatched to the experts' ranks and
+    combined back (ds4f_gpu_ep_prefill). value = the chunk's tokens / time."""
     import numpy as np
     import torch
-    import torch.distributed as dist
     dc = ds4f_cuda()
     torch.cuda.set_device(local_rank)
     dc.init()
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-    else:
-        import tempfile
-        dist.init_process_group("gloo", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1)
-    spec = importlib.util.spec_from_file_location(
-        "ep", os.path.join(ROOT, "disk-qwen35ba3b_b200", "ep.py"))
-    ep = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(ep)
-    T = T_PREFILL
-    shard = ep.GpuShard(dc, dc.FMT_FP8, LAYERS, H, M, E, K, rank, world, seed=0)
-    pf = ep.ExpertParallelPrefill(shard)
-    sel, w = zipf_routing(LAYERS, T, E, K, seed=100)            # the same chunk on every rank
-    selg, wg = torch.from_numpy(sel).cuda(), torch.from_numpy(w).cuda()
+    dist = _init_group(world, local_rank)
+    ep = _ep_module()
+    T, NL = args.tokens, args.layers
+    fp8 = args.fmt != "mxfp4"
+    shard = ep.GpuShard(dc, dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, NL, H, M, E, K, rank, world, seed=0)
+    shard.attach()
+    sel, w = zipf_routing(NL, T, E, K, seed=100)            # the whole chunk's routing, sliced per rank
+    t0, t1 = rank * T // world, (rank + 1) * T // world
+    selg = torch.from_numpy(np.ascontiguousarray(sel[:, t0:t1])).cuda()
+    wg = torch.from_numpy(np.ascontiguousarray(w[:, t0:t1])).cuda()
     x0 = torch.empty((T, H), dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(x0, T * H, 0, 0, 4, 0, 1, 1.0)
-    x0 = x0.bfloat16().float()
+    x0 = x0.bfloat16().float()[t0:t1].contiguous()
     st = torch.empty_like(x0)
     sp = torch.cuda.current_stream().cuda_stream
     for _ in range(args.warmup):
         st.copy_(x0)
-        pf.step(st, selg, wg, sp)
+        shard.prefill(st, selg, wg, sp)
     torch.cuda.synchronize()
     dist.barrier()
     clk = Clocks(local_rank)
@@ -789,7 +797,7 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
     e0.record()
     for _ in range(args.steps):
         st.copy_(x0)
-        pf.step(st, selg, wg, sp)
+        shard.prefill(st, selg, wg, sp)
     e1.record()
     torch.cuda.synchronize()
     t_ms = e0.elapsed_time(e1)
@@ -798,13 +806,13 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
     hout = torch.empty_like(hx).pin_memory()
     dist.barrier()
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
+    ts = time.perf_counter()
     for _ in range(args.steps):
         st.copy_(hx, non_blocking=True)
-        pf.step(st, selg, wg, sp)
+        shard.prefill(st, selg, wg, sp)
         hout.copy_(st, non_blocking=True)
         torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
+    e2e_s = time.perf_counter() - ts
     tt = torch.tensor([t_ms, e2e_s], dtype=torch.float64, device="cuda" if world > 1 else "cpu")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     t_ms, e2e_s = float(tt[0]), float(tt[1])
@@ -812,24 +820,26 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
     res = None
     if rank == 0:
         ms = t_ms / args.steps
-        uniq = [len(np.unique(sel[L])) for L in range(LAYERS)]
-        slot = 3 * (M * H + (M // 128) * (H // 128) * 4)
+        uniq = [len(np.unique(sel[L])) for L in range(NL)]
+        slot = 3 * (M * H + (M // 128) * (H // 128) * 4) if fp8 else 3 * (M * H // 2 + M * H // 32)
         bytes_step = sum(u * slot + 3 * M * H * 2 + 2 * H * 2 for u in uniq)
-        flops_step = LAYERS * (2 * T * K * 3 * M * H + 2 * T * 3 * M * H)
+        flops_step = NL * (2 * T * K * 3 * M * H + 2 * T * 3 * M * H)
         peak, src = peaks()
         bw = bytes_step / (ms / 1e3) / 1e9
         tf = flops_step / (ms / 1e3) / 1e12
         res = {
-            "metric": METRIC_PREFILL.replace("1 B200 per rank", "experts sharded over the GPUs"),
+            "metric": METRIC_PREFILL.replace("1 B200 per rank", "tokens and experts partitioned over the GPUs"),
             "value": round(T * args.steps / (t_ms / 1e3), 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "fp8-e4m3 weights x 3-digit e4m3 activations, fp32 accumulate (tcgen05)",
+            "dtype": ("fp8-e4m3" if fp8 else "mxfp4 (as its exact fp8 copy)") +
+                     " weights x 3-digit e4m3 activations, fp32 accumulate (tcgen05)",
             "data": "synthetic (seeded weights, bf16 N(0,1) activations, Zipf(1.1) routing)",
-            "config": {"workload": f"config 4: prefill of a 2048-token chunk, 40-layer FP8, "
-                                   f"{E // world} experts per GPU",
-                       "tokens": T, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": LAYERS,
-                       "parallelism": f"expert-parallel x{world} (all-reduce of acc [T][H] per layer)",
+            "config": {"workload": f"config 4: prefill of a {T}-token chunk, {NL}-layer {'FP8' if fp8 else 'MXFP4'}, "
+                                   f"{T // world} tokens and {E // world} experts per GPU",
+                       "tokens": T, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": NL,
+                       "parallelism": f"expert-parallel x{world}: per layer an all-to-all dispatch of each token's "
+                                      f"row to its experts' GPUs and an all-to-all combine back (NCCL send/recv)",
                        "l2": "inputs larger than L2"},
             "roofline": {"bound": "hbm", "achieved": round(bw, 1), "peak": peak * world, "unit": "GB/s",
                          "frac": round(bw / (peak * world), 4), "traffic": None, "peak_source": src,
@@ -838,9 +848,9 @@ def run_gpu_ep_prefill(args, rank, world, local_rank):
                                     "peak_source": "nominal dense FP8 x N", "frac": round(tf / 4500.0 / world, 4),
                                     "flops_per_step": flops_step}},
             "e2e": {"value": round(T * args.steps / e2e_s, 1), "unit": "tok/s",
-                    "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
-                    "timer": "host clock, synchronous steps"},
-            "gpu_launches": args.steps * LAYERS * PREFILL_LAUNCHES_PER_LAYER,
+                    "h2d_bytes_per_step": (t1 - t0) * H * 4, "d2h_bytes_per_step": (t1 - t0) * H * 4,
+                    "timer": "host clock, synchronous steps (rank 0's share of the copies)"},
+            "gpu_launches": args.steps * NL * (2 * PREFILL_LAUNCHES_PER_LAYER + 3),
             "clocks": clocks,
         }
     dist.barrier()
@@ -1164,6 +1174,8 @@ def main():
     fn = {"prefill": run_gpu_prefill, "ep-decode": run_gpu_ep,
           "ep-prefill": run_gpu_ep_prefill, "matvec": run_gpu_matvec,
           "stream-decode": run_gpu_stream, "head": run_gpu_head}.get(args.workload, run_gpu)
+    if world > 1 and args.workload == "decode":
+        fn = run_gpu_ep            # N > 1: the expert-sharded design, not replicas
     res = fn(args, rank, world, local_rank)
     if rank == 0:
         if "unavailable" in res or args.workload in ("stream-decode", "head"):

@@ -491,6 +491,7 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     cudaGetDevice(&cur);
     cudaSetDevice(m.device);
     if (m.stream) cudaStreamSynchronize(m.stream);
+    ep_free(&m);
     if (m.graph) cudaGraphExecDestroy(m.graph);
     if (m.trace) cudaFree(m.trace);
     if (m.log_base) cudaFree(m.log_base);

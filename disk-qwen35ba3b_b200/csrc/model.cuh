@@ -99,6 +99,7 @@ struct Model {
     float *bgraph_state;         //   these states, batch and workspace
     int bgraph_B;
     void *bgraph_ws;
+    void *ep;                    // expert-parallel state (ep.cu), when attached
 };
 
 int slot_layout(int fmt, int H, int M, SlotLayout *s);
@@ -143,6 +144,19 @@ void slot_cache_stats(const SlotCache *c, int64_t *req, int64_t *hit, int64_t *d
 // shared expert (one rank of a partition).
 int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const float *w,
                   cudaStream_t st, bool first_layer, bool last_layer, float *acc_out, bool add_shared);
+
+// Batched decode of one layer (prefill.cu): the certified router and top-K
+// of B tokens, then the grouped tensor-core chain; acc_out / add_shared as
+// prefill_layer; async: errors reported by a later call.
+int decode_batch_layer(Model *m, int L, float *states, int B, int *idx, float *w, cudaStream_t st,
+                       bool first_layer, bool last_layer, float *acc_out, bool add_shared, bool async);
+// Size the batched-prefill workspace for T tokens now (it is otherwise grown
+// on demand), and report (synchronising st) a pipeline wait that gave up
+// since the last check.
+int prefill_pre_size(Model *m, int T);
+int prefill_check(Model *m, cudaStream_t st);
+// Expert parallelism (ep.cu): release the model's communicator and buffers.
+void ep_free(Model *m);
 
 // Enqueue `fn` on the model stream ordered after the caller's stream, and
 // make the caller's stream wait for it (timing on the caller's stream then

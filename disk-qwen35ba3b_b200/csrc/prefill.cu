@@ -109,7 +109,7 @@ __global__ void k_front(const float *st, const uint16_t *nw, int H, const int *s
     const int c = warp * 128 + 4 * lane;
     const int64_t off = (int64_t)t * H + c;
     if (threadIdx.x < K) {
-        const int i = t * K + threadIdx.x, e = sel[i] - first;
+        const int i = t * K + threadIdx.x, e = sel ? sel[i] - first : -1;
         rows[threadIdx.x] = (e >= 0 && e < count) ? pos[i] : -1;
     }
     const float4 v = *(const float4 *)(st + off);
@@ -207,7 +207,7 @@ __global__ void k_combine(float *states, float *acc_out, const float *O, const f
     const int t = blockIdx.x;
     if (threadIdx.x == 0) {
         int n = 0;
-        for (int j = 0; j < K; j++) {
+        for (int j = 0; j < K && sel; j++) {
             const int i = t * K + j, e = sel[i] - first;
             if (e < 0 || e >= count || w[i] == 0.0f) continue;
             prow[n] = pos[i];
@@ -345,8 +345,10 @@ int pf_workspace(Model *m, int T, PfWs *w) {
     const int E = m->d.n_experts;
     const int64_t R = (int64_t)T * K;
     const int tiles_max = (int)(R / kGemmBN) + count;
+    // the error word first: its place does not depend on T, so calls with
+    // different token counts share it
     const size_t sizes[] = {
-        al(count * 4), al(count * 4), al((size_t)tiles_max * 12), al(4), al(4), al(R * 4),
+        al(4), al(count * 4), al(count * 4), al((size_t)tiles_max * 12), al(4), al(4), al(R * 4),
         al((size_t)kND * R * H), al((size_t)R * (H / 128) * 4), al((size_t)R * 2 * M * 4),
         al((size_t)kND * R * M), al((size_t)R * (M / 128) * 4), al((size_t)R * H * 4),
         al((size_t)2 * T * H * 2), al((size_t)T * 2 * M * 4), al((size_t)2 * T * M * 2),
@@ -368,11 +370,12 @@ int pf_workspace(Model *m, int T, PfWs *w) {
     uint8_t *p = (uint8_t *)m->pf_ws;
     int k = 0;
     auto take = [&]() { uint8_t *r = p; p += sizes[k++]; return r; };
+    w->err = (unsigned *)take();
     w->cnt = (int *)take(); w->off = (int *)take(); w->tiles = (int *)take(); w->ntiles = (int *)take();
     w->nrows = (int *)take(); w->pos = (int *)take();
     w->Xg = take(); w->sxg = (float *)take(); w->GU = (float *)take(); w->Cq = take(); w->sc = (float *)take();
     w->O = (float *)take(); w->Xb = (uint16_t *)take(); w->GS = (float *)take(); w->Cb = (uint16_t *)take();
-    w->OS = (float *)take(); w->sg = (float *)take(); w->err = (unsigned *)take();
+    w->OS = (float *)take(); w->sg = (float *)take(); take();
     w->rxin = (float *)take(); w->rS = (double *)take(); w->rB = (double *)take(); w->ridx = (int *)take();
     w->rw = (float *)take();
     w->tiles_max = tiles_max;
@@ -425,19 +428,26 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     const uint16_t *tl = m->trunk + (int64_t)L * m->tr.n;
     const int64_t total_slots = (int64_t)m->d.n_layers * count;
 
-    // 1: grouping (it depends on the routing only)
-    DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));
+    // sel == nullptr: the shared expert alone (the expert-parallel prefill's
+    // own tokens; their routed selections run on the experts' ranks)
+    const bool routed = sel != nullptr;
+    DS4F_REQUIRE(routed || add_shared, "prefill: neither routed selections nor the shared expert");
     if (first_layer) DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
+    // 1: grouping (it depends on the routing only)
+    if (routed) {
+    DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));
     k_count<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.cnt);
     k_plan<<<1, ((count + 31) / 32) * 32, 0, st>>>(ws.cnt, count, L * count, ws.off, ws.tiles, ws.ntiles,
                                                    ws.nrows);
     DS4F_CUDA(cudaMemsetAsync(ws.cnt, 0, count * 4, st));       // now the per-expert fill counters
     k_place<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(sel, (int)R, first, count, ws.off, ws.cnt, ws.pos);
+    }
     // 2: RMSNorm, digits into the grouped rows, the shared expert's inputs
     k_front<<<T, 32 * (H / 128), 0, st>>>(states, tl + m->tr.norm, H, sel, K, first, count, ws.pos, ws.Xg, ws.sxg,
                                            R, add_shared ? ws.Xb : nullptr, (int64_t)T * H, tl + m->tr.sh_gw,
                                            ws.sg);
     // 3: gate, up, SiLU digits, down
+    if (routed) {
     {   // gate and up in one launch
         GemmArgs g{};
         g.sW = (const float *)(pool + sl.rel_s[0]);
@@ -461,6 +471,7 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
         g.R = H; g.C = M; g.tiles = ws.tiles; g.ntiles = ws.ntiles; g.err = ws.err;
         if (gemm_launch<kND, false>(pool + sl.rel_v[2], total_slots, sl.nbytes, ws.Cq, R, g, ws.tiles_max, st))
             return -1;
+    }
     }
     // 4: shared expert
     if (add_shared) {
@@ -487,6 +498,23 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
         DS4F_CUDA(cudaStreamSynchronize(st));
         DS4F_REQUIRE(h == 0, "prefill: a tensor-core pipeline wait gave up (code %u)", h);
     }
+    return 0;
+}
+
+int prefill_pre_size(Model *m, int T) {
+    PfWs ws;
+    return pf_workspace(m, T, &ws);
+}
+
+int prefill_check(Model *m, cudaStream_t st) {
+    DS4F_REQUIRE(m->pf_ws, "prefill: no workspace");
+    PfWs ws;
+    if (pf_workspace(m, 1, &ws)) return -1;          // the current layout, no regrowth
+    unsigned h = 0;
+    DS4F_CUDA(cudaMemcpyAsync(&h, ws.err, 4, cudaMemcpyDeviceToHost, st));
+    DS4F_CUDA(cudaStreamSynchronize(st));
+    if (h) DS4F_CUDA(cudaMemsetAsync(ws.err, 0, 4, st));
+    DS4F_REQUIRE(h == 0, "prefill: a tensor-core pipeline wait gave up (code %u)", h);
     return 0;
 }
 

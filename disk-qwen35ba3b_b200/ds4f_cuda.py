@@ -79,6 +79,13 @@ def lib():
             "ds4f_gpu_model_set_path": [_vp, C.c_int],
             "ds4f_gpu_model_trace": [_vp, C.c_int64],
             "ds4f_gpu_model_trace_read": [_vp, _vp, C.c_int64],
+            "ds4f_gpu_ep_unique_id": [_vp],
+            "ds4f_gpu_ep_attach": [_vp, _vp, C.c_int, C.c_int],
+            "ds4f_gpu_ep_detach": [_vp],
+            "ds4f_gpu_ep_abort": [_vp],
+            "ds4f_gpu_ep_stack_dev": [_vp, _vp, C.c_int, C.c_int, _vp],
+            "ds4f_gpu_ep_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
+            "ds4f_ep_plan_dispatch": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_model_set_wait_limit": [_vp, C.c_int64],
             "ds4f_gpu_model_inject_stall": [_vp, C.c_int, C.c_int],
             "ds4f_gpu_model_route_log": [_vp, C.c_int],
@@ -125,7 +132,7 @@ def header_symbols():
     import re
     txt = open(HEADER).read()
     txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    return sorted(set(re.findall(r"\b(ds4f_(?:gpu|slotcache|pool)_\w+)\s*\(", txt)))
+    return sorted(set(re.findall(r"\b(ds4f_(?:gpu|slotcache|pool|ep)_\w+)\s*\(", txt)))
 
 
 def check(rc):
@@ -417,6 +424,26 @@ class Model:
         check(lib().ds4f_gpu_model_route_log_read(self.h, ptr(idx), ptr(w), ptr(st), n_layer_steps))
         return idx, w, st
 
+    # ---- expert parallelism (the library's NCCL data plane) ----
+    def ep_attach(self, ep_id, rank, world):
+        """ep_id: the 128 bytes of ep_unique_id() made on rank 0."""
+        b = (C.c_uint8 * 128).from_buffer_copy(bytes(ep_id))
+        check(lib().ds4f_gpu_ep_attach(self.h, b, rank, world))
+
+    def ep_detach(self):
+        check(lib().ds4f_gpu_ep_detach(self.h))
+
+    def ep_stack_dev(self, states, n_steps, stream=None):
+        """states [B][H] (device), identical on every rank."""
+        B = states.shape[0] if states.dim() == 2 else 1
+        check(lib().ds4f_gpu_ep_stack_dev(self.h, ptr(states), B, n_steps, stream))
+
+    def ep_prefill_dev(self, states, sel, w, stream=None):
+        """This rank's states [T][H], routing sel / w [n_layers][T][K] (device)."""
+        T = states.shape[0]
+        check(lib().ds4f_gpu_ep_prefill(self.h, ptr(states) if T else None, T, ptr(sel) if T else None,
+                                        ptr(w) if T else None, stream))
+
     def stats(self):
         out = (C.c_uint64 * 2)()
         check(lib().ds4f_gpu_model_stats(self.h, out))
@@ -465,6 +492,25 @@ class Head:
 
 def argmax_dev(logits, out, stream=None):
     check(lib().ds4f_gpu_argmax_dev(ptr(logits), int(logits.numel()), ptr(out), stream))
+
+
+def ep_unique_id():
+    b = (C.c_uint8 * 128)()
+    check(lib().ds4f_gpu_ep_unique_id(b))
+    return bytes(b)
+
+
+def ep_plan_dispatch(sel, n_experts, world):
+    """Host-only dispatch plan of one layer: sel [T][K] global expert ids
+    -> (counts [world], send_rows [sum counts], tok_rows [T][world])."""
+    sel = np.ascontiguousarray(sel, np.int32)
+    T, K = sel.shape
+    counts = np.zeros(world, np.int32)
+    rows = np.zeros(max(1, T * world), np.int32)
+    tok = np.zeros((T, world), np.int32)
+    check(lib().ds4f_ep_plan_dispatch(ptr(sel) if T else None, T, K, n_experts, world, ptr(counts), ptr(rows),
+                                      ptr(tok)))
+    return counts, rows[:int(counts.sum())].copy(), tok
 
 
 def pool_layout_plan(json_path, fmt, hidden, moe_inter, n_layers, n_experts):

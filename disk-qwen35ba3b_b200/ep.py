@@ -1,30 +1,33 @@
-"""ep.py -- expert-parallel decode across the GPUs of one node.
+"""ep.py -- expert parallelism across the GPUs of one node.
 
 Rank r of N holds experts [r E/N, (r + 1) E/N) of every layer (the model's
-expert shard) and the whole bf16 trunk. One decode step of B tokens, per
-layer:
+expert shard) and the whole bf16 trunk. The reference runs on one host and
+has no counterpart; this is the partitioning the expert pool's layout
+invites (experts are independent slots, src/st.c:127-180).
 
-  1. ds4f_gpu_moe_layer_partial_dev (one token) or
-     ds4f_gpu_moe_layer_batch_partial_dev (B > 1: the grouped tensor-core
-     chain) on every rank: RMSNorm, router and certified top-K on the full
-     state (the same result on every rank, the state being identical),
-     gate/up/SiLU/down of the selections this rank holds, their part of the
-     selection-order combine; the shared expert on rank 0 only;
-  2. one all-reduce (sum) of acc [B][H] fp32 over the ranks (NCCL over
-     NVLink on GPUs);
-  3. state += acc on every rank (the residual, src/moe.c:1424).
+On GPUs the data plane is the library's (libds4f_cuda, NCCL inside it, no
+torch on it): `attach` moves the communicator id from rank 0 to the others
+over the caller's process group and every rank attaches its model; then
+`GpuShard.decode` (ds4f_gpu_ep_stack_dev) and `GpuShard.prefill`
+(ds4f_gpu_ep_prefill) run whole steps.
 
-The reference runs on one host and has no counterpart; this is the
-partitioning the expert pool's layout invites (experts are independent
-slots, src/st.c:127-180).
+The same two algorithms are written out below over torch.distributed with a
+pluggable per-rank backend, so that their host-side logic (the partition,
+the dispatch plan of ds4f_ep_plan_dispatch, the exchange and combine order)
+runs on CPU ranks (gloo) against the oracle:
 
-Batched prefill (ExpertParallelPrefill) follows the same pattern with
-the tensor-core grouped GEMMs of the selections each rank's experts
-received and one all-reduce of acc [T][H] per layer.
-
-The per-rank layer step is a backend: `GpuShard` wraps the library; tests
-drive the same drivers on CPU ranks (gloo) with an oracle backend.
+  ExpertParallelDecoder: per layer every rank routes the full state (the
+    same certified top-K everywhere), runs the selections its experts
+    received plus, on rank 0, the shared expert; one all-reduce of the
+    partial combine acc [B][H]; state += acc (src/moe.c:1424).
+  TokenParallelPrefill: the chunk's tokens partitioned over the ranks; per
+    layer each token's row (state, selections, weights) goes to every rank
+    owning one of its experts (all-to-all), each rank runs its experts on
+    the rows it received, the partial combines come back (all-to-all) and
+    the owner adds them in rank order, then its own tokens' shared expert
+    and the residual (grouping src/moe.c:1516-1530, combine :1614-1630).
 """
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -46,26 +49,32 @@ class GpuShard:
         self.model = dc.Model(fmt, n_layers, hidden, moe_inter, n_experts, topk,
                               expert_first=first, expert_count=count)
         self.model.synth(seed)
+        self.dc, self.rank, self.world = dc, rank, world
         self.n_layers, self.hidden = n_layers, hidden
 
-    def layer_partial(self, L, states, acc, add_shared, stream=None):
-        # one token: the per-token kernels (fp32 chains); a batch: the
-        # routing of every token at once and the grouped tensor-core chain,
-        # each expert's weights streamed once for all its tokens
-        if states.dim() == 2 and states.shape[0] > 1:
-            self.model.layer_batch_partial_dev(L, states, acc, add_shared, stream)
-        else:
-            self.model.layer_partial_dev(L, states, acc, add_shared, stream)
+    def attach(self, group=None):
+        """Every rank: the library's communicator, its id made on rank 0
+        and sent to the others over `group` (the only use of the caller's
+        process group)."""
+        box = [self.dc.ep_unique_id() if self.rank == 0 else None]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0, group=group)
+        self.model.ep_attach(box[0], self.rank, self.world)
 
-    def prefill_partial(self, L, states, sel, w, acc, add_shared, stream=None):
-        self.model.prefill_partial_dev(L, states, sel, w, acc, add_shared, stream)
+    def decode(self, states, n_steps, stream=None):
+        """n_steps decode steps of states [B][H] (device, the same on every rank)."""
+        self.model.ep_stack_dev(states, n_steps, stream)
+
+    def prefill(self, states, sel, w, stream=None):
+        """This rank's tokens: states [T][H], sel / w [n_layers][T][K] (device)."""
+        self.model.ep_prefill_dev(states, sel, w, stream)
 
     def close(self):
         self.model.close()
 
 
 class ExpertParallelDecoder:
-    """Decode steps of a token batch over an expert-sharded process group."""
+    """Decode steps of a token batch over an expert-sharded process group;
+    backend.layer_partial(L, states, acc, add_shared) fills acc [B][H]."""
 
     def __init__(self, backend, group=None):
         self.b = backend
@@ -75,8 +84,8 @@ class ExpertParallelDecoder:
         self.acc = None
 
     def step(self, states, stream=None):
-        """states [B][H] (this rank's device), updated in place; identical on
-        every rank before and after."""
+        """states [B][H], updated in place; identical on every rank before
+        and after."""
         if self.acc is None or self.acc.shape != states.shape:
             self.acc = torch.empty_like(states)
         for L in range(self.b.n_layers):
@@ -87,27 +96,53 @@ class ExpertParallelDecoder:
         return states
 
 
-class ExpertParallelPrefill:
-    """Batched prefill of a token chunk over an expert-sharded process
-    group: every rank holds the chunk's states and routing, runs the grouped
-    tensor-core GEMMs of the selections its experts received (the shared
-    expert on rank 0), and one all-reduce of acc [T][H] per layer completes
-    the combine before the residual."""
+class TokenParallelPrefill:
+    """Batched prefill with the tokens partitioned over an expert-sharded
+    process group (the algorithm of ds4f_gpu_ep_prefill). plan(sel, E, N)
+    is ds4f_ep_plan_dispatch; backend.rows_partial(L, states, sel, w) returns
+    each received row's partial combine over this rank's experts, and
+    backend.shared(L, states) each own token's shared-expert term."""
 
-    def __init__(self, backend, group=None):
-        self.b = backend
+    def __init__(self, backend, plan, n_experts, group=None):
+        self.b, self.plan, self.E = backend, plan, n_experts
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.acc = None
 
-    def step(self, states, sel, w, stream=None):
-        """states [T][H]; sel / w [n_layers][T][K] (global expert ids)."""
-        if self.acc is None or self.acc.shape != states.shape:
-            self.acc = torch.empty_like(states)
+    def _a2a(self, send, send_counts, recv_counts, width):
+        out = torch.empty((int(sum(recv_counts)), width), dtype=send.dtype)
+        if self.world == 1:
+            out.copy_(send)
+        else:
+            dist.all_to_all_single(out, send, output_split_sizes=[int(c) for c in recv_counts],
+                                   input_split_sizes=[int(c) for c in send_counts], group=self.group)
+        return out
+
+    def step(self, states, sel, w):
+        """states [T][H] (this rank's tokens, updated in place); sel / w
+        [n_layers][T][K]."""
+        T, H = states.shape
+        K = sel.shape[-1]
+        N = self.world
         for L in range(self.b.n_layers):
-            self.b.prefill_partial(L, states, sel[L], w[L], self.acc, self.rank == 0, stream)
-            if self.world > 1:
-                dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
-            states.add_(self.acc)
+            counts, rows, tok = self.plan(sel[L].numpy(), self.E, N)
+            send_counts = torch.from_numpy(counts.astype(np.int64))
+            recv_counts = torch.empty_like(send_counts)
+            if N > 1:
+                dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+            else:
+                recv_counts.copy_(send_counts)
+            rws = torch.from_numpy(rows.astype(np.int64))
+            send = torch.cat([states[rws], sel[L][rws].view(torch.float32), w[L][rws]], 1)
+            recv = self._a2a(send, counts, recv_counts.tolist(), H + 2 * K)
+            racc = self.b.rows_partial(L, recv[:, :H].contiguous(), recv[:, H:H + K].contiguous().view(torch.int32),
+                                       recv[:, H + K:].contiguous())
+            acc_sh = self.b.shared(L, states)
+            back = self._a2a(racc, recv_counts.tolist(), counts, H)
+            for t in range(T):
+                acc = torch.zeros(H, dtype=torch.float32)
+                for d in range(N):
+                    if tok[t, d] >= 0:
+                        acc = acc + back[int(tok[t, d])]
+                states[t] += acc + acc_sh[t]
         return states

@@ -443,6 +443,54 @@ int  ds4f_gpu_moe_layer_batch_partial_dev(Ds4fGpuModel *m, int layer, const floa
 int  ds4f_gpu_moe_stack_batch_dev(Ds4fGpuModel *m, float *states_dev, int B, int n_steps,
                                   void *stream);
 
+/* ---- expert parallelism across the GPUs of one node ------------------ */
+
+/* No reference counterpart (the reference runs on one host, its experts
+ * streamed from one disk): the pool's experts partitioned over N GPUs, one
+ * process (or host thread) and one model per GPU, NCCL over NVLink inside
+ * this library (loaded at the first call: libnccl.so.2). Rank r's model is
+ * created with expert_first = r E / N, expert_count = E / N and holds the
+ * whole trunk. The caller moves the 128-byte id from rank 0 to the other
+ * ranks (any channel), then every rank attaches. */
+#define DS4F_EP_ID_BYTES 128
+int  ds4f_gpu_ep_unique_id(uint8_t id[DS4F_EP_ID_BYTES]);
+/* Collective over the N ranks: builds the communicator on the model's
+ * device and connects every peer. */
+int  ds4f_gpu_ep_attach(Ds4fGpuModel *m, const uint8_t id[DS4F_EP_ID_BYTES], int rank, int world);
+int  ds4f_gpu_ep_detach(Ds4fGpuModel *m);
+/* A collective waits for every peer. If a peer is lost, another host
+ * thread calls this to abort the communicator: the waiting calls then
+ * return -1 and the model must be detached (no further expert-parallel
+ * calls). */
+int  ds4f_gpu_ep_abort(Ds4fGpuModel *m);
+/* n_steps decode steps of B (<= 64) tokens through every layer, the
+ * expert-parallel form of ds4f_gpu_moe_stack_dev (src/main.c:848-1138, MoE
+ * part): states [B][H] (device), the same on every rank before and after.
+ * Per layer: the router and certified top-K on every rank, this rank's
+ * selections (and on rank 0 the shared expert), one all-reduce of the
+ * partial combine acc [B][H], state += acc (src/moe.c:1224-1225, 1424).
+ * The first step of a (states, B) pair runs eagerly, the later ones replay
+ * one captured CUDA graph of a whole step. Enqueued on `stream`. */
+int  ds4f_gpu_ep_stack_dev(Ds4fGpuModel *m, float *states, int B, int n_steps, void *stream);
+/* Batched prefill of every layer with the chunk's tokens partitioned over
+ * the ranks (the expert-parallel ds4f_moe_step_batch, src/moe.c:1480-1707):
+ * this rank's T states [T][H] (device, in/out) and their routing sel / w
+ * [n_layers][T][K] (device; global expert ids). Per layer each token's row
+ * goes to every rank owning one of its selected experts (NCCL send/recv),
+ * each rank runs the grouped tensor-core step on the rows it received (its
+ * experts only), the partial combines come back to the owner, which adds
+ * them in rank order, its shared expert and the residual. T may differ
+ * between ranks, and be 0. Synchronous on `stream`. */
+int  ds4f_gpu_ep_prefill(Ds4fGpuModel *m, float *states, int T, const int *sel, const float *w,
+                         void *stream);
+/* The dispatch plan of one layer (host only): for T tokens' K selections
+ * (global ids, < 0 skipped) over `world` ranks of n_experts / world experts,
+ * counts[world] = tokens with a selection on each rank; send_rows = those
+ * tokens rank by rank, ascending (may be NULL); tok_rows [T][world] = each
+ * token's position in send_rows for each rank, or -1 (may be NULL). */
+int  ds4f_ep_plan_dispatch(const int *sel, int T, int K, int n_experts, int world, int *counts,
+                           int *send_rows, int *tok_rows);
+
 #ifdef __cplusplus
 }
 #endif

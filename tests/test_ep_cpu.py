@@ -102,37 +102,74 @@ def test_expert_parallel_decode_two_ranks_matches_single_host():
     assert err < TOL, err
 
 
-# ---- expert-parallel prefill ------------------------------------------------
+# ---- token-parallel prefill with all-to-all dispatch / combine ----------------
 
-T_PF = 6
+T_PF = 7                 # tokens per rank (rank 1 holds T_PF - 2: uneven on purpose)
 
 
-class OraclePrefillShard:
-    """Per-rank partial of the batched step, from the oracle's reference
-    batched step (orc_moe_batch_sel): the shard's selections (others -1),
-    minus the shared expert's part on ranks other than 0."""
+def _dc():
+    spec = importlib.util.spec_from_file_location("ds4f_cuda", os.path.join(ROOT, "disk-qwen35ba3b_b200",
+                                                                            "ds4f_cuda.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class OracleTokenShard:
+    """One rank of the token-parallel prefill from oracle pieces: each
+    received row's partial combine over this rank's experts (its own
+    RMSNorm, the chains in selection order), and the shared expert of the
+    rank's own tokens."""
 
     def __init__(self, layers, first, count):
         self.layers, self.first, self.count = layers, first, count
         self.n_layers, self.hidden = len(layers), H
 
-    def prefill_partial(self, L, states, sel, w, acc, add_shared, stream=None):
+    def _xin(self, lay, st):
+        xin = np.array(st, np.float32, copy=True)
+        po.lib().orc_rmsnorm(po.ptr(lay.norm), H, po.ptr(xin))
+        return xin
+
+    def rows_partial(self, L, states, sel, w):
         lay = self.layers[L]
-        st = states.numpy()
-        s = sel.numpy().copy()
-        s[(s < self.first) | (s >= self.first + self.count)] = -1
-        part = lay.moe_batch_sel(st, s, w.numpy()) - st
-        if not add_shared:
-            part = part - (lay.moe_batch_sel(st, np.full_like(s, -1), w.numpy()) - st)
-        acc.copy_(torch.from_numpy(part.astype(np.float32)))
+        out = np.zeros((states.shape[0], H), np.float32)
+        for i in range(states.shape[0]):
+            xin = self._xin(lay, states[i].numpy())
+            a = np.zeros(H, np.float32)
+            for j in range(K):
+                e = int(sel[i, j])
+                if not (self.first <= e < self.first + self.count):
+                    continue
+                o = np.zeros(H, np.float32)
+                po.lib().orc_expert_chain(lay.fmt, po.ptr(lay.experts[e]), po.C.byref(lay.lay), H, M,
+                                          po.ptr(xin), po.ptr(o))
+                a = (a + np.float32(w[i, j]) * o).astype(np.float32)
+            out[i] = a
+        return torch.from_numpy(out)
+
+    def shared(self, L, states):
+        lay = self.layers[L]
+        out = np.zeros((states.shape[0], H), np.float32)
+        lw = lay.w()
+        for t in range(states.shape[0]):
+            xin = self._xin(lay, states[t].numpy())
+            po.lib().orc_shared_add(po.C.byref(lw), H, M, po.ptr(xin), po.ptr(out[t]))
+        return torch.from_numpy(out)
 
 
-def _routing_pf():
-    rng = np.random.default_rng(5)
-    sel = np.stack([np.stack([rng.choice(E, K, replace=False) for _ in range(T_PF)]) for _ in range(NL)])
-    w = rng.random((NL, T_PF, K)).astype(np.float32)
+def _tokens_pf(rank):
+    T = T_PF if rank == 0 else T_PF - 2
+    x = po.fill_f32(T * H, po.key(4, 0, 4, rank, 0), 1.0).reshape(T, H).copy()
+    rng = np.random.default_rng(5 + rank)
+    # every token on rank 1's experts for layer 0 and on rank 0's for layer
+    # 1 of rank 1's tokens: some peers receive nothing from a rank
+    sel = np.stack([np.stack([rng.choice(E, K, replace=False) for _ in range(T)]) for _ in range(NL)])
+    if rank == 1:
+        sel[0] = np.stack([rng.choice(np.arange(E // 2, E), K, replace=False) for _ in range(T)])
+    sel[0, 0, 3] = -1                                    # a skipped selection
+    w = rng.random((NL, T, K)).astype(np.float32)
     w /= w.sum(-1, keepdims=True)
-    return sel.astype(np.int32), w.astype(np.float32)
+    return x, sel.astype(np.int32), w.astype(np.float32)
 
 
 def _rank_pf(rank, world, port, out):
@@ -140,17 +177,21 @@ def _rank_pf(rank, world, port, out):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     ep = _ep_module()
+    dc = _dc()
     first, count = ep.shard_of(rank, world, E)
-    pf = ep.ExpertParallelPrefill(OraclePrefillShard(_layers(), first, count))
-    st = torch.from_numpy(po.fill_f32(T_PF * H, po.key(4, 0, 4, 0, 0), 1.0).reshape(T_PF, H).copy())
-    sel, w = _routing_pf()
+    pf = ep.TokenParallelPrefill(OracleTokenShard(_layers(), first, count), dc.ep_plan_dispatch, E)
+    x, sel, w = _tokens_pf(rank)
+    st = torch.from_numpy(x)
     pf.step(st, torch.from_numpy(sel), torch.from_numpy(w))
     out[rank] = st.numpy().copy()
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_expert_parallel_prefill_two_ranks_matches_single_host():
+def test_token_parallel_prefill_two_ranks_matches_single_host():
+    """Each rank's tokens, after every layer of the all-to-all prefill, equal
+    the single-host reference batched step (orc_moe_batch_sel) on the same
+    tokens within fp32 reassociation of the combine."""
     import socket
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -161,12 +202,47 @@ def test_expert_parallel_prefill_two_ranks_matches_single_host():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(120)
+        p.join(180)
         assert p.exitcode == 0
-    assert np.array_equal(out[0], out[1])
-    want = po.fill_f32(T_PF * H, po.key(4, 0, 4, 0, 0), 1.0).reshape(T_PF, H).copy()
-    sel, w = _routing_pf()
-    for L, lay in enumerate(_layers()):
-        want = lay.moe_batch_sel(want, sel[L], w[L])
-    err = np.abs(out[0] - want).max() / np.abs(want).max()
-    assert err < TOL, err
+    for r in range(2):
+        x, sel, w = _tokens_pf(r)
+        want = x.copy()
+        for L, lay in enumerate(_layers()):
+            want = lay.moe_batch_sel(want, sel[L], w[L])
+        err = np.abs(out[r] - want).max() / np.abs(want - x).max()
+        assert err < TOL, (r, err)
+
+
+def test_dispatch_plan():
+    """ds4f_ep_plan_dispatch (host only) against a direct restatement:
+    random routing, skipped selections, a rank nobody selects, one token,
+    none, and the refusals."""
+    dc = _dc()
+    rng = np.random.default_rng(2)
+    for T, Kp, Ep, N in [(37, 8, 64, 4), (1, 8, 64, 8), (0, 8, 64, 2), (50, 4, 16, 16), (20, 8, 256, 1)]:
+        sel = np.array([rng.choice(Ep // 2 if N > 1 else Ep, Kp, replace=False) for _ in range(T)],
+                       np.int32).reshape(T, Kp)
+        if T:
+            sel[rng.random(sel.shape) < 0.1] = -1
+        counts, rows, tok = dc.ep_plan_dispatch(sel, Ep, N)
+        per = Ep // N
+        need = np.zeros((T, N), bool)
+        for t in range(T):
+            for e in sel[t]:
+                if e >= 0:
+                    need[t, e // per] = True
+        want_rows = [t for d in range(N) for t in range(T) if need[t, d]]
+        assert counts.tolist() == need.sum(0).tolist()
+        assert rows.tolist() == want_rows
+        for t in range(T):
+            for d in range(N):
+                i = tok[t, d]
+                assert (i >= 0) == need[t, d]
+                if i >= 0:
+                    assert rows[i] == t and sum(counts[:d]) <= i < sum(counts[:d + 1])
+        if N > 1:
+            assert counts[N - 1] == 0                     # the upper half of the experts is never selected
+    with pytest.raises(dc.GpuError, match="expert 64 of 64"):
+        dc.ep_plan_dispatch(np.full((2, 4), 64, np.int32), 64, 4)
+    with pytest.raises(dc.GpuError):
+        dc.ep_plan_dispatch(np.zeros((2, 4), np.int32), 64, 3)            # 64 experts over 3 ranks
