@@ -413,6 +413,8 @@ def run_gpu(args, rank, world, local_rank):
     model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K)
     model.synth(0)
     model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
+    if args.prefetch is not None:
+        model.set_prefetch(args.prefetch)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(state, H, 0, 0, 4, rank, 0, 1.0)
     torch.cuda.synchronize()
@@ -1146,6 +1148,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode / prefill: layers of the stack (fewer: a profiling case, not a bench line)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per chunk")
+    ap.add_argument("--prefetch", type=int, default=None,
+                    help="decode: next-layer experts the persistent kernel prefetches into L2 (default 12, 0 off)")
     ap.add_argument("--trace", action="store_true",
                     help="decode: print k_decode's per-phase trace (stderr) and add it to the line")
     ap.add_argument("--slots", type=int, default=0,
