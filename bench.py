@@ -413,8 +413,6 @@ def run_gpu(args, rank, world, local_rank):
     model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K)
     model.synth(0)
     model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
-    if args.prefetch is not None:
-        model.set_prefetch(args.prefetch)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(state, H, 0, 0, 4, rank, 0, 1.0)
     torch.cuda.synchronize()
@@ -876,6 +874,7 @@ def run_gpu_matvec(args, rank, world, local_rank):
     dc.init()
     NSET = 16                     # distinct copies, rotated: 16 x 38 MB, every launch misses L2
     keep, jobs = [], {"fp8": [[] for _ in range(NSET)], "mxfp4": [[] for _ in range(NSET)]}
+    host = []
     bytes_fmt = {"fp8": 0, "mxfp4": 0}
     for e in range(8):
         for t, (R, Cc) in enumerate(((M, H), (M, H), (H, M))):
@@ -896,6 +895,7 @@ def run_gpu_matvec(args, rank, world, local_rank):
                                                      R, Cc, 1, 1, dc.FMT_MXFP4, 0, 32, 0))
             bytes_fmt["fp8"] += W.nbytes + s.nbytes
             bytes_fmt["mxfp4"] += v.nbytes + sm.nbytes
+            host.append((W, s, R, Cc, x))
     sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     out = {}
     for fmt in ("fp8", "mxfp4"):
@@ -917,7 +917,17 @@ def run_gpu_matvec(args, rank, world, local_rank):
         ms = sum(a.elapsed_time(b) for a, b in ts) / args.steps
         out[fmt] = (ms, bytes_fmt[fmt] / (ms / 1e3) / 1e9, clocks)
         del plans
-    # e2e: host vectors in (24 x), outputs out, through the per-matvec C calls
+    # e2e: the 24 matvecs through the reference-facing host-buffer call
+    # ds4f_gpu_f8_matvec (ds4f_f8_matvec's arguments: weights, scales and x
+    # in host memory, y back), one call per matrix as the reference calls it
+    for W, s_, R, Cc, x in host[:3]:
+        dc.f8_matvec(W, dc.SCALE_F32, s_, R // 128, Cc // 128, x)
+    n_e2e = max(1, min(args.steps, 20))
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        for W, s_, R, Cc, x in host:
+            dc.f8_matvec(W, dc.SCALE_F32, s_, R // 128, Cc // 128, x)
+    e2e_s = (time.perf_counter() - t0) / n_e2e
     peak, src = peaks()
     ms8, gbs8, clocks = out["fp8"]
     msm, gbsm, _ = out["mxfp4"]
@@ -933,6 +943,11 @@ def run_gpu_matvec(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "achieved": round(gbs8, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs8 / peak, 4), "traffic": None, "peak_source": src,
                      "algorithmic_bytes_per_step": bytes_fmt["fp8"]},
+        "e2e": {"value": round(bytes_fmt["fp8"] / e2e_s / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": bytes_fmt["fp8"] + sum(x.nbytes for _, _, _, _, x in host),
+                "d2h_bytes_per_step": sum(R * 4 for _, _, R, _, _ in host),
+                "timer": "host clock around 24 synchronous ds4f_gpu_f8_matvec calls on host buffers "
+                         "(weights copied in every call)"},
         "gpu_launches": args.steps * 1,
         "clocks": clocks,
     }
@@ -1148,8 +1163,6 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode / prefill: layers of the stack (fewer: a profiling case, not a bench line)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per chunk")
-    ap.add_argument("--prefetch", type=int, default=None,
-                    help="decode: next-layer experts the persistent kernel prefetches into L2 (default 12, 0 off)")
     ap.add_argument("--trace", action="store_true",
                     help="decode: print k_decode's per-phase trace (stderr) and add it to the line")
     ap.add_argument("--slots", type=int, default=0,

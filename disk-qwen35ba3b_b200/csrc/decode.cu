@@ -30,8 +30,6 @@
 // (src/main.c:1014-1088), per layer of the decode loop (src/main.c:848).
 #include "model.cuh"
 
-#include <cuda_bf16.h>
-
 #include <algorithm>
 
 namespace ds4f {
@@ -70,11 +68,6 @@ __device__ __forceinline__ void bulk(void *dst, const void *src, uint32_t bytes,
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(sa(dst)), "l"(src), "r"(bytes), "r"(sa(b)) : "memory");
-}
-// L2 prefetch of a global range (16-byte aligned address and size), no
-// destination and no completion to wait for
-__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void fence_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -164,9 +157,7 @@ struct Smem {
     static constexpr int o_tk = o_red + 1024;                         // [E] doubles
     static constexpr int o_cand = o_tk + a16(E * 8);                  // [E] ints
     static constexpr int o_sel = o_cand + a16(E * 4);                 // sel[64], wsel[64], ctl[16]
-    // the normalised state x / r as bf16 (the router lookahead's input)
-    static constexpr int o_xn = a16(o_sel + 64 * 4 + 64 * 4 + 16 * 4);
-    static constexpr int bytes = o_xn + H * 2;
+    static constexpr int bytes = o_sel + 64 * 4 + 64 * 4 + 16 * 4;
 };
 
 struct DecodeArgs {
@@ -188,8 +179,6 @@ struct DecodeArgs {
     uint64_t *ch_ll;            // [(K+1) M + 1] tagged chains, then the shared-gate logit
     unsigned *diag;             // [4]: layers, fallbacks, error code, failing CTA
     unsigned long long *trace;  // optional [T][G][kTracePts] %globaltimer stamps
-    uint64_t *pr_ll;            // [E] tagged router-lookahead logits of the next layer
-    int predict;                // experts of the next layer prefetched into L2 (0: off)
     int *log_idx;               // optional route log, layer-steps t < log_n:
     float *log_w;               //   selections [t][K], weights [t][K],
     float *log_state;           //   the layer's output state [t][H]
@@ -262,7 +251,6 @@ k_decode(DecodeArgs a) {
     // 2..5: gate/up copy groups; 6: routed down rows; 7: tagged gathers
     uint64_t *bar = (uint64_t *)(sm + L::o_bar);
     float *xin = (float *)(sm + L::o_xin);
-    uint16_t *xn = (uint16_t *)(sm + L::o_xn);
     uint16_t *nw = (uint16_t *)(sm + L::o_nw);
     uint16_t *rt = (uint16_t *)(sm + L::o_rt);
     uint16_t *sd = (uint16_t *)(sm + L::o_sd);
@@ -294,7 +282,6 @@ k_decode(DecodeArgs a) {
 #define FLIP(i) (phb ^= 1u << (i))
 #define PEND(i, v) (pendb = (v) ? (pendb | (1u << (i))) : (pendb & ~(1u << (i))))
     bool ok = true;
-    bool rt_ready = false;      // bar 0 (next router rows + norm weights) consumed early
 
     if (tid == 0) {
         for (int i = 0; i < 9; i++) mbar_init(bar + i, 1);
@@ -440,17 +427,12 @@ k_decode(DecodeArgs a) {
                 rd[16] = s2;
             }
             // (B) norm weights arrive with the router rows (bar 0)
-            // (the router lookahead of the previous layer consumed bar 0 already)
-            bool okb = rt_ready || mbar_wait(a, bar + 0, PH(0), 2);
+            bool okb = mbar_wait(a, bar + 0, PH(0), 2);
             if (!__syncthreads_and(okb)) { ok = false; break; }
-            if (!rt_ready) { FLIP(0); PEND(0, false); }
-            rt_ready = false;
+            FLIP(0); PEND(0, false);
             float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(rd[16], (double)H)), 1e-6f));
-            for (int i = tid; i < H; i += kThreads) {
-                const float q = __fdiv_rn(xin[i], r);
-                xin[i] = __fmul_rn(q, bf16_to_f32(nw[i]));
-                xn[i] = __bfloat16_as_ushort(__float2bfloat16_rn(q));
-            }
+            for (int i = tid; i < H; i += kThreads)
+                xin[i] = __fmul_rn(__fdiv_rn(xin[i], r), bf16_to_f32(nw[i]));
             __syncthreads();
         }
         DS4F_TRACE(2);
@@ -556,95 +538,72 @@ k_decode(DecodeArgs a) {
             break;
         }
         DS4F_TRACE(18);        // every router word visible; the top-K follows
-        {
+        if (warp == 0) {
+            constexpr int NE = E / 32;
+            static_assert(K == 8 && NE <= 8, "the sorting network selects 8");
             // expert e's words 4e .. 4e+2: S, and its interval's ends (fp32)
             const uint64_t *sbw = (const uint64_t *)gu;
             auto word_f = [&](int w) { return __uint_as_float((uint32_t)sbw[w]); };
-            static_assert(E <= 256 && E % 8 == 0 && K == 8, "expert index in the key's low byte; 8 key groups");
-            // 1. thread e < E: expert e's key (the fp32 logit's order-preserving
-            //    bits, low byte 255 - e: the lower index wins exact ties), and
-            //    the largest key of each of 8 groups of E / 8 experts
-            constexpr int GS = E / 8;
-            uint32_t *gmax = (uint32_t *)(red + 224);          // 8 words, clear of rd[] and the shared sums
-            int *ncand = ctl + 4;
-            int *cl = candf;                                   // candidate list, before the candidate flags
-            uint32_t key = 0u;
+            // the first 8 by key in selection order, in every lane (lane l
+            // starts from experts l + 32 i)
+            static_assert(E <= 256, "expert index in the key's low byte");
+            uint32_t k8[8];
             bool fin = true;
-            if (tid < E) {
-                const float sv = word_f(4 * tid);
-                key = tk_key(sv, tid);
-                fin = isfinite(sv) && isfinite(word_f(4 * tid + 1)) && isfinite(word_f(4 * tid + 2));
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                k8[i] = 0u;
+                if (i < NE) {
+                    const int e = lane + 32 * i;
+                    const float sv = word_f(4 * e);
+                    k8[i] = tk_key(sv, e);
+                    tk[e] = (double)sv;
+                    fin = fin && isfinite(sv) && isfinite(word_f(4 * e + 1)) && isfinite(word_f(4 * e + 2));
+                }
             }
-            static_assert(GS <= 32, "a key group within one warp");
-            if (tid < E) {
-                const unsigned gm = GS == 32 ? 0xFFFFFFFFu : (((1u << GS) - 1u) << (lane & ~(GS - 1)));
-                const uint32_t mx = __reduce_max_sync(gm, key);
-                if ((lane & (GS - 1)) == 0) gmax[tid / GS] = mx;
-            }
-            if (tid == 0) { ctl[3] = 1; ctl[1] = 0; *ncand = 0; }
             // a logit that is not finite: no interval orders it; every
             // expert's exact logit then goes through the reference's own
             // insertion rule (tk_insertion) in the fallback below
-            const bool nonfin = __syncthreads_or(!fin);
-            // 2. the 8 group maxima are 8 distinct keys >= their minimum tau,
-            //    so an expert below tau ranks 8th or lower: only keys >= tau
-            //    are ranked, among themselves (a key above a candidate's is
-            //    itself a candidate)
-            uint32_t tau = 0xFFFFFFFFu;
+            const bool nonfin = !__all_sync(0xFFFFFFFFu, fin);
+            if (lane == 0) { ctl[3] = 1; ctl[1] = 0; ctl[2] = nonfin ? 1 : 0; }
+            tk_sort8(k8);
+            tk_warp_top8(k8);
+            // lane r < 8: the r-th selection's interval
+            int er = 0;
 #pragma unroll
-            for (int g = 0; g < 8; g++) tau = min(tau, gmax[g]);
-            if (tid < E && key >= tau) {
-                const int slot = atomicAdd(ncand, 1);
-                cl[slot] = tid;
+            for (int j = 0; j < 8; j++) if (j == lane) er = tk_expert(k8[j]);
+            float lor = 3.0e38f, hir = -3.0e38f;
+            if (lane < K) {
+                lor = word_f(4 * er + 1);
+                hir = word_f(4 * er + 2);
             }
-            __syncthreads();
-            const int nc = *ncand;
-            if (tid < nc) {
-                const int e = cl[tid];
-                const uint32_t ke = tk_key(word_f(4 * e), e);
-                int r = 0;
-                for (int i = 0; i < nc; i++) {
-                    const int f = cl[i];
-                    r += tk_key(word_f(4 * f), f) > ke;
-                }
-                if (r < K) sel[r] = e;
-            }
-            __syncthreads();
-            if (tid < E) tk[tid] = (double)word_f(4 * tid);      // the softmax's logits
-            // 3. certified when consecutive selections' intervals separate and
-            //    only the 8 selections reach the last one's lower bound (then
-            //    every reference-order logit ranks the same); otherwise the
-            //    exact fallback recomputes every expert whose interval reaches
-            //    the lowest lower bound among the 8 (a superset of the true 8)
-            float lo8 = 0.f, lmin = 0.f;
-            bool sep = true;
-            {
-                float lor = 3.0e38f, hir = -3.0e38f;
-                if (lane < K) {
-                    const int er = sel[lane];
-                    lor = word_f(4 * er + 1);
-                    hir = word_f(4 * er + 2);
-                }
-                const float hin = __shfl_down_sync(0xFFFFFFFFu, hir, 1);
-                sep = __all_sync(0xFFFFFFFFu, lane >= K - 1 || lor > hin);
-                lo8 = __shfl_sync(0xFFFFFFFFu, lor, K - 1);
-                lmin = lor;
+            // certified when consecutive selections' intervals separate and
+            // only the 8 selections reach the last one's lower bound (then
+            // every reference-order logit ranks the same); otherwise the
+            // exact fallback recomputes every expert whose interval reaches
+            // the lowest lower bound among the 8 (a superset of the true 8)
+            const float hin = __shfl_down_sync(0xFFFFFFFFu, hir, 1);
+            const bool sep = lane >= K - 1 || lor > hin;
+            const float lo8 = __shfl_sync(0xFFFFFFFFu, lor, K - 1);
+            float lmin = lor;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xFFFFFFFFu, lmin, o));
+            for (int o = 16; o > 0; o >>= 1) lmin = fminf(lmin, __shfl_xor_sync(0xFFFFFFFFu, lmin, o));
+            int nmine = 0;
+#pragma unroll
+            for (int i = 0; i < NE; i++) {
+                const int e = lane + 32 * i;
+                const float hi = word_f(4 * e + 2);
+                nmine += hi >= lo8;
+                candf[e] = a.exact_all || nonfin || hi >= lmin;
             }
-            bool reach = false;
-            if (tid < E) {
-                const float hi = word_f(4 * tid + 2);
-                reach = hi >= lo8;
-                candf[tid] = a.exact_all || nonfin || hi >= lmin;
-            }
-            const int nreach = __syncthreads_count(reach);
-            const bool cert = !a.exact_all && !nonfin && sep && nreach == K;
-            if (tid == 0) { ctl[1] = cert ? 1 : 0; ctl[2] = nonfin ? 1 : 0; }
-            if (cert && warp == 0) {
+            const int nreach = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
+            const bool cert = !a.exact_all && !nonfin && __all_sync(0xFFFFFFFFu, sep) && nreach == K;
+            if (cert && lane < K) sel[lane] = er;
+            if (lane == 0) ctl[1] = cert ? 1 : 0;
+            if (cert) {
                 // the routing is final: the gate/up copies start now (their
-                // buffers' last readers, the previous layer's gate/up and the
-                // look at the router words above, are done)
+                // buffers' last readers, the previous layer's gate/up and this
+                // warp's look at the router words, are done)
+                __syncwarp();
                 fence_async();
                 issue_group_lane(l, lane);
             }
@@ -824,41 +783,6 @@ k_decode(DecodeArgs a) {
             // may land past the gathers' region of the buffer
             if (tid == 0 && more) { fence_async(); prefetch_sh(ln); }
             PEND(8, more);
-            // router lookahead: the next layer's router rows of this CTA
-            // (landed with its norm weights on bar 0) on this layer's
-            // normalised state, x / r times the next norm weights -- plain
-            // fp32 dots, a prediction only (the routing itself is certified
-            // on the next layer's own state). Warp 0 publishes them with its
-            // chains (one flush).
-            if (a.predict && more) {
-                const bool okr = mbar_wait(a, bar + 0, PH(0), 2);
-                if (!__syncthreads_and(okr)) { ok = false; break; }
-                FLIP(0); PEND(0, false);
-                rt_ready = true;
-                if (warp == 0) {
-                    for (int rr = 0; rr < nrt; rr++) {
-                        const uint16_t *row = rt + rr * H;
-                        float acc = 0.f;
-                        for (int k = lane; k < H / 8; k += 32) {
-                            const uint4 w8 = lds16(row + 8 * k), x8 = lds16(xn + 8 * k), n8 = lds16(nw + 8 * k);
-                            const uint32_t ww[4] = {w8.x, w8.y, w8.z, w8.w};
-                            const uint32_t xx[4] = {x8.x, x8.y, x8.z, x8.w};
-                            const uint32_t nn[4] = {n8.x, n8.y, n8.z, n8.w};
-#pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                acc = fmaf(__uint_as_float(ww[u] << 16),
-                                           __uint_as_float(xx[u] << 16) * __uint_as_float(nn[u] << 16), acc);
-                                acc = fmaf(__uint_as_float(ww[u] & 0xFFFF0000u),
-                                           __uint_as_float(xx[u] & 0xFFFF0000u) * __uint_as_float(nn[u] & 0xFFFF0000u),
-                                           acc);
-                            }
-                        }
-                        acc = warp_sum(acc);
-                        if (lane == 0) st_tag(a.pr_ll + rt0 + rr, tg, __float_as_uint(acc));
-                    }
-                    if (lane == 0 && np == 0) publish_flush();
-                }
-            }
             if (tid < np) {
                 constexpr int HALF = kGroups * kGroupPairs * 2;
                 const int q = p0 + tid;
@@ -999,60 +923,6 @@ k_decode(DecodeArgs a) {
         DS4F_TRACE(11);        // (stamps 12, 13: inside the down phase, above)
         if (tid == 0 && more) { fence_async(); prefetch_sd(ln); }
         PEND(1, more);
-        // the lookahead's prefetch: every CTA's lookahead logits (one copy,
-        // no retry -- a word not yet visible skips this layer's prefetch),
-        // their top a.predict by rank (the threshold of the top-8 with 16
-        // groups), and this CTA's 1/G share of those experts' slots of the
-        // next layer issued as L2 prefetches: they stream while HBM is idle
-        // (the exchanges, the norm, the router) and the next layer's copies
-        // of correctly predicted experts then hit L2
-        if (a.predict && more) {
-            gather_issue(bar + 7, pendb, (uint64_t *)gu, a.pr_ll, E);
-            const bool okp = mbar_wait(a, bar + 7, (phb >> 7) & 1u, 10);
-            if (!__syncthreads_and(okp)) { ok = false; break; }
-            phb ^= 1u << 7;
-            pendb &= ~(1u << 7);
-            const uint64_t *pw = (const uint64_t *)gu;
-            if (__syncthreads_and(tid >= E || (uint32_t)(pw[tid] >> 32) == tg)) {
-                constexpr int PG = 16, GS2 = E / PG;
-                static_assert(E % PG == 0 && GS2 <= 32, "16 lookahead groups within warps");
-                uint32_t *gmax = (uint32_t *)(red + 224);      // 16 words
-                int *ncand = ctl + 4;
-                int *cl = candf;
-                const int P = min(a.predict, PG);
-                uint32_t key = 0u;
-                if (tid < E) {
-                    key = tk_key(__uint_as_float((uint32_t)pw[tid]), tid);
-                    const unsigned gm = GS2 == 32 ? 0xFFFFFFFFu : (((1u << GS2) - 1u) << (lane & ~(GS2 - 1)));
-                    const uint32_t mx = __reduce_max_sync(gm, key);
-                    if ((lane & (GS2 - 1)) == 0) gmax[tid / GS2] = mx;
-                }
-                if (tid == 0) *ncand = 0;
-                __syncthreads();
-                uint32_t tau = 0xFFFFFFFFu;
-#pragma unroll
-                for (int g = 0; g < PG; g++) tau = min(tau, gmax[g]);
-                if (tid < E && key >= tau) cl[atomicAdd(ncand, 1)] = tid;
-                __syncthreads();
-                const int nc = *ncand;
-                if (tid < nc) {
-                    const int e = cl[tid];
-                    const uint32_t ke = tk_key(__uint_as_float((uint32_t)pw[e]), e);
-                    int r = 0;
-                    for (int i = 0; i < nc; i++) {
-                        const int f = cl[i];
-                        r += tk_key(__uint_as_float((uint32_t)pw[f]), f) > ke;
-                    }
-                    if (r < P) {
-                        const int64_t S = a.slot_bytes;
-                        const int64_t o0 = ((int64_t)c * S / G) & ~(int64_t)15;
-                        const int64_t o1 = c == G - 1 ? S : (((int64_t)(c + 1) * S / G) & ~(int64_t)15);
-                        if (o1 > o0) prefetch_l2(expert(ln, e) + o0, (uint32_t)(o1 - o0));
-                    }
-                }
-                __syncthreads();
-            }
-        }
     }
     // drain this CTA's copies before exit (bounded)
     for (int i = 0; i < 9; i++)
@@ -1093,8 +963,6 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     a.spin = m->wait_limit > 0 ? (long)m->wait_limit : kSpin;
     a.rounds = std::max(16L, a.spin / 16);
     a.stall_cta = m->stall_cta;
-    a.pr_ll = m->w.pr_ll;
-    a.predict = m->predict;
     a.stall_t = m->stall_t;
     DS4F_CUDA(cudaMemsetAsync(m->w.diag + 2, 0, 2 * sizeof(unsigned), st));
     // tags carry 16 bits of layer-step: split long runs into launches

@@ -52,7 +52,6 @@ struct Work {
     uint64_t *st_ll;      // [H] persistent kernel: tagged state words
     uint64_t *sb_ll;      // [E][4] tagged router logits and interval ends (fp32)
     uint64_t *ch_ll;      // [(K+1) M + 1] tagged chains + shared-gate logit
-    uint64_t *pr_ll;      // [E] tagged router-lookahead logits (next layer's experts)
 };
 
 struct Model {
@@ -78,7 +77,6 @@ struct Model {
     int epoch;                   // last persistent launch's tag epoch
     int64_t wait_limit;          // persistent kernel: polls before a wait gives up (0: default)
     int stall_cta, stall_t;      // test hook of the persistent kernel (-1: off)
-    int predict;                 // persistent kernel: next-layer experts prefetched into L2
     int *log_idx;                // route log of the persistent kernel (log_n layer-steps
     float *log_w, *log_state;    //   of the next launch): selections, weights, output state
     int log_n;

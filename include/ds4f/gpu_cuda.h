@@ -327,17 +327,6 @@ int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
  * ("decode kernel gave up waiting (code C at CTA N)"); the model stays
  * usable. 0 restores the default, 2^24 polls (about a second). */
 int  ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *m, int64_t polls);
-/* Router lookahead of the persistent decode kernel (no reference
- * counterpart; the reference found speculative fetches of the next layer's
- * experts useless for its disk cache, because consecutive layers share no
- * experts). During layer l every CTA also computes its rows of layer l+1's
- * router on layer l's normalised state -- a prediction, the routing itself
- * stays certified on layer l+1's own state -- and the top n_experts of that
- * prediction are prefetched into L2 while HBM is otherwise idle (the
- * exchanges, the norm, the router), so that layer l+1's copies of correctly
- * predicted experts hit L2. Results do not depend on it. Default 12; 0 turns
- * it off; at most 16. */
-int  ds4f_gpu_model_set_prefetch(Ds4fGpuModel *m, int n_experts);
 /* Failure injection for tests (no reference counterpart): in the following
  * persistent launches CTA `cta` does not publish its rows of the state at
  * layer-step `layer_step` of a launch (0 = the first layer of its first

@@ -62,23 +62,3 @@ def test_wait_limit_alone_changes_nothing():
     assert np.array_equal(m.stack(x, 2), want)
     m.close()
 
-
-@pytest.mark.parametrize("fmt", [dc.FMT_FP8, dc.FMT_MXFP4])
-def test_router_lookahead_changes_no_result(fmt):
-    """The lookahead prefetch only warms L2: with it off, at 8 and at 16
-    experts the persistent kernel's states, routes and weights are
-    bit-identical."""
-    m = dc.Model(fmt, 6, 2048, 512, 256, 8)
-    m.synth(14)
-    m.set_path(dc.PATH_PERSISTENT)
-    m.route_log(12)
-    x = po.fill_f32(2048, po.key(14, 0, 4, 0, 0), 1.0)
-    outs = []
-    for n in (0, 8, 16):
-        m.set_prefetch(n)
-        st = m.stack(x, 2)
-        outs.append((st, *m.route_log_read(12)))
-    for o in outs[1:]:
-        for a, b in zip(o, outs[0]):
-            assert np.array_equal(a, b)
-    m.close()
