@@ -129,6 +129,8 @@ using namespace ds4f;
 struct Ds4fMvPlan {
     MvJob *jobs_dev;
     int njobs, nitems, device;
+    MvStream sp;          // the expert-shaped jobs, streamed by TMA (mvstream.cu)
+    unsigned *err_h;      // pinned copy of sp.err after each run, read by the next
 };
 
 namespace ds4f {
@@ -322,19 +324,25 @@ int ds4f_gpu_mv_plan(const Ds4fMvJob *jobs, int njobs, Ds4fMvPlan **plan) {
         J.canon = jobs[j].canon;
         DS4F_REQUIRE(J.fmt != DS4F_FMT_MLX4, "mv_plan: MLX4 jobs go through ds4f_gpu_mlx4_batch");
     }
-    int items = plan_jobs(v.data(), njobs);
-    if (items < 0) return -1;
     Ds4fMvPlan *p = new Ds4fMvPlan();
+    memset(p, 0, sizeof *p);
+    // the expert-shaped jobs go to the stream kernel, the rest to k_mv_jobs
+    if (stream_plan(v.data(), njobs, &p->sp)) { delete p; return -1; }
+    int items = plan_jobs(v.data(), njobs);
+    if (items < 0) { stream_free(&p->sp); delete p; return -1; }
     p->njobs = njobs; p->nitems = items;
     cudaGetDevice(&p->device);
     if (cudaMalloc(&p->jobs_dev, sizeof(MvJob) * njobs) != cudaSuccess ||
         cudaMemcpy(p->jobs_dev, v.data(), sizeof(MvJob) * njobs, cudaMemcpyHostToDevice) !=
-            cudaSuccess) {
+            cudaSuccess ||
+        cudaHostAlloc((void **)&p->err_h, 4, cudaHostAllocDefault) != cudaSuccess) {
         cudaFree(p->jobs_dev);
+        stream_free(&p->sp);
         delete p;
         set_error("mv_plan: device allocation failed");
         return -1;
     }
+    *p->err_h = 0;
     *plan = p;
     return 0;
 }
@@ -343,12 +351,24 @@ int ds4f_gpu_mv_run(const Ds4fMvPlan *plan, void *stream) {
     DS4F_REQUIRE(plan, "mv_run: null plan");
     cudaStream_t st;
     if (stream_of(stream, &st)) return -1;
+    if (*(volatile unsigned *)plan->err_h) {
+        *plan->err_h = 0;
+        cudaMemsetAsync(plan->sp.err, 0, 4, st);
+        set_error("mv_run: a weight copy of an earlier run did not complete (its outputs are invalid)");
+        return -1;
+    }
+    if (stream_launch(plan->jobs_dev, plan->sp, st)) return -1;
+    if (plan->sp.nunits) DS4F_CUDA(cudaMemcpyAsync(plan->err_h, plan->sp.err, 4, cudaMemcpyDeviceToHost, st));
     return launch_jobs(plan->jobs_dev, plan->njobs, plan->nitems, st);
 }
 
 void ds4f_gpu_mv_plan_free(Ds4fMvPlan *plan) {
     if (!plan) return;
+    cudaSetDevice(plan->device);
+    cudaDeviceSynchronize();
     cudaFree(plan->jobs_dev);
+    stream_free(&plan->sp);
+    if (plan->err_h) cudaFreeHost(plan->err_h);
     delete plan;
 }
 

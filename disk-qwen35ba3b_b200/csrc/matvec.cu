@@ -307,6 +307,10 @@ int plan_jobs(MvJob *jobs, int njobs) {
     for (int j = 0; j < njobs; j++) {
         MvJob &J = jobs[j];
         DS4F_REQUIRE(J.R >= 0 && J.C >= 1, "matvec: bad shape %d x %d", J.R, J.C);
+        if (J.streamed) {                       // the stream kernel's job: no items here
+            J.item0 = items;
+            continue;
+        }
         DS4F_REQUIRE(J.fmt == DS4F_FMT_FP8 || J.fmt == DS4F_FMT_MXFP4 ||
                      J.fmt == DS4F_FMT_BF16 || J.fmt == DS4F_FMT_MLX4,
                      "matvec: unknown format %d", J.fmt);

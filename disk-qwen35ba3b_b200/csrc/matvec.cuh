@@ -36,7 +36,29 @@ struct MvJob {
     int item0;        // first work item (prefix over jobs)
     int lpr;          // lanes per row in the vector path
     int nq;           // 16-byte chunks per row
+    int streamed;     // taken by the TMA stream kernel (mvstream.cu), not by k_mv_jobs
 };
+
+// The stream kernel's work: units of up to 64 rows of one job (<= 32 KB),
+// CTA c taking units [ranges[c], ranges[c+1]).
+struct MvUnit {
+    int job, row0, nrows, bytes;
+};
+struct MvStream {
+    void *base;
+    MvUnit *units;
+    int *ranges;
+    unsigned *err;    // set when a copy wait gave up
+    int nunits, grid;
+};
+// Host: mark the jobs the stream kernel takes (J.streamed; expert-shaped
+// FP8 / MXFP4 / BF16 rows of 128..2048 columns, 16-byte aligned) and upload
+// its units, balanced by bytes over the SMs. plan_jobs then leaves them out.
+int stream_plan(MvJob *jobs, int njobs, MvStream *sp);
+void stream_free(MvStream *sp);
+int stream_launch(const MvJob *jobs_dev, const MvStream &sp, cudaStream_t st);
+// Synchronous: -1 if a copy wait of an earlier launch gave up (then cleared).
+int stream_check(const MvStream &sp);
 
 // Host: fill fast/lpr/nq/item0 and return the total work items.
 int plan_jobs(MvJob *jobs, int njobs);

@@ -211,6 +211,68 @@ def test_mv_plan_config1_microbench():
         assert relerr(tym.cpu().numpy(), rm) < MV_TOL
 
 
+def test_mv_plan_stream_kernel_shapes_and_formats():
+    """Job lists through the TMA stream kernel (expert-shaped jobs) and the
+    job kernel (the rest) in one plan, run twice: FP8 with E8M0 block scales
+    and raw bytes (e=15 canonicalised in-kernel), FP8 with fp32 scales, MXFP4,
+    BF16 with and without bias; odd row counts; 64 MB of FP8 rows so that
+    every CTA's ring of copy slots wraps its phase; a 96-column job that the
+    stream kernel does not take."""
+    import torch
+    rng = np.random.default_rng(5)
+    jobs, checks, keep = [], [], []
+
+    def dev(a):
+        t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        keep.append(t)
+        return t
+
+    def add(fmt, W, s, x, R, Cc, SR, SC, kind, canon, ref):
+        tW, tx = dev(W), dev(x)
+        ts = dev(s) if s is not None else None
+        ty = torch.zeros(R, device="cuda")
+        keep.append(ty)
+        jobs.append(dc.Ds4fMvJob(tW.data_ptr(), ts.data_ptr() if ts is not None else 0, tx.data_ptr(),
+                                 ty.data_ptr(), R, Cc, SR, SC, fmt, kind, 32, canon))
+        checks.append((ty, ref))
+
+    for (R, Cc) in ((100, 2048), (300, 512), (2048, 128), (640, 384)):
+        W = rng.integers(0, 256, (R, Cc), dtype=np.uint8)            # e=15 bytes included
+        SR, SC = max(1, R // 128), Cc // 128
+        s8 = rng.integers(110, 125, (SR, SC), dtype=np.uint8)
+        x = xvec(Cc, R)
+        add(dc.FMT_FP8, W, s8, x, R, Cc, SR, SC, dc.SCALE_E8M0, 1,
+            po.f8_matvec(W, po.SCALE_E8M0, s8, SR, SC, x))
+    for (R, Cc) in ((4096, 2048),) * 8:                                 # 64 MB
+        k = po.key(2, 0, 3, len(jobs), 0)
+        W, s = po.quant_fp8(R, Cc, k, 0.02)
+        x = xvec(Cc, len(jobs) + 7)
+        add(dc.FMT_FP8, W, s, x, R, Cc, R // 128, Cc // 128, dc.SCALE_F32, 0,
+            po.f8_matvec(W, po.SCALE_F32, s, R // 128, Cc // 128, x))
+    for (R, Cc) in ((333, 1024), (2048, 512)):
+        v, sm = po.quant_mxfp4(R, Cc, po.key(3, 0, 3, R, 0), 0.02)
+        x = xvec(Cc, 11)
+        add(dc.FMT_MXFP4, v, sm, x, R, Cc, 1, 1, 0, 0, po.mxfp4_matvec(v, sm, R, Cc, x))
+    for (R, Cc, bias) in ((256, 2048, False), (2048, 512, True), (77, 256, True)):
+        W = (rng.standard_normal((R, Cc), dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        b = rng.standard_normal(R).astype(np.float32) if bias else None
+        x = xvec(Cc, 13)
+        add(3, W, b, x, R, Cc, 1, 1, 0, 0, po.bf16_matvec(W, x, b))
+    W = rng.integers(0, 120, (64, 96), dtype=np.uint8)                   # job kernel, not streamed
+    x = xvec(96, 17)
+    add(dc.FMT_FP8, W, None, x, 64, 96, 1, 1, dc.SCALE_F32, 0, po.f8_matvec(W, po.SCALE_F32, None, 1, 1, x))
+    p = dc.MvPlan(jobs)
+    sp = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        for ty, _ in checks:
+            ty.fill_(float("nan"))
+        p.run(sp)
+        torch.cuda.synchronize()
+        for i, (ty, ref) in enumerate(checks):
+            assert relerr(ty.cpu().numpy(), ref) < MV_TOL, i
+    del p
+
+
 def test_bad_arguments_fail_loudly():
     with pytest.raises(dc.GpuError, match="bsize"):
         dc.mxfp4_matvec(np.zeros(8, np.uint8), np.zeros(1, np.uint8), 1, 16, np.zeros(16, np.float32), 8)
