@@ -516,7 +516,6 @@ void ds4f_gpu_model_destroy(Ds4fGpuModel *h) {
     if (m.trace) cudaFree(m.trace);
     if (m.log_base) cudaFree(m.log_base);
     if (m.pf_ws) cudaFree(m.pf_ws);
-    if (m.pf8) cudaFree(m.pf8);
     if (m.pf_err_h) cudaFreeHost(m.pf_err_h);
     if (m.bgraph) cudaGraphExecDestroy(m.bgraph);
     if (m.host_pool) cudaHostUnregister(const_cast<uint8_t *>(m.host_pool));

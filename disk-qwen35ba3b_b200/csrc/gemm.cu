@@ -88,6 +88,31 @@ int tmap_u8_3d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, 
     return 0;
 }
 
+// 4-bit tensor [planes][rows][inner] (E2M1 nibbles, two to a byte, row
+// stride `row_stride` bytes), boxes of [1][box_rows][128 elements] landing in
+// shared memory unpacked (each 16 nibbles in a 16-byte chunk, the layout the
+// block-scaled MMA reads 4-bit operands in: a 128-byte row holds 128
+// elements, as for 8-bit ones) with the 128-byte swizzle.
+int tmap_u4_3d(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t planes,
+               uint64_t row_stride, uint64_t plane_stride, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) { set_error("cuTensorMapEncodeTiled is unavailable"); return -1; }
+    if (((uintptr_t)base & 31) || (row_stride & 31) || (plane_stride & 31) || inner % 128 || box_rows < 1 ||
+        box_rows > 256) {
+        set_error("tensor map (4-bit): base and strides must be 32-byte aligned, inner a multiple of 128");
+        return -1;
+    }
+    cuuint64_t dims[3] = {inner, rows, planes};
+    cuuint64_t strides[2] = {row_stride, plane_stride};
+    cuuint32_t box[3] = {128, box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled (4-bit) failed (%d)", (int)r); return -1; }
+    return 0;
+}
+
 namespace {
 
 // ---- activation quantiser -------------------------------------------------------
@@ -237,8 +262,13 @@ struct PSmem {
     static constexpr int NMX = kGemmBN * ND;          // widest MMA N (one TMEM buffer)
     static constexpr int A = 128 * 128;
     static constexpr int STAGE = A + NMX * 128;
-    static constexpr int o_bar = kPStages * STAGE;    // full[S], empty[S], tfull[2], tempty[2], done
-    static constexpr int o_slot = o_bar + ((2 * kPStages + 5) * 8 + 127) / 128 * 128;
+    // full[S], empty[S], tfull[2], tempty[2], done, sfull[S] (block-scaled)
+    static constexpr int o_bar = kPStages * STAGE;
+    static constexpr int o_slot = o_bar + ((3 * kPStages + 5) * 8 + 127) / 128 * 128;
+    // TMEM: two accumulator buffers, then (block-scaled) the A scale factors
+    // of each stage in 4 columns, then 8 columns of B scale factors (1.0)
+    static constexpr uint32_t SFA = 2 * NMX, SFB = SFA + 4 * kPStages;
+    static_assert(SFB + 16 <= 512, "TMEM columns for the scale factors");
     static constexpr int o_sx = o_slot + 16;          // two [kb][64] activation-scale tiles
     static constexpr int bytes(int kb) { return o_sx + 2 * kGemmBN * kb * 4 + 1024; }
     static_assert(STAGE % 1024 == 0 && 2 * NMX <= 512, "stage alignment and TMEM columns");
@@ -321,8 +351,10 @@ __device__ __forceinline__ void p_sx_store(float *sxt, int KB, int e, const floa
     }
 }
 
-template <int ND>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+// MX: A is MXFP4 (unpacked E2M1 tiles, block-scaled MMA); four more warps,
+// one per TMEM lane quadrant, write each stage's A scale factors into TMEM.
+template <int ND, bool MX>
+__global__ void __launch_bounds__(MX ? kGemmThreads + 128 : kGemmThreads, 1)
 k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtensorMap tW2,
          const __grid_constant__ CUtensorMap tX16, const __grid_constant__ CUtensorMap tX32,
          const __grid_constant__ CUtensorMap tX48, const __grid_constant__ CUtensorMap tX64, GemmArgs g) {
@@ -330,9 +362,10 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
     uint64_t *full = (uint64_t *)(sm + L::o_bar), *empty = full + kPStages;
-    uint64_t *tfull = empty + kPStages, *tempty = tfull + 2, *done = tempty + 2;
+    uint64_t *tfull = empty + kPStages, *tempty = tfull + 2, *done = tempty + 2, *sfull = done + 1;
     uint32_t *slot = (uint32_t *)(sm + L::o_slot);
     float *sxt = (float *)(sm + L::o_sx);
+    constexpr uint32_t kTmemCols = (MX || 2 * L::NMX > 256) ? 512 : 256;
 
     const int MT = g.R / 128, RT = MT * g.nmat, KB = g.KB;
     const int n_items = (g.tiles ? *g.ntiles : (g.N + kGemmBN - 1) / kGemmBN) * RT;
@@ -340,9 +373,11 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned *err = g.err;
 
-    if (warp == 1) tc::tmem_alloc(slot, 2 * L::NMX <= 256 ? 256 : 512);
+    if (warp == 1) tc::tmem_alloc(slot, kTmemCols);
     if (tid == 0) {
         for (int s = 0; s < kPStages; s++) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+        if (MX)
+            for (int s = 0; s < kPStages; s++) tc::mbar_init(sfull + s, 4);
         for (int b = 0; b < 2; b++) { tc::mbar_init(tfull + b, 1); tc::mbar_init(tempty + b, kEpiWarps); }
         tc::mbar_init(done, 1);
         tc::mbar_fence_init();
@@ -388,6 +423,7 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
                 for (int kb = 0; kb < KB; kb++, k++) {
                     const int s = k % kPStages, b = k & 1;
                     if (!tc::mbar_wait(full + s, (k / kPStages) & 1, err, 3) ||
+                        (MX && !tc::mbar_wait(sfull + s, (k / kPStages) & 1, err, 7)) ||
                         (k >= 2 && !tc::mbar_wait(tempty + b, ((k >> 1) - 1) & 1, err, 4))) {
                         ok = false;
                         break;
@@ -395,9 +431,18 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
                     tc::fence_after_sync();
                     const uint8_t *a = sm + s * L::STAGE;
 #pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        tc::mma_f8f6f4(taddr + b * L::NMX, tc::sdesc_sw128(a + 32 * q),
-                                       tc::sdesc_sw128(a + L::A + 32 * q), id, q > 0);
+                    for (int q = 0; q < 4; q++) {
+                        if constexpr (MX)
+                            // K step q: byte q of each row's scale word (the 4
+                            // sub-blocks of 32 in this 128-column block)
+                            tc::mma_mx_bs(taddr + b * L::NMX, tc::sdesc_sw128(a + 32 * q),
+                                          tc::sdesc_sw128(a + L::A + 32 * q), tc::idesc_bs(128, ND * it.w, 5, 0, q),
+                                          (taddr + L::SFA + 4 * s) | ((uint32_t)q << 30),
+                                          (taddr + L::SFB) | ((uint32_t)q << 30), q > 0);
+                        else
+                            tc::mma_f8f6f4(taddr + b * L::NMX, tc::sdesc_sw128(a + 32 * q),
+                                           tc::sdesc_sw128(a + L::A + 32 * q), id, q > 0);
+                    }
                     tc::commit(empty + s);
                     tc::commit(tfull + b);
                 }
@@ -405,7 +450,7 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
             tc::commit(done);
             tc::mbar_wait(done, 0, err, 5, true);      // every MMA finished
         }
-    } else {
+    } else if (warp < 2 + kEpiWarps) {
         // epilogue: warp quadrant q reads TMEM lanes 32q .. 32q + 31 = rows;
         // the four warps of a quadrant take 16 columns each. After a failed
         // wait the warps keep walking the items without waiting, so every
@@ -425,8 +470,10 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
             const bool has_next = p_item(g, i + gridDim.x, n_items, RT, MT, nx);
             p_sx_load(g, nx, has_next, e, pre);
             const float *sxi = sxt + (j & 1) * kGemmBN * KB;
-            const float *swr = (it.mat ? g.sW2 : g.sW) + it.zs * g.sw_slot +
-                               (g.row_scales ? (int64_t)(it.r0 + row) * KB : (int64_t)(it.r0 / 128) * KB);
+            // the weights' block scales (MX: applied by the tensor core)
+            const float *swr = MX ? nullptr
+                                  : (it.mat ? g.sW2 : g.sW) + it.zs * g.sw_slot +
+                                        (g.row_scales ? (int64_t)(it.r0 + row) * KB : (int64_t)(it.r0 / 128) * KB);
             float2 acc[kEpiCols / 2];
 #pragma unroll
             for (int c = 0; c < kEpiCols / 2; c++) acc[c] = make_float2(0.f, 0.f);
@@ -435,7 +482,9 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
                 if (ok) ok = tc::mbar_wait(tfull + b, (k >> 1) & 1, err, 6);
                 if (ok) {
                     tc::fence_after_sync();
-                    if (c0 < it.w) promote_w<ND>(tq + b * L::NMX, it.w, c0, sxi + kb * kGemmBN, __ldg(swr + kb), acc);
+                    if (c0 < it.w)
+                        promote_w<ND>(tq + b * L::NMX, it.w, c0, sxi + kb * kGemmBN, MX ? 1.0f : __ldg(swr + kb),
+                                      acc);
                     tc::fence_before_sync();
                 }
                 __syncwarp();
@@ -450,12 +499,41 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
             p_sx_store(sxt + ((j + 1) & 1) * kGemmBN * KB, KB, e, pre);
             asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
         }
+    } else if constexpr (MX) {
+        // scale factors: warp quadrant q writes rows 32q .. 32q + 31 of A's
+        // E8M0 scales, for each stage one 32-bit word per row (the 4 scales
+        // of the 128-column K block, byte i = sub-block i) into 4 columns
+        // of its lanes, once the stage's previous MMAs are done; B's are 1.0
+        // (127) in 16 columns of every lane, written once
+        const int q = warp & 3;
+        const uint32_t tq = taddr + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) tc::tmem_st4(tq + L::SFB + c, 0x7F7F7F7Fu);
+        const int rb = g.C / 32;                            // scale bytes per row
+        int k = 0;
+        bool ok = true;
+        for (int i = blockIdx.x; ok && p_item(g, i, n_items, RT, MT, it); i += gridDim.x) {
+            const uint8_t *sr = (it.mat ? g.sfa2 : g.sfa) + (int64_t)it.zs * g.sfa_slot +
+                                (int64_t)(it.r0 + q * 32 + lane) * rb;
+            for (int kb = 0; kb < KB; kb++, k++) {
+                const int s = k % kPStages;
+                bool okw = true;
+                if (k >= kPStages && lane == 0) okw = tc::mbar_wait(empty + s, ((k / kPStages) - 1) & 1, err, 8);
+                if (!__shfl_sync(0xFFFFFFFFu, okw, 0)) { ok = false; break; }
+                tc::fence_after_sync();
+                tc::tmem_st4(tq + L::SFA + 4 * s, __ldg((const uint32_t *)(sr + 4 * kb)));
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(sfull + s);
+            }
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 1) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(taddr, 2 * L::NMX <= 256 ? 256 : 512);
+        tc::tmem_dealloc(taddr, kTmemCols);
     }
 }
 
@@ -503,16 +581,50 @@ int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X
         return -1;
     }
     static SmemOptIn opt;
-    if (opt.set(k_gemm_p<ND>, 227 * 1024)) return -1;
+    if (opt.set(k_gemm_p<ND, false>, 227 * 1024)) return -1;
     g.nmat = A2 ? 2 : 1;
     const int64_t items = (int64_t)ntiles_max * (g.R / 128) * (A2 ? 2 : 1);
     const int grid = (int)std::min<int64_t>(items, sm_count());
-    k_gemm_p<ND><<<grid, kGemmThreads, psmem, st>>>(tW, tW2, tX16, tX32, tX48, tX, g);
+    k_gemm_p<ND, false><<<grid, kGemmThreads, psmem, st>>>(tW, tW2, tX16, tX32, tX48, tX, g);
     DS4F_CUDA(cudaGetLastError());
     return 0;
 }
 template int gemm_launch<3, false>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int,
                                    cudaStream_t, const void *);
+
+template <int ND>
+int gemm_launch_mx(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows, GemmArgs g,
+                   int ntiles_max, cudaStream_t st, const void *A2) {
+    if (g.R <= 0 || g.C <= 0 || g.R % 128 || g.C % 128 || ntiles_max <= 0 || !g.sfa || (A2 && !g.sfa2)) {
+        set_error("gemm (MXFP4): R and C must be positive multiples of 128, scales given");
+        return -1;
+    }
+    CUtensorMap tW, tW2, tX16, tX32, tX48, tX64;
+    if (tmap_u4_3d(&tW, A, (uint64_t)g.C, g.R, slots, (uint64_t)g.C / 2, slot_stride, 128) ||
+        tmap_u4_3d(&tW2, A2 ? A2 : A, (uint64_t)g.C, g.R, slots, (uint64_t)g.C / 2, slot_stride, 128) ||
+        tmap_u8_3d(&tX16, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 16, ND) ||
+        tmap_u8_3d(&tX32, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 32, ND) ||
+        tmap_u8_3d(&tX48, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, 48, ND) ||
+        tmap_u8_3d(&tX64, X, (uint64_t)g.C, xrows, ND, (uint64_t)g.C, (uint64_t)xrows * g.C, kGemmBN, ND))
+        return -1;
+    g.KB = g.C / 128;
+    using P = PSmem<ND>;
+    const int psmem = P::bytes(g.KB);
+    if (psmem > 227 * 1024 || kGemmBN * g.KB > kPSxRegs * 32 * kEpiWarps) {
+        set_error("gemm: C too large for the scale tiles");
+        return -1;
+    }
+    static SmemOptIn opt;
+    if (opt.set(k_gemm_p<ND, true>, 227 * 1024)) return -1;
+    g.nmat = A2 ? 2 : 1;
+    const int64_t items = (int64_t)ntiles_max * (g.R / 128) * (A2 ? 2 : 1);
+    const int grid = (int)std::min<int64_t>(items, sm_count());
+    k_gemm_p<ND, true><<<grid, kGemmThreads + 128, psmem, st>>>(tW, tW2, tX16, tX32, tX48, tX64, g);
+    DS4F_CUDA(cudaGetLastError());
+    return 0;
+}
+template int gemm_launch_mx<3>(const void *, int64_t, int64_t, const void *, int64_t, GemmArgs, int, cudaStream_t,
+                               const void *);
 
 int bf16_gemm_launch(const uint16_t *A, const uint16_t *X, GemmArgs g, cudaStream_t st, const uint16_t *A2) {
     using L = BfSmem;

@@ -19,8 +19,11 @@ struct GemmArgs {
     float *Y;                 // Y[(first row + n) * ldy + ycol0 + r]
     int64_t ldy;
     int ycol0, R, C, KB;      // KB: K blocks of 128 bytes (set by gemm_launch)
-    int row_scales;           // 1: sW holds a scale per (row, K block) (an MXFP4
-                              //    pool's FP8 copy), [R][KB]; 0: per 128x128 block
+    int row_scales;           // 1: sW holds a scale per (row, K block), [R][KB];
+                              //    0: per 128x128 block
+    const uint8_t *sfa;       // MXFP4 A (gemm_launch_mx): E8M0 scales of slot 0,
+    const uint8_t *sfa2;      //   [R][C/32] bytes (the second A matrix's in sfa2),
+    int64_t sfa_slot;         //   bytes between consecutive slots' scales
     const int *tiles;         // grouped: [*ntiles][3] = slot, first B row, valid rows
     const int *ntiles;
     int N;                    // dense: B rows
@@ -37,6 +40,13 @@ template <int ND, bool BF>
 int gemm_launch(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
                 GemmArgs g, int ntiles_max, cudaStream_t st, const void *A2 = nullptr);
 
+// The same GEMM with MXFP4 A (E2M1 nibbles [R][C] per slot, C / 2 bytes a
+// row, `slot_stride` bytes apart; E8M0 scales per 32 in g.sfa / g.sfa2): the
+// tensor core's block-scaled MMA (kind::mxf8f6f4.block_scale) applies the
+// weights' scales itself, the epilogue only the activations'.
+template <int ND>
+int gemm_launch_mx(const void *A, int64_t slots, int64_t slot_stride, const void *X, int64_t xrows,
+                   GemmArgs g, int ntiles_max, cudaStream_t st, const void *A2 = nullptr);
 // bf16 GEMM (tcgen05 kind::f16): Y = A . X~, A [R][C] bf16 (A2 as above),
 // X~ = hi + lo, two bf16 planes [N][C]; dense over g.N rows.
 int bf16_gemm_launch(const uint16_t *A, const uint16_t *X, GemmArgs g, cudaStream_t st,

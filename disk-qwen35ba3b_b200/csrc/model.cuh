@@ -83,8 +83,6 @@ struct Model {
     void *log_base;
     void *pf_ws;                 // batched-prefill workspace (prefill.cu), grown on demand
     size_t pf_bytes;
-    uint8_t *pf8;                // MXFP4 models: the pool's exact FP8 copy for the
-    SlotLayout slot8;            //   tensor-core prefill (row scales), built on first use
     unsigned *pf_err_h;          // pinned copy of the prefill pipeline error word,
                                  //   written after each asynchronous step
     // streaming pool (ds4f_gpu_model_create_streaming): the experts live in

@@ -252,81 +252,6 @@ __global__ void k_combine(float *states, float *acc_out, const float *O, const f
 }
 
 // ---- MXFP4 pools: the exact FP8 copy ---------------------------------------------------
-// Matrix [R][C] of E2M1 nibbles (even index low nibble) with E8M0 scales per
-// 32 along the row -> E4M3 bytes [R][C] and fp32 scales [R][C/128]: in each
-// (row, 128-column) block with sub-block exponents s_j and smax = max s_j,
-// element = E2M1 value x 2^(s_j - smax) (exact in E4M3 while s_j - smax >=
-// -6; checked per element, *bad counts the others), scale = 2^(smax - 127).
-// One warp per block, 4 elements per lane.
-__global__ void k_mx_to_f8(const uint8_t *vals, const uint8_t *sc, int R, int C, uint8_t *q, float *s,
-                           unsigned *bad) {
-    const int nb = C / 128;
-    const int64_t blk = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (blk >= (int64_t)R * nb) return;
-    const int lane = threadIdx.x & 31;
-    const int r = (int)(blk / nb), b = (int)(blk % nb);
-    const uint8_t *sr = sc + (int64_t)r * (C / 32) + b * 4;
-    int smax = max(max(sr[0], sr[1]), max(sr[2], sr[3]));
-    const int sj = sr[lane >> 3];                      // lane covers elements 4 lane .. 4 lane + 3
-    const int64_t e0 = (int64_t)r * C + b * 128 + 4 * lane;
-    const uint16_t two = *(const uint16_t *)(vals + (e0 >> 1));
-    float v[4];
-    bool ok = smax < 255;
-    const float f = ldexpf(1.0f, sj - smax);
-#pragma unroll
-    for (int i = 0; i < 4; i++) v[i] = e2m1_raw((two >> (4 * i)) & 0xFu) * DS4F_E2M1_UNSCALE * f;
-    const uint32_t w = e4m3_2(v[0], v[1]) | (e4m3_2(v[2], v[3]) << 16);
-#pragma unroll
-    for (int i = 0; i < 4; i++) ok = ok && e4m3_val((w >> (8 * i)) & 0xFF) == v[i];
-    *(uint32_t *)(q + e0) = w;
-    if (lane == 0) s[blk] = ldexpf(1.0f, smax - 127);
-    if (!ok) atomicAdd(bad, 1u);
-}
-
-int ensure_f8_copy(Model *m, cudaStream_t st) {
-    if (m->pf8) return 0;
-    const int H = m->d.hidden, M = m->d.moe_inter;
-    SlotLayout &s8 = m->slot8;
-    int64_t off = 0;
-    const int64_t vb[3] = {(int64_t)M * H, (int64_t)M * H, (int64_t)H * M};
-    const int64_t sb[3] = {(int64_t)M * (H / 128) * 4, (int64_t)M * (H / 128) * 4, (int64_t)H * (M / 128) * 4};
-    for (int t = 0; t < 3; t++) { s8.rel_v[t] = off; off += vb[t]; }
-    for (int t = 0; t < 3; t++) { s8.rel_s[t] = off; off += sb[t]; }
-    s8.nbytes = off;
-    const int64_t slots = (int64_t)m->d.n_layers * m->d.expert_count;
-    const size_t bytes = (size_t)slots * s8.nbytes;
-    size_t fre = 0, tot = 0;
-    DS4F_CUDA(cudaMemGetInfo(&fre, &tot));
-    DS4F_REQUIRE((double)bytes <= 0.95 * (double)fre,
-                 "prefill: the MXFP4 pool's FP8 copy needs %.2f GB, %.2f GB free", bytes / 1e9, fre / 1e9);
-    DS4F_CUDA(cudaMalloc(&m->pf8, bytes));
-    unsigned *bad = nullptr;
-    DS4F_CUDA(cudaMalloc(&bad, 4));
-    DS4F_CUDA(cudaMemsetAsync(bad, 0, 4, st));
-    for (int64_t z = 0; z < slots; z++)
-        for (int t = 0; t < 3; t++) {
-            const int R = t < 2 ? M : H, C = t < 2 ? H : M;
-            const uint8_t *src = m->pool + z * m->slot.nbytes;
-            uint8_t *dst = m->pf8 + z * s8.nbytes;
-            const int64_t warps = (int64_t)R * (C / 128);
-            k_mx_to_f8<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
-                src + m->slot.rel_v[t], src + m->slot.rel_s[t], R, C, dst + s8.rel_v[t],
-                (float *)(dst + s8.rel_s[t]), bad);
-        }
-    unsigned h = 0;
-    DS4F_CUDA(cudaMemcpyAsync(&h, bad, 4, cudaMemcpyDeviceToHost, st));
-    DS4F_CUDA(cudaStreamSynchronize(st));
-    cudaFree(bad);
-    if (h) {
-        cudaFree(m->pf8);
-        m->pf8 = nullptr;
-        set_error("prefill: %u MXFP4 elements are not exact in E4M3 at their block's scale "
-                  "(sub-block exponents more than 6 apart)", h);
-        return -1;
-    }
-    return 0;
-}
-
 // ---- workspace -----------------------------------------------------------------------
 struct PfWs {
     int *cnt, *off, *tiles, *ntiles, *nrows, *pos;
@@ -412,11 +337,12 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
                   bool first_layer, bool last_layer, float *acc_out, bool add_shared) {
     DS4F_REQUIRE(T > 0 && L >= 0 && L < m->d.n_layers, "prefill: layer %d / tokens %d", L, T);
     DS4F_REQUIRE(!m->cache, "prefill: not available for a streaming model (its experts are not resident)");
+    // the tensor core reads the pool itself: FP8 bytes (their fp32 block
+    // scales applied in the epilogue) or MXFP4 nibbles (their E8M0 scales
+    // applied by the block-scaled MMA)
     const bool mx = m->d.fmt == DS4F_FMT_MXFP4;
-    if (mx && ensure_f8_copy(m, st)) return -1;
-    // the tensor core reads FP8: the pool itself, or an MXFP4 pool's exact copy
-    const uint8_t *pool = mx ? m->pf8 : m->pool;
-    const SlotLayout &sl = mx ? m->slot8 : m->slot;
+    const uint8_t *pool = m->pool;
+    const SlotLayout &sl = m->slot;
     const int H = m->d.hidden, M = m->d.moe_inter, K = m->d.topk;
     const int first = m->d.expert_first, count = m->d.expert_count;
     DS4F_REQUIRE(count <= 1024, "prefill: at most 1024 experts per shard");
@@ -450,27 +376,42 @@ int prefill_layer(Model *m, int L, float *states, int T, const int *sel, const f
     if (routed) {
     {   // gate and up in one launch
         GemmArgs g{};
-        g.sW = (const float *)(pool + sl.rel_s[0]);
-        g.sW2 = (const float *)(pool + sl.rel_s[1]);
-        g.sw_slot = sl.nbytes / 4;
-        g.row_scales = mx;
         g.sX = ws.sxg; g.Y = ws.GU; g.ldy = 2 * M; g.ycol0 = 0; g.ycol2 = M;
         g.R = M; g.C = H; g.tiles = ws.tiles; g.ntiles = ws.ntiles; g.err = ws.err;
-        if (gemm_launch<kND, false>(pool + sl.rel_v[0], total_slots, sl.nbytes, ws.Xg, R, g,
-                                    ws.tiles_max, st, pool + sl.rel_v[1]))
-            return -1;
+        if (mx) {
+            g.sfa = pool + sl.rel_s[0];
+            g.sfa2 = pool + sl.rel_s[1];
+            g.sfa_slot = sl.nbytes;
+            if (gemm_launch_mx<kND>(pool + sl.rel_v[0], total_slots, sl.nbytes, ws.Xg, R, g, ws.tiles_max, st,
+                                    pool + sl.rel_v[1]))
+                return -1;
+        } else {
+            g.sW = (const float *)(pool + sl.rel_s[0]);
+            g.sW2 = (const float *)(pool + sl.rel_s[1]);
+            g.sw_slot = sl.nbytes / 4;
+            if (gemm_launch<kND, false>(pool + sl.rel_v[0], total_slots, sl.nbytes, ws.Xg, R, g,
+                                        ws.tiles_max, st, pool + sl.rel_v[1]))
+                return -1;
+        }
     }
     k_silu_digits<<<(unsigned)((R * (M / 128) * 32 + 255) / 256), 256, 0, st>>>(ws.GU, M, ws.nrows, ws.Cq,
                                                                                 ws.sc, (int)R);
     {
         GemmArgs g{};
-        g.sW = (const float *)(pool + sl.rel_s[2]);
-        g.sw_slot = sl.nbytes / 4;
-        g.row_scales = mx;
         g.sX = ws.sc; g.Y = ws.O; g.ldy = H; g.ycol0 = 0;
         g.R = H; g.C = M; g.tiles = ws.tiles; g.ntiles = ws.ntiles; g.err = ws.err;
-        if (gemm_launch<kND, false>(pool + sl.rel_v[2], total_slots, sl.nbytes, ws.Cq, R, g, ws.tiles_max, st))
-            return -1;
+        if (mx) {
+            g.sfa = pool + sl.rel_s[2];
+            g.sfa_slot = sl.nbytes;
+            if (gemm_launch_mx<kND>(pool + sl.rel_v[2], total_slots, sl.nbytes, ws.Cq, R, g, ws.tiles_max, st))
+                return -1;
+        } else {
+            g.sW = (const float *)(pool + sl.rel_s[2]);
+            g.sw_slot = sl.nbytes / 4;
+            if (gemm_launch<kND, false>(pool + sl.rel_v[2], total_slots, sl.nbytes, ws.Cq, R, g, ws.tiles_max,
+                                        st))
+                return -1;
+        }
     }
     }
     // 4: shared expert

@@ -124,6 +124,34 @@ __device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
         ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc) : "memory");
 }
+// Block-scaled instruction descriptor (kind::mxf8f6f4.block_scale, fp32
+// accumulator, both K-major): B scale-factor byte id at bits 4..5, A/B
+// formats at 7..9 / 10..12 (0 E4M3, 5 E2M1), N >> 3 at 17..22, scale format
+// E8M0 at bit 23, M >> 4 at 24..28, A scale-factor byte id at 29..30; K = 32.
+__host__ __device__ constexpr uint32_t idesc_bs(int M, int N, uint32_t afmt, uint32_t bfmt, uint32_t sfid) {
+    return (sfid << 4) | (afmt << 7) | (bfmt << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+           ((uint32_t)(M >> 4) << 24) | (sfid << 29);
+}
+// D[tmem] (+)= (A . sA)[smem] . (B . sB)[smem]^T with UE8M0 scale factors per
+// 32 K-elements read from TMEM (byte `sfid` of each lane's 32-bit word at
+// sfa / sfb, the byte id also in the address's top bits), one instruction.
+__device__ __forceinline__ void mma_mx_bs(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t sfa,
+                                          uint32_t sfb, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p; }"
+        ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(sfa), "r"(sfb) : "memory");
+}
+// The warp's 32 TMEM lanes (its lane quadrant), 4 consecutive 32-bit
+// columns from taddr, all given the value w; tmem_wait_st before relying on it.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t w) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %1, %1, %1};" ::"r"(taddr), "r"(w)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Arrive on *b once every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void commit(uint64_t *b) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(b))

@@ -75,38 +75,6 @@ int orc_f8_gemm_digits(const uint8_t *W, const float *sW, const uint8_t *X, cons
     return 0;
 }
 
-/* An MXFP4 matrix [R][C] (E2M1 nibbles, even index low nibble; E8M0 per
- * 32 along the row) as the GPU prefill's exact FP8 copy: per (row,
- * 128-column block) with sub-block exponents s_j, smax = max s_j, bytes
- * E4M3(E2M1 x 2^(s_j - smax)) and scale 2^(smax - 127). Returns the number
- * of elements not exact in E4M3 (the GPU refuses such a pool). */
-int orc_mxfp4_to_f8rows(const uint8_t *vals, const uint8_t *sc, int R, int C, uint8_t *q, float *s) {
-    int bad = 0;
-    float mag16[16];                                    /* the E2M1 values, via the restated decode */
-    for (int n = 0; n < 16; n++) {
-        uint8_t one[1] = {(uint8_t)(n | (n << 4))}, sone[1] = {127};
-        orc_mxfp4_decode(one, sone, 1, 32, mag16 + n);
-    }
-    for (int r = 0; r < R; r++)
-        for (int b = 0; b < C / 128; b++) {
-            const uint8_t *sr = sc + (int64_t)r * (C / 32) + b * 4;
-            int smax = sr[0];
-            for (int j = 1; j < 4; j++) if (sr[j] > smax) smax = sr[j];
-            if (smax == 255) bad++;
-            s[(int64_t)r * (C / 128) + b] = ldexpf(1.0f, smax - 127);
-            for (int i = 0; i < 128; i++) {
-                const int64_t e = (int64_t)r * C + b * 128 + i;
-                const uint8_t nib = (vals[e >> 1] >> ((e & 1) ? 4 : 0)) & 0xF;
-                const float v = ldexpf(mag16[nib], sr[i / 32] - smax);
-                uint8_t byte = fx_f8_encode(v);
-                if (byte == 0 && signbit(v)) byte = 0x80;
-                if (orc_f8_value(byte) != v) bad++;
-                q[e] = byte;
-            }
-        }
-    return bad;
-}
-
 /* ---- one layer of the GPU batched prefill (prefill.cu), restated ------ */
 
 /* sum over one K block of W[c] (E4M3 bytes) times the digit planes' values
@@ -136,6 +104,29 @@ static float f8_row_dot(const uint8_t *w, const float *sw_row, const uint8_t *co
     return acc;
 }
 
+/* The same for an MXFP4 row (E2M1 nibbles, E8M0 scale per 32): the weights
+ * exactly dequantised (wrow, C floats, from orc_mxfp4_decode), each 128-column
+ * block's sum with each digit plane in double rounded to float (the
+ * block-scaled MMA applies the weights' scales to exact products), the
+ * digits combined as above and acc = fma(v, sX, acc): the weight scale is
+ * already inside the sums. */
+static float mx_row_dot(const float *wrow, const uint8_t *const *xd, const float *sx, int C, int ND) {
+    float acc = 0.0f;
+    for (int kb = 0; kb < C / 128; kb++) {
+        float D[3];
+        for (int d = 0; d < ND; d++) {
+            double sum = 0.0;
+            for (int c = kb * 128; c < kb * 128 + 128; c++) sum += (double)wrow[c] * (double)orc_f8_value(xd[d][c]);
+            D[d] = (float)sum;
+        }
+        float v = D[0];
+        if (ND > 1) v = v + D[1] * 0.0625f;
+        if (ND > 2) v = v + D[2] * 0.00390625f;
+        acc = fmaf(v, 1.0f * sx[kb], acc);
+    }
+    return acc;
+}
+
 /* bf16 hi/lo digits of x */
 static void bf16_digits(float x, float *hi, float *lo) {
     *hi = orc_bf16_to_f32(fx_bf16_rne(x));
@@ -158,14 +149,6 @@ static float bf16_row_dot(const uint16_t *w, const float *hi, const float *lo, i
     return acc;
 }
 
-/* The FP8 view of one expert slot: bytes and scales of gate, up, down, with
- * the scale of row r, 128-column block kb at scale[t][srow(r) * (C/128) + kb]
- * (srow = r / 128 for the FP8 pool's 128x128 blocks, r for row scales). */
-typedef struct F8View {
-    const uint8_t *v[3];
-    const float *s[3];
-    int row_scales;
-} F8View;
 
 int orc_prefill_layer(int fmt, int H, int M, int K, const OrcLayerW *lw, const OrcExpertLayout *lay, int T,
                       float *states, const int *sel, const float *w) {
@@ -181,12 +164,9 @@ int orc_prefill_layer(int fmt, int H, int M, int K, const OrcLayerW *lw, const O
     float *out = (float *)malloc((size_t)K * H * sizeof(float));
     float *hi = (float *)malloc((size_t)H * sizeof(float)), *lo = (float *)malloc((size_t)H * sizeof(float));
     float *so = (float *)malloc((size_t)H * sizeof(float));
-    /* MXFP4: the exact FP8 copy of one slot at a time */
-    uint8_t *cv = fmt == ORC_FMT_MXFP4 ? (uint8_t *)malloc((size_t)3 * M * H) : NULL;
-    float *cs = fmt == ORC_FMT_MXFP4 ? (float *)malloc((size_t)3 * M * (H / 128) * sizeof(float)) : NULL;
-    if (!xin || !xq || !sx || !gu || !ch || !cq || !sc || !out || !hi || !lo || !so) goto done;
-    if (fmt == ORC_FMT_MXFP4 && (!cv || !cs)) goto done;
-    int last_e = -1;                  /* expert whose FP8 copy is in cv / cs */
+    /* MXFP4: one dequantised row (the widest, H or M columns) */
+    float *wrow = (float *)malloc((size_t)(H > M ? H : M) * sizeof(float));
+    if (!xin || !xq || !sx || !gu || !ch || !cq || !sc || !out || !hi || !lo || !so || !wrow) goto done;
     memcpy(xin, states, (size_t)T * H * sizeof(float));
     for (int t = 0; t < T; t++) orc_rmsnorm(lw->norm, H, xin + (int64_t)t * H);
     if (orc_quant_f8_digits(xin, T, H, ND, xq, sx)) goto done;
@@ -199,41 +179,35 @@ int orc_prefill_layer(int fmt, int H, int M, int K, const OrcLayerW *lw, const O
             const int e = sel[(int64_t)t * K + j];
             if (e < 0) continue;
             const uint8_t *slot = lw->experts + (int64_t)e * lay->nbytes;
-            F8View fv;
-            if (fmt == ORC_FMT_MXFP4 && e == last_e) {
-                for (int t2 = 0; t2 < 3; t2++) {
-                    fv.v[t2] = cv + (int64_t)t2 * M * H;
-                    fv.s[t2] = cs + (int64_t)t2 * M * (H / 128);
-                }
-                fv.row_scales = 1;
-            } else if (fmt == ORC_FMT_MXFP4) {
-                last_e = e;
-                for (int t2 = 0; t2 < 3; t2++) {
-                    const int R = t2 < 2 ? M : H, Cc = t2 < 2 ? H : M;
-                    fv.v[t2] = cv + (int64_t)t2 * M * H;
-                    fv.s[t2] = cs + (int64_t)t2 * M * (H / 128);
-                    if (orc_mxfp4_to_f8rows(slot + lay->rel_v[t2], slot + lay->rel_s[t2], R, Cc,
-                                            (uint8_t *)fv.v[t2], (float *)fv.s[t2]) != 0)
-                        goto done;
-                }
-                fv.row_scales = 1;
+            if (fmt == ORC_FMT_MXFP4) {
+                /* gate, up: rows of H nibbles (H / 2 bytes, H / 32 scales) */
+                for (int mat = 0; mat < 2; mat++)
+                    for (int m = 0; m < M; m++) {
+                        orc_mxfp4_decode(slot + lay->rel_v[mat] + (int64_t)m * (H / 2),
+                                         slot + lay->rel_s[mat] + (int64_t)m * (H / 32), H, 32, wrow);
+                        gu[mat * M + m] = mx_row_dot(wrow, xd, sxt, H, ND);
+                    }
             } else {
-                for (int t2 = 0; t2 < 3; t2++) {
-                    fv.v[t2] = slot + lay->rel_v[t2];
-                    fv.s[t2] = (const float *)(slot + lay->rel_s[t2]);
-                }
-                fv.row_scales = 0;
+                for (int mat = 0; mat < 2; mat++)
+                    for (int m = 0; m < M; m++)
+                        gu[mat * M + m] = f8_row_dot(slot + lay->rel_v[mat] + (int64_t)m * H,
+                                                     (const float *)(slot + lay->rel_s[mat]) + (m / 128) * (H / 128),
+                                                     xd, sxt, H, ND);
             }
-            for (int mat = 0; mat < 2; mat++)
-                for (int m = 0; m < M; m++)
-                    gu[mat * M + m] = f8_row_dot(fv.v[mat] + (int64_t)m * H,
-                                                 fv.s[mat] + (fv.row_scales ? m : m / 128) * (H / 128), xd, sxt, H, ND);
             for (int m = 0; m < M; m++) ch[m] = orc_silu_mul(gu[m], gu[M + m]);
             if (orc_quant_f8_digits(ch, 1, M, ND, cq, sc)) goto done;
             const uint8_t *cd[3] = {cq, cq + M, cq + 2 * M};
-            for (int r = 0; r < H; r++)
-                out[(int64_t)j * H + r] = f8_row_dot(fv.v[2] + (int64_t)r * M,
-                                                     fv.s[2] + (fv.row_scales ? r : r / 128) * (M / 128), cd, sc, M, ND);
+            for (int r = 0; r < H; r++) {
+                if (fmt == ORC_FMT_MXFP4) {
+                    orc_mxfp4_decode(slot + lay->rel_v[2] + (int64_t)r * (M / 2),
+                                     slot + lay->rel_s[2] + (int64_t)r * (M / 32), M, 32, wrow);
+                    out[(int64_t)j * H + r] = mx_row_dot(wrow, cd, sc, M, ND);
+                } else {
+                    out[(int64_t)j * H + r] = f8_row_dot(slot + lay->rel_v[2] + (int64_t)r * M,
+                                                         (const float *)(slot + lay->rel_s[2]) + (r / 128) * (M / 128),
+                                                         cd, sc, M, ND);
+                }
+            }
         }
         /* shared expert (bf16 hi/lo digits) and its gate */
         const float *x = xin + (int64_t)t * H;
@@ -263,6 +237,6 @@ int orc_prefill_layer(int fmt, int H, int M, int K, const OrcLayerW *lw, const O
     rc = 0;
 done:
     free(xin); free(xq); free(sx); free(gu); free(ch); free(cq); free(sc); free(out);
-    free(hi); free(lo); free(so); free(cv); free(cs);
+    free(hi); free(lo); free(so); free(wrow);
     return rc;
 }

@@ -30,9 +30,6 @@ struct OrcExpertLayout;
 int orc_prefill_layer(int fmt, int H, int M, int K, const struct OrcLayerW *lw,
                       const struct OrcExpertLayout *lay, int T, float *states, const int *sel, const float *w);
 
-/* An MXFP4 matrix as the GPU prefill's exact FP8 copy (bytes [R][C], row
- * scales [R][C/128]); returns the count of elements not exact in E4M3. */
-int orc_mxfp4_to_f8rows(const uint8_t *vals, const uint8_t *sc, int R, int C, uint8_t *q, float *s);
 
 #ifdef __cplusplus
 }

@@ -116,7 +116,6 @@ def lib():
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]
         L.orc_shared_add.argtypes = [C.POINTER(OrcLayerW), C.c_int, C.c_int, C.c_void_p, C.c_void_p]
-        L.orc_mxfp4_to_f8rows.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_prefill_layer.argtypes = [C.c_int] * 4 + [
             C.POINTER(OrcLayerW), C.POINTER(OrcExpertLayout), C.c_int,
             C.c_void_p, C.c_void_p, C.c_void_p]
@@ -380,13 +379,3 @@ def f8_gemm_digits(W, sW, q, sx):
     Y = np.zeros((N, R), np.float64)
     assert lib().orc_f8_gemm_digits(ptr(W), ptr(sW), ptr(q), ptr(sx), ptr(Y), R, Cc, N, nd) == 0
     return Y
-
-
-def mxfp4_to_f8rows(vals, scales, R, Cc):
-    """An MXFP4 matrix as the GPU prefill's exact FP8 copy: (bytes [R][C],
-    row scales [R][C/128], count of inexact elements)."""
-    q = np.zeros((R, Cc), np.uint8)
-    s = np.zeros((R, Cc // 128), np.float32)
-    bad = lib().orc_mxfp4_to_f8rows(ptr(np.ascontiguousarray(vals, np.uint8)),
-                                    ptr(np.ascontiguousarray(scales, np.uint8)), R, Cc, ptr(q), ptr(s))
-    return q, s, bad

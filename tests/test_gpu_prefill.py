@@ -3,8 +3,10 @@ ds4f_gpu_prefill) against the oracle, through the C ABI.
 
 Two references, both fed the GPU's own weight bytes:
   * orc_prefill_layer -- the GPU prefill's arithmetic restated (the same
-    3-digit E4M3 activations, bf16 hi/lo digits in the shared expert):
-    within 1e-4 of max |acc| (block-sum order and CUDA vs libm exp only);
+    3-digit E4M3 activations, bf16 hi/lo digits in the shared expert; FP8
+    weights with their block scales in the promotion, MXFP4 weights exactly
+    dequantised as the block-scaled MMA reads them): within 1e-4 of max |acc|
+    (block-sum order and CUDA vs libm exp only);
   * orc_moe_batch_sel -- the reference's batched step with fp32
     activations (src/moe.c:1480-1707): within the BASELINE chain tolerance
     2e-3 of max |acc|.
@@ -103,4 +105,38 @@ def test_prefill_stack_two_layers():
     for L in range(NL):
         want = oracle_layer(m, L, sel[L].ravel()).prefill(want, sel[L], w[L])
     assert relerr(got - states, want - states) < OWN_TOL
+    m.close()
+
+
+def test_prefill_mxfp4_wide_exponent_spread():
+    """MXFP4 experts whose four E8M0 sub-block scales in each 128-column block
+    lie up to 14 binades apart (offsets -9, 0, +2, -12 on the synthetic
+    scales): legal MXFP4 that the reference decodes (src/kernels.c:34-62),
+    read by the block-scaled MMA as stored. The layer must match both
+    references as for ordinary pools."""
+    H, M, E, K, T = 1024, 256, 64, 8, 48
+    m = dc.Model(dc.FMT_MXFP4, 1, H, M, E, K)
+    m.synth(31)
+    offs = np.array([-9, 0, 2, -12], np.int16)
+    ends = [m.rel_v[1], m.rel_v[2], m.slot_bytes]
+    for e in range(16):
+        slot = m.get_expert(0, e).copy()
+        for t in range(3):
+            sc = slot[m.rel_s[t]:ends[t]].astype(np.int16)
+            sc = np.clip(sc + np.resize(offs, sc.size), 1, 254)
+            slot[m.rel_s[t]:ends[t]] = sc.astype(np.uint8)
+        m.set_expert(0, e, slot)
+    states = po.fill_f32(T * H, po.key(31, 0, 4, 0, 0), 1.0).reshape(T, H)
+    sel, w = routing(T, K, np.arange(16), seed=4)
+    got = run_layer(m, 0, states, sel, w)
+    lay = oracle_layer(m, 0, sel.ravel(), dc.FMT_MXFP4)
+    sv = lay.experts[sel[0, 0]]
+    spread = np.ptp(sv[m.rel_s[0]:m.rel_v[1]].reshape(-1, 4).astype(int), axis=1)
+    assert spread.max() > 6
+    own = lay.prefill(states, sel, w)
+    ref = lay.moe_batch_sel(states, sel, w)
+    acc = got.astype(np.float64) - states
+    assert np.isfinite(got).all()
+    assert relerr(acc, own - states) < OWN_TOL
+    assert relerr(acc, ref - states) < CHAIN_TOL
     m.close()

@@ -395,17 +395,3 @@ def test_prefill_digits_reconstruct_activations():
     assert err.max() < 2.0 ** -12
     assert (q[:, 0, :128] == 0).all() and (s[0, 0] == 1.0)
     assert np.abs(val[q]).max() <= 240.0          # digits stay where both E4M3 tables agree
-
-
-def test_prefill_mxfp4_fp8_copy_is_exact():
-    """The MXFP4 pool's FP8 copy (E4M3 bytes x per-row 128-block scales)
-    reproduces every dequantised MXFP4 value exactly (oracle/prefill.c)."""
-    R, Cc = 64, 512
-    v, s = po.quant_mxfp4(R, Cc, po.key(31, 0, 3, 0, 0), 0.02)
-    q, rs, bad = po.mxfp4_to_f8rows(v, s, R, Cc)
-    assert bad == 0
-    deq = np.zeros(R * Cc, np.float32)
-    po.lib().orc_mxfp4_decode(po.ptr(v), po.ptr(s), R * Cc, 32, po.ptr(deq))
-    val = np.array([po.lib().orc_f8_value(b) for b in range(256)], np.float64)
-    got = val[q] * np.repeat(rs.astype(np.float64), 128, 1)
-    assert np.array_equal(got.ravel(), deq.astype(np.float64))
