@@ -355,6 +355,7 @@ def decode_config(fp8, world, layers=LAYERS, parallelism=None):
 
 
 N_STAMPS = 20          # phase-trace stamp slots per (layer-step, CTA) in k_decode
+LOOKAHEAD_DEFAULT = 0   # the library's default expert lookahead (experts prefetched ahead)
 PHASES = ["start", "state", "norm", "rows_done", "routes_vis", "topk", "issued",
           "softmax", "grp0", "chains", "down_in", "written"]
 
@@ -413,6 +414,8 @@ def run_gpu(args, rank, world, local_rank):
     model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K)
     model.synth(0)
     model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
+    if args.lookahead is not None:
+        model.set_lookahead(args.lookahead)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(state, H, 0, 0, 4, rank, 0, 1.0)
     torch.cuda.synchronize()
@@ -493,6 +496,7 @@ def run_gpu(args, rank, world, local_rank):
                     "timer": "host clock around the synchronous C-ABI call"},
             "gpu_launches": (4 * layers if args.layered else 1) * args.steps,
             "router_exact_fallbacks": int(fallbacks),
+            "expert_lookahead": LOOKAHEAD_DEFAULT if args.lookahead is None else args.lookahead,
             "clocks": clocks,
         }
         if trace is not None:
@@ -1163,6 +1167,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode / prefill: layers of the stack (fewer: a profiling case, not a bench line)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per chunk")
+    ap.add_argument("--lookahead", type=int, default=None,
+                    help="decode: experts of the next layer prefetched into L2 (0: off; default: the library's)")
     ap.add_argument("--trace", action="store_true",
                     help="decode: print k_decode's per-phase trace (stderr) and add it to the line")
     ap.add_argument("--slots", type=int, default=0,

@@ -69,6 +69,11 @@ __device__ __forceinline__ void bulk(void *dst, const void *src, uint32_t bytes,
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(sa(dst)), "l"(src), "r"(bytes), "r"(sa(b)) : "memory");
 }
+// L2 prefetch of a global range (16-byte aligned address and size): no
+// shared memory, no barrier; the lines are simply warm when a copy comes.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void fence_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -135,8 +140,11 @@ struct Smem {
     static constexpr int o_dsc = o_dn + a16(K * RR * S::drow_b);
     // gate rows then up rows; between uses it receives the tagged-word
     // gathers (state, router logits, chains)
-    static constexpr int GATH = 8 * ((H > 4 * E ? H : 4 * E) > (K + 1) * M + 2
-                                         ? (H > 4 * E ? H : 4 * E) : (K + 1) * M + 2);
+    // (the chain gather: (K+1) M chain words, the shared-gate logit, a pad
+    // word, then E lookahead logits of the next layer)
+    static constexpr int NCWP = (K + 1) * M + 2;
+    static constexpr int GATH = 8 * ((H > 4 * E ? H : 4 * E) > NCWP + E
+                                         ? (H > 4 * E ? H : 4 * E) : NCWP + E);
     // + the chains unpacked to floats after the tagged words
     static constexpr int UNP = GATH + 4 * ((K + 1) * M + 4);
     // + the next layer's shared gate/up rows and the shared-gate row, past
@@ -157,7 +165,8 @@ struct Smem {
     static constexpr int o_tk = o_red + 1024;                         // [E] doubles
     static constexpr int o_cand = o_tk + a16(E * 8);                  // [E] ints
     static constexpr int o_sel = o_cand + a16(E * 4);                 // sel[64], wsel[64], ctl[16]
-    static constexpr int bytes = o_sel + 64 * 4 + 64 * 4 + 16 * 4;
+    static constexpr int o_xr = a16(o_sel + 64 * 4 + 64 * 4 + 16 * 4); // [H] bf16 x / r (lookahead)
+    static constexpr int bytes = o_xr + H * 2;
 };
 
 struct DecodeArgs {
@@ -173,10 +182,12 @@ struct DecodeArgs {
     long rounds;                // copy rounds of a tagged-word gather before giving up
     int stall_cta, stall_t;     // test hook: this CTA withholds its state words
                                 // at this layer-step (-1: off)
+    int lookahead;              // L2 prefetch of the next layer's predicted experts
     float *state;               // [H] in (read at layer 0) / out (last layer)
     uint64_t *st_ll;            // [H] tagged state words
     uint64_t *sb_ll;            // [E][4] tagged words: S, its interval's ends (fp32), 0
-    uint64_t *ch_ll;            // [(K+1) M + 1] tagged chains, then the shared-gate logit
+    uint64_t *ch_ll;            // [(K+1) M + 2 + E] tagged chains, the shared-gate logit, a
+                                // pad word, the next layer's lookahead logits
     unsigned *diag;             // [4]: layers, fallbacks, error code, failing CTA
     unsigned long long *trace;  // optional [T][G][kTracePts] %globaltimer stamps
     int *log_idx;               // optional route log, layer-steps t < log_n:
@@ -266,6 +277,7 @@ k_decode(DecodeArgs a) {
     int *sel = (int *)(sm + L::o_sel);
     float *wsel = (float *)(sel + 64);
     int *ctl = (int *)(wsel + 64);
+    uint16_t *xr16 = (uint16_t *)(sm + L::o_xr);      // x / r as bf16 (the lookahead's input)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, c = blockIdx.x;
@@ -282,6 +294,7 @@ k_decode(DecodeArgs a) {
 #define FLIP(i) (phb ^= 1u << (i))
 #define PEND(i, v) (pendb = (v) ? (pendb | (1u << (i))) : (pendb & ~(1u << (i))))
     bool ok = true;
+    bool rt_early = false;      // bar 0 (this layer's router rows) consumed by the lookahead
 
     if (tid == 0) {
         for (int i = 0; i < 9; i++) mbar_init(bar + i, 1);
@@ -385,6 +398,7 @@ k_decode(DecodeArgs a) {
     for (int t = 0; t < T; t++) {
         const int l = t % a.n_layers, ln = (t + 1) % a.n_layers;
         const bool more = t + 1 < T;
+        const bool pred = a.lookahead > 0 && more;   // this layer predicts the next one's experts
         const uint32_t tg = tag_of(t);            // words this layer publishes
         DS4F_TRACE(0);
         // (A) input state: PER words per thread
@@ -427,12 +441,16 @@ k_decode(DecodeArgs a) {
                 rd[16] = s2;
             }
             // (B) norm weights arrive with the router rows (bar 0)
-            bool okb = mbar_wait(a, bar + 0, PH(0), 2);
+            bool okb = rt_early || mbar_wait(a, bar + 0, PH(0), 2);
             if (!__syncthreads_and(okb)) { ok = false; break; }
-            FLIP(0); PEND(0, false);
+            if (!rt_early) { FLIP(0); PEND(0, false); }
+            rt_early = false;
             float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(rd[16], (double)H)), 1e-6f));
-            for (int i = tid; i < H; i += kThreads)
-                xin[i] = __fmul_rn(__fdiv_rn(xin[i], r), bf16_to_f32(nw[i]));
+            for (int i = tid; i < H; i += kThreads) {
+                const float xq = __fdiv_rn(xin[i], r);
+                if (pred) xr16[i] = bf16_bits_rn(xq);
+                xin[i] = __fmul_rn(xq, bf16_to_f32(nw[i]));
+            }
             __syncthreads();
         }
         DS4F_TRACE(2);
@@ -524,7 +542,10 @@ k_decode(DecodeArgs a) {
             }
             acc = warp_sum(acc);
             if (lane == 0 && okd) {
-                if (gl) st_tag(a.ch_ll + (K + 1) * M, tg, __float_as_uint(acc));
+                if (gl) {
+                    st_tag(a.ch_ll + (K + 1) * M, tg, __float_as_uint(acc));
+                    st_tag(a.ch_ll + (K + 1) * M + 1, tg, 0u);     // the pad word
+                }
                 else red[192 + w2] = acc;       // bytes 768..: clear of rd[0..63]
             }
         }
@@ -713,6 +734,7 @@ k_decode(DecodeArgs a) {
             }
         }
         DS4F_TRACE(7);
+        bool okla = true;
         // (H) gate/up: warp w -> pair w % 8 of every group, gate and up
         //     rows over column half w / 8 (the two halves meet in red[]);
         //     each warp takes a group as soon as it has landed (its own wait,
@@ -791,11 +813,48 @@ k_decode(DecodeArgs a) {
                                                 red[2 * tid + 1] + red[HALF + 2 * tid + 1])));
                 publish_flush();
             }
+            // lookahead (a prefetch hint, never a routing input): this CTA's
+            // router rows of the next layer, landed on bar 0 with their norm
+            // weights, on this layer's x / r (bf16) -- warps 1 .. nrt one row
+            // each, fp32 sums, published beside the chains
+            if (pred) {
+                // (warp 1 waits even without a router row: the norm weights
+                // ride on bar 0 too, and the next layer skips its wait)
+                if (warp >= 1 && warp <= max(nrt, 1)) {
+                    okla = mbar_wait(a, bar + 0, PH(0), 2);
+                    if (okla && warp <= nrt) {
+                        const uint16_t *row = rt + (warp - 1) * H;
+                        float acc = 0.f;
+                        static_assert(H % 256 == 0, "lookahead rows: whole 8-element chunks per lane");
+#pragma unroll
+                        for (int k = lane; k < H / 8; k += 32) {
+                            const uint4 w8 = lds16(row + 8 * k), x8 = lds16(xr16 + 8 * k), n8 = lds16(nw + 8 * k);
+                            auto dot2 = [](uint32_t w, uint32_t x, uint32_t n, float acc) {
+                                acc = fmaf(__uint_as_float(w << 16),
+                                           __uint_as_float(x << 16) * __uint_as_float(n << 16), acc);
+                                return fmaf(__uint_as_float(w & 0xFFFF0000u),
+                                            __uint_as_float(x & 0xFFFF0000u) * __uint_as_float(n & 0xFFFF0000u), acc);
+                            };
+                            acc = dot2(w8.x, x8.x, n8.x, acc);
+                            acc = dot2(w8.y, x8.y, n8.y, acc);
+                            acc = dot2(w8.z, x8.z, n8.z, acc);
+                            acc = dot2(w8.w, x8.w, n8.w, acc);
+                        }
+                        acc = warp_sum(acc);
+                        if (lane == 0) {
+                            st_tag(a.ch_ll + L::NCWP + rt0 + warp - 1, tg, __float_as_uint(acc));
+                            publish_flush();
+                        }
+                    }
+                }
+                FLIP(0); PEND(0, false);
+                rt_early = true;
+            }
         }
         DS4F_TRACE(9);
         // (I) down rows: routed (bar 6) and shared (bar 1); chains polled
         {
-            const bool okd = mbar_wait(a, bar + 6, PH(6), 6) && mbar_wait(a, bar + 1, PH(1), 7);
+            const bool okd = okla && mbar_wait(a, bar + 6, PH(6), 6) && mbar_wait(a, bar + 1, PH(1), 7);
             if (!__syncthreads_and(okd)) { ok = false; break; }
             FLIP(6); PEND(6, false);
             FLIP(1); PEND(1, false);
@@ -804,9 +863,12 @@ k_decode(DecodeArgs a) {
             // into shared memory, over the gate/up rows (H) is done with
             // (K+1) M chain words + the logit, copied as an even count (the
             // workspace allocation is padded past the last word)
+            // With the lookahead, also the pad word and the next layer's E
+            // lookahead logits.
             constexpr int NCW = (K + 1) * M + 1;
-            if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.ch_ll, (NCW + 1) / 2 * 2,
-                           NCW, tg, 5, DS4F_ROUNDS(16))) {
+            static_assert(L::NCWP == NCW + 1 && L::NCWP % 2 == 0 && E % 2 == 0, "even gathers");
+            if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.ch_ll, pred ? L::NCWP + E : L::NCWP,
+                           pred ? L::NCWP + E : NCW, tg, 5, DS4F_ROUNDS(16))) {
                 ok = false;
                 break;
             }
@@ -819,8 +881,41 @@ k_decode(DecodeArgs a) {
                     chf[i] = i < K * M ? v * DS4F_X_PRESCALE : v;
                 }
             }
+            // lookahead: the maxima of 32 groups of E / 32 experts
+            uint32_t *gmax = (uint32_t *)(red + 224);
+            constexpr int LG = E / 32;
+            static_assert(E % 32 == 0 && (LG & (LG - 1)) == 0 && E <= 256, "32 lookahead groups");
+            uint32_t lkey = 0u;
+            if (pred && tid < E) {
+                lkey = tk_key(__uint_as_float((uint32_t)((const uint64_t *)gu)[L::NCWP + tid]), tid);
+                const unsigned gm = LG == 32 ? 0xFFFFFFFFu : (((1u << LG) - 1u) << (lane & ~(LG - 1)));
+                const uint32_t mx = __reduce_max_sync(gm, lkey);
+                if ((lane & (LG - 1)) == 0) gmax[tid / LG] = mx;
+            }
             __syncthreads();
             DS4F_TRACE(12);
+            // lookahead: the a.lookahead-th largest group maximum bounds the
+            // next layer's predicted top-a.lookahead from below; every expert
+            // at or above it gets this CTA's 1/G of its slot prefetched into
+            // L2, where the next layer's copies of it will find it (HBM idles
+            // from here to the next layer's routing)
+            if (pred && tid < E) {
+                uint32_t v = gmax[lane];
+#pragma unroll
+                for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+                    for (int j = k >> 1; j > 0; j >>= 1) {
+                        const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, v, j);
+                        v = (((lane & k) == 0) == ((lane & j) == 0)) ? max(v, o) : min(v, o);
+                    }
+                const uint32_t tau = __shfl_sync(0xFFFFFFFFu, v, min(a.lookahead, 32) - 1);
+                if (lkey >= tau) {
+                    const int64_t sb = a.slot_bytes;
+                    const int64_t o0 = ((int64_t)c * sb / G) & ~(int64_t)15;
+                    const int64_t o1 = (c == G - 1 ? sb : (int64_t)(c + 1) * sb / G) & ~(int64_t)15;
+                    if (o1 > o0) prefetch_l2(expert(ln, tid) + o0, (uint32_t)(o1 - o0));
+                }
+            }
             // row-dot d: selection d / nr (K = the shared expert), output row
             // d % nr. Warp w takes a contiguous range of dots, keeps the
             // chain's floats of its current selection in registers and runs
@@ -964,6 +1059,7 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     a.rounds = std::max(16L, a.spin / 16);
     a.stall_cta = m->stall_cta;
     a.stall_t = m->stall_t;
+    a.lookahead = m->lookahead;
     DS4F_CUDA(cudaMemsetAsync(m->w.diag + 2, 0, 2 * sizeof(unsigned), st));
     // tags carry 16 bits of layer-step: split long runs into launches
     const int per = std::max(1, 65000 / m->d.n_layers);
@@ -999,6 +1095,7 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
 bool decode_eligible(const Model *m) {
     const ModelDesc &d = m->d;
     if (d.expert_count != d.n_experts || d.topk != 8 || m->cache) return false;
+    if (m->slot.nbytes % 16) return false;       // every slot 16-byte aligned (bulk copies)
     if (!((d.hidden == 2048 && d.moe_inter == 512) || (d.hidden == 1024 && d.moe_inter == 256)))
         return false;
     return d.n_experts == 256 || d.n_experts == 64;

@@ -397,7 +397,9 @@ k_gemm_p(const __grid_constant__ CUtensorMap tW, const __grid_constant__ CUtenso
             for (int i = blockIdx.x; ok && p_item(g, i, n_items, RT, MT, it); i += gridDim.x) {
                 const CUtensorMap *tA = it.mat ? &tW2 : &tW;
                 const CUtensorMap *tB = it.w == 16 ? &tX16 : it.w == 32 ? &tX32 : it.w == 48 ? &tX48 : &tX64;
-                const uint32_t bytes = L::A + ND * it.w * 128;
+                // a 4-bit A tile lands unpacked (16 KB of shared memory) but
+                // its transaction counts the 8 KB read
+                const uint32_t bytes = (MX ? L::A / 2 : L::A) + ND * it.w * 128;
                 for (int kb = 0; kb < KB; kb++, k++) {
                     const int s = k % kPStages;
                     if (k >= kPStages && !tc::mbar_wait(empty + s, ((k / kPStages) - 1) & 1, err, 1)) {

@@ -327,6 +327,18 @@ int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
  * ("decode kernel gave up waiting (code C at CTA N)"); the model stays
  * usable. 0 restores the default, 2^24 polls (about a second). */
 int  ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *m, int64_t polls);
+/* Expert lookahead of the persistent decode path (no reference counterpart;
+ * the reference reads each expert when its layer routes to it,
+ * src/moe.c:598-753): while layer l runs, the next layer's router rows are
+ * applied to layer l's normalised state and the experts whose predicted
+ * logits reach the n-th largest of 32 group maxima (n or a few more) are
+ * prefetched into L2, 1/G of each slot by each CTA, in the stretch where
+ * HBM idles (the exchanges, the norm and the router). A hint only: the
+ * routing itself is certified on each layer's own state, so results are
+ * identical for every n. 0 turns it off (the default: measured on B200,
+ * the gate/up phase is bound by the dequantising dot products, not by the
+ * bytes' arrival, so the prefetch only adds traffic); n <= 32. */
+int  ds4f_gpu_model_set_lookahead(Ds4fGpuModel *m, int n_experts);
 /* Failure injection for tests (no reference counterpart): in the following
  * persistent launches CTA `cta` does not publish its rows of the state at
  * layer-step `layer_step` of a launch (0 = the first layer of its first
