@@ -354,7 +354,7 @@ def decode_config(fp8, world, layers=LAYERS, parallelism=None):
             "parallelism": parallelism or ("single GPU" if world == 1 else f"replicas x{world}")}
 
 
-N_STAMPS = 20          # phase-trace stamp slots per (layer-step, CTA) in k_decode
+N_STAMPS = 28          # phase-trace stamp slots per (layer-step, CTA) in k_decode
 LOOKAHEAD_DEFAULT = 0   # the library's default expert lookahead (experts prefetched ahead)
 PHASES = ["start", "state", "norm", "rows_done", "routes_vis", "topk", "issued",
           "softmax", "grp0", "chains", "down_in", "written"]
@@ -380,6 +380,20 @@ def phase_table(tr):
                      float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
     inner = np.diff(tr[:, :, [3, 18, 4]], axis=2)
     for k, name in enumerate(["routes: gather", "routes: top-K"]):
+        rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
+                     float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
+    # gate/up: groups landing and dots finishing, as offsets from the softmax
+    # (stamp 7); down: warp 0's first row-dot pair and the rest
+    for k, name in [(8, "gate/up: group 0 landed"), (21, "gate/up: group 1 landed"),
+                    (22, "gate/up: group 2 landed"), (23, "gate/up: group 3 landed"),
+                    (24, "gate/up: warp 0 dots done"), (25, "gate/up: all warps done"),
+                    (9, "gate/up: chains published")]:
+        off = (tr[:, :, k] - tr[:, :, 7]).astype(np.float64)
+        ok = tr[:, :, k] > 0
+        if ok.any():
+            rows.append(("  +" + name, float(np.median(off[ok]) / 1e3), float(np.median(np.max(np.where(ok, off, 0), axis=1)) / 1e3)))
+    inner = np.diff(tr[:, :, [12, 26, 13]], axis=2)
+    for k, name in enumerate(["down: first row-dot pair", "down: other row-dots"]):
         rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
                      float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
     out["phases_us"] = rows

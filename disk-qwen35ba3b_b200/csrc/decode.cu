@@ -43,7 +43,7 @@ constexpr int kGroupPairs = 8;             // gate/up pairs per copy group
 constexpr int kGroups = 4;
 constexpr long kSpin = 1L << 24;           // default polls (with backoff) before giving up
 constexpr double kU = 5.9604644775390625e-08;
-constexpr int kTracePts = 20;
+constexpr int kTracePts = 28;
 
 // ---- PTX helpers ------------------------------------------------------------
 __device__ __forceinline__ uint32_t sa(const void *p) {
@@ -332,17 +332,17 @@ k_decode(DecodeArgs a) {
         mbar_expect(bar + 1, b);
         if (b) bulk(sd, trunk_l(l) + a.tr.sh_down + (int64_t)r0 * M, b, bar + 1);
     };
-    // Copies are issued one per lane: a bulk copy holds its issuing thread
-    // for ~160 ns whatever its size, while a warp's lanes together get one
-    // accepted every ~40 ns.
-    // Lane (g, k) of warp 0, g = lane / 8: copy k of gate/up group g of
-    // layer l (bar 2 + g). A group is <= 2 segments (one per expert), each
-    // gate rows (k & 3 == 0), up rows (1), gate scales (2), up scales (3).
-    auto issue_group_lane = [&](int l, int lane) {
-        const int g = lane >> 3, sg = (lane >> 2) & 1, kind = lane & 3;
+    // Copies are issued two or three per warp by every warp: a warp's
+    // lanes get one bulk copy accepted every ~57 cycles whatever its size,
+    // while different warps issue side by side (32 copies: ~1,840 cycles
+    // from one warp, ~400-800 from sixteen, measured on B200).
+    // Copy k of gate/up group g of layer l (bar 2 + g), for
+    // L = 8 g + k: a group is <= 2 segments (one per expert), each gate
+    // rows (k & 3 == 0), up rows (1), gate scales (2), up scales (3).
+    // Thread g of warp 0 sets group g's byte count first (expect_groups).
+    auto expect_groups = [&](int g) {
         const int q0 = p0 + g * kGroupPairs, q1 = min(q0 + kGroupPairs, p0 + np);
-        const int split = min(q1, (q0 / M + 1) * M);
-        if (g < ngroups && (lane & 7) == 0) {
+        if (g < ngroups) {
             uint32_t total = 0;
             for (int q = q0; q < q1;) {
                 int i0 = q % M, n = min(q1 - q, M - i0);
@@ -351,7 +351,11 @@ k_decode(DecodeArgs a) {
             }
             mbar_expect(bar + 2 + g, total);
         }
-        __syncwarp();                        // every lane: expects before copies
+    };
+    auto issue_group_copy = [&](int l, int L) {
+        const int g = L >> 3, sg = (L >> 2) & 1, kind = L & 3;
+        const int q0 = p0 + g * kGroupPairs, q1 = min(q0 + kGroupPairs, p0 + np);
+        const int split = min(q1, (q0 / M + 1) * M);
         if (g >= ngroups) return;
         const int qa = sg == 0 ? q0 : split, qb = sg == 0 ? split : q1;
         if (qa >= qb) return;
@@ -370,12 +374,12 @@ k_decode(DecodeArgs a) {
     const int sa0 = FMT == DS4F_FMT_FP8 ? 0 : (r0 * S::dsc_b) / 16 * 16;
     const int sab = FMT == DS4F_FMT_FP8 ? S::dsc_b : ((r0 + nr) * S::dsc_b + 15) / 16 * 16 - sa0;
     const uint32_t dn_total = K * (nr * S::drow_b + sab);
-    // lane 2 j + h < 2 K of warp 1: down rows (h = 0) or scales (h = 1) of
+    // copy 2 j + h < 2 K: down rows (h = 0) or scales (h = 1) of
     // selection j (bar 6)
-    auto issue_down_lane = [&](int l, int lane) {
-        const int j = lane >> 1;
+    auto issue_down_copy = [&](int l, int L) {
+        const int j = L >> 1;
         const uint8_t *ex = expert(l, sel[j]);
-        if ((lane & 1) == 0) {
+        if ((L & 1) == 0) {
             if (nr)
                 bulk(dn + j * L::RR * S::drow_b, ex + a.slot.rel_v[2] + (int64_t)r0 * S::drow_b,
                      nr * S::drow_b, bar + 6);
@@ -621,12 +625,15 @@ k_decode(DecodeArgs a) {
             if (cert && lane < K) sel[lane] = er;
             if (lane == 0) ctl[1] = cert ? 1 : 0;
             if (cert) {
-                // the routing is final: the gate/up copies start now (their
-                // buffers' last readers, the previous layer's gate/up and this
-                // warp's look at the router words, are done)
+                // the routing is final: the byte counts of this layer's
+                // copies, then group 0's copies at once (the other groups
+                // follow from the other warps after the barrier below, the
+                // down rows after group 0's dots: the first group lands first)
                 __syncwarp();
-                fence_async();
-                issue_group_lane(l, lane);
+                if (lane < kGroups) expect_groups(lane);
+                if (lane == kGroups) mbar_expect(bar + 6, dn_total);
+                __syncwarp();
+                if (lane < 8) { fence_async(); issue_group_copy(l, lane); }
             }
         }
         // ctl[] is read after the barrier (a __syncthreads_and predicate
@@ -663,27 +670,30 @@ k_decode(DecodeArgs a) {
             }
             if (tid == 0 && !a.exact_all && c == 0) atomicAdd(a.diag + 1, 1u);
             __syncthreads();
+            if (tid < kGroups) expect_groups(tid);
+            if (tid == kGroups) mbar_expect(bar + 6, dn_total);
+            __syncthreads();
+            if (tid < 8) { fence_async(); issue_group_copy(l, tid); }
         }
         DS4F_TRACE(5);
-        // (G) every routed byte of this CTA in flight, one copy per lane:
-        //     warp 0 the gate/up groups (already at the top-8 when it
-        //     certified), warp 1 the down rows, warp 2 the next
-        //     layer's router rows + norm weights (buffers (B) and (C) are
-        //     done with). Meanwhile the other warps load their x registers
-        //     and the last warp takes the softmax alone.
-        static_assert(kGroups * 8 <= 32 && 2 * K <= 32, "one copy per lane");
-        if (warp == 0) {
-            if (!ctl[1]) {           // after the exact fallback (certified: issued above)
-                fence_async();
-                issue_group_lane(l, lane);
-            }
-        } else if (warp == 1) {
+        // (G) the gate/up copies of groups 1.. (group 0's went out with the
+        //     routing): warp w >= 1 issues copies 8 + 2 (w - 1) + (0, 1)
+        //     (lanes 0, 1); the last warp also the next layer's router rows +
+        //     norm weights (buffers (B) and (C) are done with). Their last
+        //     readers (the previous layer's gate/up, the top-k's look at the
+        //     router words) are ordered by the barriers above. The down copies
+        //     go out after group 0's dots (every warp's lane 2, copy w), or
+        //     here when the CTA has no gate/up pairs.
+        static_assert(kGroups * 8 <= 8 + 2 * (kWarps - 1) && 2 * K == kWarps, "copy roles");
+        if (warp >= 1 && lane < 2 && 8 + 2 * (warp - 1) + lane < kGroups * 8) {
             fence_async();
-            if (lane == 0) mbar_expect(bar + 6, dn_total);
-            __syncwarp();
-            if (lane < 2 * K) issue_down_lane(l, lane);
-        } else if (warp == 2) {
-            if (lane == 0 && more) { fence_async(); prefetch_rt(ln); }
+            issue_group_copy(l, 8 + 2 * (warp - 1) + lane);
+        } else if (lane == 2 && ngroups == 0) {
+            fence_async();
+            issue_down_copy(l, warp);
+        } else if (lane == 3 && warp == kWarps - 1 && more) {
+            fence_async();
+            prefetch_rt(ln);
         }
 #pragma unroll
         for (int g = 0; g < kGroups; g++) PEND(2 + g, g < ngroups);
@@ -750,7 +760,11 @@ k_decode(DecodeArgs a) {
             for (int g = 0; g < ngroups; g++) {
                 okg = mbar_wait(a, bar + 2 + g, PH(2 + g), 4);
                 if (!okg) break;
-                if (g == 0) DS4F_TRACE(8);
+                if (g == 0) {
+                    DS4F_TRACE(8);
+                } else {
+                    DS4F_TRACE(20 + g);
+                }
                 // rows past the CTA's pairs read slot 0 and are dropped
                 const int q0 = p0 + g * kGroupPairs;
                 const bool valid = ps < min(kGroupPairs, p0 + np - q0);
@@ -796,8 +810,11 @@ k_decode(DecodeArgs a) {
                     red[((hcol * kGroups + g) * kGroupPairs + ps) * 2] = ag;
                     red[((hcol * kGroups + g) * kGroupPairs + ps) * 2 + 1] = au;
                 }
+                if (g == 0 && lane == 2) { fence_async(); issue_down_copy(l, warp); }
             }
+            DS4F_TRACE(24);
             if (!__syncthreads_and(okg)) { ok = false; break; }
+            DS4F_TRACE(25);
 #pragma unroll
             for (int g = 0; g < kGroups; g++)
                 if (g < ngroups) { FLIP(2 + g); PEND(2 + g, false); }
@@ -916,20 +933,38 @@ k_decode(DecodeArgs a) {
                     if (o1 > o0) prefetch_l2(expert(ln, tid) + o0, (uint32_t)(o1 - o0));
                 }
             }
-            // row-dot d: selection d / nr (K = the shared expert), output row
-            // d % nr. Warp w takes a contiguous range of dots, keeps the
-            // chain's floats of its current selection in registers and runs
-            // two rows of that selection at once. Lane l reads the row's
-            // granules 32 g + l and the chain's matching floats (16-byte
-            // reads, consecutive lanes consecutive addresses).
-            constexpr int XC = S::dg * S::gb > 4 * S::bn ? S::dg * S::gb : 4 * S::bn;
-            float xc[XC];
-            auto row_dot = [&](int j, int rr) -> float {
-                if (j < K) {
-                    const uint8_t *row = dn + (j * L::RR + rr) * S::drow_b;
+            // row-dots: warp w takes up to 8 of the CTA's output rows of
+            // routed selection w / 2 (rows [(w & 1) hr, ...), hr = ceil(nr / 2))
+            // and shared-expert row w. Lane l reads granules 32 g + l of each
+            // row against the chain's matching floats, held in registers; the
+            // 8 rows' lane partials then meet in one butterfly (9 shuffles for
+            // 8 sums), the shared row's in a warp sum.
+            static_assert(kWarps == 2 * K && L::RR <= 16 && L::RR <= kWarps, "row-dot warp roles");
+            constexpr int XC = S::dg * S::gb;
+            static_assert(4 * S::bn <= 16 && XC <= 16, "at most 16 chain floats per lane");
+            {
+                const int jw = warp >> 1, hr = (nr + 1) >> 1;
+                const int rw0 = (warp & 1) * hr, nrw = min(hr, nr - rw0);
+                float xc[XC], xs[4 * S::bn];
+#pragma unroll
+                for (int g = 0; g < S::dg; g++)
+#pragma unroll
+                    for (int u = 0; u < S::gb; u += 4) {
+                        const float4 v4 = *(const float4 *)(chf + jw * M + (32 * g + lane) * S::gb + u);
+                        xc[g * S::gb + u] = v4.x; xc[g * S::gb + u + 1] = v4.y;
+                        xc[g * S::gb + u + 2] = v4.z; xc[g * S::gb + u + 3] = v4.w;
+                    }
+#pragma unroll
+                for (int g = 0; g < S::bn; g++) {
+                    const float4 v4 = *(const float4 *)(chf + K * M + 4 * (32 * g + lane));
+                    xs[4 * g] = v4.x; xs[4 * g + 1] = v4.y; xs[4 * g + 2] = v4.z; xs[4 * g + 3] = v4.w;
+                }
+                // the lane partial of routed row rr of selection jw
+                auto row_part = [&](int rr) -> float {
+                    const uint8_t *row = dn + (jw * L::RR + rr) * S::drow_b;
                     if constexpr (FMT == DS4F_FMT_FP8) {
                         // granule g lies in column block g
-                        const float *sc = (const float *)(dsc + j * L::DSC) + ((r0 + rr) >> 7) * (M / 128);
+                        const float *sc = (const float *)(dsc + jw * L::DSC) + ((r0 + rr) >> 7) * (M / 128);
                         float2 a2 = make_float2(0.f, 0.f);
 #pragma unroll
                         for (int g = 0; g < S::dg; g++)
@@ -938,7 +973,7 @@ k_decode(DecodeArgs a) {
                                          make_float2(xc[4 * g + 2], xc[4 * g + 3]), sc[g], a2);
                         return (a2.x + a2.y) * DS4F_X_UNSCALE;
                     } else {
-                        const uint8_t *s4 = dsc + j * L::DSC + (r0 + rr) * S::dsc_b - sa0;
+                        const uint8_t *s4 = dsc + jw * L::DSC + (r0 + rr) * S::dsc_b - sa0;
                         float v = 0.f;
 #pragma unroll
                         for (int g = 0; g < S::dg; g++) {
@@ -948,52 +983,42 @@ k_decode(DecodeArgs a) {
                         }
                         return v * DS4F_E2M1_POST;
                     }
+                };
+                float pv[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) pv[i] = i < nrw ? row_part(rw0 + i) : 0.f;
+                float sh = 0.f;
+                if (warp < nr) {
+                    const uint16_t *row = sd + warp * M;
+#pragma unroll
+                    for (int g = 0; g < S::bn; g++)
+                        sh += bf16_dot4(*(const uint2 *)(row + 4 * (32 * g + lane)),
+                                        make_float4(xs[4 * g], xs[4 * g + 1], xs[4 * g + 2], xs[4 * g + 3]));
                 }
-                const uint16_t *row = sd + rr * M;
-                float v = 0.f;
+                if (warp == 0) DS4F_TRACE(26);
+                // butterfly: after the step at offset 16 a lane holds 4 rows'
+                // partials (bit 4 picks the half), at 8 two, at 4 one; offsets
+                // 2 and 1 finish that row's sum, row = 4 b4 + 2 b3 + b2
+                const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+                float w4[4];
 #pragma unroll
-                for (int g = 0; g < S::bn; g++)
-                    v += bf16_dot4(*(const uint2 *)(row + 4 * (32 * g + lane)),
-                                   make_float4(xc[4 * g], xc[4 * g + 1], xc[4 * g + 2], xc[4 * g + 3]));
-                return v;
-            };
-            const int ndots = (K + 1) * nr;
-            const int d0 = warp * ndots / kWarps, d1 = (warp + 1) * ndots / kWarps;
-            int jcur = -1;
-            for (int d = d0; d < d1;) {
-                const int j = d / nr, rr = d % nr;
-                if (j != jcur) {
-                    jcur = j;
-                    if (j < K) {
-#pragma unroll
-                        for (int g = 0; g < S::dg; g++)
-#pragma unroll
-                            for (int u = 0; u < S::gb; u += 4) {
-                                const float4 v4 = *(const float4 *)(chf + j * M + (32 * g + lane) * S::gb + u);
-                                xc[g * S::gb + u] = v4.x; xc[g * S::gb + u + 1] = v4.y;
-                                xc[g * S::gb + u + 2] = v4.z; xc[g * S::gb + u + 3] = v4.w;
-                            }
-                    } else {
-#pragma unroll
-                        for (int g = 0; g < S::bn; g++) {
-                            const float4 v4 = *(const float4 *)(chf + K * M + 4 * (32 * g + lane));
-                            xc[4 * g] = v4.x; xc[4 * g + 1] = v4.y; xc[4 * g + 2] = v4.z; xc[4 * g + 3] = v4.w;
-                        }
-                    }
+                for (int i = 0; i < 4; i++) {
+                    const float r = __shfl_xor_sync(0xFFFFFFFFu, b4 ? pv[i] : pv[i + 4], 16);
+                    w4[i] = (b4 ? pv[i + 4] : pv[i]) + r;
                 }
-                const bool two = d + 1 < d1 && rr + 1 < nr;
-                float v0 = row_dot(j, rr);
-                float v1 = two ? row_dot(j, rr + 1) : 0.f;
+                float w2[2];
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    v0 += __shfl_xor_sync(0xFFFFFFFFu, v0, o);
-                    v1 += __shfl_xor_sync(0xFFFFFFFFu, v1, o);
+                for (int i = 0; i < 2; i++) {
+                    const float r = __shfl_xor_sync(0xFFFFFFFFu, b3 ? w4[i] : w4[i + 2], 8);
+                    w2[i] = (b3 ? w4[i + 2] : w4[i]) + r;
                 }
-                if (lane == 0) {
-                    outs[j * L::RR + rr] = v0;
-                    if (two) outs[j * L::RR + rr + 1] = v1;
-                }
-                d += two ? 2 : 1;
+                float z = (b2 ? w2[1] : w2[0]) + __shfl_xor_sync(0xFFFFFFFFu, b2 ? w2[0] : w2[1], 4);
+                z += __shfl_xor_sync(0xFFFFFFFFu, z, 2);
+                z += __shfl_xor_sync(0xFFFFFFFFu, z, 1);
+                sh = warp_sum(sh);
+                const int slot = (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0);
+                if ((lane & 3) == 0 && slot < nrw) outs[jw * L::RR + rw0 + slot] = z;
+                if (lane == 0 && warp < nr) outs[K * L::RR + warp] = sh;
             }
             DS4F_TRACE(13);
             if (tid == 0) red[0] = sigmoid_ref(chf[(K + 1) * M]);

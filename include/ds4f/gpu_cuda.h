@@ -292,15 +292,17 @@ int  ds4f_gpu_moe_layer_partial_dev(Ds4fGpuModel *m, int layer, const float *sta
 int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
 /* Phase trace of the persistent decode kernel (the counterpart of the
  * reference's per-phase timers, src/main.c:253-258, 1522-1546): with
- * n_stamps > 0 every launch whose layers x steps x SMs x 20 stamps fit
- * records %globaltimer (ns) per (layer-step, CTA) in 20 slots, of which
+ * n_stamps > 0 every launch whose layers x steps x SMs x 28 stamps fit
+ * records %globaltimer (ns) per (layer-step, CTA) in 28 slots, of which
  * 0..13 are used: start, state ready, normed, router rows done, routes
  * visible, top-k done, copies issued, softmax done, first gate/up group
  * landed, chains done, down rows landed, state written (11), chains
  * gathered (12), row-dots done (13); 14..16 hold the copy rounds of the
  * state, router-logit and chain gathers, 17 a bitmask of the gate/up copy
  * groups that had landed before their compute, 18 the time every router
- * word was visible (before the top-k).
+ * word was visible (before the top-k), 21..23 gate/up copy groups 1..3
+ * landed, 24 the gate/up dots of warp 0 done, 25 every warp's done, 26 the
+ * first down row-dot of warp 0 done.
  * n_stamps = 0 turns it off. */
 int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
 int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
