@@ -360,7 +360,7 @@ PHASES = ["start", "state", "norm", "rows_done", "routes_vis", "topk", "issued",
           "softmax", "grp0", "chains", "down_in", "written"]
 
 
-def phase_table(tr):
+def phase_table(tr, ep=False):
     """k_decode's %globaltimer phase trace of one step (the counterpart of
     the reference's per-phase timers, src/main.c:253-258, 1522-1546):
     tr int64 [L, G, N_STAMPS] -> per phase the median over layers of the
@@ -396,6 +396,12 @@ def phase_table(tr):
     for k, name in enumerate(["down: first row-dot pair", "down: other row-dots"]):
         rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
                      float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
+    if ep:
+        # the other GPUs' rows: stored to them (after the row-dots), theirs arrived
+        inner = np.diff(tr[:, :, [13, 19, 20, 11]], axis=2)
+        for k, name in enumerate(["ep: rows stored to peers", "ep: peers' rows arrived", "ep: combine + state"]):
+            rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
+                         float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
     out["phases_us"] = rows
     rounds = tr[:, :, 14:17].astype(np.float64)
     if L > 1:
@@ -698,20 +704,25 @@ def run_gpu_ep(args, rank, world, local_rank):
     ep = _ep_module()
     fp8 = args.fmt == "fp8"
     layers = args.layers
-    shard = ep.GpuShard(dc, dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K, rank, world, seed=0)
+    shard = ep.GpuShard(dc, dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K, rank, world, seed=0,
+                        whole=args.ep_whole and world > 1)
     shard.attach()
     Bt = args.batch
+    shard.model.ep_set_fused(not args.ep_layered)
+    fused = Bt == 1 and shard.model.ep_fused_ready()
     st = torch.empty((Bt, H), dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(st, Bt * H, 0, 0, 4, 0, 2, 1.0)            # the same tokens on every rank
     sp = torch.cuda.current_stream().cuda_stream
-    shard.decode(st, max(1, args.warmup), sp)
+    for _ in range(max(1, args.warmup)):
+        shard.decode(st, 1, sp)
     torch.cuda.synchronize()
     dist.barrier()
     clk = Clocks(local_rank)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    shard.decode(st, args.steps, sp)
+    for _ in range(args.steps):                 # one call (fused: one launch per rank) per token
+        shard.decode(st, 1, sp)
     e1.record()
     torch.cuda.synchronize()
     t_ms = e0.elapsed_time(e1)
@@ -727,6 +738,21 @@ def run_gpu_ep(args, rank, world, local_rank):
         hst.copy_(st, non_blocking=True)
         torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
+    trace = None
+    if args.trace and fused:
+        # every rank records (they run in step); rank 0's stamps are printed
+        import numpy as np
+        G = torch.cuda.get_device_properties(local_rank).multi_processor_count
+        n = layers * G * N_STAMPS
+        shard.model.trace(n)
+        dist.barrier()
+        shard.decode(st, 1, sp)
+        torch.cuda.synchronize()
+        raw = shard.model.trace_read(n).astype(np.int64).reshape(layers, G, N_STAMPS)
+        trace = phase_table(raw, ep=True)
+        shard.model.trace(0)
+        if args.trace_dump:
+            np.save(f"{args.trace_dump}.r{rank}.npy", raw)
     tt = torch.tensor([t_ms, e2e_s], dtype=torch.float64, device="cuda" if world > 1 else "cpu")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     t_ms, e2e_s = float(tt[0]), float(tt[1])
@@ -753,7 +779,13 @@ def run_gpu_ep(args, rank, world, local_rank):
             "config": {"workload": (f"config {'2' if fp8 else '3'} sharded: {layers}-layer {'FP8' if fp8 else 'MXFP4'} "
                                     f"decode, batch {Bt}, {E // world} experts per GPU"),
                        "batch": Bt, "hidden": H, "moe_inter": M, "experts": E, "topk": K, "layers": layers,
-                       "parallelism": (f"expert-parallel x{world}: per layer the partial chains of each GPU's "
+                       "parallelism": (f"expert-parallel x{world}, fused: one persistent launch per GPU per token; "
+                                       + ("every expert on every GPU, the K selections split by index"
+                                          if args.ep_whole else f"{E // world} experts per GPU") +
+                                       f"; each GPU's selections' down rows stored into the others' memory over "
+                                       f"NVLink, every row combined in selection order on every GPU (no "
+                                       f"collective call)" if fused else
+                                       f"expert-parallel x{world}: per layer the partial chains of each GPU's "
                                        f"experts, one NCCL all-reduce of acc [{Bt}][{H}] fp32, residual; "
                                        f"one CUDA graph per step"),
                        "l2": "inputs larger than L2"},
@@ -766,9 +798,14 @@ def run_gpu_ep(args, rank, world, local_rank):
                     "timer": "host clock, synchronous steps"},
             # per layer: route, top-K, gate/up, down (B = 1; a batch: route,
             # top-K and the grouped tensor-core layer), the all-reduce, the add
-            "gpu_launches": args.steps * layers * ((4 if Bt == 1 else 2 + PREFILL_LAUNCHES_PER_LAYER) + 2),
+            "gpu_launches": (args.steps if fused else
+                             args.steps * layers * ((4 if Bt == 1 else 2 + PREFILL_LAUNCHES_PER_LAYER) + 2)),
             "clocks": clocks,
         }
+        if trace is not None:
+            for name, med, mx in trace.pop("phases_us"):
+                print(f"  {name:<24s} {med:8.2f} {mx:8.2f}   (us: median, max over CTAs)", file=sys.stderr)
+            res["trace"] = trace
         if headline:
             res["metric"] = METRIC
             res["note"] = ("N > 1: the 40-layer FP8 decode of config 2 with its experts sharded over the GPUs "
@@ -1181,8 +1218,15 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decode / prefill: layers of the stack (fewer: a profiling case, not a bench line)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill: tokens per chunk")
+    ap.add_argument("--ep-whole", action="store_true",
+                    help="N > 1 decode: every expert on every GPU, the K selections split by index (fused step)")
+    ap.add_argument("--ep-layered", action="store_true",
+                    help="ep-decode / N > 1: the per-layer kernels with an NCCL all-reduce per layer instead of "
+                         "the fused persistent launch")
     ap.add_argument("--lookahead", type=int, default=None,
                     help="decode: experts of the next layer prefetched into L2 (0: off; default: the library's)")
+    ap.add_argument("--trace-dump", default=None,
+                    help="N > 1 decode with --trace: save each rank's raw stamps to <prefix>.r<rank>.npy")
     ap.add_argument("--trace", action="store_true",
                     help="decode: print k_decode's per-phase trace (stderr) and add it to the line")
     ap.add_argument("--slots", type=int, default=0,

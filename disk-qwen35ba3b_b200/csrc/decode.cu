@@ -44,6 +44,7 @@ constexpr int kGroups = 4;
 constexpr long kSpin = 1L << 24;           // default polls (with backoff) before giving up
 constexpr double kU = 5.9604644775390625e-08;
 constexpr int kTracePts = 28;
+constexpr int kMaxRanks = 8;
 
 // ---- PTX helpers ------------------------------------------------------------
 __device__ __forceinline__ uint32_t sa(const void *p) {
@@ -94,6 +95,18 @@ __device__ __forceinline__ void st_tag(uint64_t *p, uint32_t tag, uint32_t bits)
 // and state publishes), not where it issues the next copies.
 __device__ __forceinline__ void publish_flush() {
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+// A tagged word stored into another GPU's memory (a peer mapping; visible
+// there ~1 us later, measured on B200 over NVLink, fence or not), and a
+// load of such a word from this GPU's memory.
+__device__ __forceinline__ void st_tag_sys(uint64_t *p, uint32_t tag, uint32_t bits) {
+    uint64_t w = ((uint64_t)tag << 32) | bits;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_sys(const uint64_t *p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
@@ -183,6 +196,15 @@ struct DecodeArgs {
     int stall_cta, stall_t;     // test hook: this CTA withholds its state words
                                 // at this layer-step (-1: off)
     int lookahead;              // L2 prefetch of the next layer's predicted experts
+    // expert parallelism: this GPU's pool holds experts [efirst, efirst +
+    // ecount) of every layer; world > 1: every rank's [2][K][H] tagged
+    // down-output words (pout[rank] is this GPU's, the others peer mappings)
+    int efirst, ecount, rank, world;
+    int split_sel;              // 1: every GPU holds the whole pool and takes selections
+                                // [rank K / world, (rank + 1) K / world); 0: its shard's
+    int par0;                   // parity of this launch's first layer-step, counted over
+                                // every fused launch (the words' buffer alternates per step)
+    uint64_t *pout[kMaxRanks];
     float *state;               // [H] in (read at layer 0) / out (last layer)
     uint64_t *st_ll;            // [H] tagged state words
     uint64_t *sb_ll;            // [E][4] tagged words: S, its interval's ends (fp32), 0
@@ -212,6 +234,22 @@ __device__ bool mbar_wait(const DecodeArgs &a, uint64_t *b, uint32_t parity, uns
     return true;
 }
 
+// One thread: wait (bounded) until the word at p, written by another GPU,
+// carries `tag`; its value in v. false after the limit or an abort.
+__device__ bool poll_word(const DecodeArgs &a, const uint64_t *p, uint32_t tag, float &v) {
+    for (long it = 0;; it++) {
+        uint64_t w;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+        if ((uint32_t)(w >> 32) == tag) { v = __uint_as_float((uint32_t)w); return true; }
+        if (it > a.spin || ((it & 1023) == 1023 && aborted(a))) {
+            if (!aborted(a)) give_up(a, 11);
+            v = 0.f;
+            return false;
+        }
+        if (it > 16) __nanosleep(64);
+    }
+}
+
 // CTA-wide, every thread calls it: TMA-copy the tagged words src[0, n)
 // into shared memory until the first `ncheck` of them carry `tag` (re-copy
 // while any is still from an earlier layer); n is even (16-byte copies).
@@ -232,9 +270,13 @@ __device__ __forceinline__ void gather_issue(uint64_t *bar, uint32_t &pendb, uin
 // Copy n tagged words into dst until the first ncheck carry `tag`. Each
 // round is one bulk copy and two block barriers (the copy's round trip
 // spaces the polls); every 16th round also checks the limit and an abort.
+// Words i < km belong to selection i >> mshift and are checked only where
+// bit (i >> mshift) of locmask is set (a sharded model's chains of the
+// selections another GPU holds are never written here).
 __device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uint32_t &pendb,
                           uint64_t *dst, const uint64_t *src, int n, int ncheck, uint32_t tag,
-                          unsigned code, unsigned long long *rounds = nullptr, bool issued = false) {
+                          unsigned code, unsigned long long *rounds = nullptr, bool issued = false,
+                          int km = 0, int mshift = 0, unsigned locmask = ~0u) {
     const int tid = threadIdx.x;
     for (long it = 0;; it++) {
         if (rounds && tid == 0) *rounds = (unsigned long long)(it + 1);
@@ -243,7 +285,8 @@ __device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uin
         phb ^= 1u << 7;
         pendb &= ~(1u << 7);
         bool all = true;
-        for (int i = tid; i < ncheck; i += kThreads) all = all && (uint32_t)(dst[i] >> 32) == tag;
+        for (int i = tid; i < ncheck; i += kThreads)
+            all = all && ((i < km && !((locmask >> (i >> mshift)) & 1u)) || (uint32_t)(dst[i] >> 32) == tag);
         if (__syncthreads_and(all)) return true;
         if ((it & 15) == 15 && __syncthreads_or(it > a.rounds || aborted(a))) {
             if (tid == 0 && !aborted(a)) give_up(a, code);
@@ -252,7 +295,9 @@ __device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uin
     }
 }
 
-template <int FMT, int H, int M, int E, int K>
+// EP: this GPU holds a shard of every layer's experts and exchanges the
+// down outputs with the other GPUs (world > 1); false: the whole pool here.
+template <int FMT, int H, int M, int E, int K, bool EP>
 __global__ void __launch_bounds__(kThreads, 1)
 k_decode(DecodeArgs a) {
     using S = Shape<FMT, H, M>;
@@ -277,15 +322,26 @@ k_decode(DecodeArgs a) {
     int *sel = (int *)(sm + L::o_sel);
     float *wsel = (float *)(sel + 64);
     int *ctl = (int *)(wsel + 64);
+    int *locs = ctl + 8;      // the selections held here, in selection order (ctl[4]: count, ctl[5]: mask)
     uint16_t *xr16 = (uint16_t *)(sm + L::o_xr);      // x / r as bf16 (the lookahead's input)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, c = blockIdx.x;
     const int rt0 = c * E / G, nrt = (c + 1) * E / G - rt0;
     const int sg0 = c * M / G, nsg = (c + 1) * M / G - sg0;
-    const int p0 = c * (K * M) / G, np = (c + 1) * (K * M) / G - p0;
+    // routed (selection, row) pairs: the CTA's slice of the nloc M pairs of
+    // the selections this GPU holds (all K with every expert here), set per
+    // layer once the routing is known (set_pairs)
+    int nloc = K, p0 = c * (K * M) / G, np = (c + 1) * (K * M) / G - p0;
+    unsigned lmask = (1u << K) - 1;     // bit j: selection j's expert is here
     const int r0 = c * H / G, nr = (c + 1) * H / G - r0;
-    const int ngroups = (np + kGroupPairs - 1) / kGroupPairs;
+    int ngroups = (np + kGroupPairs - 1) / kGroupPairs;
+    auto set_pairs = [&](int nl) {
+        nloc = nl;
+        p0 = c * (nl * M) / G;
+        np = (c + 1) * (nl * M) / G - p0;
+        ngroups = (np + kGroupPairs - 1) / kGroupPairs;
+    };
 
     // mbarrier i: its phase parity (bit i of phb) and whether a copy on it
     // is still in flight (bit i of pendb) -- two registers, not sixteen
@@ -303,7 +359,9 @@ k_decode(DecodeArgs a) {
     __syncthreads();
 
     auto trunk_l = [&](int l) { return a.trunk + (int64_t)l * a.trunk_n; };
-    auto expert = [&](int l, int e) { return a.pool + ((int64_t)l * a.E + e) * a.slot_bytes; };
+    auto expert = [&](int l, int e) {
+        return a.pool + ((int64_t)l * a.ecount + (e - a.efirst)) * a.slot_bytes;
+    };
     auto tag_of = [&](int t) { return (a.epoch << 16) | (uint32_t)(t + 1); };
 
     // one thread: router rows + norm weights of layer l (bar 0)
@@ -340,6 +398,20 @@ k_decode(DecodeArgs a) {
     // L = 8 g + k: a group is <= 2 segments (one per expert), each gate
     // rows (k & 3 == 0), up rows (1), gate scales (2), up scales (3).
     // Thread g of warp 0 sets group g's byte count first (expect_groups).
+    // warp 0, once the routing is final: which selections' experts this GPU
+    // holds (mask and count into ctl[5], ctl[4], their list in selection
+    // order into locs) and this thread's pair slice
+    auto route_local = [&]() {
+        if constexpr (!EP) return;
+        const bool here = lane < K && (a.split_sel ? lane >= a.rank * K / a.world && lane < (a.rank + 1) * K / a.world
+                                                   : sel[lane] >= a.efirst && sel[lane] < a.efirst + a.ecount);
+        const unsigned mk = __ballot_sync(0xFFFFFFFFu, here);
+        if (here) locs[__popc(mk & ((1u << lane) - 1u))] = lane;
+        if (lane == 0) { ctl[4] = __popc(mk); ctl[5] = (int)mk; }
+        lmask = mk;
+        set_pairs(__popc(mk));
+        __syncwarp();
+    };
     auto expect_groups = [&](int g) {
         const int q0 = p0 + g * kGroupPairs, q1 = min(q0 + kGroupPairs, p0 + np);
         if (g < ngroups) {
@@ -359,7 +431,7 @@ k_decode(DecodeArgs a) {
         if (g >= ngroups) return;
         const int qa = sg == 0 ? q0 : split, qb = sg == 0 ? split : q1;
         if (qa >= qb) return;
-        const int j = qa / M, i0 = qa % M, n = qb - qa, slot = qa - p0, mat = kind & 1;
+        const int j = EP ? locs[qa / M] : qa / M, i0 = qa % M, n = qb - qa, slot = qa - p0, mat = kind & 1;
         const uint8_t *ex = expert(l, sel[j]);
         if (kind < 2)
             bulk(gu + (mat * L::PP + slot) * S::row_b, ex + a.slot.rel_v[mat] + (int64_t)i0 * S::row_b,
@@ -373,11 +445,12 @@ k_decode(DecodeArgs a) {
     // bytes of the routed down copies (rows + scales of K experts)
     const int sa0 = FMT == DS4F_FMT_FP8 ? 0 : (r0 * S::dsc_b) / 16 * 16;
     const int sab = FMT == DS4F_FMT_FP8 ? S::dsc_b : ((r0 + nr) * S::dsc_b + 15) / 16 * 16 - sa0;
-    const uint32_t dn_total = K * (nr * S::drow_b + sab);
+    const uint32_t dn_sel = nr * S::drow_b + sab;      // per selection held here
     // copy 2 j + h < 2 K: down rows (h = 0) or scales (h = 1) of
     // selection j (bar 6)
     auto issue_down_copy = [&](int l, int L) {
         const int j = L >> 1;
+        if (EP && !((lmask >> j) & 1u)) return;
         const uint8_t *ex = expert(l, sel[j]);
         if ((L & 1) == 0) {
             if (nr)
@@ -625,13 +698,15 @@ k_decode(DecodeArgs a) {
             if (cert && lane < K) sel[lane] = er;
             if (lane == 0) ctl[1] = cert ? 1 : 0;
             if (cert) {
-                // the routing is final: the byte counts of this layer's
-                // copies, then group 0's copies at once (the other groups
-                // follow from the other warps after the barrier below, the
-                // down rows after group 0's dots: the first group lands first)
+                // the routing is final: the selections held here, the byte
+                // counts of this layer's copies, then group 0's copies at
+                // once (the other groups follow from the other warps after
+                // the barrier below, the down rows after group 0's dots: the
+                // first group lands first)
                 __syncwarp();
+                route_local();
                 if (lane < kGroups) expect_groups(lane);
-                if (lane == kGroups) mbar_expect(bar + 6, dn_total);
+                if (lane == kGroups) mbar_expect(bar + 6, (EP ? nloc : K) * dn_sel);
                 __syncwarp();
                 if (lane < 8) { fence_async(); issue_group_copy(l, lane); }
             }
@@ -670,10 +745,18 @@ k_decode(DecodeArgs a) {
             }
             if (tid == 0 && !a.exact_all && c == 0) atomicAdd(a.diag + 1, 1u);
             __syncthreads();
-            if (tid < kGroups) expect_groups(tid);
-            if (tid == kGroups) mbar_expect(bar + 6, dn_total);
+            if (warp == 0) {
+                route_local();
+                if (lane < kGroups) expect_groups(lane);
+                if (lane == kGroups) mbar_expect(bar + 6, (EP ? nloc : K) * dn_sel);
+            }
             __syncthreads();
             if (tid < 8) { fence_async(); issue_group_copy(l, tid); }
+        }
+        // every thread: this layer's selections held here and its pairs
+        if constexpr (EP) {
+            lmask = (unsigned)ctl[5];
+            set_pairs(ctl[4]);
         }
         DS4F_TRACE(5);
         // (G) the gate/up copies of groups 1.. (group 0's went out with the
@@ -825,7 +908,7 @@ k_decode(DecodeArgs a) {
             if (tid < np) {
                 constexpr int HALF = kGroups * kGroupPairs * 2;
                 const int q = p0 + tid;
-                st_tag(a.ch_ll + (q / M) * M + (q % M), tg,
+                st_tag(a.ch_ll + (EP ? locs[q / M] : q / M) * M + (q % M), tg,
                        __float_as_uint(silu_mul(red[2 * tid] + red[HALF + 2 * tid],
                                                 red[2 * tid + 1] + red[HALF + 2 * tid + 1])));
                 publish_flush();
@@ -884,8 +967,10 @@ k_decode(DecodeArgs a) {
             // lookahead logits.
             constexpr int NCW = (K + 1) * M + 1;
             static_assert(L::NCWP == NCW + 1 && L::NCWP % 2 == 0 && E % 2 == 0, "even gathers");
+            static_assert((M & (M - 1)) == 0, "chain words of selection j: j << log2 M ..");
+            constexpr int MSH = __builtin_ctz(M);
             if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.ch_ll, pred ? L::NCWP + E : L::NCWP,
-                           pred ? L::NCWP + E : NCW, tg, 5, DS4F_ROUNDS(16))) {
+                           pred ? L::NCWP + E : NCW, tg, 5, DS4F_ROUNDS(16), false, EP ? K * M : 0, MSH, lmask)) {
                 ok = false;
                 break;
             }
@@ -926,7 +1011,7 @@ k_decode(DecodeArgs a) {
                         v = (((lane & k) == 0) == ((lane & j) == 0)) ? max(v, o) : min(v, o);
                     }
                 const uint32_t tau = __shfl_sync(0xFFFFFFFFu, v, min(a.lookahead, 32) - 1);
-                if (lkey >= tau) {
+                if (lkey >= tau && (!EP || (tid >= a.efirst && tid < a.efirst + a.ecount))) {
                     const int64_t sb = a.slot_bytes;
                     const int64_t o0 = ((int64_t)c * sb / G) & ~(int64_t)15;
                     const int64_t o1 = (c == G - 1 ? sb : (int64_t)(c + 1) * sb / G) & ~(int64_t)15;
@@ -944,7 +1029,7 @@ k_decode(DecodeArgs a) {
             static_assert(4 * S::bn <= 16 && XC <= 16, "at most 16 chain floats per lane");
             {
                 const int jw = warp >> 1, hr = (nr + 1) >> 1;
-                const int rw0 = (warp & 1) * hr, nrw = min(hr, nr - rw0);
+                const int rw0 = (warp & 1) * hr, nrw = (!EP || ((lmask >> jw) & 1u)) ? min(hr, nr - rw0) : 0;
                 float xc[XC], xs[4 * S::bn];
 #pragma unroll
                 for (int g = 0; g < S::dg; g++)
@@ -1017,14 +1102,45 @@ k_decode(DecodeArgs a) {
                 z += __shfl_xor_sync(0xFFFFFFFFu, z, 1);
                 sh = warp_sum(sh);
                 const int slot = (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0);
-                if ((lane & 3) == 0 && slot < nrw) outs[jw * L::RR + rw0 + slot] = z;
+                if ((lane & 3) == 0 && slot < nrw) {
+                    outs[jw * L::RR + rw0 + slot] = z;
+                    if constexpr (EP) {
+                        // several GPUs: the row goes to every other GPU at once
+                        // (their words for layer parity (par0 + t) & 1), plain
+                        // stores into its memory; the others' arrive in ours
+                        const int64_t par = (int64_t)((a.par0 + t) & 1) * K * H;
+                        for (int p = 0; p < a.world; p++)
+                            if (p != a.rank)
+                                st_tag_sys(a.pout[p] + par + jw * H + r0 + rw0 + slot, tg, __float_as_uint(z));
+                    }
+                }
                 if (lane == 0 && warp < nr) outs[K * L::RR + warp] = sh;
             }
             DS4F_TRACE(13);
             if (tid == 0) red[0] = sigmoid_ref(chf[(K + 1) * M]);
             __syncthreads();
+            // several GPUs: the other GPUs' rows of this CTA's selections
+            // they hold into outs[] (read below exactly as this GPU's own)
+            if (EP && tid < nr) {
+                DS4F_TRACE(19);
+                // every word read at once (one round trip), then only the
+                // ones not yet there polled
+                const uint64_t *base = a.pout[a.rank] + (int64_t)((a.par0 + t) & 1) * K * H + r0 + tid;
+                uint64_t w[K];
+#pragma unroll
+                for (int j = 0; j < K; j++) w[j] = ((lmask >> j) & 1u) ? 0ull : ld_sys(base + (int64_t)j * H);
+#pragma unroll
+                for (int j = 0; j < K; j++) {
+                    if ((lmask >> j) & 1u) continue;
+                    float v = __uint_as_float((uint32_t)w[j]);
+                    if ((uint32_t)(w[j] >> 32) != tg) poll_word(a, base + (int64_t)j * H, tg, v);
+                    outs[j * L::RR + tid] = v;
+                }
+                DS4F_TRACE(20);
+            }
             // selection-order combine (src/moe.c:1224-1225), shared gate
-            // (:1279-1282), residual (:1424)
+            // (:1279-1282), residual (:1424); a selection held elsewhere
+            // contributes the word its GPU stored here
             if (tid < nr) {
                 const int r = r0 + tid;
                 float acc = 0.0f;
@@ -1055,12 +1171,13 @@ k_decode(DecodeArgs a) {
 }
 
 template <int FMT, int H, int M, int E, int K>
-int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
+int launch_t(Model *m, float *state, int n_steps, cudaStream_t st, const DecodePeers *pe) {
     using L = Smem<FMT, H, M, E, K>;
     static_assert(L::bytes <= 227 * 1024, "decode kernel shared memory over budget");
-    static SmemOptIn opt;
-    auto kern = k_decode<FMT, H, M, E, K>;
-    if (opt.set(kern, L::bytes)) return -1;
+    static SmemOptIn opt, opt_ep;
+    const bool ep = pe && pe->world > 1;
+    auto kern = ep ? k_decode<FMT, H, M, E, K, true> : k_decode<FMT, H, M, E, K, false>;
+    if ((ep ? opt_ep : opt).set(kern, L::bytes)) return -1;
     int dev = 0, sms = 0;
     DS4F_CUDA(cudaGetDevice(&dev));
     DS4F_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1074,6 +1191,15 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     a.tr = m->tr;
     a.n_layers = m->d.n_layers;
     a.E = E;
+    a.efirst = m->d.expert_first;
+    a.ecount = m->d.expert_count;
+    a.rank = pe ? pe->rank : 0;
+    a.world = pe ? pe->world : 1;
+    a.split_sel = pe ? pe->split_sel : 0;
+    for (int p = 0; p < kMaxRanks; p++) a.pout[p] = pe && p < pe->world ? pe->out[p] : nullptr;
+    int *epoch = pe ? pe->epoch : &m->epoch;
+    int64_t lsteps0 = 0;
+    int64_t *lsteps = pe ? pe->lsteps : &lsteps0;
     a.renorm = m->d.renorm;
     a.exact_all = m->d.router_exact;
     a.st_ll = m->w.st_ll;
@@ -1090,8 +1216,10 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
     const int per = std::max(1, 65000 / m->d.n_layers);
     for (int s0 = 0; s0 < n_steps; s0 += per) {
         const int ns = std::min(per, n_steps - s0);
-        m->epoch = m->epoch % 65535 + 1;
-        a.epoch = (uint32_t)m->epoch;
+        *epoch = *epoch % 65535 + 1;
+        a.epoch = (uint32_t)*epoch;
+        a.par0 = (int)(*lsteps & 1);
+        *lsteps += (int64_t)ns * m->d.n_layers;
         a.n_steps = ns;
         a.state = state;
         a.trace = nullptr;
@@ -1117,30 +1245,44 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st) {
 
 }  // namespace
 
-bool decode_eligible(const Model *m) {
+namespace {
+bool decode_shape_ok(const Model *m) {
     const ModelDesc &d = m->d;
-    if (d.expert_count != d.n_experts || d.topk != 8 || m->cache) return false;
+    if (d.topk != 8 || m->cache) return false;
     if (m->slot.nbytes % 16) return false;       // every slot 16-byte aligned (bulk copies)
     if (!((d.hidden == 2048 && d.moe_inter == 512) || (d.hidden == 1024 && d.moe_inter == 256)))
         return false;
     return d.n_experts == 256 || d.n_experts == 64;
 }
+}  // namespace
 
-int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st) {
+bool decode_eligible(const Model *m) {
+    return m->d.expert_first == 0 && m->d.expert_count == m->d.n_experts && decode_shape_ok(m);
+}
+
+bool decode_eligible_ep(const Model *m, int rank, int world, int split_sel) {
+    const int E = m->d.n_experts;
+    if (world < 1 || world > kMaxRanks || !decode_shape_ok(m)) return false;
+    if (split_sel) return m->d.expert_first == 0 && m->d.expert_count == E;
+    return E % world == 0 && m->d.expert_first == rank * (E / world) && m->d.expert_count == E / world;
+}
+
+int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st, const DecodePeers *pe) {
     const ModelDesc &d = m->d;
-    DS4F_REQUIRE(decode_eligible(m), "decode: shape not supported by the persistent kernel");
+    DS4F_REQUIRE(pe ? decode_eligible_ep(m, pe->rank, pe->world, pe->split_sel) : decode_eligible(m),
+                 "decode: shape or shard not supported by the persistent kernel");
     const bool f8 = d.fmt == DS4F_FMT_FP8;
     if (d.hidden == 2048 && d.n_experts == 256)
-        return f8 ? launch_t<DS4F_FMT_FP8, 2048, 512, 256, 8>(m, state, n_steps, st)
-                  : launch_t<DS4F_FMT_MXFP4, 2048, 512, 256, 8>(m, state, n_steps, st);
+        return f8 ? launch_t<DS4F_FMT_FP8, 2048, 512, 256, 8>(m, state, n_steps, st, pe)
+                  : launch_t<DS4F_FMT_MXFP4, 2048, 512, 256, 8>(m, state, n_steps, st, pe);
     if (d.hidden == 2048 && d.n_experts == 64)
-        return f8 ? launch_t<DS4F_FMT_FP8, 2048, 512, 64, 8>(m, state, n_steps, st)
-                  : launch_t<DS4F_FMT_MXFP4, 2048, 512, 64, 8>(m, state, n_steps, st);
+        return f8 ? launch_t<DS4F_FMT_FP8, 2048, 512, 64, 8>(m, state, n_steps, st, pe)
+                  : launch_t<DS4F_FMT_MXFP4, 2048, 512, 64, 8>(m, state, n_steps, st, pe);
     if (d.n_experts == 256)
-        return f8 ? launch_t<DS4F_FMT_FP8, 1024, 256, 256, 8>(m, state, n_steps, st)
-                  : launch_t<DS4F_FMT_MXFP4, 1024, 256, 256, 8>(m, state, n_steps, st);
-    return f8 ? launch_t<DS4F_FMT_FP8, 1024, 256, 64, 8>(m, state, n_steps, st)
-              : launch_t<DS4F_FMT_MXFP4, 1024, 256, 64, 8>(m, state, n_steps, st);
+        return f8 ? launch_t<DS4F_FMT_FP8, 1024, 256, 256, 8>(m, state, n_steps, st, pe)
+                  : launch_t<DS4F_FMT_MXFP4, 1024, 256, 256, 8>(m, state, n_steps, st, pe);
+    return f8 ? launch_t<DS4F_FMT_FP8, 1024, 256, 64, 8>(m, state, n_steps, st, pe)
+              : launch_t<DS4F_FMT_MXFP4, 1024, 256, 64, 8>(m, state, n_steps, st, pe);
 }
 
 }  // namespace ds4f

@@ -203,17 +203,89 @@ struct EpState {
     // prefill buffers, grown on demand
     void *pf = nullptr;
     size_t pf_bytes = 0;
+    // the fused one-token decode (the persistent kernel on every rank, the
+    // down outputs stored straight into the other GPUs' memory): this GPU's
+    // [2][K][H] words, every rank's mapping of them, the shared launch epoch
+    bool fused = true;                // use it where eligible (ds4f_gpu_ep_set_fused)
+    bool fused_ok = false;            // buffers mapped on every rank
+    uint64_t *pout_own = nullptr;
+    uint64_t *pout[8] = {};
+    bool opened[8] = {};
+    int epoch = 0;
+    int64_t lsteps = 0;
+    // every rank holds the whole pool: the fused step splits the K
+    // selections by index instead (no per-layer imbalance; one-token fused
+    // steps only)
+    bool split_sel = false;
 };
 
 void ep_free(Model *m) {
     EpState *ep = (EpState *)m->ep;
     if (!ep) return;
     if (ep->graph) cudaGraphExecDestroy(ep->graph);
+    for (int p = 0; p < 8; p++)
+        if (ep->opened[p]) cudaIpcCloseMemHandle(ep->pout[p]);
+    if (ep->pout_own) cudaFree(ep->pout_own);
     if (ep->acc) cudaFree(ep->acc);
     if (ep->pf) cudaFree(ep->pf);
     if (ep->comm && nccl().ok) nccl().CommDestroy(ep->comm);
     delete ep;
     m->ep = nullptr;
+}
+
+// The fused decode's exchange buffers: each rank allocates its [2][K][H]
+// words, the ranks all-gather (NCCL) the CUDA IPC handle and device UUID of
+// each, and every rank maps the others'. Ranks sharing a device (kernels
+// that wait on one another must not share a GPU) or a mapping that fails
+// leave the fused path off; the per-layer path with its all-reduce stays.
+void ep_map_peers(Model &m, EpState *ep) {
+    const int N = ep->world, me = ep->rank;
+    const size_t ob = (size_t)2 * m.d.topk * m.d.hidden * 8;
+    if (N > 8) return;
+    if (cudaMalloc(&ep->pout_own, ob) != cudaSuccess) { cudaGetLastError(); ep->pout_own = nullptr; return; }
+    cudaMemset(ep->pout_own, 0, ob);
+    ep->pout[me] = ep->pout_own;
+    if (N == 1) { ep->fused_ok = true; return; }
+    struct Rec { cudaIpcMemHandle_t h; char uuid[16]; };
+    Rec mine = {};
+    cudaDeviceProp prop;
+    if (cudaIpcGetMemHandle(&mine.h, ep->pout_own) != cudaSuccess ||
+        cudaGetDeviceProperties(&prop, m.device) != cudaSuccess) { cudaGetLastError(); return; }
+    memcpy(mine.uuid, &prop.uuid, 16);
+    std::vector<Rec> all(N);
+    Rec *dev = nullptr;
+    if (cudaMalloc(&dev, sizeof(Rec) * N) != cudaSuccess) { cudaGetLastError(); return; }
+    cudaMemcpy(dev + me, &mine, sizeof(Rec), cudaMemcpyHostToDevice);
+    const ncclResult_t r = nccl().AllGather(dev + me, dev, sizeof(Rec), ncclUint8, ep->comm, m.stream);
+    cudaStreamSynchronize(m.stream);
+    cudaMemcpy(all.data(), dev, sizeof(Rec) * N, cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (r != ncclSuccess) return;
+    for (int p = 0; p < N; p++)
+        for (int q = 0; q < p; q++)
+            if (!memcmp(all[p].uuid, all[q].uuid, 16)) return;      // two ranks on one GPU
+    for (int p = 0; p < N; p++) {
+        if (p == me) continue;
+        void *ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            return;
+        }
+        ep->pout[p] = (uint64_t *)ptr;
+        ep->opened[p] = true;
+    }
+    // every rank mapped every peer before any fused launch (a rank whose
+    // mapping failed stays on the other path, so all of them must agree)
+    int *flag = nullptr;
+    if (cudaMalloc(&flag, 4) != cudaSuccess) { cudaGetLastError(); return; }
+    const int one = 1;
+    cudaMemcpy(flag, &one, 4, cudaMemcpyHostToDevice);
+    const ncclResult_t r2 = nccl().AllReduce(flag, flag, 1, ncclInt32, ncclMin, ep->comm, m.stream);
+    cudaStreamSynchronize(m.stream);
+    int all_ok = 0;
+    cudaMemcpy(&all_ok, flag, 4, cudaMemcpyDeviceToHost);
+    cudaFree(flag);
+    ep->fused_ok = r2 == ncclSuccess && all_ok == 1;
 }
 
 namespace {
@@ -276,13 +348,15 @@ int ds4f_gpu_ep_attach(Ds4fGpuModel *h, const uint8_t id[128], int rank, int wor
     DS4F_REQUIRE(!m.ep, "ep_attach: the model is attached already");
     DS4F_REQUIRE(!m.cache, "ep_attach: a streaming model cannot be sharded");
     const int E = m.d.n_experts;
-    DS4F_REQUIRE(E % world == 0 && m.d.expert_first == rank * (E / world) && m.d.expert_count == E / world,
-                 "ep_attach: rank %d of %d must hold experts [%d, %d); the model holds [%d, %d)", rank, world,
-                 rank * (E / world), (rank + 1) * (E / world), m.d.expert_first,
+    const bool whole = world > 1 && m.d.expert_first == 0 && m.d.expert_count == E;
+    DS4F_REQUIRE(whole || (E % world == 0 && m.d.expert_first == rank * (E / world) && m.d.expert_count == E / world),
+                 "ep_attach: rank %d of %d must hold experts [%d, %d) (or every expert); the model holds [%d, %d)",
+                 rank, world, rank * (E / world), (rank + 1) * (E / world), m.d.expert_first,
                  m.d.expert_first + m.d.expert_count);
     EpState *ep = new EpState();
     ep->rank = rank;
     ep->world = world;
+    ep->split_sel = whole;
     ncclUniqueId u;
     memcpy(&u, id, 128);
     DS4F_CUDA(cudaSetDevice(m.device));
@@ -314,8 +388,24 @@ int ds4f_gpu_ep_attach(Ds4fGpuModel *h, const uint8_t id[128], int rank, int wor
             return 0;
         }();
     }
-    if (rc) ds4f::ep_free(&m);
-    return rc;
+    if (rc) {
+        ds4f::ep_free(&m);
+        return rc;
+    }
+    ds4f::ep_map_peers(m, ep);
+    return 0;
+}
+
+int ds4f_gpu_ep_set_fused(Ds4fGpuModel *h, int on) {
+    DS4F_REQUIRE(h && h->m.ep, "ep_set_fused: model not attached");
+    ((EpState *)h->m.ep)->fused = on != 0;
+    return 0;
+}
+
+int ds4f_gpu_ep_fused_ready(const Ds4fGpuModel *h) {
+    DS4F_REQUIRE(h && h->m.ep, "ep_fused_ready: model not attached");
+    const EpState *ep = (const EpState *)h->m.ep;
+    return ep->fused_ok && ds4f::decode_eligible_ep(&h->m, ep->rank, ep->world, ep->split_sel) ? 1 : 0;
 }
 
 int ds4f_gpu_ep_detach(Ds4fGpuModel *h) {
@@ -345,6 +435,21 @@ int ds4f_gpu_ep_stack_dev(Ds4fGpuModel *h, float *states, int B, int n_steps, vo
     EpState *ep = (EpState *)m.ep;
     DS4F_REQUIRE(ep && ep->comm, "ep_stack: model not attached to a communicator (ds4f_gpu_ep_attach)");
     DS4F_REQUIRE(B <= m.bmax, "ep_stack: batch %d above %d", B, m.bmax);
+    if (B == 1 && ep->fused && ep->fused_ok && ds4f::decode_eligible_ep(&m, ep->rank, ep->world, ep->split_sel)) {
+        // one persistent launch per rank for all n_steps x layers
+        return ds4f::on_model_stream(m, stream, [&](cudaStream_t st) -> int {
+            ds4f::DecodePeers pe;
+            for (int p = 0; p < 8; p++) pe.out[p] = ep->pout[p];
+            pe.rank = ep->rank;
+            pe.world = ep->world;
+            pe.epoch = &ep->epoch;
+            pe.lsteps = &ep->lsteps;
+            pe.split_sel = ep->split_sel;
+            return n_steps > 0 ? ds4f::decode_launch(&m, states, n_steps, st, &pe) : 0;
+        });
+    }
+    DS4F_REQUIRE(!ep->split_sel, "ep_stack: with every expert on every rank only fused one-token steps run "
+                                 "(B = 1, ds4f_gpu_ep_fused_ready)");
     return ds4f::on_model_stream(m, stream, [&](cudaStream_t st) -> int {
         int s = 0;
         const bool fresh = !ep->graph || ep->g_states != states || ep->g_B != B ||
@@ -378,6 +483,7 @@ int ds4f_gpu_ep_prefill(Ds4fGpuModel *h, float *states, int T, const int *sel, c
     ds4f::Model &m = h->m;
     EpState *ep = (EpState *)m.ep;
     DS4F_REQUIRE(ep && ep->comm, "ep_prefill: model not attached to a communicator (ds4f_gpu_ep_attach)");
+    DS4F_REQUIRE(!ep->split_sel, "ep_prefill: needs each rank's shard of E / N experts");
     const ds4f::NcclApi &n = ds4f::nccl();
     const int NL = m.d.n_layers, H = m.d.hidden, K = m.d.topk, E = m.d.n_experts, N = ep->world, me = ep->rank;
     const int RW = H + 2 * K;                       // floats per dispatched row

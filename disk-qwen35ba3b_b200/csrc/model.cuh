@@ -123,8 +123,19 @@ int route_batch_launch(Model *m, int L, const float *states, int B, float *xin, 
                        int *idx, float *w, cudaStream_t st);
 
 // Whole decode steps in one persistent cooperative launch (decode.cu).
-bool decode_eligible(const Model *m);
-int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st);
+// Several GPUs, one persistent launch each (decode.cu): every rank's
+// [2][K][H] tagged down-output words (out[rank] its own, the others peer
+// mappings) and the launch-epoch counter every rank advances in step.
+struct DecodePeers {
+    uint64_t *out[8];
+    int rank, world;
+    int *epoch;
+    int64_t *lsteps;             // layer-steps of every fused launch so far (buffer parity)
+    int split_sel;               // 1: whole pool on every GPU, selections split by index
+};
+bool decode_eligible(const Model *m);                         // the whole pool on this GPU
+bool decode_eligible_ep(const Model *m, int rank, int world, int split_sel);  // shard or whole pool
+int decode_launch(Model *m, float *state, int n_steps, cudaStream_t st, const DecodePeers *peers = nullptr);
 
 // GPU copy of the seeded fixture generator (oracle/fixture.c): fills the
 // model's trunk and expert shard.

@@ -82,6 +82,8 @@ def lib():
             "ds4f_gpu_ep_unique_id": [_vp],
             "ds4f_gpu_ep_attach": [_vp, _vp, C.c_int, C.c_int],
             "ds4f_gpu_ep_detach": [_vp],
+            "ds4f_gpu_ep_fused_ready": [_vp],
+            "ds4f_gpu_ep_set_fused": [_vp, C.c_int],
             "ds4f_gpu_ep_abort": [_vp],
             "ds4f_gpu_ep_stack_dev": [_vp, _vp, C.c_int, C.c_int, _vp],
             "ds4f_gpu_ep_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
@@ -438,6 +440,17 @@ class Model:
 
     def ep_detach(self):
         check(lib().ds4f_gpu_ep_detach(self.h))
+
+    def ep_fused_ready(self):
+        """True when one-token EP steps run as one persistent launch per rank."""
+        r = lib().ds4f_gpu_ep_fused_ready(self.h)
+        if r < 0:
+            check(r)
+        return r == 1
+
+    def ep_set_fused(self, on):
+        """Fused one-token EP steps where ready (True) or the per-layer path."""
+        check(lib().ds4f_gpu_ep_set_fused(self.h, 1 if on else 0))
 
     def ep_stack_dev(self, states, n_steps, stream=None):
         """states [B][H] (device), identical on every rank."""

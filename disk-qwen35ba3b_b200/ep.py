@@ -44,8 +44,10 @@ class GpuShard:
     """One rank's expert shard on its GPU (the library's model with
     expert_first / expert_count set)."""
 
-    def __init__(self, dc, fmt, n_layers, hidden, moe_inter, n_experts, topk, rank, world, seed=0):
-        first, count = shard_of(rank, world, n_experts)
+    def __init__(self, dc, fmt, n_layers, hidden, moe_inter, n_experts, topk, rank, world, seed=0, whole=False):
+        """whole: every expert on this rank too (the fused one-token step then
+        splits the K selections by index; N times the memory)."""
+        first, count = (0, n_experts) if whole else shard_of(rank, world, n_experts)
         self.model = dc.Model(fmt, n_layers, hidden, moe_inter, n_experts, topk,
                               expert_first=first, expert_count=count)
         self.model.synth(seed)

@@ -302,7 +302,8 @@ int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
  * groups that had landed before their compute, 18 the time every router
  * word was visible (before the top-k), 21..23 gate/up copy groups 1..3
  * landed, 24 the gate/up dots of warp 0 done, 25 every warp's done, 26 the
- * first down row-dot of warp 0 done.
+ * first down row-dot of warp 0 done; with expert parallelism 19 this GPU's
+ * down rows stored to the other GPUs, 20 theirs arrived.
  * n_stamps = 0 turns it off. */
 int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
 int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
@@ -465,12 +466,25 @@ int  ds4f_gpu_moe_stack_batch_dev(Ds4fGpuModel *m, float *states_dev, int B, int
  * this library (loaded at the first call: libnccl.so.2). Rank r's model is
  * created with expert_first = r E / N, expert_count = E / N and holds the
  * whole trunk. The caller moves the 128-byte id from rank 0 to the other
- * ranks (any channel), then every rank attaches. */
+ * ranks (any channel), then every rank attaches. A model holding every
+ * expert on every rank (N > 1) attaches too: its fused one-token step
+ * splits the K selections by index, rank r taking [r K / N, (r + 1) K / N)
+ * (the same work on every rank each layer, at N times the memory); only
+ * that step runs on it. */
 #define DS4F_EP_ID_BYTES 128
 int  ds4f_gpu_ep_unique_id(uint8_t id[DS4F_EP_ID_BYTES]);
 /* Collective over the N ranks: builds the communicator on the model's
- * device and connects every peer. */
+ * device and connects every peer; with one rank per GPU it also maps every
+ * rank's down-output words of the fused decode (CUDA IPC handles exchanged
+ * over the communicator). */
 int  ds4f_gpu_ep_attach(Ds4fGpuModel *m, const uint8_t id[DS4F_EP_ID_BYTES], int rank, int world);
+/* 1 when one-token steps run fused (below): attached, every rank's words
+ * mapped (each rank on its own GPU) and the shape one the persistent
+ * kernel covers. */
+int  ds4f_gpu_ep_fused_ready(const Ds4fGpuModel *m);
+/* Choose the fused one-token step where ready (1, the default) or the
+ * per-layer kernels with an all-reduce per layer (0), e.g. to compare. */
+int  ds4f_gpu_ep_set_fused(Ds4fGpuModel *m, int on);
 int  ds4f_gpu_ep_detach(Ds4fGpuModel *m);
 /* A collective waits for every peer. If a peer is lost, another host
  * thread calls this to abort the communicator: the waiting calls then
@@ -484,7 +498,16 @@ int  ds4f_gpu_ep_abort(Ds4fGpuModel *m);
  * selections (and on rank 0 the shared expert), one all-reduce of the
  * partial combine acc [B][H], state += acc (src/moe.c:1224-1225, 1424).
  * The first step of a (states, B) pair runs eagerly, the later ones replay
- * one captured CUDA graph of a whole step. Enqueued on `stream`. */
+ * one captured CUDA graph of a whole step. Enqueued on `stream`.
+ * B = 1 with ds4f_gpu_ep_fused_ready: instead, one persistent launch per
+ * rank runs every step and layer (the kernel of DS4F_PATH_PERSISTENT on the
+ * rank's shard): each rank routes the whole state, runs the chains of the
+ * selections it holds, stores their output rows straight into every other
+ * GPU's memory (tagged words, plain stores over NVLink) and combines every
+ * selection's rows in selection order itself -- the same bits as one GPU
+ * holding every expert, with no collective call. Ranks wait for each other
+ * inside the kernel, bounded: a lost peer makes the call return -1 ("gave
+ * up waiting (code 11 ...)") after about a second. */
 int  ds4f_gpu_ep_stack_dev(Ds4fGpuModel *m, float *states, int B, int n_steps, void *stream);
 /* Batched prefill of every layer with the chunk's tokens partitioned over
  * the ranks (the expert-parallel ds4f_moe_step_batch, src/moe.c:1480-1707):

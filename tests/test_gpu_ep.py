@@ -1,10 +1,17 @@
-"""Expert-parallel decode on 2 GPUs (one process per GPU, NCCL): each rank
-holds half of every layer's experts; after each step every rank's state
-equals the single-GPU full model's within fp32 reassociation of the combine
-(the partial sums meet in the all-reduce): one token against the per-token
-layer steps, a batch against the batched (tensor-core) stack, which is in
-turn within the chain tolerance of the per-token fp32 path. Skipped with
-fewer than 2 GPUs."""
+"""Expert-parallel decode on 2 GPUs (one process per GPU): each rank holds
+half of every layer's experts.
+
+* The fused one-token step (one persistent launch per rank, the down
+  outputs of each rank's selections stored into the other GPU's memory,
+  every row combined in selection order on every rank) gives the same bits
+  as the single-GPU persistent kernel with every expert.
+* The per-layer path (NCCL all-reduce of the partial combine per layer)
+  equals the single-GPU full model within fp32 reassociation of the
+  combine: one token against the per-token layer steps, a batch against the
+  batched (tensor-core) stack, which is in turn within the chain tolerance
+  of the per-token fp32 path.
+
+Skipped with fewer than 2 GPUs."""
 import importlib.util
 import os
 
@@ -35,8 +42,8 @@ def _ep_module():
     return mod
 
 
-def _x0(B):
-    return po.fill_f32(B * H, po.key(21, 0, 4, 0, 0), 1.0).reshape(B, H).copy()
+def _x0(B, h=H):
+    return po.fill_f32(B * h, po.key(21, 0, 4, 0, 0), 1.0).reshape(B, h).copy()
 
 
 def _init(rank, world, port):
@@ -55,15 +62,18 @@ def _init(rank, world, port):
     return dc, dist
 
 
-def _rank(rank, world, port, fmt, B, out):
+def _rank(rank, world, port, fmt, B, out, fused=False, shape=(H, M, E, NL), whole=False):
     import torch
     dc, dist = _init(rank, world, port)
     ep = _ep_module()
-    shard = ep.GpuShard(dc, fmt, NL, H, M, E, K, rank, world, seed=21)
+    h, m, e, nl = shape
+    shard = ep.GpuShard(dc, fmt, nl, h, m, e, K, rank, world, seed=21, whole=whole)
     shard.attach()
-    st = torch.from_numpy(_x0(B)).cuda()
+    shard.model.ep_set_fused(fused)
+    out[f"ready{rank}"] = shard.model.ep_fused_ready()
+    st = torch.from_numpy(_x0(B, h)).cuda()
     sp = torch.cuda.current_stream().cuda_stream
-    shard.decode(st, 1, sp)                  # eager first step
+    shard.decode(st, 1, sp)                  # per-layer path: the eager first step
     shard.decode(st, 2, sp)                  # then the captured step, twice
     torch.cuda.synchronize()
     out[rank] = st.cpu().numpy()
@@ -72,24 +82,54 @@ def _rank(rank, world, port, fmt, B, out):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("B", [1, 2])
-@pytest.mark.parametrize("fmt", [2, 0])            # FP8, MXFP4
-def test_expert_parallel_two_gpus(fmt, B):
+def _spawn(target, args_of):
     import socket
-    import torch
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, fmt, B, out)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=args_of(r, port, out)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(300)
         assert p.exitcode == 0
+    return dict(out)
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("whole", [False, True], ids=["shard", "whole-split-by-selection"])
+@pytest.mark.parametrize("shape", [(1024, 256, 64, 3), (2048, 512, 256, 4)], ids=["small", "config2-4-layers"])
+@pytest.mark.parametrize("fmt", [2, 0])            # FP8, MXFP4
+def test_fused_one_token_two_gpus_bit_exact(fmt, shape, whole):
+    """3 steps (two launches) of the fused step on 2 GPUs against the
+    single-GPU persistent kernel holding every expert: identical bits, with
+    each GPU holding half of the experts (selections split by owner) or all
+    of them (selections split by index)."""
+    out = _spawn(_rank, lambda r, port, out: (r, 2, port, fmt, 1, out, True, shape, whole))
+    assert out["ready0"] and out["ready1"]
+    assert np.array_equal(out[0], out[1])
+    h, m, e, nl = shape
+    dc = ds4f_cuda()
+    dc.init()
+    full = dc.Model(fmt, nl, h, m, e, K)
+    full.synth(21)
+    full.set_path(dc.PATH_PERSISTENT)
+    want = full.stack(_x0(1, h)[0], 3)
+    full.close()
+    assert np.array_equal(out[0][0].view(np.uint32), want.view(np.uint32)), \
+        float(np.abs(out[0][0] - want).max())
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("B", [1, 2])
+@pytest.mark.parametrize("fmt", [2, 0])            # FP8, MXFP4
+def test_expert_parallel_two_gpus(fmt, B):
+    """The per-layer path (fused off)."""
+    import torch
+    out = _spawn(_rank, lambda r, port, out: (r, 2, port, fmt, B, out, False))
     assert np.array_equal(out[0], out[1])
     # the single-GPU full model (two steps): per-token layer steps, and for
     # a batch the batched stack
