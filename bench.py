@@ -68,8 +68,8 @@ def bytes_per_token(fmt_fp8=True):
 # script (--layers 4, 3.2 GB pool, 130 MB of weights per launch, larger than
 # L2), scaled by 10: every layer reads its own weights. Re-measured whenever
 # k_decode changes; KERNEL_REV names the kernel revision it belongs to.
-KERNEL_REV = "k_decode r1"
-TRAFFIC_PER_LAUNCH = 10 * 133_950_000
+KERNEL_REV = "k_decode r2"
+TRAFFIC_PER_LAUNCH = 10 * (130_202_368 + 5_310_976)
 # kernels of one batched-prefill layer (csrc/prefill.cu): count, plan, place,
 # front end, gate/up GEMM, SiLU digits, down GEMM, shared gate/up and down
 # GEMMs, shared SiLU digits, combine

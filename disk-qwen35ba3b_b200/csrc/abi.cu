@@ -402,6 +402,7 @@ static int model_create_impl(const Ds4fGpuModelDesc *desc, int64_t pool_slots, D
     memset(&m, 0, sizeof m);
     m.d = d;
     m.stall_cta = m.stall_t = -1;
+    m.stall_peer_t = -1;
     m.lookahead = kLookaheadDefault;
     if (slot_layout(d.fmt, d.hidden, d.moe_inter, &m.slot)) return -1;
     trunk_layout(d.hidden, d.moe_inter, d.n_experts, &m.tr);
@@ -854,6 +855,12 @@ int ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *h, int64_t polls) {
 int ds4f_gpu_model_set_lookahead(Ds4fGpuModel *h, int n_experts) {
     DS4F_REQUIRE(h && n_experts >= 0 && n_experts <= 32, "model_set_lookahead: 0 <= n <= 32");
     h->m.lookahead = n_experts;
+    return 0;
+}
+
+int ds4f_gpu_model_inject_peer_stall(Ds4fGpuModel *h, int layer_step) {
+    DS4F_REQUIRE(h, "model_inject_peer_stall: null model");
+    h->m.stall_peer_t = layer_step < 0 ? -1 : layer_step;
     return 0;
 }
 

@@ -195,6 +195,8 @@ struct DecodeArgs {
     long rounds;                // copy rounds of a tagged-word gather before giving up
     int stall_cta, stall_t;     // test hook: this CTA withholds its state words
                                 // at this layer-step (-1: off)
+    int stall_peer_t;           // test hook (several GPUs): no down rows stored to the
+                                // other GPUs at this layer-step (-1: off)
     int lookahead;              // L2 prefetch of the next layer's predicted experts
     // expert parallelism: this GPU's pool holds experts [efirst, efirst +
     // ecount) of every layer; world > 1: every rank's [2][K][H] tagged
@@ -1110,7 +1112,7 @@ k_decode(DecodeArgs a) {
                         // stores into its memory; the others' arrive in ours
                         const int64_t par = (int64_t)((a.par0 + t) & 1) * K * H;
                         for (int p = 0; p < a.world; p++)
-                            if (p != a.rank)
+                            if (p != a.rank && t != a.stall_peer_t)
                                 st_tag_sys(a.pout[p] + par + jw * H + r0 + rw0 + slot, tg, __float_as_uint(z));
                     }
                 }
@@ -1210,6 +1212,7 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st, const DecodeP
     a.rounds = std::max(16L, a.spin / 16);
     a.stall_cta = m->stall_cta;
     a.stall_t = m->stall_t;
+    a.stall_peer_t = m->stall_peer_t;
     a.lookahead = m->lookahead;
     DS4F_CUDA(cudaMemsetAsync(m->w.diag + 2, 0, 2 * sizeof(unsigned), st));
     // tags carry 16 bits of layer-step: split long runs into launches

@@ -80,6 +80,7 @@ struct Model {
     int epoch;                   // last persistent launch's tag epoch
     int64_t wait_limit;          // persistent kernel: polls before a wait gives up (0: default)
     int stall_cta, stall_t;      // test hook of the persistent kernel (-1: off)
+    int stall_peer_t;            // test hook of the fused multi-GPU step (-1: off)
     int lookahead;               // persistent kernel: experts of the next layer predicted and
                                  // prefetched into L2 per layer (0: off)
     int *log_idx;                // route log of the persistent kernel (log_n layer-steps

@@ -91,6 +91,7 @@ def lib():
             "ds4f_gpu_model_set_wait_limit": [_vp, C.c_int64],
             "ds4f_gpu_model_set_lookahead": [_vp, C.c_int],
             "ds4f_gpu_model_inject_stall": [_vp, C.c_int, C.c_int],
+            "ds4f_gpu_model_inject_peer_stall": [_vp, C.c_int],
             "ds4f_gpu_model_route_log": [_vp, C.c_int],
             "ds4f_gpu_model_route_log_read": [_vp, _vp, _vp, _vp, C.c_int],
             "ds4f_gpu_synth_f32": [_vp, C.c_int64, C.c_uint64, C.c_uint32, C.c_uint32,
@@ -416,6 +417,11 @@ class Model:
         """Persistent decode: predicted experts of the next layer prefetched
         into L2 per layer (0: off). Results do not depend on it."""
         check(lib().ds4f_gpu_model_set_lookahead(self.h, n_experts))
+
+    def inject_peer_stall(self, layer_step):
+        """Test hook of the fused multi-GPU step: no down rows stored to the
+        other GPUs at layer_step (< 0: off)."""
+        check(lib().ds4f_gpu_model_inject_peer_stall(self.h, layer_step))
 
     def inject_stall(self, cta, layer_step):
         """Test hook: CTA `cta` withholds its state words at `layer_step` (cta < 0: off)."""

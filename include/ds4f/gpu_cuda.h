@@ -350,6 +350,13 @@ int  ds4f_gpu_model_set_lookahead(Ds4fGpuModel *m, int n_experts);
  * cta < 0 turns it off. Nothing faults: the missing words are never
  * written, and every wait for them is bounded. */
 int  ds4f_gpu_model_inject_stall(Ds4fGpuModel *m, int cta, int layer_step);
+/* The same for the fused multi-GPU step (ds4f_gpu_ep_stack_dev): in the
+ * following launches this rank stores none of its down rows to the other
+ * GPUs at layer-step `layer_step`, as a stalled GPU would not; the others'
+ * bounded waits for them run out and their calls return -1 with code 11,
+ * then this rank's own waits for the next layer's rows of the GPUs that gave
+ * up do too. layer_step < 0 turns it off. */
+int  ds4f_gpu_model_inject_peer_stall(Ds4fGpuModel *m, int layer_step);
 
 /* ---- allocation-free layer step ------------------------------------- */
 

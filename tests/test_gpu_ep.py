@@ -225,3 +225,62 @@ def test_token_parallel_prefill_two_gpus(fmt):
     got = np.concatenate([out[0], out[1]])
     err = np.abs(got - want).max() / np.abs(want - x0).max()
     assert err < REASSOC_TOL, err
+
+
+# ---- failure detection of the fused step (no GPU fault) ----------------------
+
+def _rank_stall(rank, world, port, fmt, out):
+    """Rank 1 withholds its down rows at layer-step 2 of a 2-step launch
+    (6 layer-steps): rank 0's bounded wait for them runs out (code 11), then
+    rank 1's wait for rank 0's rows of layer-step 3. Both calls return -1
+    within the limit's time; the next launch, hook off, gives the clean bits."""
+    import time
+    import torch
+    dc, dist = _init(rank, world, port)
+    ep = _ep_module()
+    shard = ep.GpuShard(dc, fmt, NL, H, M, E, K, rank, world, seed=21)
+    shard.attach()
+    assert shard.model.ep_fused_ready()
+    sp = torch.cuda.current_stream().cuda_stream
+    st = torch.from_numpy(_x0(1)).cuda()
+    shard.model.set_wait_limit(1 << 14)
+    if rank == 1:
+        shard.model.inject_peer_stall(2)
+    dist.barrier()
+    t0 = time.time()
+    try:
+        shard.decode(st, 2, sp)              # enqueued; the kernel's error word is read next
+        torch.cuda.synchronize()
+        shard.model.stats()
+        out[f"err{rank}"] = ""
+    except dc.GpuError as e:
+        out[f"err{rank}"] = str(e)
+    out[f"secs{rank}"] = time.time() - t0
+    shard.model.inject_peer_stall(-1)
+    shard.model.set_wait_limit(0)
+    dist.barrier()
+    st = torch.from_numpy(_x0(1)).cuda()
+    shard.decode(st, 1, sp)
+    shard.decode(st, 2, sp)
+    torch.cuda.synchronize()
+    out[rank] = st.cpu().numpy()
+    shard.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_ngpu() < 2, reason="needs 2 GPUs")
+def test_fused_peer_stall_times_out_and_recovers():
+    out = _spawn(_rank_stall, lambda r, port, out: (r, 2, port, 2, out))
+    for r in (0, 1):
+        assert "gave up waiting (code 11" in out[f"err{r}"], out[f"err{r}"]
+        assert out[f"secs{r}"] < 10.0
+    assert np.array_equal(out[0], out[1])
+    dc = ds4f_cuda()
+    dc.init()
+    full = dc.Model(2, NL, H, M, E, K)
+    full.synth(21)
+    full.set_path(dc.PATH_PERSISTENT)
+    want = full.stack(_x0(1)[0], 3)
+    full.close()
+    assert np.array_equal(out[0][0].view(np.uint32), want.view(np.uint32))
