@@ -354,8 +354,7 @@ def decode_config(fp8, world, layers=LAYERS, parallelism=None):
             "parallelism": parallelism or ("single GPU" if world == 1 else f"replicas x{world}")}
 
 
-N_STAMPS = 28          # phase-trace stamp slots per (layer-step, CTA) in k_decode
-LOOKAHEAD_DEFAULT = 0   # the library's default expert lookahead (experts prefetched ahead)
+N_STAMPS = 32          # phase-trace stamp slots per (layer-step, CTA) in k_decode
 PHASES = ["start", "state", "norm", "rows_done", "routes_vis", "topk", "issued",
           "softmax", "grp0", "chains", "down_in", "written"]
 
@@ -378,8 +377,9 @@ def phase_table(tr, ep=False):
     for k, name in enumerate(["down: chain gather", "down: row-dots", "down: combine"]):
         rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
                      float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
-    inner = np.diff(tr[:, :, [3, 18, 4]], axis=2)
-    for k, name in enumerate(["routes: gather", "routes: top-K"]):
+    inner = np.diff(tr[:, :, [3, 18, 27, 28, 29, 30, 31, 4]], axis=2)
+    for k, name in enumerate(["routes: gather", "routes: keys", "routes: top-8 network", "routes: certificate",
+                              "routes: byte counts", "routes: group 0 issue", "routes: to barrier"]):
         rows.append((name, float(np.median(inner[:, :, k]) / 1e3),
                      float(np.median(np.max(inner[:, :, k], axis=1)) / 1e3)))
     # gate/up: groups landing and dots finishing, as offsets from the softmax
@@ -434,8 +434,6 @@ def run_gpu(args, rank, world, local_rank):
     model = dc.Model(dc.FMT_FP8 if fp8 else dc.FMT_MXFP4, layers, H, M, E, K)
     model.synth(0)
     model.set_path(dc.PATH_LAYERED if args.layered else dc.PATH_PERSISTENT)
-    if args.lookahead is not None:
-        model.set_lookahead(args.lookahead)
     state = torch.empty(H, dtype=torch.float32, device="cuda")
     dc.synth_f32_dev(state, H, 0, 0, 4, rank, 0, 1.0)
     torch.cuda.synchronize()
@@ -516,7 +514,6 @@ def run_gpu(args, rank, world, local_rank):
                     "timer": "host clock around the synchronous C-ABI call"},
             "gpu_launches": (4 * layers if args.layered else 1) * args.steps,
             "router_exact_fallbacks": int(fallbacks),
-            "expert_lookahead": LOOKAHEAD_DEFAULT if args.lookahead is None else args.lookahead,
             "clocks": clocks,
         }
         if trace is not None:
@@ -1223,8 +1220,6 @@ def main():
     ap.add_argument("--ep-layered", action="store_true",
                     help="ep-decode / N > 1: the per-layer kernels with an NCCL all-reduce per layer instead of "
                          "the fused persistent launch")
-    ap.add_argument("--lookahead", type=int, default=None,
-                    help="decode: experts of the next layer prefetched into L2 (0: off; default: the library's)")
     ap.add_argument("--trace-dump", default=None,
                     help="N > 1 decode with --trace: save each rank's raw stamps to <prefix>.r<rank>.npy")
     ap.add_argument("--trace", action="store_true",

@@ -403,7 +403,6 @@ static int model_create_impl(const Ds4fGpuModelDesc *desc, int64_t pool_slots, D
     m.d = d;
     m.stall_cta = m.stall_t = -1;
     m.stall_peer_t = -1;
-    m.lookahead = kLookaheadDefault;
     if (slot_layout(d.fmt, d.hidden, d.moe_inter, &m.slot)) return -1;
     trunk_layout(d.hidden, d.moe_inter, d.n_experts, &m.tr);
     DS4F_CUDA(cudaGetDevice(&m.device));
@@ -416,7 +415,7 @@ static int model_create_impl(const Ds4fGpuModelDesc *desc, int64_t pool_slots, D
     size_t ws_b = al256(H * 4) + al256(E * 8) * 2 + al256(K * 4) * 2 +
                   al256((size_t)(K + 1) * M * 4) + al256(4) + al256(H * 4) + al256(16) +
                   al256((size_t)m.bmax * H * 4) + al256((size_t)m.bmax * K * 4) * 2 +
-                  al256((size_t)H * 8) + al256((size_t)E * 32) + al256(((size_t)(K + 1) * M + 2 + E) * 8);
+                  al256((size_t)H * 8) + al256((size_t)E * 32) + al256(((size_t)(K + 1) * M + 2) * 8);
     // memory plan first (invariant 5 of the reference, ds4f.h:32-35 /
     // mem.c): refuse past 95% of free device memory, allocate nothing.
     size_t fre = 0, tot = 0;
@@ -447,7 +446,7 @@ static int model_create_impl(const Ds4fGpuModelDesc *desc, int64_t pool_slots, D
     m.w_dev = (float *)take((size_t)m.bmax * K * 4);
     m.w.st_ll = (uint64_t *)take((size_t)H * 8);
     m.w.sb_ll = (uint64_t *)take((size_t)E * 32);
-    m.w.ch_ll = (uint64_t *)take(((size_t)(K + 1) * M + 2 + E) * 8);   // + pad word + lookahead
+    m.w.ch_ll = (uint64_t *)take(((size_t)(K + 1) * M + 2) * 8);   // + pad word
     if ((size_t)(p - (uint8_t *)m.ws_base) != ws_b) {       // the size above and the layout agree
         cudaFree(m.pool); cudaFree(m.trunk); cudaFree(m.ws_base);
         set_error("model: workspace layout (%zu bytes) differs from its size (%zu)",
@@ -849,12 +848,6 @@ int ds4f_gpu_model_trace_read(const Ds4fGpuModel *h, uint64_t *out, int64_t n_st
 int ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *h, int64_t polls) {
     DS4F_REQUIRE(h && polls >= 0, "model_set_wait_limit: bad arguments");
     h->m.wait_limit = polls;
-    return 0;
-}
-
-int ds4f_gpu_model_set_lookahead(Ds4fGpuModel *h, int n_experts) {
-    DS4F_REQUIRE(h && n_experts >= 0 && n_experts <= 32, "model_set_lookahead: 0 <= n <= 32");
-    h->m.lookahead = n_experts;
     return 0;
 }
 

@@ -62,11 +62,6 @@ struct SmemOptIn {
 __device__ __forceinline__ float bf16_to_f32(uint16_t h) {
     return __uint_as_float((uint32_t)h << 16);
 }
-// fp32 -> bf16 bits, round to nearest even (finite inputs; a hint's precision)
-__device__ __forceinline__ uint16_t bf16_bits_rn(float f) {
-    const uint32_t u = __float_as_uint(f);
-    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
-}
 
 // E8M0 scale 2^(b-127) built from bits: b >= 1 is a normal float with
 // exponent field b; b = 0 is the subnormal 2^-127 (mantissa bit 22); b =

@@ -43,7 +43,7 @@ constexpr int kGroupPairs = 8;             // gate/up pairs per copy group
 constexpr int kGroups = 4;
 constexpr long kSpin = 1L << 24;           // default polls (with backoff) before giving up
 constexpr double kU = 5.9604644775390625e-08;
-constexpr int kTracePts = 28;
+constexpr int kTracePts = 32;
 constexpr int kMaxRanks = 8;
 
 // ---- PTX helpers ------------------------------------------------------------
@@ -69,11 +69,6 @@ __device__ __forceinline__ void bulk(void *dst, const void *src, uint32_t bytes,
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(sa(dst)), "l"(src), "r"(bytes), "r"(sa(b)) : "memory");
-}
-// L2 prefetch of a global range (16-byte aligned address and size): no
-// shared memory, no barrier; the lines are simply warm when a copy comes.
-__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void fence_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -131,6 +126,36 @@ struct Shape {
     static_assert(cpl % 8 == 0, "router rows: whole 8-element chunks per lane");
 };
 
+// The exact fallback's selection, out of line (rarely run, so kept out of
+// the layer loop's instruction stream): every candidate's logit in the
+// reference's sequential order (src/kernels.c:97-102), one thread each,
+// then the top K among the candidates -- or, when a logit is not finite,
+// the reference's insertion rule over every expert. CTA-wide.
+template <int H, int E, int K>
+__device__ __noinline__ void exact_select(const uint16_t *router, const float *xin, const int *candf, double *tk,
+                                          int *sel, bool nonfin) {
+    const int tid = threadIdx.x;
+    for (int e = tid; e < E; e += kThreads) {
+        if (!candf[e]) continue;
+        const uint16_t *row = router + (int64_t)e * H;
+        float acc = 0.0f;
+        for (int cc = 0; cc < H; cc++) acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(__ldg(row + cc)), xin[cc]));
+        tk[e] = (double)acc;
+    }
+    __syncthreads();
+    if (nonfin) {
+        if (tid == 0) tk_insertion(tk, E, K, sel);
+    } else {
+        for (int e = tid; e < E; e += kThreads) {
+            if (!candf[e]) continue;
+            int r = 0;
+            const double ve = tk[e];
+            for (int f = 0; f < E; f++) r += candf[f] && (tk[f] > ve || (tk[f] == ve && f < e));
+            if (r < K) sel[r] = e;
+        }
+    }
+}
+
 template <int FMT, int H, int M, int E, int K>
 struct Smem {
     using S = Shape<FMT, H, M>;
@@ -153,11 +178,10 @@ struct Smem {
     static constexpr int o_dsc = o_dn + a16(K * RR * S::drow_b);
     // gate rows then up rows; between uses it receives the tagged-word
     // gathers (state, router logits, chains)
-    // (the chain gather: (K+1) M chain words, the shared-gate logit, a pad
-    // word, then E lookahead logits of the next layer)
+    // (the chain gather: (K+1) M chain words, the shared-gate logit and a
+    // pad word)
     static constexpr int NCWP = (K + 1) * M + 2;
-    static constexpr int GATH = 8 * ((H > 4 * E ? H : 4 * E) > NCWP + E
-                                         ? (H > 4 * E ? H : 4 * E) : NCWP + E);
+    static constexpr int GATH = 8 * ((H > 4 * E ? H : 4 * E) > NCWP ? (H > 4 * E ? H : 4 * E) : NCWP);
     // + the chains unpacked to floats after the tagged words
     static constexpr int UNP = GATH + 4 * ((K + 1) * M + 4);
     // + the next layer's shared gate/up rows and the shared-gate row, past
@@ -178,8 +202,7 @@ struct Smem {
     static constexpr int o_tk = o_red + 1024;                         // [E] doubles
     static constexpr int o_cand = o_tk + a16(E * 8);                  // [E] ints
     static constexpr int o_sel = o_cand + a16(E * 4);                 // sel[64], wsel[64], ctl[16]
-    static constexpr int o_xr = a16(o_sel + 64 * 4 + 64 * 4 + 16 * 4); // [H] bf16 x / r (lookahead)
-    static constexpr int bytes = o_xr + H * 2;
+    static constexpr int bytes = o_sel + 64 * 4 + 64 * 4 + 16 * 4;
 };
 
 struct DecodeArgs {
@@ -197,7 +220,6 @@ struct DecodeArgs {
                                 // at this layer-step (-1: off)
     int stall_peer_t;           // test hook (several GPUs): no down rows stored to the
                                 // other GPUs at this layer-step (-1: off)
-    int lookahead;              // L2 prefetch of the next layer's predicted experts
     // expert parallelism: this GPU's pool holds experts [efirst, efirst +
     // ecount) of every layer; world > 1: every rank's [2][K][H] tagged
     // down-output words (pout[rank] is this GPU's, the others peer mappings)
@@ -210,8 +232,7 @@ struct DecodeArgs {
     float *state;               // [H] in (read at layer 0) / out (last layer)
     uint64_t *st_ll;            // [H] tagged state words
     uint64_t *sb_ll;            // [E][4] tagged words: S, its interval's ends (fp32), 0
-    uint64_t *ch_ll;            // [(K+1) M + 2 + E] tagged chains, the shared-gate logit, a
-                                // pad word, the next layer's lookahead logits
+    uint64_t *ch_ll;            // [(K+1) M + 2] tagged chains, the shared-gate logit, a pad word
     unsigned *diag;             // [4]: layers, fallbacks, error code, failing CTA
     unsigned long long *trace;  // optional [T][G][kTracePts] %globaltimer stamps
     int *log_idx;               // optional route log, layer-steps t < log_n:
@@ -299,7 +320,10 @@ __device__ bool gather_ll(const DecodeArgs &a, uint64_t *bar, uint32_t &phb, uin
 
 // EP: this GPU holds a shard of every layer's experts and exchanges the
 // down outputs with the other GPUs (world > 1); false: the whole pool here.
-template <int FMT, int H, int M, int E, int K, bool EP>
+// TR: record the phase trace. A separate instance: a layer's code does not
+// fit in the instruction cache, and the ~30 stamps' code alone, branched
+// over, cost 3.7 % of the step (1,343 vs 1,393 tok/s measured).
+template <int FMT, int H, int M, int E, int K, bool EP, bool TR>
 __global__ void __launch_bounds__(kThreads, 1)
 k_decode(DecodeArgs a) {
     using S = Shape<FMT, H, M>;
@@ -325,7 +349,6 @@ k_decode(DecodeArgs a) {
     float *wsel = (float *)(sel + 64);
     int *ctl = (int *)(wsel + 64);
     int *locs = ctl + 8;      // the selections held here, in selection order (ctl[4]: count, ctl[5]: mask)
-    uint16_t *xr16 = (uint16_t *)(sm + L::o_xr);      // x / r as bf16 (the lookahead's input)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, c = blockIdx.x;
@@ -352,7 +375,6 @@ k_decode(DecodeArgs a) {
 #define FLIP(i) (phb ^= 1u << (i))
 #define PEND(i, v) (pendb = (v) ? (pendb | (1u << (i))) : (pendb & ~(1u << (i))))
     bool ok = true;
-    bool rt_early = false;      // bar 0 (this layer's router rows) consumed by the lookahead
 
     if (tid == 0) {
         for (int i = 0; i < 9; i++) mbar_init(bar + i, 1);
@@ -472,12 +494,11 @@ k_decode(DecodeArgs a) {
 
     const int T = a.n_layers * a.n_steps;
 #define DS4F_TRACE(k) \
-    if (a.trace && tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + (k)] = gtimer()
-#define DS4F_ROUNDS(k) (a.trace ? a.trace + ((int64_t)t * G + c) * kTracePts + (k) : nullptr)
+    if constexpr (TR) { if (tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + (k)] = gtimer(); }
+#define DS4F_ROUNDS(k) (TR ? a.trace + ((int64_t)t * G + c) * kTracePts + (k) : nullptr)
     for (int t = 0; t < T; t++) {
         const int l = t % a.n_layers, ln = (t + 1) % a.n_layers;
         const bool more = t + 1 < T;
-        const bool pred = a.lookahead > 0 && more;   // this layer predicts the next one's experts
         const uint32_t tg = tag_of(t);            // words this layer publishes
         DS4F_TRACE(0);
         // (A) input state: PER words per thread
@@ -520,16 +541,12 @@ k_decode(DecodeArgs a) {
                 rd[16] = s2;
             }
             // (B) norm weights arrive with the router rows (bar 0)
-            bool okb = rt_early || mbar_wait(a, bar + 0, PH(0), 2);
+            bool okb = mbar_wait(a, bar + 0, PH(0), 2);
             if (!__syncthreads_and(okb)) { ok = false; break; }
-            if (!rt_early) { FLIP(0); PEND(0, false); }
-            rt_early = false;
+            FLIP(0); PEND(0, false);
             float r = __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(rd[16], (double)H)), 1e-6f));
-            for (int i = tid; i < H; i += kThreads) {
-                const float xq = __fdiv_rn(xin[i], r);
-                if (pred) xr16[i] = bf16_bits_rn(xq);
-                xin[i] = __fmul_rn(xq, bf16_to_f32(nw[i]));
-            }
+            for (int i = tid; i < H; i += kThreads)
+                xin[i] = __fmul_rn(__fdiv_rn(xin[i], r), bf16_to_f32(nw[i]));
             __syncthreads();
         }
         DS4F_TRACE(2);
@@ -599,12 +616,7 @@ k_decode(DecodeArgs a) {
             }
         }
         DS4F_TRACE(3);
-        // the first copy of the router-logit gather flies while the shared
-        // expert's rows are computed (its words land in the gathers' region,
-        // clear of the shared rows; the last reads of that region, the state
-        // words, were ordered by the barriers of (B))
         static_assert(E % 32 == 0 && (4 * E * 8) % 16 == 0, "router width: whole warps of experts");
-        gather_issue(bar + 7, pendb, (uint64_t *)gu, a.sb_ll, 4 * E);
         // (D) shared gate (even) / up (odd) rows and, CTA 0 warp 15, the
         //     shared-gate row: prefetched into shared memory (bar 8)
         if (warp < 2 * nsg || (warp == kWarps - 1 && c == 0)) {
@@ -630,6 +642,14 @@ k_decode(DecodeArgs a) {
         }
         FLIP(8);
         PEND(8, false);
+        // the router-logit gather's first copy goes out only now: issued
+        // before the shared rows (to fly while they are computed) it landed
+        // before most CTAs' words were visible and nearly always needed a
+        // second round (1.95 vs 1.38 rounds; 1,318 -> 1,341 tok/s). Its words
+        // land in the gathers' region, clear of the shared rows; the last
+        // reads of that region, the state words, were ordered by the
+        // barriers of (B).
+        gather_issue(bar + 7, pendb, (uint64_t *)gu, a.sb_ll, 4 * E);
         // (F) routing: gather every S/B word, then warp 0 takes the
         //     certified top-K
         if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.sb_ll, 4 * E, 4 * E, tg, 3,
@@ -665,8 +685,10 @@ k_decode(DecodeArgs a) {
             // insertion rule (tk_insertion) in the fallback below
             const bool nonfin = !__all_sync(0xFFFFFFFFu, fin);
             if (lane == 0) { ctl[3] = 1; ctl[1] = 0; ctl[2] = nonfin ? 1 : 0; }
+            DS4F_TRACE(27);
             tk_sort8(k8);
             tk_warp_top8(k8);
+            DS4F_TRACE(28);
             // lane r < 8: the r-th selection's interval
             int er = 0;
 #pragma unroll
@@ -697,6 +719,7 @@ k_decode(DecodeArgs a) {
             }
             const int nreach = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)nmine);
             const bool cert = !a.exact_all && !nonfin && __all_sync(0xFFFFFFFFu, sep) && nreach == K;
+            DS4F_TRACE(29);
             if (cert && lane < K) sel[lane] = er;
             if (lane == 0) ctl[1] = cert ? 1 : 0;
             if (cert) {
@@ -710,7 +733,9 @@ k_decode(DecodeArgs a) {
                 if (lane < kGroups) expect_groups(lane);
                 if (lane == kGroups) mbar_expect(bar + 6, (EP ? nloc : K) * dn_sel);
                 __syncwarp();
+                DS4F_TRACE(30);
                 if (lane < 8) { fence_async(); issue_group_copy(l, lane); }
+                DS4F_TRACE(31);
             }
         }
         // ctl[] is read after the barrier (a __syncthreads_and predicate
@@ -722,29 +747,7 @@ k_decode(DecodeArgs a) {
             st_tag(a.ch_ll + K * M + sg0 + tid, tg,
                    __float_as_uint(silu_mul(red[192 + 2 * tid], red[192 + 2 * tid + 1])));
         if (!ctl[1]) {
-            // exact reference-order logits (src/kernels.c:97-102) of every
-            // candidate, one thread each, then select on them
-            const uint16_t *router = trunk_l(l) + a.tr.router;
-            for (int e = tid; e < E; e += kThreads) {
-                if (!candf[e]) continue;
-                const uint16_t *row = router + (int64_t)e * H;
-                float acc = 0.0f;
-                for (int cc = 0; cc < H; cc++)
-                    acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(__ldg(row + cc)), xin[cc]));
-                tk[e] = (double)acc;
-            }
-            __syncthreads();
-            if (ctl[2]) {
-                if (tid == 0) tk_insertion(tk, E, K, sel);
-            } else {
-                for (int e = tid; e < E; e += kThreads) {
-                    if (!candf[e]) continue;
-                    int r = 0;
-                    const double ve = tk[e];
-                    for (int f = 0; f < E; f++) r += candf[f] && (tk[f] > ve || (tk[f] == ve && f < e));
-                    if (r < K) sel[r] = e;
-                }
-            }
+            exact_select<H, E, K>(trunk_l(l) + a.tr.router, xin, candf, tk, sel, ctl[2] != 0);
             if (tid == 0 && !a.exact_all && c == 0) atomicAdd(a.diag + 1, 1u);
             __syncthreads();
             if (warp == 0) {
@@ -829,16 +832,15 @@ k_decode(DecodeArgs a) {
             }
         }
         DS4F_TRACE(7);
-        bool okla = true;
         // (H) gate/up: warp w -> pair w % 8 of every group, gate and up
         //     rows over column half w / 8 (the two halves meet in red[]);
         //     each warp takes a group as soon as it has landed (its own wait,
         //     no block barrier)
         {
             unsigned landed = 0;
-            if (a.trace && tid == 0)
+            if (TR && tid == 0)
                 for (int g = 0; g < ngroups; g++) landed |= (unsigned)mbar_test(bar + 2 + g, PH(2 + g)) << g;
-            if (a.trace && tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + 17] = landed;
+            if (TR && tid == 0) a.trace[((int64_t)t * G + c) * kTracePts + 17] = landed;
             const int ps = warp & 7;
             bool okg = true;
 #pragma unroll 1
@@ -915,48 +917,11 @@ k_decode(DecodeArgs a) {
                                                 red[2 * tid + 1] + red[HALF + 2 * tid + 1])));
                 publish_flush();
             }
-            // lookahead (a prefetch hint, never a routing input): this CTA's
-            // router rows of the next layer, landed on bar 0 with their norm
-            // weights, on this layer's x / r (bf16) -- warps 1 .. nrt one row
-            // each, fp32 sums, published beside the chains
-            if (pred) {
-                // (warp 1 waits even without a router row: the norm weights
-                // ride on bar 0 too, and the next layer skips its wait)
-                if (warp >= 1 && warp <= max(nrt, 1)) {
-                    okla = mbar_wait(a, bar + 0, PH(0), 2);
-                    if (okla && warp <= nrt) {
-                        const uint16_t *row = rt + (warp - 1) * H;
-                        float acc = 0.f;
-                        static_assert(H % 256 == 0, "lookahead rows: whole 8-element chunks per lane");
-#pragma unroll
-                        for (int k = lane; k < H / 8; k += 32) {
-                            const uint4 w8 = lds16(row + 8 * k), x8 = lds16(xr16 + 8 * k), n8 = lds16(nw + 8 * k);
-                            auto dot2 = [](uint32_t w, uint32_t x, uint32_t n, float acc) {
-                                acc = fmaf(__uint_as_float(w << 16),
-                                           __uint_as_float(x << 16) * __uint_as_float(n << 16), acc);
-                                return fmaf(__uint_as_float(w & 0xFFFF0000u),
-                                            __uint_as_float(x & 0xFFFF0000u) * __uint_as_float(n & 0xFFFF0000u), acc);
-                            };
-                            acc = dot2(w8.x, x8.x, n8.x, acc);
-                            acc = dot2(w8.y, x8.y, n8.y, acc);
-                            acc = dot2(w8.z, x8.z, n8.z, acc);
-                            acc = dot2(w8.w, x8.w, n8.w, acc);
-                        }
-                        acc = warp_sum(acc);
-                        if (lane == 0) {
-                            st_tag(a.ch_ll + L::NCWP + rt0 + warp - 1, tg, __float_as_uint(acc));
-                            publish_flush();
-                        }
-                    }
-                }
-                FLIP(0); PEND(0, false);
-                rt_early = true;
-            }
         }
         DS4F_TRACE(9);
         // (I) down rows: routed (bar 6) and shared (bar 1); chains polled
         {
-            const bool okd = okla && mbar_wait(a, bar + 6, PH(6), 6) && mbar_wait(a, bar + 1, PH(1), 7);
+            const bool okd = mbar_wait(a, bar + 6, PH(6), 6) && mbar_wait(a, bar + 1, PH(1), 7);
             if (!__syncthreads_and(okd)) { ok = false; break; }
             FLIP(6); PEND(6, false);
             FLIP(1); PEND(1, false);
@@ -965,14 +930,11 @@ k_decode(DecodeArgs a) {
             // into shared memory, over the gate/up rows (H) is done with
             // (K+1) M chain words + the logit, copied as an even count (the
             // workspace allocation is padded past the last word)
-            // With the lookahead, also the pad word and the next layer's E
-            // lookahead logits.
             constexpr int NCW = (K + 1) * M + 1;
-            static_assert(L::NCWP == NCW + 1 && L::NCWP % 2 == 0 && E % 2 == 0, "even gathers");
+            static_assert(L::NCWP == NCW + 1 && L::NCWP % 2 == 0, "even gathers");
             static_assert((M & (M - 1)) == 0, "chain words of selection j: j << log2 M ..");
             constexpr int MSH = __builtin_ctz(M);
-            if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.ch_ll, pred ? L::NCWP + E : L::NCWP,
-                           pred ? L::NCWP + E : NCW, tg, 5, DS4F_ROUNDS(16), false, EP ? K * M : 0, MSH, lmask)) {
+            if (!gather_ll(a, bar + 7, phb, pendb, (uint64_t *)gu, a.ch_ll, L::NCWP, NCW, tg, 5, DS4F_ROUNDS(16), false, EP ? K * M : 0, MSH, lmask)) {
                 ok = false;
                 break;
             }
@@ -985,41 +947,8 @@ k_decode(DecodeArgs a) {
                     chf[i] = i < K * M ? v * DS4F_X_PRESCALE : v;
                 }
             }
-            // lookahead: the maxima of 32 groups of E / 32 experts
-            uint32_t *gmax = (uint32_t *)(red + 224);
-            constexpr int LG = E / 32;
-            static_assert(E % 32 == 0 && (LG & (LG - 1)) == 0 && E <= 256, "32 lookahead groups");
-            uint32_t lkey = 0u;
-            if (pred && tid < E) {
-                lkey = tk_key(__uint_as_float((uint32_t)((const uint64_t *)gu)[L::NCWP + tid]), tid);
-                const unsigned gm = LG == 32 ? 0xFFFFFFFFu : (((1u << LG) - 1u) << (lane & ~(LG - 1)));
-                const uint32_t mx = __reduce_max_sync(gm, lkey);
-                if ((lane & (LG - 1)) == 0) gmax[tid / LG] = mx;
-            }
             __syncthreads();
             DS4F_TRACE(12);
-            // lookahead: the a.lookahead-th largest group maximum bounds the
-            // next layer's predicted top-a.lookahead from below; every expert
-            // at or above it gets this CTA's 1/G of its slot prefetched into
-            // L2, where the next layer's copies of it will find it (HBM idles
-            // from here to the next layer's routing)
-            if (pred && tid < E) {
-                uint32_t v = gmax[lane];
-#pragma unroll
-                for (int k = 2; k <= 32; k <<= 1)
-#pragma unroll
-                    for (int j = k >> 1; j > 0; j >>= 1) {
-                        const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, v, j);
-                        v = (((lane & k) == 0) == ((lane & j) == 0)) ? max(v, o) : min(v, o);
-                    }
-                const uint32_t tau = __shfl_sync(0xFFFFFFFFu, v, min(a.lookahead, 32) - 1);
-                if (lkey >= tau && (!EP || (tid >= a.efirst && tid < a.efirst + a.ecount))) {
-                    const int64_t sb = a.slot_bytes;
-                    const int64_t o0 = ((int64_t)c * sb / G) & ~(int64_t)15;
-                    const int64_t o1 = (c == G - 1 ? sb : (int64_t)(c + 1) * sb / G) & ~(int64_t)15;
-                    if (o1 > o0) prefetch_l2(expert(ln, tid) + o0, (uint32_t)(o1 - o0));
-                }
-            }
             // row-dots: warp w takes up to 8 of the CTA's output rows of
             // routed selection w / 2 (rows [(w & 1) hr, ...), hr = ceil(nr / 2))
             // and shared-expert row w. Lane l reads granules 32 g + l of each
@@ -1176,10 +1105,11 @@ template <int FMT, int H, int M, int E, int K>
 int launch_t(Model *m, float *state, int n_steps, cudaStream_t st, const DecodePeers *pe) {
     using L = Smem<FMT, H, M, E, K>;
     static_assert(L::bytes <= 227 * 1024, "decode kernel shared memory over budget");
-    static SmemOptIn opt, opt_ep;
+    static SmemOptIn opt[4];
     const bool ep = pe && pe->world > 1;
-    auto kern = ep ? k_decode<FMT, H, M, E, K, true> : k_decode<FMT, H, M, E, K, false>;
-    if ((ep ? opt_ep : opt).set(kern, L::bytes)) return -1;
+    decltype(&k_decode<FMT, H, M, E, K, false, false>) kerns[4] = {
+        k_decode<FMT, H, M, E, K, false, false>, k_decode<FMT, H, M, E, K, true, false>,
+        k_decode<FMT, H, M, E, K, false, true>, k_decode<FMT, H, M, E, K, true, true>};
     int dev = 0, sms = 0;
     DS4F_CUDA(cudaGetDevice(&dev));
     DS4F_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1213,7 +1143,6 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st, const DecodeP
     a.stall_cta = m->stall_cta;
     a.stall_t = m->stall_t;
     a.stall_peer_t = m->stall_peer_t;
-    a.lookahead = m->lookahead;
     DS4F_CUDA(cudaMemsetAsync(m->w.diag + 2, 0, 2 * sizeof(unsigned), st));
     // tags carry 16 bits of layer-step: split long runs into launches
     const int per = std::max(1, 65000 / m->d.n_layers);
@@ -1231,6 +1160,9 @@ int launch_t(Model *m, float *state, int n_steps, cudaStream_t st, const DecodeP
         a.log_w = a.log_n ? m->log_w + (int64_t)s0 * m->d.n_layers * K : nullptr;
         a.log_state = a.log_n ? m->log_state + (int64_t)s0 * m->d.n_layers * H : nullptr;
         if (m->trace && (int64_t)m->d.n_layers * ns * sms * kTracePts <= m->trace_n) a.trace = m->trace;
+        const int ki = (ep ? 1 : 0) + (a.trace ? 2 : 0);
+        auto kern = kerns[ki];
+        if (opt[ki].set(kern, L::bytes)) return -1;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(sms);
         cfg.blockDim = dim3(kThreads);

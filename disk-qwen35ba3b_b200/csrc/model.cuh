@@ -10,9 +10,6 @@ namespace ds4f {
 
 struct SlotCache;                // stream.cu: the expert-cache policy
 
-constexpr int kLookaheadDefault = 0;     // persistent decode: experts prefetched ahead (off: the
-                                         // gate/up and down phases are bound by the dequant, not HBM)
-
 struct ModelDesc {
     int fmt;              // DS4F_FMT_FP8 or DS4F_FMT_MXFP4 (routed experts)
     int n_layers;
@@ -81,8 +78,6 @@ struct Model {
     int64_t wait_limit;          // persistent kernel: polls before a wait gives up (0: default)
     int stall_cta, stall_t;      // test hook of the persistent kernel (-1: off)
     int stall_peer_t;            // test hook of the fused multi-GPU step (-1: off)
-    int lookahead;               // persistent kernel: experts of the next layer predicted and
-                                 // prefetched into L2 per layer (0: off)
     int *log_idx;                // route log of the persistent kernel (log_n layer-steps
     float *log_w, *log_state;    //   of the next launch): selections, weights, output state
     int log_n;

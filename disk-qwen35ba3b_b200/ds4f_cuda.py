@@ -89,7 +89,6 @@ def lib():
             "ds4f_gpu_ep_prefill": [_vp, _vp, C.c_int, _vp, _vp, _vp],
             "ds4f_ep_plan_dispatch": [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp],
             "ds4f_gpu_model_set_wait_limit": [_vp, C.c_int64],
-            "ds4f_gpu_model_set_lookahead": [_vp, C.c_int],
             "ds4f_gpu_model_inject_stall": [_vp, C.c_int, C.c_int],
             "ds4f_gpu_model_inject_peer_stall": [_vp, C.c_int],
             "ds4f_gpu_model_route_log": [_vp, C.c_int],
@@ -412,11 +411,6 @@ class Model:
     def set_wait_limit(self, polls):
         """Persistent kernel: polls before a bounded wait gives up (0: default)."""
         check(lib().ds4f_gpu_model_set_wait_limit(self.h, polls))
-
-    def set_lookahead(self, n_experts):
-        """Persistent decode: predicted experts of the next layer prefetched
-        into L2 per layer (0: off). Results do not depend on it."""
-        check(lib().ds4f_gpu_model_set_lookahead(self.h, n_experts))
 
     def inject_peer_stall(self, layer_step):
         """Test hook of the fused multi-GPU step: no down rows stored to the

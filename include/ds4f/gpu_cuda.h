@@ -292,8 +292,8 @@ int  ds4f_gpu_moe_layer_partial_dev(Ds4fGpuModel *m, int layer, const float *sta
 int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
 /* Phase trace of the persistent decode kernel (the counterpart of the
  * reference's per-phase timers, src/main.c:253-258, 1522-1546): with
- * n_stamps > 0 every launch whose layers x steps x SMs x 28 stamps fit
- * records %globaltimer (ns) per (layer-step, CTA) in 28 slots, of which
+ * n_stamps > 0 every launch whose layers x steps x SMs x 32 stamps fit
+ * records %globaltimer (ns) per (layer-step, CTA) in 32 slots, of which
  * 0..13 are used: start, state ready, normed, router rows done, routes
  * visible, top-k done, copies issued, softmax done, first gate/up group
  * landed, chains done, down rows landed, state written (11), chains
@@ -303,7 +303,9 @@ int  ds4f_gpu_model_set_path(Ds4fGpuModel *m, int path);
  * word was visible (before the top-k), 21..23 gate/up copy groups 1..3
  * landed, 24 the gate/up dots of warp 0 done, 25 every warp's done, 26 the
  * first down row-dot of warp 0 done; with expert parallelism 19 this GPU's
- * down rows stored to the other GPUs, 20 theirs arrived.
+ * down rows stored to the other GPUs, 20 theirs arrived; 27..31 inside the
+ * top-k (keys read, network done, certificate, byte counts, group 0's
+ * copies issued).
  * n_stamps = 0 turns it off. */
 int  ds4f_gpu_model_trace(Ds4fGpuModel *m, int64_t n_stamps);
 int  ds4f_gpu_model_trace_read(const Ds4fGpuModel *m, uint64_t *out, int64_t n_stamps);
@@ -330,18 +332,6 @@ int  ds4f_gpu_model_stats(const Ds4fGpuModel *m, uint64_t out[2]);
  * ("decode kernel gave up waiting (code C at CTA N)"); the model stays
  * usable. 0 restores the default, 2^24 polls (about a second). */
 int  ds4f_gpu_model_set_wait_limit(Ds4fGpuModel *m, int64_t polls);
-/* Expert lookahead of the persistent decode path (no reference counterpart;
- * the reference reads each expert when its layer routes to it,
- * src/moe.c:598-753): while layer l runs, the next layer's router rows are
- * applied to layer l's normalised state and the experts whose predicted
- * logits reach the n-th largest of 32 group maxima (n or a few more) are
- * prefetched into L2, 1/G of each slot by each CTA, in the stretch where
- * HBM idles (the exchanges, the norm and the router). A hint only: the
- * routing itself is certified on each layer's own state, so results are
- * identical for every n. 0 turns it off (the default: measured on B200,
- * the gate/up phase is bound by the dequantising dot products, not by the
- * bytes' arrival, so the prefetch only adds traffic); n <= 32. */
-int  ds4f_gpu_model_set_lookahead(Ds4fGpuModel *m, int n_experts);
 /* Failure injection for tests (no reference counterpart): in the following
  * persistent launches CTA `cta` does not publish its rows of the state at
  * layer-step `layer_step` of a launch (0 = the first layer of its first

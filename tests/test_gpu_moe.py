@@ -277,32 +277,3 @@ def test_persistent_router_exact_mode():
         st, _, _, _, _ = oracle_layer(m, layer, dc.FMT_MXFP4, st).moe(st, 8)
     assert relerr(got - x, st - x) < CHAIN_TOL
     m.close()
-
-
-@pytest.mark.parametrize("fmt", [dc.FMT_FP8, dc.FMT_MXFP4])
-@pytest.mark.parametrize("shape", [(1024, 256, 64, 5), (2048, 512, 256, 6)])
-def test_persistent_lookahead_is_only_a_hint(fmt, shape):
-    """The expert lookahead prefetches predicted experts of the next layer
-    into L2; the routing stays certified on each layer's own state, so the
-    states and the route log are bit-identical for every setting, including
-    off, one predicted expert and the maximum of 32."""
-    H, M, E, L = shape
-    m = dc.Model(fmt, L, H, M, E, 8)
-    m.synth(43)
-    m.set_path(dc.PATH_PERSISTENT)
-    x0 = po.fill_f32(H, po.key(43, 0, 4, 0, 0), 1.0)
-    n = 3 * L
-    runs = []
-    for look in (0, 1, 10, 32):
-        m.set_lookahead(look)
-        m.route_log(n)
-        got = m.stack(x0, 3)
-        runs.append((got, *m.route_log_read(n)))
-        m.route_log(0)
-    bits = [[np.ascontiguousarray(v).view(np.uint32) for v in r] for r in runs]
-    for r in bits[1:]:
-        for a, b in zip(bits[0], r):
-            assert np.array_equal(a, b)
-    with pytest.raises(dc.GpuError):
-        m.set_lookahead(33)
-    m.close()
