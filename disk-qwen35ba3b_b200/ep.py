@@ -74,6 +74,63 @@ class GpuShard:
         self.model.close()
 
 
+def selection_owner(j, idx, n_experts, world, by_index):
+    """The rank that runs selection j of a token routed to experts idx: the
+    owner of its expert (E / N experts per rank), or, with every expert on
+    every rank, rank r for j in [r K / N, (r + 1) K / N) -- the split of the
+    library's fused one-token step (ds4f_gpu_ep_stack_dev)."""
+    K = len(idx)
+    if by_index:
+        for r in range(world):
+            if r * K // world <= j < (r + 1) * K // world:
+                return r
+        raise ValueError("selection index out of range")
+    return int(idx[j]) // (n_experts // world)
+
+
+class SelectionExchangeDecoder:
+    """The algorithm of the library's fused one-token step over a process
+    group: every rank routes the full state and runs the expert chains of
+    the selections it owns (selection_owner); the ranks exchange those
+    output rows (the kernel stores them into each other's memory; here an
+    all-gather); every rank then combines all K rows in selection order and
+    adds the shared expert and the residual itself -- so every rank holds
+    exactly the single-host result (src/moe.c:1224-1225, 1279-1282, 1424).
+    backend: route(L, state) -> (idx, w, xin), chain(L, e, xin) -> [H]
+    float32, shared_add(L, xin, acc) (acc in place), n_layers, hidden,
+    n_experts."""
+
+    def __init__(self, backend, by_index=False, group=None):
+        self.b = backend
+        self.by_index = by_index
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def step(self, states):
+        """states [B][H] float32 (CPU), updated in place; identical on every
+        rank before and after."""
+        H = self.b.hidden
+        for L in range(self.b.n_layers):
+            for t in range(states.shape[0]):
+                x = states[t].numpy()
+                idx, w, xin = self.b.route(L, x)
+                K = len(idx)
+                mine = torch.zeros((K, H), dtype=torch.float32)
+                for j in range(K):
+                    if selection_owner(j, idx, self.b.n_experts, self.world, self.by_index) == self.rank:
+                        mine[j] = torch.from_numpy(self.b.chain(L, int(idx[j]), xin))
+                rows = [torch.empty_like(mine) for _ in range(self.world)]
+                dist.all_gather(rows, mine, group=self.group)
+                acc = np.zeros(H, np.float32)
+                for j in range(K):
+                    r = selection_owner(j, idx, self.b.n_experts, self.world, self.by_index)
+                    acc = (acc + np.float32(w[j]) * rows[r][j].numpy()).astype(np.float32)
+                self.b.shared_add(L, xin, acc)
+                states[t] = torch.from_numpy((x + acc).astype(np.float32))
+        return states
+
+
 class ExpertParallelDecoder:
     """Decode steps of a token batch over an expert-sharded process group;
     backend.layer_partial(L, states, acc, add_shared) fills acc [B][H]."""

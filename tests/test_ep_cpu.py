@@ -102,6 +102,85 @@ def test_expert_parallel_decode_two_ranks_matches_single_host():
     assert err < TOL, err
 
 
+# ---- the fused one-token step's algorithm: rows exchanged, combined in order --
+
+class OracleSelections:
+    """Backend of ep.SelectionExchangeDecoder from oracle pieces: the
+    oracle's own routing (orc_moe_layer's, so indices and weights carry the
+    same bits), one expert chain, the shared expert add."""
+
+    def __init__(self, layers):
+        self.layers = layers
+        self.n_layers, self.hidden, self.n_experts = len(layers), H, E
+
+    def route(self, L, x):
+        lay = self.layers[L]
+        _, idx, w, _, _ = lay.moe(x, K)
+        xin = np.array(x, np.float32, copy=True)
+        po.lib().orc_rmsnorm(po.ptr(lay.norm), H, po.ptr(xin))
+        return idx, w, xin
+
+    def chain(self, L, e, xin):
+        lay = self.layers[L]
+        out = np.zeros(H, np.float32)
+        po.lib().orc_expert_chain(lay.fmt, po.ptr(lay.experts[e]), po.C.byref(lay.lay), H, M,
+                                  po.ptr(xin), po.ptr(out))
+        return out
+
+    def shared_add(self, L, xin, acc):
+        lw = self.layers[L].w()
+        po.lib().orc_shared_add(po.C.byref(lw), H, M, po.ptr(xin), po.ptr(acc))
+
+
+def _rank_sel(rank, world, port, by_index, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ep = _ep_module()
+    dec = ep.SelectionExchangeDecoder(OracleSelections(_layers()), by_index=by_index)
+    st = torch.from_numpy(po.fill_f32(B * H, po.key(3, 0, 4, 0, 0), 1.0).reshape(B, H).copy())
+    dec.step(st)
+    out[rank] = st.numpy().copy()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("by_index", [False, True], ids=["by-expert-owner", "by-selection-index"])
+def test_selection_exchange_two_ranks_bit_exact(by_index):
+    """Two gloo ranks run the fused step's algorithm (each rank its own
+    selections' chains, the rows exchanged, every row combined in selection
+    order on every rank): both ranks hold exactly the single-host oracle's
+    bits after every layer, with the selections split by expert owner (half
+    of the experts per rank) or by index (every expert on every rank)."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    procs = [ctx.Process(target=_rank_sel, args=(r, 2, port, by_index, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    want = po.fill_f32(B * H, po.key(3, 0, 4, 0, 0), 1.0).reshape(B, H).copy()
+    for lay in _layers():
+        for b in range(B):
+            want[b], _, _, _, _ = lay.moe(want[b], K)
+    for r in (0, 1):
+        assert np.array_equal(out[r].view(np.uint32), want.view(np.uint32))
+
+
+def test_selection_owner():
+    ep = _ep_module()
+    idx = np.array([3, 12, 7, 9, 0, 15, 8, 1])
+    assert [ep.selection_owner(j, idx, 16, 2, False) for j in range(8)] == [0, 1, 0, 1, 0, 1, 1, 0]
+    assert [ep.selection_owner(j, idx, 16, 2, True) for j in range(8)] == [0, 0, 0, 0, 1, 1, 1, 1]
+    assert [ep.selection_owner(j, idx, 16, 3, True) for j in range(8)] == [0, 0, 1, 1, 1, 2, 2, 2]
+    assert [ep.selection_owner(j, idx, 16, 8, True) for j in range(8)] == list(range(8))
+
+
 # ---- token-parallel prefill with all-to-all dispatch / combine ----------------
 
 T_PF = 7                 # tokens per rank (rank 1 holds T_PF - 2: uneven on purpose)
