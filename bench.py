@@ -798,6 +798,13 @@ def run_gpu_ep(args, rank, world, local_rank):
             "gpu_launches": (args.steps if fused else
                              args.steps * layers * ((4 if Bt == 1 else 2 + PREFILL_LAUNCHES_PER_LAYER) + 2)),
             "clocks": clocks,
+            # what bounds this N (measured on 2 x B200, NVLink 5; see the design notes)
+            "limiter": ("one token is latency-bound: per layer the serial chain of one GPU (norm, router, "
+                        "top-8, three on-GPU exchanges) plus one cross-GPU exchange of the down rows "
+                        "(~1 us NVLink store latency + the slower GPU's skew); sharding divides only the "
+                        "gate/up and down work" if fused else
+                        "per layer: 4 kernel launches and one NCCL all-reduce of acc (launch and "
+                        "collective latency, not bytes)"),
         }
         if trace is not None:
             for name, med, mx in trace.pop("phases_us"):
